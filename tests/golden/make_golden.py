@@ -1,0 +1,115 @@
+"""Write the committed golden fixtures under tests/golden/ from the reference's own code and data.
+
+Run once in a container where the reference checkout is available:
+
+    python tests/golden/make_golden.py <reference_root>
+
+It writes two kinds of fixture (all fp32, npz):
+
+* ``ref_golden_tiny.npz`` / ``ref_golden_bulk.npz`` -- the reference's committed fairchem goldens
+  (tests/data/golden_tiny.npz: ethanol, 9 atoms, 72 edges, aperiodic; golden_bulk_tiny.npz: Si
+  diamond x(2,1,1), 4 atoms, 112 edges, periodic), reduced to config, weights, tables, inputs,
+  the gamma-independent host terms and the outputs (energy, forces, node embedding).
+* ``ref_run_*.npz`` -- this framework's seeded inputs and random-init weights evaluated by the
+  reference's OWN CPU path: ``tt_atom.geometry.radius_graph`` + ``HostGeometry`` +
+  ``tests/mirror.py`` + torch autograd, with the strain leaf of tt_atom/forces.py:515-524 for the
+  virial. These pin the neighbour list (edge_index, shifts: bit-exact) and E/F/virial.
+
+Nothing at test time reads the reference; the tests read only these files.
+"""
+import json
+import pathlib
+import sys
+
+import numpy as np
+import torch
+
+HERE = pathlib.Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+
+
+def _reduce_fairchem(ref_root, name, out):
+    z = np.load(ref_root / "tests" / "data" / name)
+    zt = np.load(ref_root / "tests" / "data" / "golden_tiny.npz")   # tables shared by both
+    keep = {"config": z["config"]}
+    for k in z.files:
+        if k.startswith("w@") or k.startswith("in@") or k.startswith("out@"):
+            keep[k] = z[k]
+    for k in ("x_edge", "edge_envelope", "x_message_init", "sys_node_embedding", "edge_distance",
+              "to_m", "gauss_offset", "gauss_coeff", "to_grid_mat", "from_grid_mat"):
+        src = z if f"host@{k}" in z.files else zt
+        if f"host@{k}" in src.files:
+            keep[f"host@{k}"] = src[f"host@{k}"]
+    np.savez_compressed(HERE / out, **keep)
+    print("wrote", out, len(keep), "arrays")
+
+
+def _run_reference(ref_root, out, cfg, w, tables, sysd, compute_stress):
+    # this framework's package is also called tt_atom: drop it so the reference's is imported
+    for mod in [m for m in sys.modules if m == "tt_atom" or m.startswith("tt_atom.")]:
+        del sys.modules[mod]
+    sys.path[:] = [p for p in sys.path if not p.endswith("tt-atom_b200")]
+    sys.path.insert(0, str(ref_root))
+    sys.path.insert(0, str(ref_root / "tests"))
+    import mirror                                           # noqa: E402 (reference)
+    from tt_atom.geometry import HostGeometry, csd_embedding, radius_graph   # noqa: E402
+
+    pos = torch.from_numpy(sysd["pos"]).float()
+    Z = torch.from_numpy(sysd["Z"]).long()
+    cell = torch.from_numpy(sysd["cell"]).float() if sysd["pbc"] else None
+    pbc = [True] * 3 if sysd["pbc"] else None
+    ei, shift = radius_graph(pos, cfg["cutoff"], cell=cell, pbc=pbc)
+    C = cfg["sphere_channels"]
+    se = csd_embedding(w, torch.tensor([0.0]), torch.tensor([0.0]), C, dataset=cfg["task"])
+    se = se[torch.zeros(Z.shape[0], dtype=torch.long)]
+    geo = HostGeometry(w, cfg, tables["to_m"], tables["gauss_offset"], tables["gauss_coeff"])
+    p = pos.clone().requires_grad_(True)
+    strain, edge_vec = None, None
+    if compute_stress:
+        strain = torch.zeros(3, 3, requires_grad=True)
+        ev = p[ei[0]] - p[ei[1]] + shift
+        edge_vec = ev + ev @ (0.5 * (strain + strain.T))
+    t = geo(p, Z, ei, se, edge_vec=edge_vec, edge_cell_shift=shift if sysd["pbc"] else None)
+    ne = mirror.backbone(w, cfg, t["x_init"], t["wigner"], t["wigner_inv"], t["x_edge"],
+                         t["edge_envelope"], se, ei, tables["to_grid_mat"], tables["from_grid_mat"])
+    E = mirror.energy(ne, w)
+    ins = [p] if strain is None else [p, strain]
+    g = torch.autograd.grad(E, ins)
+    arrs = {"config": np.frombuffer(json.dumps(cfg).encode(), dtype=np.uint8),
+            "in@pos": sysd["pos"], "in@Z": sysd["Z"],
+            "in@cell": sysd["cell"] if sysd["pbc"] else np.zeros((3, 3), np.float32),
+            "in@pbc": np.array(sysd["pbc"]),
+            "out@edge_index": ei.numpy(), "out@shift": shift.numpy().astype(np.float32),
+            "out@sys_emb": se[0].detach().numpy(),
+            "out@energy": np.array([E.item()], np.float32),
+            "out@forces": (-g[0]).numpy(), "out@node_embedding": ne.detach().numpy()}
+    if compute_stress:
+        arrs["out@virial"] = g[1].numpy()
+    arrs.update({f"w@{k}": v.numpy() for k, v in w.items()})
+    for k in ("to_m", "gauss_offset", "gauss_coeff", "to_grid_mat", "from_grid_mat"):
+        arrs[f"host@{k}"] = tables[k].numpy()
+    np.savez_compressed(HERE / out, **arrs)
+    print("wrote", out, "N", len(sysd["Z"]), "E", ei.shape[1], "energy", E.item())
+
+
+def main(ref_root):
+    ref_root = pathlib.Path(ref_root)
+    _reduce_fairchem(ref_root, "golden_tiny.npz", "ref_golden_tiny.npz")
+    _reduce_fairchem(ref_root, "golden_bulk_tiny.npz", "ref_golden_bulk.npz")
+    sys.path.insert(0, str(REPO / "tt-atom_b200"))
+    from tt_atom import configs                              # seeded inputs and weights
+    cfg = configs.model_config("tiny")
+    w = configs.random_weights(cfg, seed=0)
+    t = configs.lmax2_tables()
+    off, coeff = configs.gaussian_basis(cfg)
+    tables = dict(t, gauss_offset=off, gauss_coeff=coeff)
+    mol = configs.tiny_molecule(seed=0)
+    fcc = configs.fcc_alloy(reps=(2, 2, 2), seed=1)
+    _run_reference(ref_root, "ref_run_tiny_molecule.npz", cfg, w, tables, mol, False)
+    _run_reference(ref_root, "ref_run_tiny_fcc.npz", cfg, w, tables, fcc, True)
+
+
+if __name__ == "__main__":
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <reference_root>")
+    main(sys.argv[1])
