@@ -1,0 +1,274 @@
+"""Benchmark: eSCN-MD (uma-s-1 shape) energy + forces + stress, atom-steps/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (N = 1): the periodic 2,000-atom fcc Cu/Ni alloy (10x10x5 conventional cells,
+a = 3.55 A, jitter 0.05 A, seed 1), uma-s-1 shape (128 channels, 4 layers, 512 Gaussians,
+cutoff 6 A, at most 30 neighbours), random-init fp32 weights (seed 0).
+
+* ``value``: atom-steps/s of the device step (geometry -> forward -> hand-written backward ->
+  forces + virial) replayed from a CUDA graph with positions resident in HBM; timed with CUDA
+  events over exactly K steps; the per-step working set (~10 GB) is far larger than L2.
+* ``e2e``: the same metric through the public API (``TTAtomCalculator.calculate``): host
+  positions -> H2D copy -> GPU neighbour list -> step -> D2H of energy, forces, stress.
+* Multi-GPU (torchrun, N ranks): each rank runs its own replica structure (independent
+  systems, no collective on the data path); value = all ranks' atoms x steps / max-over-ranks
+  time ("scaling": "weak").
+* ``--impl reference``: the reference's CPU path (this repo's CPU restatement of it, the oracle)
+  on the box's host cores, on a bounded sample of the workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "tt-atom_b200"))
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "atom-steps/s (E+F+stress)"
+WORKLOAD = "uma-s-1-shape eSCN-MD, periodic 2000-atom fcc Cu/Ni, E+F+stress"
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, index):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.flush()
+        self.f.seek(0)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_workload(device):
+    from tt_atom import configs
+    from tt_atom.calculator import TTAtomCalculator
+    from tt_atom.weights import WeightBundle
+    cfg = configs.model_config("uma-s-1")
+    bundle = WeightBundle.from_arrays(configs.random_bundle_arrays(cfg, seed=0))
+    s = configs.fcc_alloy()
+    calc = TTAtomCalculator(bundle, device=device)
+    return cfg, bundle, s, calc
+
+
+def run_ours(args):
+    ws_n, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws_n > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=device)
+    from tt_atom.ase_compat import SimpleAtoms
+    from tt_atom.engine import CapturedStep
+    cfg, bundle, s, calc = make_workload(device)
+    N = len(s["Z"])
+    cell, pbc = s["cell"], [True] * 3
+    # ---- device step on a fixed topology (CUDA graph)
+    E_, F_, V_ = calc._evaluate(s["pos"], s["Z"], cell, pbc, [0.0], [0.0], forces=True,
+                                stress=True)
+    ws = calc._ws
+    eng = calc.engine
+    step = CapturedStep(eng, ws, forces=True, virial=True)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if ws_n > 1:
+        torch.distributed.barrier()
+    clk = ClockSampler(local)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    clocks = clk.stop()
+    # ---- dominant kernel, timed live with CUDA events on its own stream
+    kern = eng.time_kernels(ws, reps=3)
+    # ---- end to end through the public API (host positions in, host results out)
+    atoms = SimpleAtoms(s["Z"], s["pos"], cell, True)
+    atoms.calc = calc
+    for _ in range(max(1, args.warmup)):
+        calc.calculate(atoms, ("energy", "forces", "stress"))
+    torch.cuda.synchronize()
+    e2e_steps = max(3, min(args.steps, 20))
+    te = time.perf_counter()
+    for _ in range(e2e_steps):
+        calc.calculate(atoms, ("energy", "forces", "stress"))
+    te = time.perf_counter() - te
+    e2e_ms = 1e3 * te / e2e_steps
+    ms_t = torch.tensor([ms, e2e_ms], device=device)
+    if ws_n > 1:
+        import torch.distributed as dist
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = ms_t.tolist()
+    if rank != 0:
+        if ws_n > 1:
+            torch.distributed.destroy_process_group()
+        return
+    ms_step = ms / args.steps
+    value = N * ws_n * args.steps / (ms / 1e3)
+    hbm, bf16, src = peaks()
+    achieved = kern["flop"] / (kern["ms"] / 1e3) / 1e12
+    traffic = None
+    prof = ROOT / "profiles" / "traffic.json"
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get(kern["name"])
+    out = {
+        "metric": METRIC, "value": value, "unit": "atom-steps/s", "n_gpus": ws_n,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded fcc Cu/Ni, random-init weights)",
+        "config": {"workload": WORKLOAD, "atoms_per_gpu": N, "edges_per_gpu": ws.graph.E,
+                   "cutoff": cfg["cutoff"], "max_neighbors": cfg["max_neighbors"],
+                   "precision": "fp32", "parallelism": f"replicas x{ws_n}",
+                   "l2": "per-step working set %.1f GB > 126 MB L2" % (ws.nbytes() / 1e9)},
+        "e2e": {"value": N * ws_n / (e2e_ms / 1e3), "unit": "atom-steps/s",
+                "h2d_bytes_per_step": N * 3 * 4 + N * 8,
+                "d2h_bytes_per_step": 8 + N * 3 * 8 + 9 * 8},
+        "gpu_launches": eng.launches_per_step(ws) * args.steps,
+        "roofline": {"bound": "tensor", "kernel": kern["name"], "achieved": achieved,
+                     "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16,
+                     "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)",
+                     "traffic": traffic, "launch_ms": kern["ms"], "flop_per_launch": kern["flop"]},
+        "clocks": clocks,
+    }
+    cpu = cpu_baseline(bounded=True)
+    out["cpu_baseline"] = cpu
+    print(json.dumps(out))
+    if ws_n > 1:
+        torch.distributed.destroy_process_group()
+
+
+def _cpu_sample():
+    """The bounded CPU sample: the same model and alloy, 4x4x4 fcc cells (256 atoms)."""
+    from tt_atom import configs
+    cfg = configs.model_config("uma-s-1")
+    arrs = configs.random_bundle_arrays(cfg, seed=0)
+    s = configs.fcc_alloy(reps=(4, 4, 4), seed=1)
+    return cfg, arrs, s
+
+
+def cpu_baseline(bounded=True, steps=1, warmup=0):
+    from oracle import uma as O
+    from tt_atom import configs
+    from tt_atom.weights import WeightBundle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg, arrs, s = _cpu_sample()
+    w = WeightBundle.from_arrays(arrs).weights
+    t = configs.lmax2_tables()
+    off, coeff = configs.gaussian_basis(cfg)
+    tables = dict(t, gauss_offset=off, gauss_coeff=coeff)
+    pos = torch.from_numpy(s["pos"])
+    cell = torch.from_numpy(s["cell"])
+
+    def one():
+        ei, sh = O.neighbor_list(pos, cfg["cutoff"], cell, [True] * 3, cfg["max_neighbors"])
+        return O.energy_forces(w, cfg, tables, pos, torch.from_numpy(s["Z"]), ei, sh,
+                               compute_stress=True)
+    for _ in range(warmup):
+        one()
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+    n = len(s["Z"])
+    v = n / statistics.median(times)
+    return {"value": v, "unit": "atom-steps/s", "cores": threads, "kind": "port",
+            "sample": f"{n}-atom fcc Cu/Ni (4x4x4 cells), same model/cap, E+F+stress, "
+                      f"median of {steps} step(s)", "seconds_per_step": statistics.median(times)}
+
+
+def run_reference(args):
+    ws_n, rank, _ = dist_env()
+    if rank != 0:
+        return
+    steps = args.steps
+    cpu = cpu_baseline(bounded=True, steps=steps, warmup=args.warmup)
+    out = {"metric": METRIC, "value": cpu["value"], "unit": "atom-steps/s", "n_gpus": ws_n,
+           "steps": steps, "warmup": args.warmup,
+           "ms_per_step": 1e3 * cpu["seconds_per_step"], "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+           "data": "synthetic (seeded fcc Cu/Ni, random-init weights)",
+           "config": {"workload": WORKLOAD, "sample": cpu["sample"]},
+           "impl": "reference", "cpu_baseline": cpu,
+           "e2e": {"value": cpu["value"], "unit": "atom-steps/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(out))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,280 @@
+/*
+ * atom_b200.h -- C ABI of the B200 (sm_100a) eSCN-MD energy/force/stress kernels.
+ *
+ * Conventions for every entry point:
+ *  - Pointers are CUDA device pointers unless named *_host; sizes are element counts.
+ *  - All floating-point buffers are fp32, row-major, densely packed unless a leading dimension
+ *    (ld*) is given. Index buffers are int32.
+ *  - Outputs are allocated by the caller. No entry point allocates device memory, except
+ *    atom_neighbor_list, which uses caller-provided scratch (see its comment).
+ *  - `stream` is a cudaStream_t passed as void*; work is stream-ordered and asynchronous.
+ *  - Return value: ATOM_OK (0) or an error code; atom_last_error() gives the message of the
+ *    last failing call on this host thread. No C++ exception crosses this boundary.
+ *
+ * Node features are [N, 9, C] in the standard (l, m) spherical-harmonic order (lmax = 2).
+ * Per-edge Wigner matrices are passed packed: the 35 structural nonzeros of the m-primed
+ * rotation, row-major by m-primed row (row degrees 0,1,2,1,2,1,2,2,2; each row holds the
+ * 2l+1 columns of its degree block).
+ * Edges are processed in receiver-major order with a receiver CSR (recv_ptr[N+1]) and a sender
+ * CSR (send_ptr[N+1], send_eid[E]: edge ids grouped by source node, ascending within a group).
+ */
+#ifndef ATOM_B200_H
+#define ATOM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    ATOM_OK = 0,
+    ATOM_ERR_ARG = 1,          /* invalid argument, shape or alignment */
+    ATOM_ERR_CUDA = 2,         /* CUDA runtime / launch error */
+    ATOM_ERR_CAPACITY = 3,     /* a device-side capacity was exceeded (retry with more room) */
+    ATOM_ERR_UNSUPPORTED = 4   /* shape the kernels do not implement */
+};
+
+/* Copies the last error message of this host thread into buf (NUL-terminated); returns its
+ * full length. */
+int atom_last_error(char* buf, size_t n);
+/* ABI version of this library. */
+int atom_abi_version(void);
+
+/* ------------------------------------------------------------------------------------------
+ * Reference-op equivalents. These four replace the nanobind ops of the reference's custom
+ * kernel library (custom_kernels/fused_rotate/fused_rotate_nanobind.cpp:17-96) with the same
+ * argument meaning; the reference returns a new tensor, here the caller passes the output.
+ * ---------------------------------------------------------------------------------------- */
+
+/* fused_rotate (fused_rotate_nanobind.cpp:71-93; semantics custom_kernels/README.md "contract"):
+ *   out[e, i*W + w] = sum over the deg[i] nonzeros k of block i: coef[e, ks[k]] * x[e, js[k]*W + w]
+ * x [E, n_in*W], coef [E, nnz] (compact: the reference's tile-broadcast coef_exp is a ttnn layout
+ * detail), out [E, n_out*W]. deg[n_out], ks[nnz], js[nnz] are HOST arrays grouped by output
+ * block in order. Limits: n_in, n_out <= 32, nnz <= 128, W % 4 == 0. */
+int atom_fused_rotate(const float* x, const float* coef, int64_t E, int n_in, int n_out, int W,
+                      int nnz, const int* deg_host, const int* ks_host, const int* js_host,
+                      float* out, void* stream);
+
+/* fused_rotate_gc (fused_rotate_nanobind.cpp:52-70): coefficient adjoint
+ *   gc[e, k] = sum_w gout[e, is_[k]*W + w] * xin[e, js[k]*W + w]
+ * gout [E, n_out*W], xin [E, n_in*W], gc [E, nnz]; is_/js HOST arrays of length nnz.
+ * The reference's column-selector operand `sel` is a Tensix matmul-reduce device and has no
+ * counterpart here. */
+int atom_fused_rotate_gc(const float* gout, const float* xin, int64_t E, int n_out, int n_in,
+                         int W, int nnz, const int* is_host, const int* js_host, float* gc,
+                         void* stream);
+
+/* fused_gate (fused_rotate_nanobind.cpp:35-51; tt_atom/activation.py:53-70):
+ *   mode 0: out = [silu(a[:, :H]) | a[:, H:] * gate]
+ *   mode 1: out = [a[:, :H] * silu'(b[:, :H]) | a[:, H:] * gate]
+ * a, b, out [E, H + G]; gate [E, G] (the gate already expanded per vector coefficient). The
+ * reference passes H, G and H+G in 32-column tiles (Ht, Gt, Wt); here they are columns. */
+int atom_fused_gate(const float* a, const float* gate, const float* b, int64_t E, int H, int G,
+                    int mode, float* out, void* stream);
+
+/* fused_ln_bw (fused_rotate_nanobind.cpp:18-34; tt_atom/so2.py:117-128): LayerNorm backward
+ * with the SiLU backward and the affine scale folded in:
+ *   gy = g * silu'(n) * gamma;  dx = rstd * (gy - mean(gy) - xhat * mean(gy * xhat))
+ * g, x (the LN input), n (the LN output = SiLU input), dx [rows, W]; gamma [W]. */
+int atom_fused_ln_bw(const float* g, const float* x, const float* n, const float* gamma,
+                     int64_t rows, int W, float eps, float* dx, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Graph construction. Replaces tt_atom/geometry.py:48-81 (radius_graph) on the device, with
+ * the same fp32 predicate and the same edge order, plus an optional per-receiver cap.
+ * ---------------------------------------------------------------------------------------- */
+
+/* Neighbour list of `nsys` independent systems stored back to back (sys_ptr[nsys+1] atom
+ * offsets, host array). Each system is periodic with `nshift` image shifts (shifts [nshift,3],
+ * device; the zero shift alone for aperiodic systems) -- all systems share pbc and shifts.
+ * Aperiodic: keep (a, b) with ||pos[a]-pos[b]|| < cutoff, a != b. Periodic: keep (i, j, c) with
+ * |pos[i] - (pos[j] + shift[c])|^2 <= cutoff^2 and > 1e-8. Output per receiver, sources in
+ * (source, image) order; with max_nbrs > 0 only the max_nbrs nearest (ties: that order) stay.
+ *   recv_cnt [N]         edges per receiver (device, written)
+ *   cand_idx, cand_d     scratch of N * max_cand int32 / fp32 each (device; pass 1 writes,
+ *                        pass 2 reads)
+ *   small_scratch        8 * (nsys + 2) bytes of device scratch, 8-byte aligned
+ * Pass 1 (edges == NULL): fills recv_cnt, returns ATOM_ERR_CAPACITY (with the needed max_cand
+ * in *need) if a receiver has more than max_cand candidates.
+ * Pass 2 (edges != NULL, recv_ptr = exclusive scan of recv_cnt): writes edge_src[E],
+ * edge_tgt[E], edge_img[E] (image index) in receiver-major order. */
+int atom_neighbor_list(const float* pos, int64_t N, const int64_t* sys_ptr_host, int nsys,
+                       const float* shifts, int nshift, float cutoff, int periodic, int max_nbrs,
+                       int max_cand, int* cand_idx, float* cand_d, int* recv_cnt,
+                       const int* recv_ptr, int* edge_src, int* edge_tgt, int* edge_img,
+                       void* small_scratch, int* need_host, void* stream);
+
+/* Exclusive prefix sum of n int32 counts: ptr[0] = 0, ptr[i+1] = ptr[i] + cnt[i]; also copies
+ * the total to *total_host (synchronous on `stream`) when total_host is not NULL. */
+int atom_exclusive_scan(const int* cnt, int64_t n, int* ptr, int* total_host, void* stream);
+
+/* Sender CSR: send_ptr[N+1] and send_eid[E] (edge ids grouped by source, ascending), from
+ * edge_src[E]. scratch: N int32. */
+int atom_sender_csr(const int* edge_src, int64_t E, int64_t N, int* scratch, int* send_ptr,
+                    int* send_eid, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Geometry (tt_atom/geometry.py:112-280) and its VJP (replaces the host autograd finish of
+ * tt_atom/forces.py:545-589).
+ * ---------------------------------------------------------------------------------------- */
+
+/* Per edge: ev = pos[src] - pos[tgt] + shift[img]; dist = |ev|; packed Wigner coef [E,35]
+ * (Euler angles with roll 0, D_l = J Z(-beta) J Z(-alpha), rows permuted by perm9);
+ * gauss [E, NB] = exp(coeff (dist - offset_k)^2); env [E]: polynomial envelope p = 5.
+ * jd1 [9], jd2 [25] host arrays (e3nn J matrices); perm9 host [9]: m-primed row -> coefficient.
+ * ev_out [E,3] and dist_out [E] may be NULL. */
+int atom_edge_geometry(const float* pos, const int* src, const int* tgt, const int* img,
+                       const float* shifts, int64_t E, const float* jd1_host,
+                       const float* jd2_host, const int* perm9_host, const float* offset,
+                       int NB, float coeff, float cutoff, float* coef, float* gauss,
+                       float* env, float* ev_out, float* dist_out, void* stream);
+
+/* VJP of atom_edge_geometry: from g_coef [E,35], g_gauss [E,NB] (may be NULL) and g_env [E]
+ * accumulates dE/d(edge vector) into g_ev [E,3] (overwritten). */
+int atom_edge_geometry_bwd(const float* pos, const int* src, const int* tgt, const int* img,
+                           const float* shifts, int64_t E, const float* jd1_host,
+                           const float* jd2_host, const int* perm9_host, const float* offset,
+                           int NB, float coeff, float cutoff, const float* g_coef,
+                           const float* gauss, const float* g_gauss, const float* g_env,
+                           float* g_ev, void* stream);
+
+/* Forces F[n] = sum_{e: tgt=n} g_ev[e] - sum_{e: src=n} g_ev[e] (F = -dE/dpos), in a fixed
+ * order, and the virial dE/d(strain) = sym(sum_e ev[e] (x) g_ev[e]) [3,3] (may be NULL).
+ * scratch: 9 * 1024 floats when virial != NULL. */
+int atom_forces_virial(const float* g_ev, const float* ev, int64_t E, int64_t N,
+                       const int* recv_ptr, const int* send_ptr, const int* send_eid,
+                       float* forces, float* virial, float* scratch, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Dense contractions.
+ * ---------------------------------------------------------------------------------------- */
+
+/* Grouped fp32 GEMM (up to 8 groups, one launch): for each group g,
+ *   C[m, c_col[g] + n] (+)= act( sum_k A[m, a_col[g] + k] * B_g[k * ldb[g] + n] + bias_g[n]
+ *                                + T1[idx1[m] * ldt + t_col[g] + n] + T2[idx2[m] * ldt + t_col[g] + n] )
+ * for m < M, n < N_g, k < K_g. bias/T1/T2 optional (NULL). act: 0 none, 1 SiLU (then
+ * C_pre, when not NULL, receives the pre-activation). accumulate != 0 adds into C.
+ * precision: 0 = fp32 FMA; other values select tensor-core modes (see atom_gemm_modes). */
+typedef struct {
+    int ngroups;
+    int a_col[8], K[8], c_col[8], N[8], ldb[8], t_col[8];
+    const float* B[8];
+    const float* bias[8];
+} atom_gemm_groups;
+
+int atom_gemm(const float* A, int64_t lda, int64_t M, const atom_gemm_groups* groups,
+              float* Cout, int64_t ldc, float* C_pre, const float* T1, const float* T2,
+              const int* idx1, const int* idx2, int64_t ldt, int act, int accumulate,
+              int precision, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Edge-side fused ops of the edgewise block (tt_atom/edgewise.py:39-87, forces.py:352-418).
+ * ---------------------------------------------------------------------------------------- */
+
+/* Rotate-in with the radial multiplier: for each edge e and m-primed row r,
+ *   rot[e, r, 0:C]  = sum_j Wig_e[r, j] x[src[e], j, :],  rot[e, r, C:2C] = same with tgt,
+ *   A[e, r, :] = rot[e, r, :] * mult_e(r)  (rad [E, ldr] compact: rows 0-2 m=0, rows 3-4 and 5-6
+ *   share the m=1 slices, rows 7-8 share the m=2 slice; each 2C wide, starting at rad_col).
+ * rot may be NULL (not stored). rad may be NULL (no multiplier). */
+int atom_rotate_in(const float* x, const int* src, const int* tgt, const float* coef, int64_t E,
+                   int C, const float* rad, int64_t ldr, int rad_col, float* rot, float* A,
+                   void* stream);
+
+/* Gate (tt_atom/activation.py:53-70): Y [E, 2H + 9H] = [gating (2H) | rows 0..8 (9H)],
+ * G [E, 9H] = [silu(row 0) | row r * sigmoid(gating[d(r)]) ], d = 0,1,0,1,0,1,1,1 for r=1..8. */
+int atom_gate_fwd(const float* Y, int64_t E, int H, float* G, void* stream);
+/* VJP of atom_gate_fwd: gY [E, 11H] from gG [E, 9H] and Y. */
+int atom_gate_bwd(const float* Y, const float* gG, int64_t E, int H, float* gY, void* stream);
+
+/* Rotate-back + envelope + receiver reduction + residual (one node per warp, CSR order):
+ *   out[n, j, c] = resid[n, j, c] + sum_{e in recv(n)} env[e] sum_r Wig_e[r, j] Y[e, r, c].
+ * resid may be NULL. Y [E, 9C]. */
+int atom_rotate_back_reduce(const float* Y, const float* coef, const float* env, int64_t N,
+                            int C, const int* recv_ptr, const float* resid, float* out,
+                            void* stream);
+
+/* VJP of atom_rotate_back_reduce through the edge messages: with gx [N,9,C] the adjoint of out,
+ *   R[e] = Wig_e gx[tgt[e]],  gY[e] = env[e] R[e]   ([E, 9C])
+ *   g_env[e] += sum R[e] . Y[e];  g_coef[e, (r,j)] += env[e] sum_c gx[tgt, j, c] Y[e, r, c]. */
+int atom_rotate_back_bwd(const float* gx, const int* tgt, const float* coef, const float* env,
+                         const float* Y, int64_t E, int C, float* gY, float* g_env,
+                         float* g_coef, void* stream);
+
+/* VJP of atom_rotate_in, edge part: with gA [E, 9*2C]:
+ *   g_rot = gA * mult (written to g_rot [E, 9*2C]),
+ *   g_rad[e, slice] = sum over rows sharing the slice of gA * rot  (overwrites [E, ldr] slice),
+ *   g_coef[e, (r,j)] += sum_c g_rot[e,r,c] x[src,j,c] + g_rot[e,r,C+c] x[tgt,j,c]. */
+int atom_rotate_in_bwd_edge(const float* gA, const float* rot, const float* rad, int64_t ldr,
+                            int rad_col, const float* x, const int* src, const int* tgt,
+                            const float* coef, int64_t E, int C, float* g_rot, float* g_rad,
+                            float* g_coef, void* stream);
+
+/* VJP of atom_rotate_in, node part (fixed order; receiver CSR then sender CSR):
+ *   gx[n] (+)= sum_{e in recv(n)} Wig_e^T g_rot[e, :, C:2C] + sum_{e in send(n)} Wig_e^T g_rot[e, :, 0:C]. */
+int atom_rotate_in_bwd_node(const float* g_rot, const float* coef, int64_t N, int C,
+                            const int* recv_ptr, const int* send_ptr, const int* send_eid,
+                            int accumulate, float* gx, void* stream);
+
+/* Edge-degree node init (tt_atom/geometry.py:262-278):
+ *   x[n, j, c] = l0[n, c] [j = 0] + sum_{e in recv(n)} env[e]/rescale sum_{m<3} Wig_e[m, j] rad[e, m*C + c]. */
+int atom_edge_degree_fwd(const float* rad, int64_t ldr, const float* coef, const float* env,
+                         const float* l0, int64_t N, int C, const int* recv_ptr, float rescale,
+                         float* x, void* stream);
+
+/* VJP of atom_edge_degree_fwd: g_rad[e, m*C+c] = env/rescale (Wig_e gx[tgt])[m, c];
+ * g_env[e] += ...; g_coef[e] += .... */
+int atom_edge_degree_bwd(const float* gx, const int* tgt, const float* rad, int64_t ldr,
+                         const float* coef, const float* env, int64_t E, int C, float rescale,
+                         float* g_rad, int64_t ldg, float* g_env, float* g_coef, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Node-side ops (tt_atom/norm.py, grid.py, model.py energy head; forces.py VJPs).
+ * ---------------------------------------------------------------------------------------- */
+
+/* Row-group LayerNorm + SiLU over `groups` consecutive W-wide column groups of X [rows, ld]:
+ * Y = silu(LN_g(X)); gamma/beta [groups * W]. */
+int atom_ln_silu_fwd(const float* X, int64_t rows, int64_t ld, int groups, int W,
+                     const float* gamma, const float* beta, float eps, float* Y, void* stream);
+/* VJP of atom_ln_silu_fwd (per group, the fused_ln_bw contraction): dX from gY and X. */
+int atom_ln_silu_bwd(const float* X, const float* gY, int64_t rows, int64_t ld, int groups,
+                     int W, const float* gamma, const float* beta, float eps, float* dX,
+                     void* stream);
+
+/* Equivariant RMS norm (tt_atom/norm.py:24-111): out = norm(x) * affine[l] (+ bias, + add0 on
+ * l = 0); add0 [N, C] may be NULL. */
+int atom_rmsnorm_sh_fwd(const float* x, int64_t N, int C, const float* affine_w,
+                        const float* affine_b, const float* add0, float eps, float* out,
+                        void* stream);
+/* VJP: gx (+)= d norm / dx applied to gout. */
+int atom_rmsnorm_sh_bwd(const float* x, const float* gout, int64_t N, int C,
+                        const float* affine_w, float eps, int accumulate, float* gx,
+                        void* stream);
+
+/* Per-node coefficient projection: out[n, q, c] (+)= sum_p M[q, p] in[n, p, c]
+ * (M [Q, P] row-major, or transposed when trans != 0). */
+int atom_node_project(const float* in, int64_t N, int P, int C, const float* M, int Q,
+                      int trans, int accumulate, float* out, void* stream);
+
+/* Elementwise: out = g * silu'(pre) (n values). */
+int atom_silu_bwd(const float* g, const float* pre, int64_t n, float* out, void* stream);
+
+/* Deterministic sum of n floats -> out[0] (fixed reduction tree), optionally per segment:
+ * seg_ptr [nseg+1] device offsets (NULL: one segment). */
+int atom_segment_sum(const float* v, int64_t n, const int* seg_ptr, int nseg, float* out,
+                     void* stream);
+
+/* Node l = 0 init: out[n, c] = sphere[Z[n], c] + sysemb[sys_id[n], c] (sys_id NULL: system 0)
+ * -- the pos-independent part of tt_atom/geometry.py:262-266. Z, sys_id int32. */
+int atom_node_embed(const int* Z, const int* sys_id, const float* sphere, const float* sysemb,
+                    int64_t N, int C, float* out, void* stream);
+
+/* Per-edge species: zs[e] = Z[src[e]], zt[e] = Z[tgt[e]] (row indices of the radial tables). */
+int atom_edge_species(const int* Z, const int* src, const int* tgt, int64_t E, int* zs, int* zt,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ATOM_B200_H */

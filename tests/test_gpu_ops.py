@@ -1,0 +1,184 @@
+"""Per-kernel numerics on the GPU against plain torch fp32 references (through the C-ABI)."""
+import ctypes
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from tt_atom import _lib as L
+from tt_atom._lib import call, ptr
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def s():
+    return L.stream_ptr()
+
+
+def rnd(*shape, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return torch.randn(*shape, generator=g).to(dev)
+
+
+def close(a, b, tol=1e-5):
+    a, b = a.double(), b.double()
+    err = (a - b).abs().max().item()
+    scale = max(b.abs().max().item(), 1.0)
+    assert err <= tol * scale, f"max err {err} (scale {scale})"
+
+
+# ------------------------------------------------------------------- reference-op equivalents
+
+def _pattern():
+    # the uma-s 9x9 block-diagonal pattern, grouped by output row (tt_atom/rotation.py:145-165)
+    ij = [(i, j) for i in range(9) for j in range(9)
+          if (i == 0 and j == 0) or (1 <= i < 4 and 1 <= j < 4) or (i >= 4 and j >= 4)]
+    return ij
+
+
+def test_fused_rotate_and_gc():
+    ij = _pattern()
+    nnz, E, W = len(ij), 1000, 256
+    x, coef, gout = rnd(E, 9 * W), rnd(E, nnz, seed=1), rnd(E, 9 * W, seed=2)
+    deg = [sum(1 for (i, j) in ij if i == b) for b in range(9)]
+    ks = [k for b in range(9) for k, (i, j) in enumerate(ij) if i == b]
+    js = [ij[k][1] for k in ks]
+    out = torch.empty(E, 9 * W, device=dev)
+    call("atom_fused_rotate", ptr(x), ptr(coef), E, 9, 9, W, nnz, L.host_i32(deg), L.host_i32(ks),
+         L.host_i32(js), ptr(out), s())
+    Wd = torch.zeros(E, 9, 9, device=dev)
+    for k, (i, j) in enumerate(ij):
+        Wd[:, i, j] = coef[:, k]
+    ref = torch.bmm(Wd, x.view(E, 9, W)).reshape(E, -1)
+    close(out, ref)
+    gc = torch.empty(E, nnz, device=dev)
+    call("atom_fused_rotate_gc", ptr(gout), ptr(x), E, 9, 9, W, nnz,
+         L.host_i32([i for i, j in ij]), L.host_i32([j for i, j in ij]), ptr(gc), s())
+    g3, x3 = gout.view(E, 9, W), x.view(E, 9, W)
+    ref = torch.stack([(g3[:, i] * x3[:, j]).sum(-1) for i, j in ij], 1)
+    close(gc, ref, 1e-5)
+
+
+def test_fused_gate_and_ln_bw():
+    E, H, G = 513, 32, 256
+    a, gate, b = rnd(E, H + G), rnd(E, G, seed=1), rnd(E, H + G, seed=2)
+    out = torch.empty_like(a)
+    call("atom_fused_gate", ptr(a), ptr(gate), ptr(b), E, H, G, 0, ptr(out), s())
+    close(out, torch.cat([F.silu(a[:, :H]), a[:, H:] * gate], 1))
+    call("atom_fused_gate", ptr(a), ptr(gate), ptr(b), E, H, G, 1, ptr(out), s())
+    sb = torch.sigmoid(b[:, :H])
+    close(out, torch.cat([a[:, :H] * sb * (1 + b[:, :H] * (1 - sb)), a[:, H:] * gate], 1))
+    W = 128
+    x = rnd(E, W).requires_grad_()
+    gamma, beta, g = rnd(W, seed=3), rnd(W, seed=4), rnd(E, W, seed=5)
+    n = F.layer_norm(x, (W,), gamma, beta, 1e-5)
+    y = F.silu(n)
+    (ref,) = torch.autograd.grad(y, x, g)
+    dx = torch.empty(E, W, device=dev)
+    call("atom_fused_ln_bw", ptr(g), ptr(x.detach()), ptr(n.detach()), ptr(gamma), E, W, 1e-5,
+         ptr(dx), s())
+    close(dx, ref, 1e-4)
+
+
+# ------------------------------------------------------------------------------- GEMM
+
+@pytest.mark.parametrize("M", [1, 129, 1000])
+def test_grouped_gemm_with_epilogues(M):
+    K1, N1, K2, N2 = 96, 160, 64, 130
+    A = rnd(M, K1 + K2)
+    B1, B2 = rnd(K1, N1, seed=1), rnd(K2, N2, seed=2)
+    bias1 = rnd(N1, seed=3)
+    T1, T2 = rnd(10, 400, seed=4), rnd(10, 400, seed=5)
+    i1 = torch.randint(0, 10, (M,), device=dev, dtype=torch.int32)
+    i2 = torch.randint(0, 10, (M,), device=dev, dtype=torch.int32)
+    g = L.GemmGroups()
+    g.ngroups = 2
+    for k, (ac, K, cc, N, B, b, tc) in enumerate([(0, K1, 0, N1, B1, bias1, 0),
+                                                  (K1, K2, N1, N2, B2, None, 200)]):
+        g.a_col[k], g.K[k], g.c_col[k], g.N[k], g.ldb[k], g.t_col[k] = ac, K, cc, N, N, tc
+        g.B[k] = B.data_ptr()
+        g.bias[k] = b.data_ptr() if b is not None else None
+    C = torch.empty(M, N1 + N2, device=dev)
+    Cpre = torch.empty(M, N1 + N2, device=dev)
+    call("atom_gemm", ptr(A), K1 + K2, M, ctypes.byref(g), ptr(C), N1 + N2, ptr(Cpre), ptr(T1),
+         ptr(T2), ptr(i1), ptr(i2), 400, 1, 0, 0, s())
+    Ad = A.double()
+    r1 = Ad[:, :K1] @ B1.double() + bias1.double() + T1.double()[i1.long(), :N1] + \
+        T2.double()[i2.long(), :N1]
+    r2 = Ad[:, K1:] @ B2.double() + T1.double()[i1.long(), 200:200 + N2] + \
+        T2.double()[i2.long(), 200:200 + N2]
+    pre = torch.cat([r1, r2], 1)
+    close(Cpre, pre, 1e-5)
+    close(C, F.silu(pre), 1e-5)
+    # accumulate
+    C2 = C.clone()
+    call("atom_gemm", ptr(A), K1 + K2, M, ctypes.byref(g), ptr(C2), N1 + N2, None, ptr(T1),
+         ptr(T2), ptr(i1), ptr(i2), 400, 0, 1, 0, s())
+    close(C2, C.double() + pre, 1e-5)
+
+
+# --------------------------------------------------------------------- node-side kernels
+
+def _rms_ref(x, aw, ab, add0=None, eps=1e-5):
+    lc = [0, 1, 1, 1, 2, 2, 2, 2, 2]
+    bdw = torch.tensor([1.0 / (2 * l + 1) / 3 for l in lc], device=x.device).view(1, 9, 1)
+    l0 = x[:, :1]
+    xc = torch.cat([l0 - l0.mean(2, keepdim=True), x[:, 1:]], 1)
+    fn = torch.rsqrt((xc * xc * bdw).sum(1, keepdim=True).mean(2, keepdim=True) + eps)
+    out = xc * fn * aw[torch.tensor(lc, device=x.device)][None]
+    b0 = ab.view(1, 1, -1) if add0 is None else ab.view(1, 1, -1) + add0[:, None, :]
+    return torch.cat([out[:, :1] + b0, out[:, 1:]], 1)
+
+
+@pytest.mark.parametrize("C", [16, 128])
+def test_rmsnorm_sh_fwd_bwd(C):
+    N = 300
+    x = rnd(N, 9, C).requires_grad_()
+    aw, ab, add0 = 1 + 0.1 * rnd(3, C, seed=1), rnd(C, seed=2), rnd(N, C, seed=3)
+    g = rnd(N, 9, C, seed=4)
+    ref = _rms_ref(x, aw, ab, add0)
+    (gref,) = torch.autograd.grad(ref, x, g)
+    out = torch.empty(N, 9, C, device=dev)
+    call("atom_rmsnorm_sh_fwd", ptr(x.detach()), N, C, ptr(aw), ptr(ab), ptr(add0), 1e-5,
+         ptr(out), s())
+    close(out, ref, 1e-5)
+    gx = torch.ones(N, 9, C, device=dev)
+    call("atom_rmsnorm_sh_bwd", ptr(x.detach()), ptr(g), N, C, ptr(aw), 1e-5, 1, ptr(gx), s())
+    close(gx, gref + 1, 1e-4)
+
+
+def test_ln_silu_groups_and_projection():
+    E, G, W = 777, 5, 32
+    X = rnd(E, G * W).requires_grad_()
+    gam, bet, gY = 1 + 0.1 * rnd(G * W, seed=1), rnd(G * W, seed=2), rnd(E, G * W, seed=3)
+    ref = torch.cat([F.silu(F.layer_norm(X[:, g * W:(g + 1) * W], (W,), gam[g * W:(g + 1) * W],
+                                         bet[g * W:(g + 1) * W], 1e-5)) for g in range(G)], 1)
+    (gref,) = torch.autograd.grad(ref, X, gY)
+    Y = torch.empty(E, G * W, device=dev)
+    call("atom_ln_silu_fwd", ptr(X.detach()), E, G * W, G, W, ptr(gam), ptr(bet), 1e-5, ptr(Y), s())
+    close(Y, ref, 1e-5)
+    dX = torch.empty_like(Y)
+    call("atom_ln_silu_bwd", ptr(X.detach()), ptr(gY), E, G * W, G, W, ptr(gam), ptr(bet), 1e-5,
+         ptr(dX), s())
+    close(dX, gref, 1e-4)
+    N, P, C, Q = 50, 9, 64, 42
+    inp, M = rnd(N, P, C), rnd(Q, P, seed=6)
+    out = torch.empty(N, Q, C, device=dev)
+    call("atom_node_project", ptr(inp), N, P, C, ptr(M), Q, 0, 0, ptr(out), s())
+    close(out, torch.einsum("qp,npc->nqc", M, inp), 1e-5)
+    back = torch.zeros(N, P, C, device=dev)
+    call("atom_node_project", ptr(out), N, Q, C, ptr(M), P, 1, 1, ptr(back), s())
+    close(back, torch.einsum("qp,nqc->npc", M, out), 1e-5)
+
+
+def test_segment_sum_deterministic():
+    v = rnd(100003)
+    sp = torch.tensor([0, 5, 5, 70000, 100003], dtype=torch.int32, device=dev)
+    out = torch.empty(4, device=dev)
+    call("atom_segment_sum", ptr(v), v.numel(), ptr(sp), 4, ptr(out), s())
+    ref = torch.stack([v[0:5].sum(), v[5:5].sum(), v[5:70000].sum(), v[70000:].sum()])
+    close(out, ref, 1e-5)
+    out2 = torch.empty(4, device=dev)
+    call("atom_segment_sum", ptr(v), v.numel(), ptr(sp), 4, ptr(out2), s())
+    assert torch.equal(out, out2)

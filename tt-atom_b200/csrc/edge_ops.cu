@@ -1,0 +1,547 @@
+// Edge-side fused ops of the eSCN-MD edgewise block and their VJPs.
+//
+// Reference: tt_atom/edgewise.py:39-87 (forward chain), tt_atom/rotation.py:211-260 (rotation and
+// its adjoints), tt_atom/activation.py:53-70 (gate), tt_atom/forces.py:104-130,352-418 (VJPs),
+// tt_atom/geometry.py:262-278 (edge-degree init).
+//
+// Layout: node features x [N, 9, C] (standard (l, m) order); per-edge rows [E, 9, W] in m-primed
+// order; packed Wigner coefficients coef [E, 35] (see common.cuh). Each kernel maps one warp to
+// one edge (or one node for the CSR reductions) and each lane to 4 consecutive channels
+// (float4), so every row access is a coalesced 512-byte transaction at C = 128. There are no
+// float atomics: per-node sums walk the receiver / sender CSR in a fixed order, per-edge sums
+// are warp reductions.
+#include "common.cuh"
+
+namespace atom {
+
+__device__ __forceinline__ float4 f4(float a) { return make_float4(a, a, a, a); }
+__device__ __forceinline__ void fma4(float4& acc, float s, const float4& v) {
+    acc.x = fmaf(s, v.x, acc.x);
+    acc.y = fmaf(s, v.y, acc.y);
+    acc.z = fmaf(s, v.z, acc.z);
+    acc.w = fmaf(s, v.w, acc.w);
+}
+__device__ __forceinline__ float4 mul4(const float4& a, const float4& b) {
+    return make_float4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w);
+}
+__device__ __forceinline__ float dot4(const float4& a, const float4& b) {
+    return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+}
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ void st4(float* p, const float4& v) { *reinterpret_cast<float4*>(p) = v; }
+
+// Column offset (in units of the row width 2C) of the radial slice multiplying m-primed row r:
+// rows 0..2 -> slices 0..2 (m = 0), rows 3,4 and 5,6 -> slices 3,4 (m = 1), rows 7,8 -> slice 5.
+__host__ __device__ constexpr int rad_slice(int r) {
+    return r < 3 ? r : (r < 5 ? r : (r < 7 ? r - 2 : 5));
+}
+
+// Wigner row r applied to a node row set v[9]: out = sum_jj W[r][jj] v[l^2 + jj].
+template <int R>
+__device__ __forceinline__ float4 wrow(const float* w, const float4* v) {
+    constexpr int l = row_deg(R), o = row_off(R), c0 = deg_col0(l);
+    float4 acc = f4(0.f);
+#pragma unroll
+    for (int jj = 0; jj < 2 * l + 1; ++jj) fma4(acc, w[o + jj], v[c0 + jj]);
+    return acc;
+}
+
+__device__ __forceinline__ void load_coef(const float* __restrict__ coef, long long e, float* w) {
+#pragma unroll
+    for (int k = 0; k < kNnz; ++k) w[k] = __ldg(coef + e * kNnz + k);
+}
+
+// -------------------------------------------------------------------------- rotate-in (fwd)
+__global__ void __launch_bounds__(256) rotate_in_kernel(
+    const float* __restrict__ x, const int* __restrict__ src, const int* __restrict__ tgt,
+    const float* __restrict__ coef, long long E, int C, const float* __restrict__ rad,
+    long long ldr, int rad_col, float* __restrict__ rot, float* __restrict__ A) {
+    long long e = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (e >= E) return;
+    float w[kNnz];
+    load_coef(coef, e, w);
+    const float* xs = x + (long long)__ldg(src + e) * kNsph * C;
+    const float* xt = x + (long long)__ldg(tgt + e) * kNsph * C;
+    const int W2 = 2 * C;
+    float* rowA = A + e * kNsph * W2;
+    float* rowR = rot ? rot + e * kNsph * W2 : nullptr;
+    const float* rr = rad ? rad + e * ldr + rad_col : nullptr;
+    for (int c = lane * 4; c < C; c += 128) {
+        float4 vs[kNsph], vt[kNsph];
+#pragma unroll
+        for (int j = 0; j < kNsph; ++j) {
+            vs[j] = ld4(xs + j * C + c);
+            vt[j] = ld4(xt + j * C + c);
+        }
+        float4 os[kNsph], ot[kNsph];
+        os[0] = wrow<0>(w, vs); ot[0] = wrow<0>(w, vt);
+        os[1] = wrow<1>(w, vs); ot[1] = wrow<1>(w, vt);
+        os[2] = wrow<2>(w, vs); ot[2] = wrow<2>(w, vt);
+        os[3] = wrow<3>(w, vs); ot[3] = wrow<3>(w, vt);
+        os[4] = wrow<4>(w, vs); ot[4] = wrow<4>(w, vt);
+        os[5] = wrow<5>(w, vs); ot[5] = wrow<5>(w, vt);
+        os[6] = wrow<6>(w, vs); ot[6] = wrow<6>(w, vt);
+        os[7] = wrow<7>(w, vs); ot[7] = wrow<7>(w, vt);
+        os[8] = wrow<8>(w, vs); ot[8] = wrow<8>(w, vt);
+#pragma unroll
+        for (int r = 0; r < kNsph; ++r) {
+            if (rowR) {
+                st4(rowR + r * W2 + c, os[r]);
+                st4(rowR + r * W2 + C + c, ot[r]);
+            }
+            float4 a = os[r], b = ot[r];
+            if (rr) {
+                a = mul4(a, ld4(rr + rad_slice(r) * W2 + c));
+                b = mul4(b, ld4(rr + rad_slice(r) * W2 + C + c));
+            }
+            st4(rowA + r * W2 + c, a);
+            st4(rowA + r * W2 + C + c, b);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------- gate
+// Gating row (0 or 1) of vector row r = 1..8 in m-primed order (tt_atom/activation.py:19-26).
+__host__ __device__ constexpr int gate_row(int r) {
+    return (r == 1 || r == 3 || r == 5) ? 0 : 1;
+}
+
+__global__ void gate_fwd_kernel(const float* __restrict__ Y, long long E, int H,
+                                float* __restrict__ G) {
+    long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= E * H) return;
+    long long e = t / H;
+    int c = (int)(t - e * H);
+    const float* y = Y + e * 11LL * H;
+    float* g = G + e * 9LL * H;
+    float s0 = sigmoid_f(y[c]), s1 = sigmoid_f(y[H + c]);
+    g[c] = silu_f(y[2 * H + c]);
+#pragma unroll
+    for (int r = 1; r < kNsph; ++r) g[r * H + c] = y[(2 + r) * H + c] * (gate_row(r) ? s1 : s0);
+}
+
+__global__ void gate_bwd_kernel(const float* __restrict__ Y, const float* __restrict__ gG,
+                                long long E, int H, float* __restrict__ gY) {
+    long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= E * H) return;
+    long long e = t / H;
+    int c = (int)(t - e * H);
+    const float* y = Y + e * 11LL * H;
+    const float* gg = gG + e * 9LL * H;
+    float* gy = gY + e * 11LL * H;
+    float s0 = sigmoid_f(y[c]), s1 = sigmoid_f(y[H + c]);
+    gy[2 * H + c] = gg[c] * dsilu_f(y[2 * H + c]);
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int r = 1; r < kNsph; ++r) {
+        float g = gg[r * H + c];
+        float v = y[(2 + r) * H + c];
+        if (gate_row(r)) {
+            gy[(2 + r) * H + c] = g * s1;
+            a1 = fmaf(g, v, a1);
+        } else {
+            gy[(2 + r) * H + c] = g * s0;
+            a0 = fmaf(g, v, a0);
+        }
+    }
+    gy[c] = a0 * s0 * (1.f - s0);
+    gy[H + c] = a1 * s1 * (1.f - s1);
+}
+
+// --------------------------------------------------------- rotate-back + receiver reduction
+// acc[j] += s * sum over rows r of degree l(j) of W[r][j - l^2] * y[r]
+__device__ __forceinline__ void rotate_back_acc(const float* w, const float4* y, float s,
+                                                float4* acc) {
+    // l = 0: row 0
+    fma4(acc[0], s * w[row_off(0)], y[0]);
+    // l = 1: rows 1, 3, 5 -> columns 1..3
+#pragma unroll
+    for (int jj = 0; jj < 3; ++jj) {
+        fma4(acc[1 + jj], s * w[row_off(1) + jj], y[1]);
+        fma4(acc[1 + jj], s * w[row_off(3) + jj], y[3]);
+        fma4(acc[1 + jj], s * w[row_off(5) + jj], y[5]);
+    }
+    // l = 2: rows 2, 4, 6, 7, 8 -> columns 4..8
+#pragma unroll
+    for (int jj = 0; jj < 5; ++jj) {
+        fma4(acc[4 + jj], s * w[row_off(2) + jj], y[2]);
+        fma4(acc[4 + jj], s * w[row_off(4) + jj], y[4]);
+        fma4(acc[4 + jj], s * w[row_off(6) + jj], y[6]);
+        fma4(acc[4 + jj], s * w[row_off(7) + jj], y[7]);
+        fma4(acc[4 + jj], s * w[row_off(8) + jj], y[8]);
+    }
+}
+
+__global__ void __launch_bounds__(256) rotate_back_reduce_kernel(
+    const float* __restrict__ Y, const float* __restrict__ coef, const float* __restrict__ env,
+    long long N, int C, const int* __restrict__ recv_ptr, const float* __restrict__ resid,
+    float* __restrict__ out) {
+    long long n = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (n >= N) return;
+    int e0 = recv_ptr[n], e1 = recv_ptr[n + 1];
+    for (int c = lane * 4; c < C; c += 128) {
+        float4 acc[kNsph];
+#pragma unroll
+        for (int j = 0; j < kNsph; ++j) acc[j] = resid ? ld4(resid + (n * kNsph + j) * C + c) : f4(0.f);
+        for (int e = e0; e < e1; ++e) {
+            float w[kNnz];
+            load_coef(coef, e, w);
+            float s = __ldg(env + e);
+            float4 y[kNsph];
+            const float* ye = Y + (long long)e * kNsph * C;
+#pragma unroll
+            for (int r = 0; r < kNsph; ++r) y[r] = ld4(ye + r * C + c);
+            rotate_back_acc(w, y, s, acc);
+        }
+#pragma unroll
+        for (int j = 0; j < kNsph; ++j) st4(out + (n * kNsph + j) * C + c, acc[j]);
+    }
+}
+
+// -------------------------------------------------------------- rotate-back VJP (per edge)
+__global__ void __launch_bounds__(256) rotate_back_bwd_kernel(
+    const float* __restrict__ gx, const int* __restrict__ tgt, const float* __restrict__ coef,
+    const float* __restrict__ env, const float* __restrict__ Y, long long E, int C,
+    float* __restrict__ gY, float* __restrict__ g_env, float* __restrict__ g_coef) {
+    long long e = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (e >= E) return;
+    float w[kNnz];
+    load_coef(coef, e, w);
+    float s = env[e];
+    const float* gt = gx + (long long)tgt[e] * kNsph * C;
+    const float* ye = Y + e * kNsph * C;
+    float* ge = gY + e * kNsph * C;
+    float pc[kNnz];
+#pragma unroll
+    for (int k = 0; k < kNnz; ++k) pc[k] = 0.f;
+    float penv = 0.f;
+    for (int c = lane * 4; c < C; c += 128) {
+        float4 v[kNsph], y[kNsph];
+#pragma unroll
+        for (int j = 0; j < kNsph; ++j) {
+            v[j] = ld4(gt + j * C + c);
+            y[j] = ld4(ye + j * C + c);
+        }
+        float4 R[kNsph];
+        R[0] = wrow<0>(w, v); R[1] = wrow<1>(w, v); R[2] = wrow<2>(w, v);
+        R[3] = wrow<3>(w, v); R[4] = wrow<4>(w, v); R[5] = wrow<5>(w, v);
+        R[6] = wrow<6>(w, v); R[7] = wrow<7>(w, v); R[8] = wrow<8>(w, v);
+#pragma unroll
+        for (int r = 0; r < kNsph; ++r) {
+            penv += dot4(R[r], y[r]);
+            st4(ge + r * C + c, make_float4(s * R[r].x, s * R[r].y, s * R[r].z, s * R[r].w));
+        }
+#pragma unroll
+        for (int r = 0; r < kNsph; ++r) {
+            const int l = row_deg(r), o = row_off(r), c0 = deg_col0(l);
+            for (int jj = 0; jj < 2 * l + 1; ++jj) pc[o + jj] += dot4(v[c0 + jj], y[r]);
+        }
+    }
+    penv = warp_sum(penv);
+#pragma unroll
+    for (int k = 0; k < kNnz; ++k) pc[k] = warp_sum(pc[k]);
+    if (lane == 0) {
+        g_env[e] += penv;
+#pragma unroll
+        for (int k = 0; k < kNnz; ++k) g_coef[e * kNnz + k] += s * pc[k];
+    }
+}
+
+// ------------------------------------------------------------ rotate-in VJP (edge part)
+__global__ void __launch_bounds__(256) rotate_in_bwd_edge_kernel(
+    const float* __restrict__ gA, const float* __restrict__ rot, const float* __restrict__ rad,
+    long long ldr, int rad_col, const float* __restrict__ x, const int* __restrict__ src,
+    const int* __restrict__ tgt, const float* __restrict__ coef, long long E, int C,
+    float* __restrict__ g_rot, float* __restrict__ g_rad, float* __restrict__ g_coef) {
+    long long e = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (e >= E) return;
+    const int W2 = 2 * C;
+    const float* ga = gA + e * kNsph * W2;
+    const float* ro = rot + e * kNsph * W2;
+    const float* rr = rad + e * ldr + rad_col;
+    float* gr = g_rot + e * kNsph * W2;
+    float* grd = g_rad + e * ldr + rad_col;
+    const float* xs = x + (long long)src[e] * kNsph * C;
+    const float* xt = x + (long long)tgt[e] * kNsph * C;
+    float pc[kNnz];
+#pragma unroll
+    for (int k = 0; k < kNnz; ++k) pc[k] = 0.f;
+    for (int c = lane * 4; c < C; c += 128) {
+        float4 vs[kNsph], vt[kNsph];
+#pragma unroll
+        for (int j = 0; j < kNsph; ++j) {
+            vs[j] = ld4(xs + j * C + c);
+            vt[j] = ld4(xt + j * C + c);
+        }
+        // the two halves (source channels, target channels) of every row
+        float4 gsl[6], gtl[6];   // radial-slice adjoints
+#pragma unroll
+        for (int q = 0; q < 6; ++q) gsl[q] = gtl[q] = f4(0.f);
+#pragma unroll
+        for (int r = 0; r < kNsph; ++r) {
+            const int q = rad_slice(r);
+            float4 gas = ld4(ga + r * W2 + c), gat = ld4(ga + r * W2 + C + c);
+            float4 ms = ld4(rr + q * W2 + c), mt = ld4(rr + q * W2 + C + c);
+            float4 rs = ld4(ro + r * W2 + c), rt = ld4(ro + r * W2 + C + c);
+            float4 gs = mul4(gas, ms), gt = mul4(gat, mt);
+            st4(gr + r * W2 + c, gs);
+            st4(gr + r * W2 + C + c, gt);
+            float4 ps = mul4(gas, rs), pt = mul4(gat, rt);
+            gsl[q].x += ps.x; gsl[q].y += ps.y; gsl[q].z += ps.z; gsl[q].w += ps.w;
+            gtl[q].x += pt.x; gtl[q].y += pt.y; gtl[q].z += pt.z; gtl[q].w += pt.w;
+            const int l = row_deg(r), o = row_off(r), c0 = deg_col0(l);
+#pragma unroll
+            for (int jj = 0; jj < 2 * l + 1; ++jj)
+                pc[o + jj] += dot4(gs, vs[c0 + jj]) + dot4(gt, vt[c0 + jj]);
+        }
+#pragma unroll
+        for (int q = 0; q < 6; ++q) {
+            st4(grd + q * W2 + c, gsl[q]);
+            st4(grd + q * W2 + C + c, gtl[q]);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < kNnz; ++k) pc[k] = warp_sum(pc[k]);
+    if (lane == 0) {
+#pragma unroll
+        for (int k = 0; k < kNnz; ++k) g_coef[e * kNnz + k] += pc[k];
+    }
+}
+
+// acc[j] += sum over rows r of degree l(j) of W[r][j - l^2] * g[r]   (Wig^T g)
+__device__ __forceinline__ void wig_t_acc(const float* w, const float4* g, float4* acc) {
+    rotate_back_acc(w, g, 1.f, acc);
+}
+
+// ------------------------------------------------------------ rotate-in VJP (node part)
+__global__ void __launch_bounds__(256) rotate_in_bwd_node_kernel(
+    const float* __restrict__ g_rot, const float* __restrict__ coef, long long N, int C,
+    const int* __restrict__ recv_ptr, const int* __restrict__ send_ptr,
+    const int* __restrict__ send_eid, int accumulate, float* __restrict__ gx) {
+    long long n = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (n >= N) return;
+    const int W2 = 2 * C;
+    for (int c = lane * 4; c < C; c += 128) {
+        float4 acc[kNsph];
+#pragma unroll
+        for (int j = 0; j < kNsph; ++j) acc[j] = accumulate ? ld4(gx + (n * kNsph + j) * C + c) : f4(0.f);
+        // this node as receiver: target half of the rotated rows
+        for (int e = recv_ptr[n]; e < recv_ptr[n + 1]; ++e) {
+            float w[kNnz];
+            load_coef(coef, e, w);
+            float4 g[kNsph];
+            const float* ge = g_rot + (long long)e * kNsph * W2 + C;
+#pragma unroll
+            for (int r = 0; r < kNsph; ++r) g[r] = ld4(ge + r * W2 + c);
+            wig_t_acc(w, g, acc);
+        }
+        // this node as sender: source half
+        for (int k = send_ptr[n]; k < send_ptr[n + 1]; ++k) {
+            int e = send_eid[k];
+            float w[kNnz];
+            load_coef(coef, e, w);
+            float4 g[kNsph];
+            const float* ge = g_rot + (long long)e * kNsph * W2;
+#pragma unroll
+            for (int r = 0; r < kNsph; ++r) g[r] = ld4(ge + r * W2 + c);
+            wig_t_acc(w, g, acc);
+        }
+#pragma unroll
+        for (int j = 0; j < kNsph; ++j) st4(gx + (n * kNsph + j) * C + c, acc[j]);
+    }
+}
+
+// ----------------------------------------------------------------- edge-degree node init
+__global__ void __launch_bounds__(256) edge_degree_fwd_kernel(
+    const float* __restrict__ rad, long long ldr, const float* __restrict__ coef,
+    const float* __restrict__ env, const float* __restrict__ l0, long long N, int C,
+    const int* __restrict__ recv_ptr, float inv_rescale, float* __restrict__ x) {
+    long long n = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (n >= N) return;
+    for (int c = lane * 4; c < C; c += 128) {
+        float4 acc[kNsph];
+#pragma unroll
+        for (int j = 0; j < kNsph; ++j) acc[j] = f4(0.f);
+        for (int e = recv_ptr[n]; e < recv_ptr[n + 1]; ++e) {
+            float w[kNnz];
+            load_coef(coef, e, w);
+            float s = env[e] * inv_rescale;
+            const float* re = rad + (long long)e * ldr;
+            float4 y[kNsph];
+            y[0] = ld4(re + c);
+            y[1] = ld4(re + C + c);
+            y[2] = ld4(re + 2 * C + c);
+#pragma unroll
+            for (int r = 3; r < kNsph; ++r) y[r] = f4(0.f);
+            // only rows 0..2 (the m = 0 rows) carry the radial output
+            fma4(acc[0], s * w[row_off(0)], y[0]);
+#pragma unroll
+            for (int jj = 0; jj < 3; ++jj) fma4(acc[1 + jj], s * w[row_off(1) + jj], y[1]);
+#pragma unroll
+            for (int jj = 0; jj < 5; ++jj) fma4(acc[4 + jj], s * w[row_off(2) + jj], y[2]);
+        }
+        float4 z = ld4(l0 + n * C + c);
+        acc[0].x += z.x; acc[0].y += z.y; acc[0].z += z.z; acc[0].w += z.w;
+#pragma unroll
+        for (int j = 0; j < kNsph; ++j) st4(x + (n * kNsph + j) * C + c, acc[j]);
+    }
+}
+
+__global__ void __launch_bounds__(256) edge_degree_bwd_kernel(
+    const float* __restrict__ gx, const int* __restrict__ tgt, const float* __restrict__ rad,
+    long long ldr, const float* __restrict__ coef, const float* __restrict__ env, long long E,
+    int C, float inv_rescale, float* __restrict__ g_rad, long long ldg,
+    float* __restrict__ g_env, float* __restrict__ g_coef) {
+    long long e = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (e >= E) return;
+    float w[kNnz];
+    load_coef(coef, e, w);
+    float s = env[e] * inv_rescale;
+    const float* gt = gx + (long long)tgt[e] * kNsph * C;
+    const float* re = rad + e * ldr;
+    float* gr = g_rad + e * ldg;
+    float pc[9];   // rows 0..2 hold 1 + 3 + 5 = 9 coefficients (packed offsets 0..8)
+#pragma unroll
+    for (int k = 0; k < 9; ++k) pc[k] = 0.f;
+    float penv = 0.f;
+    for (int c = lane * 4; c < C; c += 128) {
+        float4 v[kNsph];
+#pragma unroll
+        for (int j = 0; j < kNsph; ++j) v[j] = ld4(gt + j * C + c);
+        float4 R0 = wrow<0>(w, v), R1 = wrow<1>(w, v), R2 = wrow<2>(w, v);
+        float4 y0 = ld4(re + c), y1 = ld4(re + C + c), y2 = ld4(re + 2 * C + c);
+        penv += dot4(R0, y0) + dot4(R1, y1) + dot4(R2, y2);
+        st4(gr + c, make_float4(s * R0.x, s * R0.y, s * R0.z, s * R0.w));
+        st4(gr + C + c, make_float4(s * R1.x, s * R1.y, s * R1.z, s * R1.w));
+        st4(gr + 2 * C + c, make_float4(s * R2.x, s * R2.y, s * R2.z, s * R2.w));
+        pc[0] += dot4(v[0], y0);
+#pragma unroll
+        for (int jj = 0; jj < 3; ++jj) pc[1 + jj] += dot4(v[1 + jj], y1);
+#pragma unroll
+        for (int jj = 0; jj < 5; ++jj) pc[4 + jj] += dot4(v[4 + jj], y2);
+    }
+    penv = warp_sum(penv);
+#pragma unroll
+    for (int k = 0; k < 9; ++k) pc[k] = warp_sum(pc[k]);
+    if (lane == 0) {
+        g_env[e] += penv * inv_rescale;
+#pragma unroll
+        for (int k = 0; k < 9; ++k) g_coef[e * kNnz + k] += s * pc[k];
+    }
+}
+
+static int check_c(int C) {
+    ATOM_REQUIRE(C > 0 && C % 4 == 0, "channel count must be a positive multiple of 4 (got %d)", C);
+    return ATOM_OK;
+}
+
+}  // namespace atom
+
+using namespace atom;
+
+#define WARP_GRID(n) ceil_div((long long)(n) * 32, 256), 256, 0, (cudaStream_t)stream
+
+extern "C" int atom_rotate_in(const float* x, const int* src, const int* tgt, const float* coef,
+                              int64_t E, int C, const float* rad, int64_t ldr, int rad_col,
+                              float* rot, float* A, void* stream) {
+    if (int s = check_c(C)) return s;
+    ATOM_REQUIRE(!rad || (ldr % 4 == 0 && rad_col % 4 == 0), "rad must be float4-aligned");
+    if (E == 0) return ATOM_OK;
+    rotate_in_kernel<<<WARP_GRID(E)>>>(x, src, tgt, coef, E, C, rad, ldr, rad_col, rot, A);
+    ATOM_CHECK_LAUNCH("rotate_in");
+    return ATOM_OK;
+}
+
+extern "C" int atom_gate_fwd(const float* Y, int64_t E, int H, float* G, void* stream) {
+    ATOM_REQUIRE(H > 0, "H must be positive");
+    if (E == 0) return ATOM_OK;
+    gate_fwd_kernel<<<ceil_div(E * H, 256), 256, 0, (cudaStream_t)stream>>>(Y, E, H, G);
+    ATOM_CHECK_LAUNCH("gate_fwd");
+    return ATOM_OK;
+}
+
+extern "C" int atom_gate_bwd(const float* Y, const float* gG, int64_t E, int H, float* gY,
+                             void* stream) {
+    ATOM_REQUIRE(H > 0, "H must be positive");
+    if (E == 0) return ATOM_OK;
+    gate_bwd_kernel<<<ceil_div(E * H, 256), 256, 0, (cudaStream_t)stream>>>(Y, gG, E, H, gY);
+    ATOM_CHECK_LAUNCH("gate_bwd");
+    return ATOM_OK;
+}
+
+extern "C" int atom_rotate_back_reduce(const float* Y, const float* coef, const float* env,
+                                       int64_t N, int C, const int* recv_ptr,
+                                       const float* resid, float* out, void* stream) {
+    if (int s = check_c(C)) return s;
+    if (N == 0) return ATOM_OK;
+    rotate_back_reduce_kernel<<<WARP_GRID(N)>>>(Y, coef, env, N, C, recv_ptr, resid, out);
+    ATOM_CHECK_LAUNCH("rotate_back_reduce");
+    return ATOM_OK;
+}
+
+extern "C" int atom_rotate_back_bwd(const float* gx, const int* tgt, const float* coef,
+                                    const float* env, const float* Y, int64_t E, int C,
+                                    float* gY, float* g_env, float* g_coef, void* stream) {
+    if (int s = check_c(C)) return s;
+    if (E == 0) return ATOM_OK;
+    rotate_back_bwd_kernel<<<WARP_GRID(E)>>>(gx, tgt, coef, env, Y, E, C, gY, g_env, g_coef);
+    ATOM_CHECK_LAUNCH("rotate_back_bwd");
+    return ATOM_OK;
+}
+
+extern "C" int atom_rotate_in_bwd_edge(const float* gA, const float* rot, const float* rad,
+                                       int64_t ldr, int rad_col, const float* x, const int* src,
+                                       const int* tgt, const float* coef, int64_t E, int C,
+                                       float* g_rot, float* g_rad, float* g_coef, void* stream) {
+    if (int s = check_c(C)) return s;
+    ATOM_REQUIRE(ldr % 4 == 0 && rad_col % 4 == 0, "rad must be float4-aligned");
+    if (E == 0) return ATOM_OK;
+    rotate_in_bwd_edge_kernel<<<WARP_GRID(E)>>>(gA, rot, rad, ldr, rad_col, x, src, tgt, coef,
+                                                E, C, g_rot, g_rad, g_coef);
+    ATOM_CHECK_LAUNCH("rotate_in_bwd_edge");
+    return ATOM_OK;
+}
+
+extern "C" int atom_rotate_in_bwd_node(const float* g_rot, const float* coef, int64_t N, int C,
+                                       const int* recv_ptr, const int* send_ptr,
+                                       const int* send_eid, int accumulate, float* gx,
+                                       void* stream) {
+    if (int s = check_c(C)) return s;
+    if (N == 0) return ATOM_OK;
+    rotate_in_bwd_node_kernel<<<WARP_GRID(N)>>>(g_rot, coef, N, C, recv_ptr, send_ptr, send_eid,
+                                                accumulate, gx);
+    ATOM_CHECK_LAUNCH("rotate_in_bwd_node");
+    return ATOM_OK;
+}
+
+extern "C" int atom_edge_degree_fwd(const float* rad, int64_t ldr, const float* coef,
+                                    const float* env, const float* l0, int64_t N, int C,
+                                    const int* recv_ptr, float rescale, float* x, void* stream) {
+    if (int s = check_c(C)) return s;
+    ATOM_REQUIRE(ldr % 4 == 0, "rad must be float4-aligned");
+    if (N == 0) return ATOM_OK;
+    edge_degree_fwd_kernel<<<WARP_GRID(N)>>>(rad, ldr, coef, env, l0, N, C, recv_ptr,
+                                             1.0f / rescale, x);
+    ATOM_CHECK_LAUNCH("edge_degree_fwd");
+    return ATOM_OK;
+}
+
+extern "C" int atom_edge_degree_bwd(const float* gx, const int* tgt, const float* rad,
+                                    int64_t ldr, const float* coef, const float* env, int64_t E,
+                                    int C, float rescale, float* g_rad, int64_t ldg,
+                                    float* g_env, float* g_coef, void* stream) {
+    if (int s = check_c(C)) return s;
+    ATOM_REQUIRE(ldr % 4 == 0 && ldg % 4 == 0, "rad/g_rad must be float4-aligned");
+    if (E == 0) return ATOM_OK;
+    edge_degree_bwd_kernel<<<WARP_GRID(E)>>>(gx, tgt, rad, ldr, coef, env, E, C, 1.0f / rescale,
+                                             g_rad, ldg, g_env, g_coef);
+    ATOM_CHECK_LAUNCH("edge_degree_bwd");
+    return ATOM_OK;
+}

@@ -1,0 +1,308 @@
+// Device neighbour list with the reference's fp32 predicate and edge order, plus the CSR
+// helpers (prefix scan, sender CSR).
+//
+// Reference: tt_atom/geometry.py:48-81 (radius_graph). Aperiodic pairs are kept when
+// ||pos[a] - pos[b]|| < cutoff (torch.linalg.norm, which on the CPU evaluates
+// sqrt(fma(z, z, fma(y, y, x*x))) correctly rounded) and the edge list is ordered by
+// (source a, target b). Periodic triples (i, j, c) are kept when
+// |pos[i] - (pos[j] + shift[c])|^2 <= cutoff^2 and > 1e-8, with the square summed as
+// (x*x + y*y) + z*z, no fused multiply-add, and ordered by (receiver i, source j, image c).
+//
+// This kernel emits receiver-major lists: receiver i, sources in (j, c) order. For periodic
+// systems that IS the reference order. For aperiodic systems the distance is symmetric, so the
+// per-receiver lists are the reference edge set transposed; the reference (source-major) order
+// is recovered from the sender CSR (atom_sender_csr).
+//
+// Optional cap (not in the reference): keep per receiver the max_nbrs candidates with the
+// smallest distance measure (aperiodic: distance, periodic: squared distance), ties broken by
+// candidate order; survivors keep candidate order.
+#include "common.cuh"
+
+namespace atom {
+
+struct SysRange {
+    // per-receiver candidate range [lo, hi) is the receiver's own system
+    const long long* sys_ptr;
+    int nsys;
+};
+
+__device__ __forceinline__ int find_sys(const long long* sp, int nsys, long long i) {
+    int lo = 0, hi = nsys;   // sp[lo] <= i < sp[hi]
+    while (hi - lo > 1) {
+        int mid = (lo + hi) >> 1;
+        if (sp[mid] <= i) lo = mid; else hi = mid;
+    }
+    return lo;
+}
+
+// Pass 1: one warp per receiver, candidates in (j, c) order tested 32 at a time; the survivors
+// are appended in order (ballot + popc) to the receiver's candidate slots.
+__global__ void nl_collect_kernel(const float* __restrict__ pos, long long N,
+                                  const long long* __restrict__ sys_ptr, int nsys,
+                                  const float* __restrict__ shifts, int S, float cutoff,
+                                  float cut2, int periodic, int max_nbrs, int max_cand,
+                                  int* __restrict__ cand_idx, float* __restrict__ cand_d,
+                                  int* __restrict__ recv_cnt, int* __restrict__ need) {
+    long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (i >= N) return;
+    int k = find_sys(sys_ptr, nsys, i);
+    long long lo = sys_ptr[k], hi = sys_ptr[k + 1];
+    float pix = pos[i * 3 + 0], piy = pos[i * 3 + 1], piz = pos[i * 3 + 2];
+    long long total = (hi - lo) * (long long)S;
+    int cnt = 0;
+    int* ci = cand_idx + i * (long long)max_cand;
+    float* cd = cand_d + i * (long long)max_cand;
+    const float tiny = 1e-8f;
+    for (long long base = 0; base < total; base += 32) {
+        long long t = base + lane;
+        bool keep = false;
+        float key = 0.f;
+        if (t < total) {
+            long long j = lo + t / S;
+            int c = (int)(t % S);
+            float pjx = pos[j * 3 + 0], pjy = pos[j * 3 + 1], pjz = pos[j * 3 + 2];
+            if (periodic) {
+                float qx = __fadd_rn(pjx, shifts[c * 3 + 0]);
+                float qy = __fadd_rn(pjy, shifts[c * 3 + 1]);
+                float qz = __fadd_rn(pjz, shifts[c * 3 + 2]);
+                float dx = __fsub_rn(pix, qx), dy = __fsub_rn(piy, qy), dz = __fsub_rn(piz, qz);
+                float d2 = __fadd_rn(__fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)),
+                                     __fmul_rn(dz, dz));
+                keep = (d2 <= cut2) && (d2 > tiny);
+                key = d2;
+            } else {
+                // the reference evaluates ||pos[a] - pos[b]|| with a = source j, b = receiver i
+                float dx = __fsub_rn(pjx, pix), dy = __fsub_rn(pjy, piy), dz = __fsub_rn(pjz, piz);
+                float d = __fsqrt_rn(__fmaf_rn(dz, dz, __fmaf_rn(dy, dy, __fmul_rn(dx, dx))));
+                keep = (d < cutoff) && (d > 0.f);
+                key = d;
+            }
+        }
+        unsigned m = __ballot_sync(0xffffffffu, keep);
+        if (keep) {
+            int slot = cnt + __popc(m & ((1u << lane) - 1u));
+            if (slot < max_cand) {
+                ci[slot] = (int)t;
+                cd[slot] = key;
+            }
+        }
+        cnt += __popc(m);
+    }
+    if (cnt > max_cand) {
+        if (lane == 0) atomicMax(need, cnt);
+        if (lane == 0) recv_cnt[i] = 0;
+        return;
+    }
+    int kept = cnt;
+    __syncwarp();
+    if (max_nbrs > 0 && cnt > max_nbrs) {
+        // rank of each candidate by (key, position); drop those ranked >= max_nbrs
+        for (int a = lane; a < cnt; a += 32) {
+            float ka = cd[a];
+            int rank = 0;
+            for (int b = 0; b < cnt; ++b) {
+                float kb = cd[b];
+                rank += (kb < ka) || (kb == ka && b < a);
+            }
+            if (rank >= max_nbrs) ci[a] |= (int)0x80000000;
+        }
+        __syncwarp();
+        // compact survivors in place, in order
+        int w = 0;
+        for (int base = 0; base < cnt; base += 32) {
+            int a = base + lane;
+            int v = a < cnt ? ci[a] : (int)0x80000000;
+            float d = a < cnt ? cd[a] : 0.f;
+            bool s = v >= 0;
+            unsigned m = __ballot_sync(0xffffffffu, s);
+            __syncwarp();
+            if (s) {
+                int slot = w + __popc(m & ((1u << lane) - 1u));
+                ci[slot] = v;
+                cd[slot] = d;
+            }
+            __syncwarp();
+            w += __popc(m);
+        }
+        kept = w;
+    }
+    if (lane == 0) recv_cnt[i] = kept;
+}
+
+// Pass 2: copy each receiver's survivors to its CSR slots.
+__global__ void nl_fill_kernel(long long N, const long long* __restrict__ sys_ptr, int nsys,
+                               int S, int max_cand, const int* __restrict__ cand_idx,
+                               const int* __restrict__ recv_cnt, const int* __restrict__ recv_ptr,
+                               int* __restrict__ esrc, int* __restrict__ etgt,
+                               int* __restrict__ eimg) {
+    long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (i >= N) return;
+    int k = find_sys(sys_ptr, nsys, i);
+    long long lo = sys_ptr[k];
+    int n = recv_cnt[i], o = recv_ptr[i];
+    const int* ci = cand_idx + i * (long long)max_cand;
+    for (int a = lane; a < n; a += 32) {
+        int t = ci[a];
+        esrc[o + a] = (int)(lo + t / S);
+        etgt[o + a] = (int)i;
+        if (eimg) eimg[o + a] = t % S;
+    }
+}
+
+// Exclusive scan, one 1024-thread block walking the array in chunks.
+__global__ void scan_kernel(const int* __restrict__ cnt, long long n, int* __restrict__ ptr) {
+    __shared__ int sh[1024];
+    __shared__ int carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (long long base = 0; base < n; base += 1024) {
+        long long i = base + threadIdx.x;
+        int v = i < n ? cnt[i] : 0;
+        sh[threadIdx.x] = v;
+        __syncthreads();
+        for (int o = 1; o < 1024; o <<= 1) {
+            int t = threadIdx.x >= o ? sh[threadIdx.x - o] : 0;
+            __syncthreads();
+            sh[threadIdx.x] += t;
+            __syncthreads();
+        }
+        if (i < n) ptr[i] = carry + sh[threadIdx.x] - v;
+        __syncthreads();
+        if (threadIdx.x == 1023) carry += sh[1023];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) ptr[n] = carry;
+}
+
+__global__ void count_src_kernel(const int* __restrict__ src, long long E, int* __restrict__ cnt) {
+    long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e < E) atomicAdd(cnt + src[e], 1);
+}
+
+__global__ void zero_int_kernel(int* p, long long n) {
+    long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < n) p[t] = 0;
+}
+
+__global__ void scatter_src_kernel(const int* __restrict__ src, long long E,
+                                   const int* __restrict__ ptr, int* __restrict__ fill,
+                                   int* __restrict__ eid) {
+    long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e < E) {
+        int s = src[e];
+        int slot = atomicAdd(fill + s, 1);
+        eid[ptr[s] + slot] = (int)e;
+    }
+}
+
+// Sort each sender's segment ascending (one warp per node; odd-even transposition over the
+// segment, which is short).
+__global__ void sort_segments_kernel(long long N, const int* __restrict__ ptr,
+                                     int* __restrict__ eid) {
+    long long n = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (n >= N) return;
+    int b = ptr[n], len = ptr[n + 1] - b;
+    int* s = eid + b;
+    for (int phase = 0; phase < len; ++phase) {
+        for (int a = 2 * lane + (phase & 1); a + 1 < len; a += 64) {
+            int x = s[a], y = s[a + 1];
+            if (x > y) {
+                s[a] = y;
+                s[a + 1] = x;
+            }
+        }
+        __syncwarp();
+    }
+}
+
+}  // namespace atom
+
+using namespace atom;
+
+extern "C" int atom_neighbor_list(const float* pos, int64_t N, const int64_t* sys_ptr_host,
+                                  int nsys, const float* shifts, int nshift, float cutoff,
+                                  int periodic, int max_nbrs, int max_cand, int* cand_idx,
+                                  float* cand_d, int* recv_cnt, const int* recv_ptr,
+                                  int* edge_src, int* edge_tgt, int* edge_img,
+                                  void* small_scratch, int* need_host, void* stream) {
+    ATOM_REQUIRE(nsys >= 1 && nsys <= 1 << 20, "nsys out of range");
+    ATOM_REQUIRE(nshift >= 1 && max_cand >= 1, "nshift and max_cand must be positive");
+    ATOM_REQUIRE(sys_ptr_host[0] == 0 && sys_ptr_host[nsys] == N, "sys_ptr must span [0, N)");
+    ATOM_REQUIRE(N * (long long)nshift < (1LL << 31), "N * nshift too large for this kernel");
+    cudaStream_t st = (cudaStream_t)stream;
+    if (N == 0) return ATOM_OK;
+    ATOM_REQUIRE(small_scratch && (reinterpret_cast<uintptr_t>(small_scratch) & 7u) == 0,
+                 "small_scratch must be 8-byte aligned");
+    // system offsets and the capacity flag live in the caller's small scratch
+    long long* sp = reinterpret_cast<long long*>(small_scratch);
+    cudaError_t ce = cudaMemcpyAsync(sp, sys_ptr_host, (nsys + 1) * sizeof(long long),
+                                     cudaMemcpyHostToDevice, st);
+    if (ce != cudaSuccess) {
+        set_error("neighbor_list: copy of system offsets failed: %s", cudaGetErrorString(ce));
+        return ATOM_ERR_CUDA;
+    }
+    if (edge_src == nullptr) {
+        int* dneed = reinterpret_cast<int*>(sp + nsys + 1);
+        cudaMemsetAsync(dneed, 0, sizeof(int), st);
+        float cut2 = (float)((double)cutoff * (double)cutoff);
+        nl_collect_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(
+            pos, N, sp, nsys, shifts, nshift, cutoff, cut2, periodic, max_nbrs, max_cand,
+            cand_idx, cand_d, recv_cnt, dneed);
+        ATOM_CHECK_LAUNCH("neighbor_list collect");
+        int h = 0;
+        ce = cudaMemcpyAsync(&h, dneed, sizeof(int), cudaMemcpyDeviceToHost, st);
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
+        if (ce != cudaSuccess) {
+            set_error("neighbor_list: %s", cudaGetErrorString(ce));
+            return ATOM_ERR_CUDA;
+        }
+        if (need_host) *need_host = h;
+        if (h > 0) {
+            set_error("neighbor_list: a receiver has %d candidates > max_cand %d", h, max_cand);
+            return ATOM_ERR_CAPACITY;
+        }
+        return ATOM_OK;
+    }
+    ATOM_REQUIRE(recv_ptr && edge_tgt, "pass 2 needs recv_ptr and edge_tgt");
+    nl_fill_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(N, sp, nsys, nshift, max_cand, cand_idx,
+                                                        recv_cnt, recv_ptr, edge_src, edge_tgt,
+                                                        edge_img);
+    ATOM_CHECK_LAUNCH("neighbor_list fill");
+    return ATOM_OK;
+}
+
+extern "C" int atom_exclusive_scan(const int* cnt, int64_t n, int* ptr, int* total_host,
+                                   void* stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    scan_kernel<<<1, 1024, 0, st>>>(cnt, n, ptr);
+    ATOM_CHECK_LAUNCH("exclusive_scan");
+    if (total_host) {
+        cudaError_t ce = cudaMemcpyAsync(total_host, ptr + n, sizeof(int), cudaMemcpyDeviceToHost, st);
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
+        if (ce != cudaSuccess) {
+            set_error("exclusive_scan: %s", cudaGetErrorString(ce));
+            return ATOM_ERR_CUDA;
+        }
+    }
+    return ATOM_OK;
+}
+
+extern "C" int atom_sender_csr(const int* edge_src, int64_t E, int64_t N, int* scratch,
+                               int* send_ptr, int* send_eid, void* stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    if (N == 0) return ATOM_OK;
+    zero_int_kernel<<<ceil_div(N, 256), 256, 0, st>>>(scratch, N);
+    if (E > 0) count_src_kernel<<<ceil_div(E, 256), 256, 0, st>>>(edge_src, E, scratch);
+    scan_kernel<<<1, 1024, 0, st>>>(scratch, N, send_ptr);
+    zero_int_kernel<<<ceil_div(N, 256), 256, 0, st>>>(scratch, N);
+    if (E > 0) {
+        scatter_src_kernel<<<ceil_div(E, 256), 256, 0, st>>>(edge_src, E, send_ptr, scratch,
+                                                              send_eid);
+        sort_segments_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(N, send_ptr, send_eid);
+    }
+    ATOM_CHECK_LAUNCH("sender_csr");
+    return ATOM_OK;
+}

@@ -1,0 +1,383 @@
+// Node-side ops: equivariant RMS norm (tt_atom/norm.py:24-111; VJP tt_atom/forces.py:73-98), the
+// radial LayerNorm+SiLU and its VJP (tt_atom/so2.py:101-163), per-node sphere-grid projections
+// (tt_atom/grid.py:63-76; VJP tt_atom/forces.py:230-252), SiLU VJP and deterministic sums.
+#include "common.cuh"
+
+namespace atom {
+
+// Degree of standard-order coefficient j and its balance weight 1/(2l+1)/(lmax+1), lmax = 2.
+__host__ __device__ constexpr int coef_deg(int j) { return j == 0 ? 0 : (j < 4 ? 1 : 2); }
+__device__ __forceinline__ float bal_w(int j) {
+    return coef_deg(j) == 0 ? (1.0f / 3.0f) : (coef_deg(j) == 1 ? (1.0f / 9.0f) : (1.0f / 15.0f));
+}
+
+// ---------------------------------------------------------------------- RMS norm SH (fwd)
+// One warp per node; the node's 9 x C values are held in registers (C <= 256).
+template <int CPL>  // channels per lane = C / 32 rounded up
+__global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(
+    const float* __restrict__ x, long long N, int C, const float* __restrict__ aw,
+    const float* __restrict__ ab, const float* __restrict__ add0, float eps,
+    float* __restrict__ out) {
+    long long n = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (n >= N) return;
+    const float* xn = x + n * kNsph * C;
+    float v[kNsph][CPL];
+    float s0 = 0.f;
+#pragma unroll
+    for (int j = 0; j < kNsph; ++j)
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+            int c = lane + 32 * q;
+            v[j][q] = c < C ? xn[j * C + c] : 0.f;
+        }
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) s0 += v[0][q];
+    float mean0 = warp_sum(s0) / C;
+#pragma unroll
+    for (int q = 0; q < CPL; ++q)
+        if (lane + 32 * q < C) v[0][q] -= mean0;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kNsph; ++j) {
+        float t = 0.f;
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) t = fmaf(v[j][q], v[j][q], t);
+        ss = fmaf(bal_w(j), t, ss);
+    }
+    float fn = rsqrtf(warp_sum(ss) / C + eps);
+    float* on = out + n * kNsph * C;
+#pragma unroll
+    for (int j = 0; j < kNsph; ++j)
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+            int c = lane + 32 * q;
+            if (c >= C) continue;
+            float r = v[j][q] * (fn * aw[coef_deg(j) * C + c]);
+            if (j == 0) {
+                r += ab[c];
+                if (add0) r += add0[n * C + c];
+            }
+            on[j * C + c] = r;
+        }
+}
+
+// ---------------------------------------------------------------------- RMS norm SH (VJP)
+// out_j = xc_j * fn * a_j (+ bias on j = 0); u_j = g_j * a_j;
+// d/dxc_j = fn u_j - fn^3 bal_j xc_j S / C with S = sum_j sum_c u_j xc_j; the l = 0 centring
+// subtracts the channel mean of the j = 0 adjoint.
+template <int CPL>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
+    const float* __restrict__ x, const float* __restrict__ g, long long N, int C,
+    const float* __restrict__ aw, float eps, int accumulate, float* __restrict__ gx) {
+    long long n = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (n >= N) return;
+    const float* xn = x + n * kNsph * C;
+    const float* gn = g + n * kNsph * C;
+    float v[kNsph][CPL];
+    float s0 = 0.f;
+#pragma unroll
+    for (int j = 0; j < kNsph; ++j)
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+            int c = lane + 32 * q;
+            v[j][q] = c < C ? xn[j * C + c] : 0.f;
+        }
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) s0 += v[0][q];
+    float mean0 = warp_sum(s0) / C;
+#pragma unroll
+    for (int q = 0; q < CPL; ++q)
+        if (lane + 32 * q < C) v[0][q] -= mean0;
+    float ss = 0.f, S = 0.f;
+#pragma unroll
+    for (int j = 0; j < kNsph; ++j) {
+        float t = 0.f;
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+            int c = lane + 32 * q;
+            t = fmaf(v[j][q], v[j][q], t);
+            if (c < C) S = fmaf(gn[j * C + c] * aw[coef_deg(j) * C + c], v[j][q], S);
+        }
+        ss = fmaf(bal_w(j), t, ss);
+    }
+    float fn = rsqrtf(warp_sum(ss) / C + eps);
+    S = warp_sum(S);
+    float k3 = fn * fn * fn * S / C;
+    float* go = gx + n * kNsph * C;
+    float gsum0 = 0.f;
+    float gr0[CPL];
+#pragma unroll
+    for (int j = 0; j < kNsph; ++j)
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+            int c = lane + 32 * q;
+            if (c >= C) {
+                if (j == 0) gr0[q] = 0.f;
+                continue;
+            }
+            float u = gn[j * C + c] * aw[coef_deg(j) * C + c];
+            float r = fn * u - k3 * bal_w(j) * v[j][q];
+            if (j == 0) {
+                gr0[q] = r;
+                gsum0 += r;
+            } else {
+                go[j * C + c] = accumulate ? go[j * C + c] + r : r;
+            }
+        }
+    float m = warp_sum(gsum0) / C;
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) {
+        int c = lane + 32 * q;
+        if (c < C) go[c] = accumulate ? go[c] + (gr0[q] - m) : (gr0[q] - m);
+    }
+}
+
+// -------------------------------------------------------------- LayerNorm + SiLU (fwd, VJP)
+// One warp per (row, group).
+__global__ void ln_silu_fwd_kernel(const float* __restrict__ X, long long rows, long long ld,
+                                   int groups, int W, const float* __restrict__ gamma,
+                                   const float* __restrict__ beta, float eps,
+                                   float* __restrict__ Y) {
+    long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (wid >= rows * groups) return;
+    long long row = wid / groups;
+    int g = (int)(wid - row * groups);
+    const float* xr = X + row * ld + (long long)g * W;
+    float* yr = Y + row * ld + (long long)g * W;
+    const float* ga = gamma + g * W;
+    const float* be = beta + g * W;
+    float s = 0.f;
+    for (int c = lane; c < W; c += 32) s += xr[c];
+    float mean = warp_sum(s) / W;
+    float v = 0.f;
+    for (int c = lane; c < W; c += 32) {
+        float d = xr[c] - mean;
+        v = fmaf(d, d, v);
+    }
+    float rstd = rsqrtf(warp_sum(v) / W + eps);
+    for (int c = lane; c < W; c += 32) yr[c] = silu_f((xr[c] - mean) * rstd * ga[c] + be[c]);
+}
+
+// gY and dX may alias (in-place)
+__global__ void ln_silu_bwd_kernel(const float* __restrict__ X, const float* gY,
+                                   long long rows, long long ld, int groups, int W,
+                                   const float* __restrict__ gamma,
+                                   const float* __restrict__ beta, float eps, float* dX) {
+    long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (wid >= rows * groups) return;
+    long long row = wid / groups;
+    int g = (int)(wid - row * groups);
+    const float* xr = X + row * ld + (long long)g * W;
+    const float* gr = gY + row * ld + (long long)g * W;
+    float* dr = dX + row * ld + (long long)g * W;
+    const float* ga = gamma + g * W;
+    const float* be = beta + g * W;
+    float s = 0.f;
+    for (int c = lane; c < W; c += 32) s += xr[c];
+    float mean = warp_sum(s) / W;
+    float v = 0.f;
+    for (int c = lane; c < W; c += 32) {
+        float d = xr[c] - mean;
+        v = fmaf(d, d, v);
+    }
+    float rstd = rsqrtf(warp_sum(v) / W + eps);
+    float s1 = 0.f, s2 = 0.f;
+    for (int c = lane; c < W; c += 32) {
+        float xh = (xr[c] - mean) * rstd;
+        float gy = gr[c] * dsilu_f(xh * ga[c] + be[c]) * ga[c];
+        s1 += gy;
+        s2 = fmaf(gy, xh, s2);
+    }
+    s1 = warp_sum(s1) / W;
+    s2 = warp_sum(s2) / W;
+    for (int c = lane; c < W; c += 32) {
+        float xh = (xr[c] - mean) * rstd;
+        float gy = gr[c] * dsilu_f(xh * ga[c] + be[c]) * ga[c];
+        dr[c] = rstd * (gy - s1 - xh * s2);
+    }
+}
+
+// ------------------------------------------------------------------- per-node projection
+// out[n, q, c] (+)= sum_p M[q, p] in[n, p, c]; one thread per (n, c); M staged in shared memory.
+__global__ void node_project_kernel(const float* __restrict__ in, long long N, int P, int C,
+                                    const float* __restrict__ M, int Q, int trans,
+                                    int accumulate, float* __restrict__ out) {
+    extern __shared__ float sm[];   // [Q * P]
+    for (int i = threadIdx.x; i < Q * P; i += blockDim.x) {
+        int q = i / P, p = i - q * P;
+        sm[i] = trans ? M[p * Q + q] : M[q * P + p];
+    }
+    __syncthreads();
+    long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= N * C) return;
+    long long n = t / C;
+    int c = (int)(t - n * C);
+    const float* xin = in + n * (long long)P * C + c;
+    float* o = out + n * (long long)Q * C + c;
+    float v[64];
+    for (int p = 0; p < P; ++p) v[p] = xin[(long long)p * C];
+    for (int q = 0; q < Q; ++q) {
+        float acc = 0.f;
+        const float* mr = sm + q * P;
+        for (int p = 0; p < P; ++p) acc = fmaf(mr[p], v[p], acc);
+        o[(long long)q * C] = accumulate ? o[(long long)q * C] + acc : acc;
+    }
+}
+
+// g and out may alias (in-place)
+__global__ void silu_bwd_kernel(const float* g, const float* __restrict__ pre, long long n,
+                                float* out) {
+    long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < n) out[t] = g[t] * dsilu_f(pre[t]);
+}
+
+// Deterministic segmented sum: one 256-thread block per segment, strided partials then a
+// fixed shared-memory tree.
+__global__ void segment_sum_kernel(const float* __restrict__ v, long long n,
+                                   const int* __restrict__ seg_ptr, float* __restrict__ out) {
+    __shared__ float sh[256];
+    long long b = seg_ptr ? seg_ptr[blockIdx.x] : 0;
+    long long e = seg_ptr ? seg_ptr[blockIdx.x + 1] : n;
+    float s = 0.f;
+    for (long long i = b + threadIdx.x; i < e; i += 256) s += v[i];
+    sh[threadIdx.x] = s;
+    __syncthreads();
+    for (int o = 128; o > 0; o >>= 1) {
+        if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) out[blockIdx.x] = sh[0];
+}
+
+}  // namespace atom
+
+using namespace atom;
+
+#define WARP_GRID(n) ceil_div((long long)(n) * 32, 256), 256, 0, (cudaStream_t)stream
+
+extern "C" int atom_rmsnorm_sh_fwd(const float* x, int64_t N, int C, const float* aw,
+                                   const float* ab, const float* add0, float eps, float* out,
+                                   void* stream) {
+    ATOM_REQUIRE(C > 0 && C <= 256, "rmsnorm: C must be in [1, 256] (got %d)", C);
+    if (N == 0) return ATOM_OK;
+    if (C <= 32)
+        rmsnorm_fwd_kernel<1><<<WARP_GRID(N)>>>(x, N, C, aw, ab, add0, eps, out);
+    else if (C <= 64)
+        rmsnorm_fwd_kernel<2><<<WARP_GRID(N)>>>(x, N, C, aw, ab, add0, eps, out);
+    else if (C <= 128)
+        rmsnorm_fwd_kernel<4><<<WARP_GRID(N)>>>(x, N, C, aw, ab, add0, eps, out);
+    else
+        rmsnorm_fwd_kernel<8><<<WARP_GRID(N)>>>(x, N, C, aw, ab, add0, eps, out);
+    ATOM_CHECK_LAUNCH("rmsnorm_sh_fwd");
+    return ATOM_OK;
+}
+
+extern "C" int atom_rmsnorm_sh_bwd(const float* x, const float* g, int64_t N, int C,
+                                   const float* aw, float eps, int accumulate, float* gx,
+                                   void* stream) {
+    ATOM_REQUIRE(C > 0 && C <= 256, "rmsnorm: C must be in [1, 256] (got %d)", C);
+    if (N == 0) return ATOM_OK;
+    if (C <= 32)
+        rmsnorm_bwd_kernel<1><<<WARP_GRID(N)>>>(x, g, N, C, aw, eps, accumulate, gx);
+    else if (C <= 64)
+        rmsnorm_bwd_kernel<2><<<WARP_GRID(N)>>>(x, g, N, C, aw, eps, accumulate, gx);
+    else if (C <= 128)
+        rmsnorm_bwd_kernel<4><<<WARP_GRID(N)>>>(x, g, N, C, aw, eps, accumulate, gx);
+    else
+        rmsnorm_bwd_kernel<8><<<WARP_GRID(N)>>>(x, g, N, C, aw, eps, accumulate, gx);
+    ATOM_CHECK_LAUNCH("rmsnorm_sh_bwd");
+    return ATOM_OK;
+}
+
+extern "C" int atom_ln_silu_fwd(const float* X, int64_t rows, int64_t ld, int groups, int W,
+                                const float* gamma, const float* beta, float eps, float* Y,
+                                void* stream) {
+    ATOM_REQUIRE(groups > 0 && W > 0 && ld >= (int64_t)groups * W, "ln_silu: bad shape");
+    if (rows == 0) return ATOM_OK;
+    ln_silu_fwd_kernel<<<WARP_GRID(rows * groups)>>>(X, rows, ld, groups, W, gamma, beta, eps, Y);
+    ATOM_CHECK_LAUNCH("ln_silu_fwd");
+    return ATOM_OK;
+}
+
+extern "C" int atom_ln_silu_bwd(const float* X, const float* gY, int64_t rows, int64_t ld,
+                                int groups, int W, const float* gamma, const float* beta,
+                                float eps, float* dX, void* stream) {
+    ATOM_REQUIRE(groups > 0 && W > 0 && ld >= (int64_t)groups * W, "ln_silu: bad shape");
+    if (rows == 0) return ATOM_OK;
+    ln_silu_bwd_kernel<<<WARP_GRID(rows * groups)>>>(X, gY, rows, ld, groups, W, gamma, beta,
+                                                     eps, dX);
+    ATOM_CHECK_LAUNCH("ln_silu_bwd");
+    return ATOM_OK;
+}
+
+extern "C" int atom_node_project(const float* in, int64_t N, int P, int C, const float* M,
+                                 int Q, int trans, int accumulate, float* out, void* stream) {
+    ATOM_REQUIRE(P > 0 && P <= 64 && Q > 0 && Q <= 64 && C > 0, "node_project: bad shape");
+    if (N == 0) return ATOM_OK;
+    node_project_kernel<<<ceil_div(N * C, 128), 128, Q * P * sizeof(float),
+                          (cudaStream_t)stream>>>(in, N, P, C, M, Q, trans, accumulate, out);
+    ATOM_CHECK_LAUNCH("node_project");
+    return ATOM_OK;
+}
+
+extern "C" int atom_silu_bwd(const float* g, const float* pre, int64_t n, float* out,
+                             void* stream) {
+    if (n == 0) return ATOM_OK;
+    silu_bwd_kernel<<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(g, pre, n, out);
+    ATOM_CHECK_LAUNCH("silu_bwd");
+    return ATOM_OK;
+}
+
+extern "C" int atom_segment_sum(const float* v, int64_t n, const int* seg_ptr, int nseg,
+                                float* out, void* stream) {
+    ATOM_REQUIRE(nseg >= 1 && (seg_ptr || nseg == 1), "segment_sum: bad segments");
+    segment_sum_kernel<<<nseg, 256, 0, (cudaStream_t)stream>>>(v, n, seg_ptr, out);
+    ATOM_CHECK_LAUNCH("segment_sum");
+    return ATOM_OK;
+}
+
+namespace atom {
+
+__global__ void node_embed_kernel(const int* __restrict__ Z, const int* __restrict__ sys,
+                                  const float* __restrict__ sphere,
+                                  const float* __restrict__ sysemb, long long N, int C,
+                                  float* __restrict__ out) {
+    long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= N * C) return;
+    long long n = t / C;
+    int c = (int)(t - n * C);
+    int s = sys ? sys[n] : 0;
+    out[t] = sphere[(long long)Z[n] * C + c] + sysemb[(long long)s * C + c];
+}
+
+__global__ void edge_species_kernel(const int* __restrict__ Z, const int* __restrict__ src,
+                                    const int* __restrict__ tgt, long long E,
+                                    int* __restrict__ zs, int* __restrict__ zt) {
+    long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= E) return;
+    zs[e] = Z[src[e]];
+    zt[e] = Z[tgt[e]];
+}
+
+}  // namespace atom
+
+extern "C" int atom_node_embed(const int* Z, const int* sys_id, const float* sphere,
+                               const float* sysemb, int64_t N, int C, float* out, void* stream) {
+    if (N == 0) return ATOM_OK;
+    node_embed_kernel<<<ceil_div(N * C, 256), 256, 0, (cudaStream_t)stream>>>(Z, sys_id, sphere,
+                                                                            sysemb, N, C, out);
+    ATOM_CHECK_LAUNCH("node_embed");
+    return ATOM_OK;
+}
+
+extern "C" int atom_edge_species(const int* Z, const int* src, const int* tgt, int64_t E,
+                                 int* zs, int* zt, void* stream) {
+    if (E == 0) return ATOM_OK;
+    edge_species_kernel<<<ceil_div(E, 256), 256, 0, (cudaStream_t)stream>>>(Z, src, tgt, E, zs, zt);
+    ATOM_CHECK_LAUNCH("edge_species");
+    return ATOM_OK;
+}

@@ -1,0 +1,150 @@
+"""ctypes binding of ``libatomb200.so`` (declarations in include/atom_b200.h).
+
+The library must exist: there is no CPU or eager fallback. Every wrapper raises RuntimeError
+with the library's own message when an entry point returns a non-zero status.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+
+import torch
+
+_LIB_PATH = pathlib.Path(__file__).resolve().with_name("libatomb200.so")
+_lib = None
+
+ATOM_ERR_CAPACITY = 3
+
+c_void_p, c_int, c_int64, c_float = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+
+
+class GemmGroups(ctypes.Structure):
+    _fields_ = [("ngroups", c_int), ("a_col", c_int * 8), ("K", c_int * 8), ("c_col", c_int * 8),
+                ("N", c_int * 8), ("ldb", c_int * 8), ("t_col", c_int * 8),
+                ("B", c_void_p * 8), ("bias", c_void_p * 8)]
+
+
+_SIGS = {
+    "atom_last_error": (ctypes.c_char_p, ctypes.c_size_t),
+    "atom_abi_version": (),
+    "atom_fused_rotate": (c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p,
+                          c_void_p, c_void_p, c_void_p, c_void_p),
+    "atom_fused_rotate_gc": (c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p,
+                             c_void_p, c_void_p, c_void_p),
+    "atom_fused_gate": (c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p,
+                        c_void_p),
+    "atom_fused_ln_bw": (c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float,
+                         c_void_p, c_void_p),
+    "atom_neighbor_list": (c_void_p, c_int64, c_void_p, c_int, c_void_p, c_int, c_float, c_int,
+                           c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p),
+    "atom_exclusive_scan": (c_void_p, c_int64, c_void_p, c_void_p, c_void_p),
+    "atom_sender_csr": (c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p),
+    "atom_edge_geometry": (c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
+                           c_void_p, c_void_p, c_void_p, c_int, c_float, c_float, c_void_p,
+                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p),
+    "atom_edge_geometry_bwd": (c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                               c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_float, c_float,
+                               c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p),
+    "atom_forces_virial": (c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                           c_void_p, c_void_p, c_void_p, c_void_p),
+    "atom_gemm": (c_void_p, c_int64, c_int64, ctypes.POINTER(GemmGroups), c_void_p, c_int64,
+                  c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int,
+                  c_void_p),
+    "atom_rotate_in": (c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_int64,
+                       c_int, c_void_p, c_void_p, c_void_p),
+    "atom_gate_fwd": (c_void_p, c_int64, c_int, c_void_p, c_void_p),
+    "atom_gate_bwd": (c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p),
+    "atom_rotate_back_reduce": (c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p,
+                                c_void_p, c_void_p),
+    "atom_rotate_back_bwd": (c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int,
+                             c_void_p, c_void_p, c_void_p, c_void_p),
+    "atom_rotate_in_bwd_edge": (c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p,
+                                c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p,
+                                c_void_p),
+    "atom_rotate_in_bwd_node": (c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p,
+                                c_int, c_void_p, c_void_p),
+    "atom_edge_degree_fwd": (c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int,
+                             c_void_p, c_float, c_void_p, c_void_p),
+    "atom_edge_degree_bwd": (c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64,
+                             c_int, c_float, c_void_p, c_int64, c_void_p, c_void_p, c_void_p),
+    "atom_ln_silu_fwd": (c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_float,
+                         c_void_p, c_void_p),
+    "atom_ln_silu_bwd": (c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p,
+                         c_float, c_void_p, c_void_p),
+    "atom_rmsnorm_sh_fwd": (c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_float,
+                            c_void_p, c_void_p),
+    "atom_rmsnorm_sh_bwd": (c_void_p, c_void_p, c_int64, c_int, c_void_p, c_float, c_int,
+                            c_void_p, c_void_p),
+    "atom_node_project": (c_void_p, c_int64, c_int, c_int, c_void_p, c_int, c_int, c_int,
+                          c_void_p, c_void_p),
+    "atom_silu_bwd": (c_void_p, c_void_p, c_int64, c_void_p, c_void_p),
+    "atom_segment_sum": (c_void_p, c_int64, c_void_p, c_int, c_void_p, c_void_p),
+    "atom_node_embed": (c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p,
+                        c_void_p),
+    "atom_edge_species": (c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p),
+}
+
+
+def lib():
+    """Load the kernel library (once). Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not _LIB_PATH.exists():
+            raise RuntimeError(f"{_LIB_PATH.name} is not built; run `python -m tt_atom.build` "
+                               "(this package has no CPU fallback)")
+        L = ctypes.CDLL(str(_LIB_PATH))
+        for name, args in _SIGS.items():
+            f = getattr(L, name)
+            f.argtypes = list(args)
+            f.restype = c_int
+        _lib = L
+    return _lib
+
+
+def declared_symbols():
+    return list(_SIGS)
+
+
+def last_error():
+    buf = ctypes.create_string_buffer(1024)
+    lib().atom_last_error(buf, 1024)
+    return buf.value.decode(errors="replace")
+
+
+class AtomError(RuntimeError):
+    def __init__(self, name, code):
+        super().__init__(f"{name} failed (status {code}): {last_error()}")
+        self.code = code
+
+
+def call(name, *args):
+    rc = getattr(lib(), name)(*args)
+    if rc != 0:
+        raise AtomError(name, rc)
+    return rc
+
+
+def ptr(t):
+    """Device pointer of a tensor (or None -> NULL)."""
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def stream_ptr(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def host_i32(values):
+    arr = (ctypes.c_int * len(values))(*[int(v) for v in values])
+    return arr
+
+
+def host_f32(values):
+    return (ctypes.c_float * len(values))(*[float(v) for v in values])
+
+
+def host_i64(values):
+    return (ctypes.c_int64 * len(values))(*[int(v) for v in values])

@@ -1,0 +1,165 @@
+"""``TTAtomCalculator``: the ASE calculator over the GPU engine (drop-in for the reference's
+tt_atom/calculator.py:23-277 and tt_atom/ase_base.py:18-54).
+
+Same constructor and methods (``calculate``, ``evaluate_batch``, ``close``), same results keys
+(energy, free_energy, energies, forces, stress), same energy normaliser
+(``E = rmsd * E_raw + mean + sum refs[Z]``, ``F = rmsd * F_raw``, stress = rmsd * virial / V as
+Voigt-6) and the same errors (no edges -> ValueError; task mismatch -> ValueError). ``device`` /
+``device_id`` name a CUDA device. ``trace=True`` captures the step in a CUDA graph per topology
+and replays it while the neighbour list (and image shifts) are unchanged.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from .ase_compat import _AseCalculator, all_changes, atoms_volume, voigt_6
+from .engine import CapturedStep, UMAEngine
+from .graph import build_graph, csd_embedding
+from .weights import WeightBundle
+
+
+def _fields(system):
+    """positions, Z, charge, spin, cell, pbc of an ASE Atoms / dict / (pos, Z) tuple
+    (tt_atom/disjoint.py:30-56)."""
+    if hasattr(system, "get_positions"):
+        pbc = np.asarray(system.get_pbc())
+        cell = np.asarray(system.get_cell(), dtype=np.float32) if pbc.any() else None
+        return (np.asarray(system.get_positions(), dtype=np.float32),
+                np.asarray(system.get_atomic_numbers(), dtype=np.int64),
+                float(system.info.get("charge", 0.0)), float(system.info.get("spin", 0.0)),
+                cell, pbc if pbc.any() else None)
+    if isinstance(system, dict):
+        return (np.asarray(system["pos"], dtype=np.float32), np.asarray(system["Z"], np.int64),
+                float(system.get("charge", 0.0)), float(system.get("spin", 0.0)),
+                system.get("cell"), system.get("pbc"))
+    pos, Z = system
+    return np.asarray(pos, np.float32), np.asarray(Z, np.int64), 0.0, 0.0, None, None
+
+
+class TTAtomCalculator(_AseCalculator):
+    implemented_properties = ["energy", "energies", "free_energy", "forces", "stress"]
+
+    def __init__(self, bundle, task_name=None, device=None, device_id=0, gamma=0.0, fast=False,
+                 trace=False, precision="fp32", max_neighbors="config", **kwargs):
+        super().__init__(**kwargs)
+        if isinstance(bundle, str):
+            bundle = WeightBundle.load(bundle)
+        if gamma != 0.0:
+            raise ValueError("only the roll gauge gamma = 0 is implemented (energy and forces "
+                             "do not depend on it)")
+        self.bundle = bundle
+        self.cfg = bundle.config
+        self.C = self.cfg["sphere_channels"]
+        self.trace = trace
+        self.fast = fast
+        if task_name is not None and task_name != bundle.task:
+            raise ValueError(
+                f"task_name={task_name!r} does not match this bundle's task {bundle.task!r}. "
+                f"UMA's MoLE routing bakes the task into the merged bundle; export a bundle for "
+                f"{task_name!r} to use that task.")
+        self.task = self.task_name = bundle.task
+        self.max_neighbors = (self.cfg.get("max_neighbors") if max_neighbors == "config"
+                              else max_neighbors)
+        if device is None:
+            device = torch.device("cuda", device_id)
+        self.device = torch.device(device)
+        w = bundle.weights
+        self._w = w
+        self.engine = UMAEngine(w, self.cfg, bundle.tables(), device=self.device,
+                                precision=precision)
+        self.scale_rmsd = bundle.scale_rmsd
+        self.scale_mean = bundle.scale_mean
+        self.elem_refs = bundle.elem_refs
+        self._ws = None
+        self._ws_key = None
+        self._step = None
+
+    # ------------------------------------------------------------------------------ core
+    def _graph(self, pos, Z, cell, pbc, sys_ptr=None):
+        return build_graph(pos, Z, self.cfg["cutoff"], cell, pbc,
+                           max_neighbors=self.max_neighbors, sys_ptr=sys_ptr, device=self.device)
+
+    def _evaluate(self, pos, Z, cell, pbc, charges, spins, sys_ptr=None, forces=True,
+                  stress=False, trace=False):
+        """Raw (unnormalised) per-system energies [nsys], forces [N, 3], virial [3, 3]|None."""
+        g = self._graph(pos, Z, cell, pbc, sys_ptr)
+        if g.E == 0:
+            raise ValueError("no edges within cutoff — system too sparse for this model")
+        se = csd_embedding(self._w, charges, spins, self.C, dataset=self.task)
+        key = (g.N, g.E, bool(stress), bool(forces))
+        reuse = (trace and self._ws is not None and self._ws_key == key
+                 and g.same_topology(self._ws.graph) and torch.equal(self._se, se))
+        if not reuse:
+            self._ws = self.engine.workspace(g, se)
+            self._ws_key, self._se, self._step = key, se, None
+        ws = self._ws
+        ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))
+        if trace:
+            if self._step is None:
+                self._step = CapturedStep(self.engine, ws, forces=forces, virial=stress)
+            self._step()
+        else:
+            self.engine.run(ws, ws.pos, forces=forces, virial=stress)
+        E = ws.energy.double().cpu()
+        F = ws.forces.double().cpu() if forces else None
+        V = ws.virial.double().cpu() if stress else None
+        return E, F, V
+
+    # ------------------------------------------------------------------------------- ASE
+    def calculate(self, atoms=None, properties=("energy", "forces"), system_changes=all_changes):
+        super().calculate(atoms, properties, system_changes)
+        pos, Z, charge, spin, cell, pbc = _fields(atoms)
+        want_stress = cell is not None and ("stress" in properties or bool(np.all(pbc)))
+        E, F, V = self._evaluate(pos, Z, cell, pbc, [charge], [spin], forces=True,
+                                 stress=want_stress, trace=self.trace and "stress" not in properties)
+        e = self.scale_rmsd * float(E[0]) + self.scale_mean
+        if self.elem_refs is not None:
+            e += float(self.elem_refs[torch.as_tensor(Z)].sum())
+        F = (self.scale_rmsd * F).numpy()
+        n = len(Z)
+        self.results["energy"] = e
+        self.results["free_energy"] = e
+        self.results["energies"] = np.full(n, e / n, dtype=np.float64)
+        self.results["forces"] = F.astype(np.float64)
+        if V is not None:
+            self.results["stress"] = voigt_6(self.scale_rmsd * V.numpy() / atoms_volume(atoms))
+
+    def evaluate_batch(self, systems, properties=("energy", "forces"), trace=False):
+        """Disjoint-union batch of aperiodic systems in one device pass
+        (tt_atom/calculator.py:168-236). Returns dict(energy [K], forces list or None)."""
+        if len(systems) == 0:
+            raise ValueError("empty batch")
+        pos_all, Z_all, chg, spn, ptr_ = [], [], [], [], [0]
+        for k, s in enumerate(systems):
+            pos, Z, c, sp, cell, pbc = _fields(s)
+            if cell is not None:
+                raise ValueError("evaluate_batch takes aperiodic systems")
+            pos_all.append(pos)
+            Z_all.append(Z)
+            chg.append(c)
+            spn.append(sp)
+            ptr_.append(ptr_[-1] + len(Z))
+        want_forces = "forces" in properties
+        pos = np.concatenate(pos_all)
+        Z = np.concatenate(Z_all)
+        g = self._graph(pos, Z, None, None, ptr_)
+        cnt = torch.diff(g.recv_ptr.long().cpu())
+        for k in range(len(systems)):
+            if int(cnt[ptr_[k]:ptr_[k + 1]].sum()) == 0:
+                raise ValueError(f"system {k} has no edges within cutoff — too sparse for this model")
+        E, F, _ = self._evaluate(pos, Z, None, None, chg, spn, sys_ptr=ptr_, forces=want_forces,
+                                 trace=trace)
+        energies, forces_out = [], []
+        for k in range(len(systems)):
+            ek = self.scale_rmsd * float(E[k]) + self.scale_mean
+            if self.elem_refs is not None:
+                ek += float(self.elem_refs[torch.as_tensor(Z_all[k])].sum())
+            energies.append(ek)
+            if want_forces:
+                forces_out.append((self.scale_rmsd * F[ptr_[k]:ptr_[k + 1]]).numpy())
+        return dict(energy=np.array(energies), forces=forces_out if want_forces else None)
+
+    def close(self):
+        self._ws = None
+        self._step = None

@@ -1,0 +1,460 @@
+"""The eSCN-MD energy + force + stress engine on the GPU.
+
+``UMAEngine`` owns the device copies of the (re-laid-out) weights; ``Workspace`` owns every
+activation buffer for one graph topology. ``UMAEngine.run`` issues the whole step -- geometry,
+radial MLPs, the L edgewise/atomwise blocks, the energy head, then the hand-written reverse pass
+down to forces and the virial -- as a fixed sequence of C-ABI kernel launches on one stream, so
+the step can be captured once in a CUDA graph and replayed (``CapturedStep``).
+
+Reference structure followed (reference tt-atom):
+  forward   tt_atom/model.py:138-247 (_Block, Backbone), tt_atom/edgewise.py:39-87,
+            tt_atom/geometry.py:226-280 (geometry + edge-degree init)
+  backward  tt_atom/forces.py:73-495 (rmsnorm_bw .. backbone_bw) and the host autograd finish of
+            tt_atom/forces.py:545-589, here done on the GPU (geometry VJP, force/virial reduce).
+
+Weight re-layouts done once at load time:
+  * radial MLPs of all layers and of the edge-degree embedding are batched: their first linear
+    is split into the Gaussian columns (one GEMM over all groups) and the source/target
+    embedding columns, which are folded with the bias into per-species tables gathered in the
+    GEMM epilogue;
+  * each SO(2) m > 0 linear becomes one GEMM on [real | imag] with the block weight
+    [[P, Q], [-Q, P]] (W^T = [P | Q]), equal to the reference's (a - d, c + b) combination;
+  * transposed copies for the reverse pass.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib as L
+from ._lib import ptr
+
+# kernels launched per entry point (all others launch one)
+_LAUNCHES = {"atom_edge_geometry": 2, "atom_forces_virial": 3}
+_counter = [0]
+
+
+def call(name, *args):
+    _counter[0] += _LAUNCHES.get(name, 1)
+    return L.call(name, *args)
+
+PRECISIONS = {"fp32": 0}
+
+
+def _dev(t, device):
+    return t.detach().to(device=device, dtype=torch.float32).contiguous()
+
+
+class _Groups:
+    """A grouped-GEMM description (up to 8 groups) kept alive with its tensors."""
+
+    def __init__(self, groups):
+        self.keep = []
+        g = L.GemmGroups()
+        g.ngroups = len(groups)
+        for i, d in enumerate(groups):
+            g.a_col[i] = d["a_col"]
+            g.K[i] = d["K"]
+            g.c_col[i] = d["c_col"]
+            g.N[i] = d["N"]
+            B = d["B"]
+            g.ldb[i] = B.shape[1]
+            g.t_col[i] = d.get("t_col", 0)
+            g.B[i] = B.data_ptr()
+            self.keep.append(B)
+            b = d.get("bias")
+            g.bias[i] = b.data_ptr() if b is not None else None
+            if b is not None:
+                self.keep.append(b)
+        self.struct = g
+
+
+def _so2_blocks(W_m0, b_m0, W_m, cin, hout, extra):
+    """Forward/backward grouped-GEMM weights of one SO(2) convolution (lmax = mmax = 2).
+
+    A layout per edge: m-primed rows x cin -> columns [rows 0..2 | rows 3,4 | rows 5,6 | 7 | 8].
+    Output: [extra | rows 0..8 x hout]."""
+    fwd, bwd = [], []
+    k0 = 3 * cin
+    n0 = extra + 3 * hout
+    fwd.append(dict(a_col=0, K=k0, c_col=0, N=n0, B=W_m0.t().contiguous(), bias=b_m0))
+    bwd.append(dict(a_col=0, K=n0, c_col=0, N=k0, B=W_m0.contiguous()))
+    a_col, c_col = k0, n0
+    for m, W in enumerate(W_m, start=1):
+        nc = 3 - m
+        k = nc * cin            # per real/imag half
+        h = nc * hout
+        Wt = W.t()              # [k, 2h]
+        P, Q = Wt[:, :h], Wt[:, h:]
+        B = torch.cat([torch.cat([P, Q], 1), torch.cat([-Q, P], 1)], 0).contiguous()  # [2k, 2h]
+        fwd.append(dict(a_col=a_col, K=2 * k, c_col=c_col, N=2 * h, B=B))
+        bwd.append(dict(a_col=c_col, K=2 * h, c_col=a_col, N=2 * k, B=B.t().contiguous()))
+        a_col += 2 * k
+        c_col += 2 * h
+    return fwd, bwd
+
+
+class UMAEngine:
+    """Device-resident eSCN-MD (UMA, lmax = mmax = 2, grid feed-forward) for E, F and stress."""
+
+    def __init__(self, weights, cfg, tables, device="cuda", precision="fp32"):
+        if cfg.get("lmax", 2) != 2 or cfg.get("mmax", 2) != 2:
+            raise RuntimeError("this build implements lmax = mmax = 2 (uma-s shape) only")
+        if cfg.get("ff_type", "grid") != "grid":
+            raise RuntimeError("only the grid feed-forward is implemented")
+        L.lib()
+        self.device = torch.device(device)
+        self.cfg = dict(cfg)
+        self.precision = PRECISIONS[precision]
+        C, H = cfg["sphere_channels"], cfg["hidden_channels"]
+        EC, NB, NL = cfg["edge_channels"], cfg["num_distance_basis"], cfg["num_layers"]
+        self.C, self.H, self.EC, self.NB, self.NL = C, H, EC, NB, NL
+        self.cutoff = float(cfg["cutoff"])
+        w = {k: v.float() for k, v in weights.items()}
+        dev = self.device
+        d = lambda t: _dev(t, dev)  # noqa: E731
+
+        # fixed tables
+        self.jd1 = L.host_f32(w["Jd_1"].reshape(-1).tolist())
+        self.jd2 = L.host_f32(w["Jd_2"].reshape(-1).tolist())
+        to_m = tables["to_m"]
+        self.perm9 = L.host_i32(to_m.abs().argmax(dim=1).tolist())
+        self.offset = d(tables["gauss_offset"].reshape(-1))
+        self.coeff = float(tables["gauss_coeff"].reshape(-1)[0])
+        tg = tables["to_grid_mat"].reshape(-1, 9)
+        fg = tables["from_grid_mat"].reshape(-1, 9)
+        self.npts = tg.shape[0]
+        self.TG, self.FG = d(tg), d(fg)
+
+        # ---- radial MLPs: groups = layers' so2_conv_1 radial functions + edge-degree
+        prefixes = [f"blocks.{i}.edge_wise.so2_conv_1.rad_func" for i in range(NL)]
+        prefixes.append("edge_degree_embedding.rad_func")
+        G = len(prefixes)
+        if G > 8:
+            raise RuntimeError("at most 7 layers are supported by the batched radial GEMM")
+        self.G = G
+        src_emb, tgt_emb = w["source_embedding.weight"], w["target_embedding.weight"]
+        w0g, ts, tt, ln1g, ln1b, ln2g, ln2b = [], [], [], [], [], [], []
+        f2, f2b, f3, f3b, r_out = [], [], [], [], []
+        for p in prefixes:
+            W0, b0 = w[f"{p}.net.0.weight"], w[f"{p}.net.0.bias"]      # [EC, NB + 2 EC]
+            w0g.append(W0[:, :NB])
+            ts.append(src_emb @ W0[:, NB:NB + EC].t() + b0)
+            tt.append(tgt_emb @ W0[:, NB + EC:].t())
+            ln1g.append(w[f"{p}.net.1.weight"]); ln1b.append(w[f"{p}.net.1.bias"])
+            ln2g.append(w[f"{p}.net.4.weight"]); ln2b.append(w[f"{p}.net.4.bias"])
+            f2.append(w[f"{p}.net.3.weight"]); f2b.append(w[f"{p}.net.3.bias"])
+            f3.append(w[f"{p}.net.6.weight"]); f3b.append(w[f"{p}.net.6.bias"])
+            r_out.append(w[f"{p}.net.6.weight"].shape[0])
+        self.W0g_cat = d(torch.cat(w0g, 0))                       # [G*EC, NB]
+        self.rad1 = _Groups([dict(a_col=0, K=NB, c_col=0, N=G * EC,
+                                  B=d(torch.cat(w0g, 0).t()))])
+        self.Tsrc, self.Ttgt = d(torch.cat(ts, 1)), d(torch.cat(tt, 1))   # [nel, G*EC]
+        self.ln1g, self.ln1b = d(torch.cat(ln1g)), d(torch.cat(ln1b))
+        self.ln2g, self.ln2b = d(torch.cat(ln2g)), d(torch.cat(ln2b))
+        self.rad2 = _Groups([dict(a_col=g * EC, K=EC, c_col=g * EC, N=EC, B=d(f2[g].t()),
+                                  bias=d(f2b[g])) for g in range(G)])
+        self.rad2_bw = _Groups([dict(a_col=g * EC, K=EC, c_col=g * EC, N=EC, B=d(f2[g]))
+                                for g in range(G)])
+        self.rad_off = [0]
+        for o in r_out:
+            self.rad_off.append(self.rad_off[-1] + o)
+        self.ldr = self.rad_off[-1]
+        self.rad3 = _Groups([dict(a_col=g * EC, K=EC, c_col=self.rad_off[g], N=r_out[g],
+                                  B=d(f3[g].t()), bias=d(f3b[g])) for g in range(G)])
+        self.rad3_bw = _Groups([dict(a_col=self.rad_off[g], K=r_out[g], c_col=g * EC, N=EC,
+                                     B=d(f3[g])) for g in range(G)])
+        self.rad1_bw = _Groups([dict(a_col=0, K=G * EC, c_col=0, N=NB, B=self.W0g_cat)])
+        for i in range(NL):
+            assert r_out[i] == 12 * C, "so2_conv_1 radial output must be 6 * 2C"
+        assert r_out[NL] == 3 * C, "edge-degree radial output must be 3C"
+
+        # ---- per block
+        self.blocks = []
+        for i in range(NL):
+            p = f"blocks.{i}"
+            e1 = f"{p}.edge_wise.so2_conv_1"
+            e2 = f"{p}.edge_wise.so2_conv_2"
+            f1, b1 = _so2_blocks(d(w[f"{e1}.fc_m0.weight"]), d(w[f"{e1}.fc_m0.bias"]),
+                                 [d(w[f"{e1}.so2_m_conv.{m}.fc.weight"]) for m in range(2)],
+                                 2 * C, H, 2 * H)
+            f2_, b2_ = _so2_blocks(d(w[f"{e2}.fc_m0.weight"]), d(w[f"{e2}.fc_m0.bias"]),
+                                   [d(w[f"{e2}.so2_m_conv.{m}.fc.weight"]) for m in range(2)],
+                                   H, C, 0)
+            self.blocks.append(dict(
+                n1w=d(w[f"{p}.norm_1.affine_weight"]), n1b=d(w[f"{p}.norm_1.affine_bias"]),
+                n2w=d(w[f"{p}.norm_2.affine_weight"]), n2b=d(w[f"{p}.norm_2.affine_bias"]),
+                so2_1=_Groups(f1), so2_1_bw=_Groups(b1), so2_2=_Groups(f2_), so2_2_bw=_Groups(b2_),
+                ga=_Groups([dict(a_col=0, K=C, c_col=0, N=C,
+                                 B=d(w[f"{p}.atom_wise.grid_mlp.0.weight"].t()))]),
+                gb=_Groups([dict(a_col=0, K=C, c_col=0, N=C,
+                                 B=d(w[f"{p}.atom_wise.grid_mlp.2.weight"].t()))]),
+                gc=_Groups([dict(a_col=0, K=C, c_col=0, N=C,
+                                 B=d(w[f"{p}.atom_wise.grid_mlp.4.weight"].t()))]),
+                ga_bw=_Groups([dict(a_col=0, K=C, c_col=0, N=C,
+                                    B=d(w[f"{p}.atom_wise.grid_mlp.0.weight"]))]),
+                gb_bw=_Groups([dict(a_col=0, K=C, c_col=0, N=C,
+                                    B=d(w[f"{p}.atom_wise.grid_mlp.2.weight"]))]),
+                gc_bw=_Groups([dict(a_col=0, K=C, c_col=0, N=C,
+                                    B=d(w[f"{p}.atom_wise.grid_mlp.4.weight"]))]),
+            ))
+        self.nfw, self.nfb = d(w["norm.affine_weight"]), d(w["norm.affine_bias"])
+        E0, E2, E4 = w["energy_block.0.weight"], w["energy_block.2.weight"], w["energy_block.4.weight"]
+        self.eh0 = _Groups([dict(a_col=0, K=C, c_col=0, N=H, B=d(E0.t()),
+                                 bias=d(w["energy_block.0.bias"]))])
+        self.eh2 = _Groups([dict(a_col=0, K=H, c_col=0, N=H, B=d(E2.t()),
+                                 bias=d(w["energy_block.2.bias"]))])
+        self.eh4 = _Groups([dict(a_col=0, K=H, c_col=0, N=1, B=d(E4.t()),
+                                 bias=d(w["energy_block.4.bias"]))])
+        self.eh2_bw = _Groups([dict(a_col=0, K=H, c_col=0, N=H, B=d(E2))])
+        self.eh0_bw = _Groups([dict(a_col=0, K=H, c_col=0, N=C, B=d(E0))])
+        self.eh4_row = d(E4.reshape(-1))
+        self.sphere = d(w["sphere_embedding.weight"])
+        self._w_host = w
+
+    # ------------------------------------------------------------------------------ helpers
+    def _gemm(self, A, lda, M, groups, Cout, ldc, *, Cpre=None, T1=None, T2=None, idx1=None,
+              idx2=None, ldt=0, act=0, accumulate=0, stream=0):
+        call("atom_gemm", ptr(A), lda, M, groups.struct, ptr(Cout), ldc, ptr(Cpre), ptr(T1),
+             ptr(T2), ptr(idx1), ptr(idx2), ldt, act, accumulate, self.precision, stream)
+
+    def workspace(self, graph, sys_emb):
+        return Workspace(self, graph, sys_emb)
+
+    def launches_per_step(self, ws, forces=True, virial=True):
+        """Number of this library's kernels one ``run`` launches (counted, not estimated)."""
+        torch.cuda.synchronize()
+        c0 = _counter[0]
+        self.run(ws, ws.pos, forces=forces, virial=virial)
+        torch.cuda.synchronize()
+        return _counter[0] - c0
+
+    def so2_flop(self, E):
+        """Algorithmic FLOPs of one forward so2_1 grouped GEMM over E edges."""
+        C, H = self.C, self.H
+        mac = 6 * C * 5 * H + 8 * C * 4 * H + 4 * C * 2 * H
+        return 2.0 * E * mac
+
+    def time_kernels(self, ws, reps=5):
+        """Average device time of the dominant kernel (the layer-0 so2_1 grouped GEMM), timed
+        with CUDA events on the stream it is launched on."""
+        st = torch.cuda.Stream(device=self.device)
+        st.wait_stream(torch.cuda.current_stream())
+        s = st.cuda_stream
+        E = ws.graph.E
+        b = self.blocks[0]
+        with torch.cuda.stream(st):
+            self._gemm(ws.A1, 18 * self.C, E, b["so2_1"], ws.Y1[0], 11 * self.H, stream=s)
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record(st)
+            for _ in range(reps):
+                self._gemm(ws.A1, 18 * self.C, E, b["so2_1"], ws.Y1[0], 11 * self.H, stream=s)
+            t1.record(st)
+        st.synchronize()
+        torch.cuda.current_stream().wait_stream(st)
+        return dict(name="so2_conv_1 grouped GEMM", ms=t0.elapsed_time(t1) / reps,
+                    flop=self.so2_flop(E))
+
+    # --------------------------------------------------------------------------------- step
+    def run(self, ws, pos, forces=True, virial=False, stream=None):
+        """One E (+F, +virial) evaluation for ``pos`` [N, 3] (device fp32) on ``ws``'s graph.
+        Results land in ``ws.energy`` [nsys], ``ws.forces`` [N, 3], ``ws.virial`` [3, 3]."""
+        s = L.stream_ptr(stream)
+        g = ws.graph
+        N, E = g.N, g.E
+        C, H, EC, NB, G = self.C, self.H, self.EC, self.NB, self.G
+        if pos.data_ptr() != ws.pos.data_ptr():
+            ws.pos.copy_(pos)
+        # ---------------- geometry
+        call("atom_edge_geometry", ptr(ws.pos), ptr(g.src), ptr(g.tgt), ptr(g.img),
+             ptr(g.shifts), E, self.jd1, self.jd2, self.perm9, ptr(self.offset), NB, self.coeff,
+             self.cutoff, ptr(ws.coef), ptr(ws.gauss), ptr(ws.env), ptr(ws.ev), None, s)
+        # ---------------- radial MLPs (all groups at once)
+        self._gemm(ws.gauss, NB, E, self.rad1, ws.R0, G * EC, T1=self.Tsrc, T2=self.Ttgt,
+                   idx1=g.zs, idx2=g.zt, ldt=G * EC, stream=s)
+        call("atom_ln_silu_fwd", ptr(ws.R0), E, G * EC, G, EC, ptr(self.ln1g), ptr(self.ln1b),
+             1e-5, ptr(ws.H1), s)
+        self._gemm(ws.H1, G * EC, E, self.rad2, ws.R1, G * EC, stream=s)
+        call("atom_ln_silu_fwd", ptr(ws.R1), E, G * EC, G, EC, ptr(self.ln2g), ptr(self.ln2b),
+             1e-5, ptr(ws.H2), s)
+        self._gemm(ws.H2, G * EC, E, self.rad3, ws.RAD, self.ldr, stream=s)
+        # ---------------- edge-degree node init
+        ede = ws.RAD[:, self.rad_off[self.NL]:]
+        call("atom_edge_degree_fwd", ptr(ede), self.ldr, ptr(ws.coef), ptr(ws.env), ptr(ws.l0),
+             N, C, ptr(g.recv_ptr), 5.0, ptr(ws.x[0]), s)
+        # ---------------- blocks
+        for i, b in enumerate(self.blocks):
+            x, nb = ws.x[i], ws.nb[i]
+            call("atom_rmsnorm_sh_fwd", ptr(x), N, C, ptr(b["n1w"]), ptr(b["n1b"]),
+                 ptr(ws.sysn), 1e-5, ptr(nb), s)
+            call("atom_rotate_in", ptr(nb), ptr(g.src), ptr(g.tgt), ptr(ws.coef), E, C,
+                 ptr(ws.RAD), self.ldr, self.rad_off[i], ptr(ws.rot[i]), ptr(ws.A1), s)
+            self._gemm(ws.A1, 18 * C, E, b["so2_1"], ws.Y1[i], 11 * H, stream=s)
+            call("atom_gate_fwd", ptr(ws.Y1[i]), E, H, ptr(ws.Gt), s)
+            self._gemm(ws.Gt, 9 * H, E, b["so2_2"], ws.Y2[i], 9 * C, stream=s)
+            call("atom_rotate_back_reduce", ptr(ws.Y2[i]), ptr(ws.coef), ptr(ws.env), N, C,
+                 ptr(g.recv_ptr), ptr(x), ptr(ws.xm[i]), s)
+            call("atom_rmsnorm_sh_fwd", ptr(ws.xm[i]), N, C, ptr(b["n2w"]), ptr(b["n2b"]), None,
+                 1e-5, ptr(ws.n2), s)
+            P = self.npts
+            call("atom_node_project", ptr(ws.n2), N, 9, C, ptr(self.TG), P, 0, 0,
+                 ptr(ws.G0), s)
+            self._gemm(ws.G0, C, N * P, b["ga"], ws.h1, C, Cpre=ws.P1[i], act=1, stream=s)
+            self._gemm(ws.h1, C, N * P, b["gb"], ws.h2, C, Cpre=ws.P2[i], act=1, stream=s)
+            self._gemm(ws.h2, C, N * P, b["gc"], ws.h1, C, stream=s)
+            ws.x[i + 1].copy_(ws.xm[i])
+            call("atom_node_project", ptr(ws.h1), N, P, C, ptr(self.FG), 9, 1, 1,
+                 ptr(ws.x[i + 1]), s)
+        # ---------------- final norm + energy head
+        call("atom_rmsnorm_sh_fwd", ptr(ws.x[self.NL]), N, C, ptr(self.nfw), ptr(self.nfb), None,
+             1e-5, ptr(ws.ne), s)
+        self._gemm(ws.ne, 9 * C, N, self.eh0, ws.e1, H, Cpre=ws.e1p, act=1, stream=s)
+        self._gemm(ws.e1, H, N, self.eh2, ws.e2, H, Cpre=ws.e2p, act=1, stream=s)
+        self._gemm(ws.e2, H, N, self.eh4, ws.enode, 1, stream=s)
+        call("atom_segment_sum", ptr(ws.enode), N, ptr(g.sys_ptr), g.nsys, ptr(ws.energy), s)
+        if not forces:
+            return
+        self._backward(ws, virial, s)
+
+    def _backward(self, ws, virial, s):
+        g = ws.graph
+        N, E = g.N, g.E
+        C, H, EC, NB, G, NL = self.C, self.H, self.EC, self.NB, self.G, self.NL
+        P = self.npts
+        ws.g_coef.zero_()
+        ws.g_env.zero_()
+        # ---------------- energy head (seed dE/d e_node = 1)
+        call("atom_silu_bwd", ptr(ws.eh4_rows), ptr(ws.e2p), N * H, ptr(ws.ge2), s)
+        self._gemm(ws.ge2, H, N, self.eh2_bw, ws.ge1, H, stream=s)
+        call("atom_silu_bwd", ptr(ws.ge1), ptr(ws.e1p), N * H, ptr(ws.ge1), s)
+        ws.gne.zero_()
+        self._gemm(ws.ge1, H, N, self.eh0_bw, ws.gne, 9 * C, stream=s)
+        call("atom_rmsnorm_sh_bwd", ptr(ws.x[NL]), ptr(ws.gne), N, C, ptr(self.nfw), 1e-5, 0,
+             ptr(ws.gx), s)
+        # ---------------- blocks, reversed
+        for i in reversed(range(NL)):
+            b = self.blocks[i]
+            # atomwise (grid) VJP
+            call("atom_node_project", ptr(ws.gx), N, 9, C, ptr(self.FG), P, 0, 0, ptr(ws.h1), s)
+            self._gemm(ws.h1, C, N * P, b["gc_bw"], ws.h2, C, stream=s)
+            call("atom_silu_bwd", ptr(ws.h2), ptr(ws.P2[i]), N * P * C, ptr(ws.h2), s)
+            self._gemm(ws.h2, C, N * P, b["gb_bw"], ws.h1, C, stream=s)
+            call("atom_silu_bwd", ptr(ws.h1), ptr(ws.P1[i]), N * P * C, ptr(ws.h1), s)
+            self._gemm(ws.h1, C, N * P, b["ga_bw"], ws.h2, C, stream=s)
+            call("atom_node_project", ptr(ws.h2), N, P, C, ptr(self.TG), 9, 1, 0, ptr(ws.gn), s)
+            call("atom_rmsnorm_sh_bwd", ptr(ws.xm[i]), ptr(ws.gn), N, C, ptr(b["n2w"]), 1e-5, 1,
+                 ptr(ws.gx), s)
+            # edgewise VJP (gx now holds the adjoint of the block's mid point)
+            call("atom_rotate_back_bwd", ptr(ws.gx), ptr(g.tgt), ptr(ws.coef), ptr(ws.env),
+                 ptr(ws.Y2[i]), E, C, ptr(ws.gY2), ptr(ws.g_env), ptr(ws.g_coef), s)
+            self._gemm(ws.gY2, 9 * C, E, b["so2_2_bw"], ws.Gt, 9 * H, stream=s)
+            call("atom_gate_bwd", ptr(ws.Y1[i]), ptr(ws.Gt), E, H, ptr(ws.gY1), s)
+            self._gemm(ws.gY1, 11 * H, E, b["so2_1_bw"], ws.A1, 18 * C, stream=s)
+            call("atom_rotate_in_bwd_edge", ptr(ws.A1), ptr(ws.rot[i]), ptr(ws.RAD), self.ldr,
+                 self.rad_off[i], ptr(ws.nb[i]), ptr(g.src), ptr(g.tgt), ptr(ws.coef), E, C,
+                 ptr(ws.grot), ptr(ws.gRAD), ptr(ws.g_coef), s)
+            call("atom_rotate_in_bwd_node", ptr(ws.grot), ptr(ws.coef), N, C, ptr(g.recv_ptr),
+                 ptr(g.send_ptr), ptr(g.send_eid), 0, ptr(ws.gn), s)
+            call("atom_rmsnorm_sh_bwd", ptr(ws.x[i]), ptr(ws.gn), N, C, ptr(b["n1w"]), 1e-5, 1,
+                 ptr(ws.gx), s)
+        # ---------------- edge-degree VJP (gx = dE/dx_init)
+        ede_off = self.rad_off[NL]
+        call("atom_edge_degree_bwd", ptr(ws.gx), ptr(g.tgt), ptr(ws.RAD[:, ede_off:]), self.ldr,
+             ptr(ws.coef), ptr(ws.env), E, C, 5.0, ptr(ws.gRAD[:, ede_off:]), self.ldr,
+             ptr(ws.g_env), ptr(ws.g_coef), s)
+        # ---------------- radial VJP (all groups), down to the Gaussian basis
+        self._gemm(ws.gRAD, self.ldr, E, self.rad3_bw, ws.H2, G * EC, stream=s)
+        call("atom_ln_silu_bwd", ptr(ws.R1), ptr(ws.H2), E, G * EC, G, EC, ptr(self.ln2g),
+             ptr(self.ln2b), 1e-5, ptr(ws.H2), s)
+        self._gemm(ws.H2, G * EC, E, self.rad2_bw, ws.H1, G * EC, stream=s)
+        call("atom_ln_silu_bwd", ptr(ws.R0), ptr(ws.H1), E, G * EC, G, EC, ptr(self.ln1g),
+             ptr(self.ln1b), 1e-5, ptr(ws.H1), s)
+        self._gemm(ws.H1, G * EC, E, self.rad1_bw, ws.g_gauss, NB, stream=s)
+        # ---------------- geometry VJP, forces, virial
+        call("atom_edge_geometry_bwd", ptr(ws.pos), ptr(g.src), ptr(g.tgt), ptr(g.img),
+             ptr(g.shifts), E, self.jd1, self.jd2, self.perm9, ptr(self.offset), NB, self.coeff,
+             self.cutoff, ptr(ws.g_coef), ptr(ws.gauss), ptr(ws.g_gauss), ptr(ws.g_env),
+             ptr(ws.g_ev), s)
+        call("atom_forces_virial", ptr(ws.g_ev), ptr(ws.ev), E, N, ptr(g.recv_ptr),
+             ptr(g.send_ptr), ptr(g.send_eid), ptr(ws.forces),
+             ptr(ws.virial) if virial else None, ptr(ws.vscratch), s)
+
+
+class Workspace:
+    """Every device buffer of one step for one graph topology."""
+
+    def __init__(self, eng, graph, sys_emb):
+        self.graph = graph
+        dev = eng.device
+        N, E = graph.N, graph.E
+        C, H, EC, NB, G, NL = eng.C, eng.H, eng.EC, eng.NB, eng.G, eng.NL
+        P = eng.npts
+        f = lambda *shape: torch.empty(*shape, device=dev, dtype=torch.float32)  # noqa: E731
+        self.pos = f(N, 3)
+        self.coef, self.gauss, self.env, self.ev = f(E, 35), f(E, NB), f(E), f(E, 3)
+        self.R0, self.H1, self.R1, self.H2 = f(E, G * EC), f(E, G * EC), f(E, G * EC), f(E, G * EC)
+        self.RAD = f(E, eng.ldr)
+        self.x = [f(N, 9, C) for _ in range(NL + 1)]
+        self.nb = [f(N, 9, C) for _ in range(NL)]
+        self.xm = [f(N, 9, C) for _ in range(NL)]
+        self.rot = [f(E, 18 * C) for _ in range(NL)]
+        self.Y1 = [f(E, 11 * H) for _ in range(NL)]
+        self.Y2 = [f(E, 9 * C) for _ in range(NL)]
+        self.G0 = f(N * P, C)
+        self.P1 = [f(N * P, C) for _ in range(NL)]
+        self.P2 = [f(N * P, C) for _ in range(NL)]
+        self.A1, self.Gt = f(E, 18 * C), f(E, 9 * H)
+        self.n2, self.h1, self.h2 = f(N, 9, C), f(N * P, C), f(N * P, C)
+        self.ne, self.e1, self.e1p, self.e2, self.e2p = f(N, 9, C), f(N, H), f(N, H), f(N, H), f(N, H)
+        self.enode = f(N)
+        self.energy = f(graph.nsys)
+        # reverse pass
+        self.gY2, self.gY1, self.grot, self.gRAD = f(E, 9 * C), f(E, 11 * H), f(E, 18 * C), f(E, eng.ldr)
+        self.g_coef, self.g_env, self.g_gauss, self.g_ev = f(E, 35), f(E), f(E, NB), f(E, 3)
+        self.gx, self.gn, self.gne = f(N, 9, C), f(N, 9, C), f(N, 9, C)
+        self.ge1, self.ge2 = f(N, H), f(N, H)
+        self.eh4_rows = eng.eh4_row.reshape(1, H).expand(N, H).contiguous()
+        self.forces, self.virial, self.vscratch = f(N, 3), f(3, 3), f(9 * 1024)
+        # node embeddings (pos-independent): l0 = sphere[Z] + sys_emb; sys_emb per node
+        se = sys_emb.to(dev, torch.float32).contiguous()            # [nsys, C]
+        self.sysn = f(N, C)
+        zero_sphere = torch.zeros_like(eng.sphere)
+        s = L.stream_ptr()
+        call("atom_node_embed", ptr(graph.Z), ptr(graph.sys_id), ptr(zero_sphere), ptr(se), N, C,
+             ptr(self.sysn), s)
+        self.l0 = f(N, C)
+        call("atom_node_embed", ptr(graph.Z), ptr(graph.sys_id), ptr(eng.sphere), ptr(se), N, C,
+             ptr(self.l0), s)
+
+    def nbytes(self):
+        tot = 0
+        for v in self.__dict__.values():
+            if torch.is_tensor(v):
+                tot += v.numel() * v.element_size()
+            elif isinstance(v, list):
+                tot += sum(t.numel() * t.element_size() for t in v if torch.is_tensor(t))
+        return tot
+
+
+class CapturedStep:
+    """A CUDA graph of one full E+F(+virial) step on a fixed topology (the CUDA-graph
+    counterpart of tt_atom/trace.py:83-215): positions are refreshed in place, then replayed."""
+
+    def __init__(self, eng, ws, forces=True, virial=False, warmup=1):
+        self.eng, self.ws = eng, ws
+        self.stream = torch.cuda.Stream(device=eng.device)
+        self.stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.stream):
+            for _ in range(warmup):
+                eng.run(ws, ws.pos, forces=forces, virial=virial, stream=self.stream)
+        torch.cuda.current_stream().wait_stream(self.stream)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            eng.run(ws, ws.pos, forces=forces, virial=virial, stream=self.stream)
+
+    def __call__(self, pos=None):
+        if pos is not None:
+            self.ws.pos.copy_(pos)
+        self.graph.replay()

@@ -1,0 +1,171 @@
+"""Graph construction on the GPU: neighbour list, receiver/sender CSR, per-edge species.
+
+``radius_graph`` keeps the reference's signature and result (tt_atom/geometry.py:48-81): the
+same fp32 cutoff predicate and edge order, computed by ``atom_neighbor_list``. ``build_graph``
+returns the receiver-major ``Graph`` the engine consumes (one or many systems back to back).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from . import _lib as L
+from ._lib import call, ptr
+
+
+def image_shifts(cell, pbc, cutoff):
+    """Cartesian image shifts ``cells @ cell`` for integer offsets in [-r, r] per periodic axis,
+    r = ceil(cutoff * |b_k|) with b_k the reciprocal rows, in cartesian-product order -- the
+    host arithmetic of tt_atom/geometry.py:66-75, kept in torch fp32 on the CPU so the shifts
+    are the reference's bit for bit."""
+    cell = torch.as_tensor(cell, dtype=torch.float32).cpu()
+    pbc = torch.as_tensor(pbc, dtype=torch.bool).reshape(-1).expand(3)
+    recip = torch.linalg.inv(cell).transpose(0, 1)
+    reps = [int(math.ceil(float(cutoff * torch.linalg.norm(recip[k])))) if bool(pbc[k]) else 0
+            for k in range(3)]
+    ranges = [torch.arange(-r, r + 1, dtype=torch.float32) for r in reps]
+    cells = torch.cartesian_prod(*ranges).reshape(-1, 3)
+    return cells @ cell
+
+
+def csd_embedding(w, charge, spin, C, dataset="omat"):
+    """System (charge / spin / dataset) embedding [nsys, C], tt_atom/geometry.py:23-45. Host
+    glue: a few hundred flops per system, computed once per system."""
+    charge = torch.as_tensor(charge, dtype=torch.float32).reshape(-1)
+    spin = torch.as_tensor(spin, dtype=torch.float32).reshape(-1)
+    if "charge_embedding.rand_emb.weight" in w:
+        chg = F.embedding(charge.long() + 100, w["charge_embedding.rand_emb.weight"])
+        sp = F.embedding(spin.long(), w["spin_embedding.rand_emb.weight"])
+    else:
+        def enc(v, W, zero_at_0):
+            a = v[:, None] * W[None, :] * 2 * math.pi
+            e = torch.cat([torch.sin(a), torch.cos(a)], -1)
+            if zero_at_0:
+                e = e.clone()
+                e[v == 0] = 0
+            return e
+        chg = enc(charge, w["charge_embedding.W"], False)
+        sp = enc(spin, w["spin_embedding.W"], True)
+    ds = w[f"dataset_embedding.dataset_emb_dict.{dataset}.weight"][0].expand(charge.shape[0], -1)
+    return F.silu(F.linear(torch.cat([chg, sp, ds], 1), w["mix_csd.weight"], w["mix_csd.bias"]))
+
+
+@dataclass
+class Graph:
+    N: int
+    E: int
+    nsys: int
+    periodic: bool
+    Z: torch.Tensor          # [N] int32
+    sys_id: torch.Tensor     # [N] int32
+    sys_ptr: torch.Tensor    # [nsys + 1] int32 (device)
+    sys_ptr_host: list
+    src: torch.Tensor        # [E] int32, receiver-major
+    tgt: torch.Tensor
+    img: torch.Tensor        # [E] int32 image index into shifts
+    shifts: torch.Tensor     # [S, 3] fp32
+    recv_ptr: torch.Tensor   # [N + 1]
+    send_ptr: torch.Tensor   # [N + 1]
+    send_eid: torch.Tensor   # [E]
+    zs: torch.Tensor         # [E] species of source
+    zt: torch.Tensor         # [E] species of target
+
+    def reference_order(self):
+        """(edge_index [2, E] int64, image index [E]) in the reference's edge order: periodic
+        graphs are receiver-major already; aperiodic ones are ordered by (source, target)."""
+        if self.periodic:
+            perm = torch.arange(self.E, device=self.src.device)
+        else:
+            perm = self.send_eid.long()
+        ei = torch.stack([self.src.long()[perm], self.tgt.long()[perm]])
+        return ei, self.img.long()[perm], perm
+
+    def same_topology(self, other):
+        return (other is not None and self.N == other.N and self.E == other.E
+                and torch.equal(self.src, other.src) and torch.equal(self.tgt, other.tgt)
+                and torch.equal(self.img, other.img) and torch.equal(self.shifts, other.shifts))
+
+
+def build_graph(pos, Z, cutoff, cell=None, pbc=None, max_neighbors=None, sys_ptr=None,
+                device="cuda", max_cand=None, stream=None):
+    """Neighbour list of one system, or of several aperiodic systems stored back to back
+    (``sys_ptr`` atom offsets; no edges between systems), on the GPU."""
+    dev = torch.device(device)
+    pos = torch.as_tensor(pos, dtype=torch.float32).to(dev).contiguous()
+    N = pos.shape[0]
+    Zt = torch.as_tensor(np.asarray(Z), dtype=torch.int32).to(dev).contiguous()
+    periodic = cell is not None and pbc is not None and bool(np.asarray(pbc).any())
+    if sys_ptr is None:
+        sys_ptr = [0, N]
+    sys_ptr = [int(v) for v in sys_ptr]
+    nsys = len(sys_ptr) - 1
+    if periodic and nsys != 1:
+        raise ValueError("periodic batches are built one system at a time")
+    shifts = (image_shifts(cell, pbc, cutoff) if periodic
+              else torch.zeros(1, 3)).to(dev).contiguous()
+    S = shifts.shape[0]
+    s = L.stream_ptr(stream)
+    if max_cand is None:
+        max_cand = 64 if max_neighbors is None else max(64, 2 * max_neighbors)
+    cap = 0 if max_neighbors is None else int(max_neighbors)
+    recv_cnt = torch.empty(N, dtype=torch.int32, device=dev)
+    small = torch.empty(nsys + 2, dtype=torch.int64, device=dev)
+    sp_host = L.host_i64(sys_ptr)
+    need = ctypes.c_int(0)
+    while True:
+        cand_idx = torch.empty(max(N * max_cand, 1), dtype=torch.int32, device=dev)
+        cand_d = torch.empty(max(N * max_cand, 1), dtype=torch.float32, device=dev)
+        rc = L.lib().atom_neighbor_list(ptr(pos), N, sp_host, nsys, ptr(shifts), S, float(cutoff),
+                                        int(periodic), cap, max_cand, ptr(cand_idx), ptr(cand_d),
+                                        ptr(recv_cnt), None, None, None, None, ptr(small),
+                                        ctypes.byref(need), s)
+        if rc == L.ATOM_ERR_CAPACITY:
+            max_cand = int(need.value * 1.25) + 32
+            continue
+        if rc != 0:
+            raise L.AtomError("atom_neighbor_list", rc)
+        break
+    recv_ptr = torch.empty(N + 1, dtype=torch.int32, device=dev)
+    total = ctypes.c_int(0)
+    call("atom_exclusive_scan", ptr(recv_cnt), N, ptr(recv_ptr), ctypes.byref(total), s)
+    E = int(total.value)
+    src = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
+    tgt = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
+    img = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
+    call("atom_neighbor_list", ptr(pos), N, sp_host, nsys, ptr(shifts), S, float(cutoff),
+         int(periodic), cap, max_cand, ptr(cand_idx), ptr(cand_d), ptr(recv_cnt), ptr(recv_ptr),
+         ptr(src), ptr(tgt), ptr(img), ptr(small), None, s)
+    src, tgt, img = src[:E], tgt[:E], img[:E]
+    send_ptr = torch.empty(N + 1, dtype=torch.int32, device=dev)
+    send_eid = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
+    scratch = torch.empty(max(N, 1), dtype=torch.int32, device=dev)
+    call("atom_sender_csr", ptr(src), E, N, ptr(scratch), ptr(send_ptr), ptr(send_eid), s)
+    send_eid = send_eid[:E]
+    zs = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
+    zt = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
+    call("atom_edge_species", ptr(Zt), ptr(src), ptr(tgt), E, ptr(zs), ptr(zt), s)
+    sys_id = torch.empty(N, dtype=torch.int32)
+    for k in range(nsys):
+        sys_id[sys_ptr[k]:sys_ptr[k + 1]] = k
+    return Graph(N=N, E=E, nsys=nsys, periodic=periodic, Z=Zt, sys_id=sys_id.to(dev),
+                 sys_ptr=torch.tensor(sys_ptr, dtype=torch.int32, device=dev),
+                 sys_ptr_host=sys_ptr, src=src, tgt=tgt, img=img, shifts=shifts,
+                 recv_ptr=recv_ptr, send_ptr=send_ptr, send_eid=send_eid, zs=zs[:E], zt=zt[:E])
+
+
+def radius_graph(pos, cutoff, cell=None, pbc=None, max_neighbors=None, device="cuda"):
+    """``(edge_index [2, E], cell_shift [E, 3])`` with the reference's edge order and fp32
+    predicate (tt_atom/geometry.py:48-81), computed on the GPU. Returns CPU tensors like the
+    reference."""
+    Z = np.zeros(len(pos), dtype=np.int64)
+    g = build_graph(pos, Z, cutoff, cell, pbc, max_neighbors=max_neighbors, device=device)
+    ei, im, _ = g.reference_order()
+    shift = g.shifts[im] if g.E else torch.zeros(0, 3, device=g.shifts.device)
+    if not g.periodic:
+        shift = torch.zeros_like(shift)
+    return ei.cpu(), shift.cpu()
