@@ -95,13 +95,13 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_workload(device):
+def make_workload(device, cells=(10, 10, 5)):
     from tt_atom import configs
     from tt_atom.calculator import TTAtomCalculator
     from tt_atom.weights import WeightBundle
     cfg = configs.model_config("uma-s-1")
     bundle = WeightBundle.from_arrays(configs.random_bundle_arrays(cfg, seed=0))
-    s = configs.fcc_alloy()
+    s = configs.fcc_alloy(reps=cells)
     calc = TTAtomCalculator(bundle, device=device)
     return cfg, bundle, s, calc
 
@@ -115,7 +115,8 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=device)
     from tt_atom.ase_compat import SimpleAtoms
     from tt_atom.engine import CapturedStep
-    cfg, bundle, s, calc = make_workload(device)
+    cells = tuple(int(v) for v in args.cells.split(","))
+    cfg, bundle, s, calc = make_workload(device, cells)
     N = len(s["Z"])
     cell, pbc = s["cell"], [True] * 3
     # ---- device step on a fixed topology (CUDA graph)
@@ -189,8 +190,10 @@ def run_ours(args):
                      "traffic": traffic, "launch_ms": kern["ms"], "flop_per_launch": kern["flop"]},
         "clocks": clocks,
     }
-    cpu = cpu_baseline(bounded=True)
-    out["cpu_baseline"] = cpu
+    if cells != (10, 10, 5):
+        out["config"]["workload"] += f" (reduced: {cells} cells, not the headline size)"
+    if not args.no_cpu:
+        out["cpu_baseline"] = cpu_baseline(bounded=True)
     print(json.dumps(out))
     if ws_n > 1:
         torch.distributed.destroy_process_group()
@@ -261,6 +264,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cells", default="10,10,5", help="fcc cells (profiling uses a smaller cell)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

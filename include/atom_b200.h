@@ -115,6 +115,20 @@ int atom_exclusive_scan(const int* cnt, int64_t n, int* ptr, int* total_host, vo
 int atom_sender_csr(const int* edge_src, int64_t E, int64_t N, int* scratch, int* send_ptr,
                     int* send_eid, void* stream);
 
+/* Scratch-free variant of atom_sender_csr. It has no counterpart in the reference.
+ * For callers that cannot allocate device memory -- e.g. a host MD engine or framework whose
+ * own pool allocator owns the device memory and forbids allocations behind its back -- and so
+ * cannot provide atom_sender_csr's N-int scratch. The per-node counters live in a static
+ * device array of ATOM_NOALLOC_MAX_NODES int32 (4 MiB) that every GPU loading this library
+ * holds until the process exits; N above that limit returns ATOM_ERR_CAPACITY. The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current, so make that first call before any stream capture. Calls share the array: calls
+ * that overlap on the GPU (other streams, other host threads) race and must be serialised by
+ * the caller. Allocates nothing (no cudaMalloc / cudaFree). Output equals atom_sender_csr's. */
+#define ATOM_NOALLOC_MAX_NODES (1 << 20)
+int atom_sender_csr_noalloc(const int* edge_src, int64_t E, int64_t N, int* send_ptr,
+                            int* send_eid, void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * Geometry (tt_atom/geometry.py:112-280) and its VJP (replaces the host autograd finish of
  * tt_atom/forces.py:545-589).

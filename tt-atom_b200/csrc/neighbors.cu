@@ -306,3 +306,74 @@ extern "C" int atom_sender_csr(const int* edge_src, int64_t E, int64_t N, int* s
     ATOM_CHECK_LAUNCH("sender_csr");
     return ATOM_OK;
 }
+
+// ------------------------------------------------------------------ scratch-free sender CSR
+// A variant of atom_sender_csr for callers that cannot allocate device memory. Its per-node
+// fill counters live in a file-scope device array instead of caller scratch. Each GPU that
+// loads this library holds the array (ATOM_NOALLOC_MAX_NODES int32, 4 MiB) until the process
+// exits. In host code the array's name is only a host-side stand-in, so its device address is
+// looked up once per device with cudaGetSymbolAddress (on the first call made with that device
+// current) and passed to the kernels.
+#include <mutex>
+
+static __device__ __align__(256) int g_noalloc_fill[ATOM_NOALLOC_MAX_NODES];
+
+namespace atom {
+constexpr int kMaxDevices = 64;
+static std::mutex g_noalloc_mu;
+static int* g_noalloc_addr[kMaxDevices];
+
+static int noalloc_scratch(int** out) {
+    int dev = -1;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess) {
+        set_error("sender_csr_noalloc: cudaGetDevice failed: %s", cudaGetErrorString(ce));
+        return ATOM_ERR_CUDA;
+    }
+    if (dev < 0 || dev >= kMaxDevices) {
+        set_error("sender_csr_noalloc: device ordinal %d out of range", dev);
+        return ATOM_ERR_UNSUPPORTED;
+    }
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        ce = cudaGetSymbolAddress(&p, g_noalloc_fill);
+        if (ce != cudaSuccess || !p) {
+            set_error("sender_csr_noalloc: cudaGetSymbolAddress failed: %s",
+                      cudaGetErrorString(ce));
+            return ATOM_ERR_CUDA;
+        }
+        g_noalloc_addr[dev] = static_cast<int*>(p);
+    }
+    *out = g_noalloc_addr[dev];
+    return ATOM_OK;
+}
+}  // namespace atom
+
+extern "C" int atom_sender_csr_noalloc(const int* edge_src, int64_t E, int64_t N, int* send_ptr,
+                                       int* send_eid, void* stream) {
+    ATOM_REQUIRE(N >= 0 && E >= 0, "sender_csr_noalloc: negative size");
+    if (N > ATOM_NOALLOC_MAX_NODES) {
+        set_error("sender_csr_noalloc: N = %lld exceeds the built-in scratch of %d nodes; use "
+                  "atom_sender_csr with caller-provided scratch", (long long)N,
+                  ATOM_NOALLOC_MAX_NODES);
+        return ATOM_ERR_CAPACITY;
+    }
+    if (N == 0) return ATOM_OK;
+    int* fill = nullptr;
+    if (int s = noalloc_scratch(&fill)) return s;
+    cudaStream_t st = (cudaStream_t)stream;
+    // the counters keep the previous call's values: clear them before counting and again
+    // before the fill pass
+    zero_int_kernel<<<ceil_div(N, 256), 256, 0, st>>>(fill, N);
+    if (E > 0) count_src_kernel<<<ceil_div(E, 256), 256, 0, st>>>(edge_src, E, fill);
+    scan_kernel<<<1, 1024, 0, st>>>(fill, N, send_ptr);
+    zero_int_kernel<<<ceil_div(N, 256), 256, 0, st>>>(fill, N);
+    if (E > 0) {
+        scatter_src_kernel<<<ceil_div(E, 256), 256, 0, st>>>(edge_src, E, send_ptr, fill,
+                                                              send_eid);
+        sort_segments_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(N, send_ptr, send_eid);
+    }
+    ATOM_CHECK_LAUNCH("sender_csr_noalloc");
+    return ATOM_OK;
+}
