@@ -95,14 +95,14 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_workload(device, cells=(10, 10, 5)):
+def make_workload(device, cells=(10, 10, 5), precision="3xtf32"):
     from tt_atom import configs
     from tt_atom.calculator import TTAtomCalculator
     from tt_atom.weights import WeightBundle
     cfg = configs.model_config("uma-s-1")
     bundle = WeightBundle.from_arrays(configs.random_bundle_arrays(cfg, seed=0))
     s = configs.fcc_alloy(reps=cells)
-    calc = TTAtomCalculator(bundle, device=device)
+    calc = TTAtomCalculator(bundle, device=device, precision=precision)
     return cfg, bundle, s, calc
 
 
@@ -116,7 +116,7 @@ def run_ours(args):
     from tt_atom.ase_compat import SimpleAtoms
     from tt_atom.engine import CapturedStep
     cells = tuple(int(v) for v in args.cells.split(","))
-    cfg, bundle, s, calc = make_workload(device, cells)
+    cfg, bundle, s, calc = make_workload(device, cells, args.precision)
     N = len(s["Z"])
     cell, pbc = s["cell"], [True] * 3
     # ---- device step on a fixed topology (CUDA graph)
@@ -163,6 +163,7 @@ def run_ours(args):
         if ws_n > 1:
             torch.distributed.destroy_process_group()
         return
+    eng_precision = {0: "fp32", 1: "tf32", 2: "3xtf32"}[eng.precision]
     ms_step = ms / args.steps
     value = N * ws_n * args.steps / (ms / 1e3)
     hbm, bf16, src = peaks()
@@ -178,7 +179,7 @@ def run_ours(args):
         "data": "synthetic (seeded fcc Cu/Ni, random-init weights)",
         "config": {"workload": WORKLOAD, "atoms_per_gpu": N, "edges_per_gpu": ws.graph.E,
                    "cutoff": cfg["cutoff"], "max_neighbors": cfg["max_neighbors"],
-                   "precision": "fp32", "parallelism": f"replicas x{ws_n}",
+                   "precision": eng_precision, "parallelism": f"replicas x{ws_n}",
                    "l2": "per-step working set %.1f GB > 126 MB L2" % (ws.nbytes() / 1e9)},
         "e2e": {"value": N * ws_n / (e2e_ms / 1e3), "unit": "atom-steps/s",
                 "h2d_bytes_per_step": N * 3 * 4 + N * 8,
@@ -266,6 +267,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cells", default="10,10,5", help="fcc cells (profiling uses a smaller cell)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "fp32", "tf32"])
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -170,18 +170,27 @@ int atom_forces_virial(const float* g_ev, const float* ev, int64_t E, int64_t N,
  *                                + T1[idx1[m] * ldt + t_col[g] + n] + T2[idx2[m] * ldt + t_col[g] + n] )
  * for m < M, n < N_g, k < K_g. bias/T1/T2 optional (NULL). act: 0 none, 1 SiLU (then
  * C_pre, when not NULL, receives the pre-activation). accumulate != 0 adds into C.
- * precision: 0 = fp32 FMA; other values select tensor-core modes (see atom_gemm_modes). */
+ * precision: 0 = fp32 FMA; 1 = TF32 tensor cores (tcgen05); 2 = 3xTF32 tensor cores (fp32-level
+ * accuracy). Modes 1 and 2 read the K-major weight copies Bt[g] ([N_g, K_g] row-major, low 13
+ * mantissa bits cleared) and, for mode 2, Bt_lo[g] = B^T - Bt; they need every K_g to be a
+ * multiple of 32, lda % 4 == 0 and 16-byte aligned A / Bt, and otherwise run the fp32 kernel. */
 typedef struct {
     int ngroups;
     int a_col[8], K[8], c_col[8], N[8], ldb[8], t_col[8];
     const float* B[8];
     const float* bias[8];
+    const float* Bt[8];
+    const float* Bt_lo[8];
 } atom_gemm_groups;
 
 int atom_gemm(const float* A, int64_t lda, int64_t M, const atom_gemm_groups* groups,
               float* Cout, int64_t ldc, float* C_pre, const float* T1, const float* T2,
               const int* idx1, const int* idx2, int64_t ldt, int act, int accumulate,
               int precision, void* stream);
+
+/* Reads and clears the device-side error code of the tensor-core kernels (0 = none; a bounded
+ * wait expired otherwise). Synchronises `stream`. */
+int atom_device_error(int* code_host, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Edge-side fused ops of the edgewise block (tt_atom/edgewise.py:39-87, forces.py:352-418).

@@ -83,8 +83,13 @@ def test_fused_gate_and_ln_bw():
 
 # ------------------------------------------------------------------------------- GEMM
 
+TOL = {0: 1e-5, 1: 5e-3, 2: 1e-5}
+
+
+@pytest.mark.parametrize("precision", [0, 1, 2])
 @pytest.mark.parametrize("M", [1, 129, 1000])
-def test_grouped_gemm_with_epilogues(M):
+def test_grouped_gemm_with_epilogues(M, precision):
+    from tt_atom.engine import _Groups
     K1, N1, K2, N2 = 96, 160, 64, 130
     A = rnd(M, K1 + K2)
     B1, B2 = rnd(K1, N1, seed=1), rnd(K2, N2, seed=2)
@@ -92,30 +97,61 @@ def test_grouped_gemm_with_epilogues(M):
     T1, T2 = rnd(10, 400, seed=4), rnd(10, 400, seed=5)
     i1 = torch.randint(0, 10, (M,), device=dev, dtype=torch.int32)
     i2 = torch.randint(0, 10, (M,), device=dev, dtype=torch.int32)
-    g = L.GemmGroups()
-    g.ngroups = 2
-    for k, (ac, K, cc, N, B, b, tc) in enumerate([(0, K1, 0, N1, B1, bias1, 0),
-                                                  (K1, K2, N1, N2, B2, None, 200)]):
-        g.a_col[k], g.K[k], g.c_col[k], g.N[k], g.ldb[k], g.t_col[k] = ac, K, cc, N, N, tc
-        g.B[k] = B.data_ptr()
-        g.bias[k] = b.data_ptr() if b is not None else None
+    g = _Groups([dict(a_col=0, K=K1, c_col=0, N=N1, B=B1, bias=bias1, t_col=0),
+                 dict(a_col=K1, K=K2, c_col=N1, N=N2, B=B2, t_col=200)])
     C = torch.empty(M, N1 + N2, device=dev)
     Cpre = torch.empty(M, N1 + N2, device=dev)
-    call("atom_gemm", ptr(A), K1 + K2, M, ctypes.byref(g), ptr(C), N1 + N2, ptr(Cpre), ptr(T1),
-         ptr(T2), ptr(i1), ptr(i2), 400, 1, 0, 0, s())
+    call("atom_gemm", ptr(A), K1 + K2, M, ctypes.byref(g.struct), ptr(C), N1 + N2, ptr(Cpre),
+         ptr(T1), ptr(T2), ptr(i1), ptr(i2), 400, 1, 0, precision, s())
     Ad = A.double()
     r1 = Ad[:, :K1] @ B1.double() + bias1.double() + T1.double()[i1.long(), :N1] + \
         T2.double()[i2.long(), :N1]
     r2 = Ad[:, K1:] @ B2.double() + T1.double()[i1.long(), 200:200 + N2] + \
         T2.double()[i2.long(), 200:200 + N2]
     pre = torch.cat([r1, r2], 1)
-    close(Cpre, pre, 1e-5)
-    close(C, F.silu(pre), 1e-5)
+    close(Cpre, pre, TOL[precision])
+    close(C, F.silu(pre), TOL[precision])
     # accumulate
     C2 = C.clone()
-    call("atom_gemm", ptr(A), K1 + K2, M, ctypes.byref(g), ptr(C2), N1 + N2, None, ptr(T1),
-         ptr(T2), ptr(i1), ptr(i2), 400, 0, 1, 0, s())
-    close(C2, C.double() + pre, 1e-5)
+    call("atom_gemm", ptr(A), K1 + K2, M, ctypes.byref(g.struct), ptr(C2), N1 + N2, None,
+         ptr(T1), ptr(T2), ptr(i1), ptr(i2), 400, 0, 1, precision, s())
+    close(C2, C.double() + pre, TOL[precision])
+    code = ctypes.c_int(-1)
+    call("atom_device_error", ctypes.byref(code), s())
+    assert code.value == 0
+
+
+@pytest.mark.parametrize("precision", [1, 2])
+def test_tensor_core_gemm_so2_shapes_many_groups(precision):
+    """The so2_conv_1 block layout (K = 768, 1024, 512) and an 8-group radial-style layout."""
+    from tt_atom.engine import _Groups
+    M = 3001
+    A = rnd(M, 2304)
+    Bs = [rnd(768, 640, seed=1) * 0.05, rnd(1024, 512, seed=2) * 0.05, rnd(512, 256, seed=3) * 0.05]
+    bias0 = rnd(640, seed=4)
+    g = _Groups([dict(a_col=0, K=768, c_col=0, N=640, B=Bs[0], bias=bias0),
+                 dict(a_col=768, K=1024, c_col=640, N=512, B=Bs[1]),
+                 dict(a_col=1792, K=512, c_col=1152, N=256, B=Bs[2])])
+    C = torch.empty(M, 1408, device=dev)
+    call("atom_gemm", ptr(A), 2304, M, ctypes.byref(g.struct), ptr(C), 1408, None, None, None,
+         None, None, 0, 0, 0, precision, s())
+    Ad = A.double()
+    ref = torch.cat([Ad[:, :768] @ Bs[0].double() + bias0.double(),
+                     Ad[:, 768:1792] @ Bs[1].double(), Ad[:, 1792:] @ Bs[2].double()], 1)
+    close(C, ref, TOL[precision])
+    G, EC = 8, 32
+    X = rnd(M, G * EC, seed=9)
+    Ws = [rnd(EC, EC + 8 * k, seed=10 + k) for k in range(G)]
+    offs = [0]
+    for w_ in Ws:
+        offs.append(offs[-1] + w_.shape[1])
+    g = _Groups([dict(a_col=k * EC, K=EC, c_col=offs[k], N=Ws[k].shape[1], B=Ws[k])
+                 for k in range(G)])
+    C = torch.empty(M, offs[-1], device=dev)
+    call("atom_gemm", ptr(X), G * EC, M, ctypes.byref(g.struct), ptr(C), offs[-1], None, None,
+         None, None, None, 0, 0, 0, precision, s())
+    ref = torch.cat([X[:, k * EC:(k + 1) * EC].double() @ Ws[k].double() for k in range(G)], 1)
+    close(C, ref, TOL[precision])
 
 
 # --------------------------------------------------------------------- node-side kernels

@@ -30,8 +30,13 @@ def bundle_from_fixture(g):
     return WeightBundle.from_arrays(arrs), cfg
 
 
-def engine_eval(bundle, pos, Z, cell=None, pbc=None, stress=False, trace=False, calc=None):
-    calc = calc or TTAtomCalculator(bundle, max_neighbors=bundle.config.get("max_neighbors"))
+PRECISIONS = ["fp32", "3xtf32"]
+
+
+def engine_eval(bundle, pos, Z, cell=None, pbc=None, stress=False, trace=False, calc=None,
+                precision="fp32"):
+    calc = calc or TTAtomCalculator(bundle, max_neighbors=bundle.config.get("max_neighbors"),
+                                    precision=precision)
     E, Fo, V = calc._evaluate(pos, Z, cell, pbc, [0.0], [0.0], forces=True, stress=stress,
                               trace=trace)
     return calc, float(E[0]), Fo, V
@@ -78,30 +83,32 @@ def test_neighbor_list_batched_systems_stay_disjoint():
     assert torch.equal(ei.cpu(), torch.cat(got, 1))
 
 
+@pytest.mark.parametrize("precision", PRECISIONS)
 @pytest.mark.parametrize("name,periodic", [("ref_golden_tiny.npz", False),
                                            ("ref_golden_bulk.npz", True)])
-def test_energy_forces_vs_fairchem_golden(fx, name, periodic):
+def test_energy_forces_vs_fairchem_golden(fx, name, periodic, precision):
     g = fx(name)
     b, cfg = bundle_from_fixture(g)
     pos = g.d["in@pos"]
     Z = g.d["in@atomic_numbers"]
     cell = g.d["in@cell"][0] if periodic else None
     pbc = [True] * 3 if periodic else None
-    calc, E, Fo, _ = engine_eval(b, pos, Z, cell, pbc)
+    calc, E, Fo, _ = engine_eval(b, pos, Z, cell, pbc, precision=precision)
     E_ref = float(g.d["out@energy"][0])
     assert abs(E - E_ref) <= E_REL * abs(E_ref), (E, E_ref)
     assert (Fo.float() - g.t("out@forces")).abs().max() <= F_ABS
 
 
+@pytest.mark.parametrize("precision", PRECISIONS)
 @pytest.mark.parametrize("name", ["ref_run_tiny_molecule.npz", "ref_run_tiny_fcc.npz"])
-def test_energy_forces_stress_vs_reference_cpu_path(fx, name):
+def test_energy_forces_stress_vs_reference_cpu_path(fx, name, precision):
     g = fx(name)
     b, cfg = bundle_from_fixture(g)
     periodic = bool(g.d["in@pbc"])
     pos, Z = g.d["in@pos"], g.d["in@Z"]
     cell = g.d["in@cell"] if periodic else None
     pbc = [True] * 3 if periodic else None
-    calc, E, Fo, V = engine_eval(b, pos, Z, cell, pbc, stress=periodic)
+    calc, E, Fo, V = engine_eval(b, pos, Z, cell, pbc, stress=periodic, precision=precision)
     E_ref = float(g.d["out@energy"][0])
     assert abs(E - E_ref) <= E_REL * abs(E_ref), (E, E_ref)
     assert (Fo.float() - g.t("out@forces")).abs().max() <= F_ABS
@@ -125,14 +132,15 @@ def _tables(cfg):
     return dict(t, gauss_offset=off, gauss_coeff=coeff)
 
 
+@pytest.mark.parametrize("precision", PRECISIONS)
 @pytest.mark.parametrize("shape,sysname", [("tiny", "tiny"), ("uma-s-1", "fcc-small")])
-def test_configs_vs_oracle(shape, sysname):
+def test_configs_vs_oracle(shape, sysname, precision):
     cfg = configs.model_config(shape)
     arrs = configs.random_bundle_arrays(cfg, seed=0)
     b = WeightBundle.from_arrays(arrs)
     s = configs.system(sysname)
     calc, E, Fo, V = engine_eval(b, s["pos"], s["Z"], s["cell"], [True] * 3 if s["pbc"] else None,
-                                 stress=s["pbc"])
+                                 stress=s["pbc"], precision=precision)
     r = _oracle(cfg, b.weights, _tables(cfg), s, s["pbc"])
     E_ref = float(r["energy"][0])
     assert abs(E - E_ref) <= E_REL * abs(E_ref), (E, E_ref)

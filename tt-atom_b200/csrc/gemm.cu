@@ -7,9 +7,18 @@
 // [c_col, c_col + N) of C.
 //
 // precision 0: register-tiled FMA kernel (128 x 128 tile, 8 x 8 outputs per thread).
+// precision 1 / 2: the tcgen05 tensor-core kernel of gemm_tc.cu (TF32 / 3xTF32) when the shape
+// allows it (every K a multiple of 32, K-major weights given); otherwise the FMA kernel, which
+// is at least as accurate.
 #include "common.cuh"
 
 namespace atom {
+
+bool gemm_tc_supported(const float* A, long long lda, const atom_gemm_groups* g, int precision);
+int gemm_tc(const float* A, long long lda, long long M, const atom_gemm_groups* g, float* C,
+            long long ldc, float* Cpre, const float* T1, const float* T2, const int* idx1,
+            const int* idx2, long long ldt, int act, int accumulate, int precision,
+            cudaStream_t st);
 
 struct GemmArgs {
     const float* A;
@@ -137,7 +146,7 @@ extern "C" int atom_gemm(const float* A, int64_t lda, int64_t M, const atom_gemm
     ATOM_REQUIRE(act == 0 || act == 1, "act must be 0 or 1");
     ATOM_REQUIRE(!T1 || idx1, "T1 needs idx1");
     ATOM_REQUIRE(!T2 || idx2, "T2 needs idx2");
-    ATOM_REQUIRE(precision == 0, "precision mode %d not available", precision);
+    ATOM_REQUIRE(precision >= 0 && precision <= 2, "precision mode %d not available", precision);
     GemmArgs p;
     p.A = A; p.lda = lda; p.M = M; p.C = Cout; p.Cpre = C_pre; p.ldc = ldc;
     p.T1 = T1; p.T2 = T2; p.idx1 = idx1; p.idx2 = idx2; p.ldt = ldt;
@@ -152,6 +161,9 @@ extern "C" int atom_gemm(const float* A, int64_t lda, int64_t M, const atom_gemm
     p.tile_start[groups->ngroups] = tiles;
     if (M == 0 || tiles == 0) return ATOM_OK;
     ATOM_REQUIRE(ceil_div(M, BM) < 65536, "M too large");
+    if (gemm_tc_supported(A, lda, groups, precision))
+        return gemm_tc(A, lda, M, groups, Cout, ldc, C_pre, T1, T2, idx1, idx2, ldt, act,
+                       accumulate, precision, (cudaStream_t)stream);
     dim3 grid(tiles, ceil_div(M, BM));
     gemm_fma_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
     ATOM_CHECK_LAUNCH("gemm");

@@ -21,7 +21,8 @@ c_void_p, c_int, c_int64, c_float = ctypes.c_void_p, ctypes.c_int, ctypes.c_int6
 class GemmGroups(ctypes.Structure):
     _fields_ = [("ngroups", c_int), ("a_col", c_int * 8), ("K", c_int * 8), ("c_col", c_int * 8),
                 ("N", c_int * 8), ("ldb", c_int * 8), ("t_col", c_int * 8),
-                ("B", c_void_p * 8), ("bias", c_void_p * 8)]
+                ("B", c_void_p * 8), ("bias", c_void_p * 8), ("Bt", c_void_p * 8),
+                ("Bt_lo", c_void_p * 8)]
 
 
 _SIGS = {
@@ -52,6 +53,7 @@ _SIGS = {
     "atom_gemm": (c_void_p, c_int64, c_int64, ctypes.POINTER(GemmGroups), c_void_p, c_int64,
                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int,
                   c_void_p),
+    "atom_device_error": (c_void_p, c_void_p),
     "atom_rotate_in": (c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_int64,
                        c_int, c_void_p, c_void_p, c_void_p),
     "atom_gate_fwd": (c_void_p, c_int64, c_int, c_void_p, c_void_p),

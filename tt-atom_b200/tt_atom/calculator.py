@@ -6,7 +6,9 @@ Same constructor and methods (``calculate``, ``evaluate_batch``, ``close``), sam
 (``E = rmsd * E_raw + mean + sum refs[Z]``, ``F = rmsd * F_raw``, stress = rmsd * virial / V as
 Voigt-6) and the same errors (no edges -> ValueError; task mismatch -> ValueError). ``device`` /
 ``device_id`` name a CUDA device. ``trace=True`` captures the step in a CUDA graph per topology
-and replays it while the neighbour list (and image shifts) are unchanged.
+and replays it while the neighbour list (and image shifts) are unchanged. ``precision``:
+"3xtf32" (default; tcgen05 tensor cores with fp32-level accuracy), "fp32" (FMA pipe) or "tf32"
+(one tensor-core pass, looser).
 """
 from __future__ import annotations
 
@@ -41,7 +43,7 @@ class TTAtomCalculator(_AseCalculator):
     implemented_properties = ["energy", "energies", "free_energy", "forces", "stress"]
 
     def __init__(self, bundle, task_name=None, device=None, device_id=0, gamma=0.0, fast=False,
-                 trace=False, precision="fp32", max_neighbors="config", **kwargs):
+                 trace=False, precision="3xtf32", max_neighbors="config", **kwargs):
         super().__init__(**kwargs)
         if isinstance(bundle, str):
             bundle = WeightBundle.load(bundle)
@@ -91,7 +93,10 @@ class TTAtomCalculator(_AseCalculator):
         reuse = (trace and self._ws is not None and self._ws_key == key
                  and g.same_topology(self._ws.graph) and torch.equal(self._se, se))
         if not reuse:
-            self._ws = self.engine.workspace(g, se)
+            if self._ws is not None and self._ws.fits(g):
+                self._ws.rebind(g, se)              # same sizes: reuse the buffers
+            else:
+                self._ws = self.engine.workspace(g, se)
             self._ws_key, self._se, self._step = key, se, None
         ws = self._ws
         ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))

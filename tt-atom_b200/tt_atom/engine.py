@@ -39,7 +39,15 @@ def call(name, *args):
     _counter[0] += _LAUNCHES.get(name, 1)
     return L.call(name, *args)
 
-PRECISIONS = {"fp32": 0}
+# "fp32": FMA-pipe GEMMs; "3xtf32": tcgen05 tensor cores with the hi/lo operand split
+# (fp32-level accuracy); "tf32": tensor cores, one pass (looser, ~1e-3 relative per product).
+PRECISIONS = {"fp32": 0, "tf32": 1, "3xtf32": 2}
+
+
+def _split_tf32(t):
+    """(hi, lo): hi = t with the low 13 mantissa bits cleared, lo = t - hi (exact)."""
+    hi = (t.contiguous().view(torch.int32) & -8192).view(torch.float32)
+    return hi.contiguous(), (t - hi).contiguous()
 
 
 def _dev(t, device):
@@ -63,6 +71,11 @@ class _Groups:
             g.t_col[i] = d.get("t_col", 0)
             g.B[i] = B.data_ptr()
             self.keep.append(B)
+            # K-major copies for the tensor-core kernel (hi part, lo part)
+            hi, lo = _split_tf32(B[:d["K"], :d["N"]].t().contiguous())
+            g.Bt[i] = hi.data_ptr()
+            g.Bt_lo[i] = lo.data_ptr()
+            self.keep += [hi, lo]
             b = d.get("bias")
             g.bias[i] = b.data_ptr() if b is not None else None
             if b is not None:
@@ -417,16 +430,28 @@ class Workspace:
         self.ge1, self.ge2 = f(N, H), f(N, H)
         self.eh4_rows = eng.eh4_row.reshape(1, H).expand(N, H).contiguous()
         self.forces, self.virial, self.vscratch = f(N, 3), f(3, 3), f(9 * 1024)
-        # node embeddings (pos-independent): l0 = sphere[Z] + sys_emb; sys_emb per node
-        se = sys_emb.to(dev, torch.float32).contiguous()            # [nsys, C]
-        self.sysn = f(N, C)
-        zero_sphere = torch.zeros_like(eng.sphere)
+        self.sysn, self.l0 = f(N, C), f(N, C)
+        self._zero_sphere = torch.zeros_like(eng.sphere)
+        self._eng = eng
+        self.rebind(graph, sys_emb)
+
+    def fits(self, graph):
+        return (graph.N == self.graph.N and graph.E == self.graph.E
+                and graph.nsys == self.graph.nsys)
+
+    def rebind(self, graph, sys_emb):
+        """Point this workspace at another graph of the same sizes (new topology, same
+        buffers) and recompute the pos-independent node embeddings
+        l0 = sphere[Z] + sys_emb and the per-node system embedding."""
+        assert graph.N == self.pos.shape[0]
+        self.graph = graph
+        eng, N, eng_C = self._eng, graph.N, self._eng.C
+        se = sys_emb.to(eng.device, torch.float32).contiguous()    # [nsys, C]
         s = L.stream_ptr()
-        call("atom_node_embed", ptr(graph.Z), ptr(graph.sys_id), ptr(zero_sphere), ptr(se), N, C,
-             ptr(self.sysn), s)
-        self.l0 = f(N, C)
-        call("atom_node_embed", ptr(graph.Z), ptr(graph.sys_id), ptr(eng.sphere), ptr(se), N, C,
-             ptr(self.l0), s)
+        call("atom_node_embed", ptr(graph.Z), ptr(graph.sys_id), ptr(self._zero_sphere), ptr(se),
+             N, eng_C, ptr(self.sysn), s)
+        call("atom_node_embed", ptr(graph.Z), ptr(graph.sys_id), ptr(eng.sphere), ptr(se), N,
+             eng_C, ptr(self.l0), s)
 
     def nbytes(self):
         tot = 0
