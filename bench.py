@@ -37,7 +37,10 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 METRIC = "atom-steps/s (E+F+stress)"
-WORKLOAD = "uma-s-1-shape eSCN-MD, periodic 2000-atom fcc Cu/Ni, E+F+stress"
+WORKLOADS = {
+    "uma": "uma-s-1-shape eSCN-MD, periodic 2000-atom fcc Cu/Ni, E+F+stress",
+    "orb": "Orb-v3-conservative-shape GNN, periodic 1002-atom amorphous SiO2, E+F+stress",
+}
 
 
 def peaks():
@@ -116,12 +119,23 @@ def run_ours(args):
     from tt_atom.ase_compat import SimpleAtoms
     from tt_atom.engine import CapturedStep
     cells = tuple(int(v) for v in args.cells.split(","))
-    cfg, bundle, s, calc = make_workload(device, cells, args.precision)
+    if args.workload == "orb":
+        from tt_atom import configs
+        from tt_atom.orb import OrbCalculator
+        cfg = configs.orb_config("orb-v3")
+        s = configs.amorphous_sio2()
+        calc = OrbCalculator(configs.orb_random_weights(cfg, seed=0), cfg, device=device,
+                             precision=args.precision)
+        cfg = dict(cfg, max_neighbors=cfg["max_num_neighbors"])
+        evaluate = lambda: calc._evaluate(s["pos"], s["Z"], s["cell"], [True] * 3, True, True)  # noqa: E731
+    else:
+        cfg, bundle, s, calc = make_workload(device, cells, args.precision)
+        evaluate = lambda: calc._evaluate(s["pos"], s["Z"], s["cell"], [True] * 3, [0.0], [0.0],  # noqa: E731
+                                          forces=True, stress=True)
     N = len(s["Z"])
     cell, pbc = s["cell"], [True] * 3
     # ---- device step on a fixed topology (CUDA graph)
-    E_, F_, V_ = calc._evaluate(s["pos"], s["Z"], cell, pbc, [0.0], [0.0], forces=True,
-                                stress=True)
+    evaluate()
     ws = calc._ws
     eng = calc.engine
     step = CapturedStep(eng, ws, forces=True, virial=True)
@@ -177,7 +191,7 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded fcc Cu/Ni, random-init weights)",
-        "config": {"workload": WORKLOAD, "atoms_per_gpu": N, "edges_per_gpu": ws.graph.E,
+        "config": {"workload": WORKLOADS[args.workload], "atoms_per_gpu": N, "edges_per_gpu": ws.graph.E,
                    "cutoff": cfg["cutoff"], "max_neighbors": cfg["max_neighbors"],
                    "precision": eng_precision, "parallelism": f"replicas x{ws_n}",
                    "l2": "per-step working set %.1f GB > 126 MB L2" % (ws.nbytes() / 1e9)},
@@ -194,10 +208,17 @@ def run_ours(args):
     if cells != (10, 10, 5):
         out["config"]["workload"] += f" (reduced: {cells} cells, not the headline size)"
     if not args.no_cpu:
-        out["cpu_baseline"] = cpu_baseline(bounded=True)
+        out["cpu_baseline"] = cpu_baseline(bounded=True, workload=args.workload)
     print(json.dumps(out))
     if ws_n > 1:
         torch.distributed.destroy_process_group()
+
+
+def _cpu_sample_orb():
+    """Bounded CPU sample for the Orb workload: the same model, 300-atom SiO2 at 2.2 g/cm^3."""
+    from tt_atom import configs
+    cfg = configs.orb_config("orb-v3")
+    return cfg, configs.orb_random_weights(cfg, seed=0), configs.amorphous_sio2(100, 200, seed=2)
 
 
 def _cpu_sample():
@@ -209,7 +230,9 @@ def _cpu_sample():
     return cfg, arrs, s
 
 
-def cpu_baseline(bounded=True, steps=1, warmup=0):
+def cpu_baseline(bounded=True, steps=1, warmup=0, workload="uma"):
+    if workload == "orb":
+        return _cpu_baseline_orb(steps, warmup)
     from oracle import uma as O
     from tt_atom import configs
     from tt_atom.weights import WeightBundle
@@ -241,18 +264,44 @@ def cpu_baseline(bounded=True, steps=1, warmup=0):
                       f"median of {steps} step(s)", "seconds_per_step": statistics.median(times)}
 
 
+def _cpu_baseline_orb(steps, warmup):
+    from oracle import orb as OB
+    from oracle import uma as O
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg, w, s = _cpu_sample_orb()
+    pos, cell = torch.from_numpy(s["pos"]), torch.from_numpy(s["cell"])
+
+    def one():
+        ei, sh = O.neighbor_list(pos, cfg["cutoff"], cell, [True] * 3, cfg["max_num_neighbors"])
+        return OB.energy_forces(w, cfg, pos, torch.from_numpy(s["Z"]), ei, sh,
+                                compute_stress=True)
+    for _ in range(warmup):
+        one()
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+    n = len(s["Z"])
+    return {"value": n / statistics.median(times), "unit": "atom-steps/s", "cores": threads,
+            "kind": "port", "sample": f"{n}-atom amorphous SiO2, same model/cap, E+F+stress, "
+                                      f"median of {steps} step(s)",
+            "seconds_per_step": statistics.median(times)}
+
+
 def run_reference(args):
     ws_n, rank, _ = dist_env()
     if rank != 0:
         return
     steps = args.steps
-    cpu = cpu_baseline(bounded=True, steps=steps, warmup=args.warmup)
+    cpu = cpu_baseline(bounded=True, steps=steps, warmup=args.warmup, workload=args.workload)
     out = {"metric": METRIC, "value": cpu["value"], "unit": "atom-steps/s", "n_gpus": ws_n,
            "steps": steps, "warmup": args.warmup,
            "ms_per_step": 1e3 * cpu["seconds_per_step"], "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
            "data": "synthetic (seeded fcc Cu/Ni, random-init weights)",
-           "config": {"workload": WORKLOAD, "sample": cpu["sample"]},
+           "config": {"workload": WORKLOADS[args.workload], "sample": cpu["sample"]},
            "impl": "reference", "cpu_baseline": cpu,
            "e2e": {"value": cpu["value"], "unit": "atom-steps/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
@@ -268,6 +317,8 @@ def main():
     ap.add_argument("--cells", default="10,10,5", help="fcc cells (profiling uses a smaller cell)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "fp32", "tf32"])
+    ap.add_argument("--workload", default="uma", choices=sorted(WORKLOADS),
+                    help="uma: config 2 (the headline); orb: config 3")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

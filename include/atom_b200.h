@@ -297,6 +297,57 @@ int atom_node_embed(const int* Z, const int* sys_id, const float* sphere, const 
 int atom_edge_species(const int* Z, const int* src, const int* tgt, int64_t E, int* zs, int* zt,
                       void* stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Orb-v3 (conservative) path (tt_atom/orb_model.py, orb_geometry.py, orb_forces.py). The graph
+ * is the UMA-style one above; Orb's senders are tgt and its receivers src, so Orb's edge vector
+ * pos[receiver] - pos[sender] + shift is the stored pos[src] - pos[tgt] + shift.
+ * ---------------------------------------------------------------------------------------- */
+
+/* Edge features (tt_atom/orb_geometry.py:65-97): feat[e, n*16 + m] = cut(r) * bessel_n(r) *
+ * sh_m(v / r) for nb Bessel bases and the 16 real SH of l <= 3 (component normalisation),
+ * cut [E] the p = 4 polynomial envelope (orb_model.py:69-82); ev [E,3] (may be NULL). */
+int atom_orb_edge_features(const float* pos, const int* src, const int* tgt, const int* img,
+                           const float* shifts, int64_t E, float rmax, int nb, float* feat,
+                           float* cut, float* ev, void* stream);
+/* VJP (replaces the host finish of tt_atom/orb_geometry.py:100-139): g_ev [E,3] from
+ * g_feat [E, 16 nb] and g_cut [E]. */
+int atom_orb_edge_features_bwd(const float* pos, const int* src, const int* tgt, const int* img,
+                               const float* shifts, int64_t E, float rmax, int nb,
+                               const float* g_feat, const float* g_cut, float* g_ev,
+                               void* stream);
+/* Row RMSNorm (orb_model.py:92-112): Y = X rsqrt(mean(X^2) + eps) w (Y may be NULL); with
+ * R_out: R_out = R_in + Y (the residual update). */
+int atom_rmsnorm_rows(const float* X, int64_t ldx, int64_t rows, int W, const float* w,
+                      float eps, float* Y, int64_t ldy, const float* R_in, int64_t ldr_in,
+                      float* R_out, int64_t ldr_out, void* stream);
+/* VJP of atom_rmsnorm_rows (orb_forces.py:67-79), X and gY dense [rows, W]; dX may alias gY. */
+int atom_rmsnorm_rows_bwd(const float* X, const float* gY, int64_t rows, int W, const float* w,
+                          float eps, float* dX, void* stream);
+/* Attention gates (orb_model.py:245-250): lin[e] = (edges[e].wr + br, edges[e].ws + bs),
+ * att[e] = sigmoid(lin[e]) * cut[e] ([E,2]: receive, send). */
+int atom_orb_attention(const float* edges, int64_t E, int C, const float* wr, float br,
+                       const float* ws, float bs, const float* cut, float* lin, float* att,
+                       void* stream);
+/* CSR segment sum: out[n] (+)= sum_{k in ptr[n]..ptr[n+1]} scale[e * sstride] X[e],
+ * e = eid ? eid[k] : k (scale may be NULL). W, ldx, ldo multiples of 4. */
+int atom_csr_sum(const float* X, int64_t ldx, const float* scale, int sstride, const int* ptr,
+                 const int* eid, int64_t N, int W, float* out, int64_t ldo, int accumulate,
+                 void* stream);
+/* VJP of the two attention-weighted aggregations and the gates (orb_forces.py:94-148):
+ * g_agg [N, 2C] = adjoint of [receiver aggregate | sender aggregate]; writes
+ * g_ue = gE_in + att_s g_agg[tgt, C:] + att_r g_agg[src, :C], gE_out = gE_in + gate adjoints
+ * (may alias gE_in), g_cut += cutoff adjoint. */
+int atom_orb_messages_bwd(const float* g_agg, const float* gE_in, const float* ue,
+                          const float* lin, const float* att, const float* cut, const int* src,
+                          const int* tgt, int64_t E, int C, const float* wr, const float* ws,
+                          float* g_ue, float* gE_out, float* g_cut, void* stream);
+/* out[c] = scale * sum_n X[n, c] (fixed order; the energy head's node mean). */
+int atom_col_mean(const float* X, int64_t ld, int64_t N, int C, float scale, float* out,
+                  void* stream);
+/* out[n, c] (+)= scale * v[c]. */
+int atom_row_broadcast(const float* v, int64_t N, int C, float scale, float* out, int64_t ld,
+                       int accumulate, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,117 @@
+"""CPU oracle for the Orb-v3 conservative energy + force + stress path -- TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU legs may import it. It
+restates, in fp32 torch on the CPU, the reference's Orb port:
+
+* edge features   -- tt_atom/orb_geometry.py:29-97 (Bessel basis, real SH lmax = 3 with
+                     component normalisation, polynomial cutoff p = 4 from
+                     tt_atom/orb_model.py:69-82); edge vector = pos[receiver] - pos[sender] +
+                     shift, receivers/senders = UMA source/target (tt_atom/orb_calculator.py:110)
+* MLPNorm         -- tt_atom/orb_model.py:92-173 (3 linears, SiLU after the first two,
+                     RMSNorm eps 1e-6 without bias)
+* interaction     -- tt_atom/orb_model.py:225-266 (sigmoid attention x cutoff, gathered edge
+                     input, two segment sums, node MLP, residuals)
+* energy head     -- tt_atom/orb_model.py:307-338 (node mean -> Linear-SiLU-Linear)
+* forces / stress -- autograd of the raw (normalised-space) energy w.r.t. positions and a
+                     symmetric strain leaf on the edge vectors (tt_atom/orb_geometry.py:83-88)
+
+Not restated: the energy normaliser / per-element references and the ZBL pair term, which are
+host-side scalar glue outside the GPU path (tt_atom/orb_model.py:491-600). Parity is unpinned by
+any committed Orb golden (the reference has none); it rests on this restatement of the
+reference's own Orb code.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+
+def bessel_basis(r, r_max=6.0, num_bases=8):
+    n = torch.arange(1, num_bases + 1, dtype=r.dtype)
+    w = math.pi / r_max * n
+    return math.sqrt(2.0 / r_max) * torch.sin(w * r[:, None]) / r[:, None]
+
+
+def spherical_harmonics_l3(u):
+    """Real SH l = 0..3 of unit vectors, component normalisation (16 columns)."""
+    x, y, z = u[:, 0], u[:, 1], u[:, 2]
+    s3 = math.sqrt(3.0)
+    y2, x2z2 = y * y, x * x + z * z
+    s20, s21 = s3 * x * z, s3 * x * y
+    s22, s23 = y2 - 0.5 * x2z2, s3 * y * z
+    s24 = s3 / 2.0 * (z * z - x * x)
+    cols = [torch.ones_like(x), x, y, z, s20, s21, s22, s23, s24,
+            math.sqrt(5.0 / 6.0) * (s20 * z + s24 * x), math.sqrt(5.0) * s20 * y,
+            math.sqrt(3.0 / 8.0) * (4.0 * y2 - x2z2) * x, 0.5 * y * (2.0 * y2 - 3.0 * x2z2),
+            math.sqrt(3.0 / 8.0) * z * (4.0 * y2 - x2z2), math.sqrt(5.0) * s24 * y,
+            math.sqrt(5.0 / 6.0) * (s24 * z - s20 * x)]
+    sh = torch.stack(cols, -1)
+    mult = torch.tensor([math.sqrt(2 * l + 1) for l in range(4) for _ in range(2 * l + 1)],
+                        dtype=sh.dtype)
+    return sh * mult
+
+
+def cutoff_env(r, r_max=6.0, p=4):
+    q = r / r_max
+    v = (1.0 - ((p + 1.0) * (p + 2.0) / 2.0) * q ** p + p * (p + 2.0) * q ** (p + 1)
+         - (p * (p + 1.0) / 2.0) * q ** (p + 2))
+    return v * (r < r_max)
+
+
+def edge_features(vectors, r_max, num_bases):
+    r = torch.linalg.norm(vectors, dim=-1)
+    rbf = bessel_basis(r, r_max, num_bases)
+    ang = spherical_harmonics_l3(F.normalize(vectors, dim=-1))
+    cut = cutoff_env(r, r_max)
+    feat = cut[:, None] * (rbf[:, :, None] * ang[:, None, :]).reshape(r.shape[0], -1)
+    return feat, cut
+
+
+def mlp_norm(x, w, p):
+    h = F.silu(F.linear(x, w[f"{p}.mlp.NN-0.weight"], w[f"{p}.mlp.NN-0.bias"]))
+    h = F.silu(F.linear(h, w[f"{p}.mlp.NN-1.weight"], w[f"{p}.mlp.NN-1.bias"]))
+    h = F.linear(h, w[f"{p}.mlp.NN-2.weight"], w[f"{p}.mlp.NN-2.bias"])
+    inv = torch.rsqrt((h * h).mean(-1, keepdim=True) + 1e-6)
+    return h * inv * w[f"{p}.layer_norm.weight"]
+
+
+def interaction(nodes, edges, w, p, senders, receivers, cut):
+    N = nodes.shape[0]
+    ra = torch.sigmoid(F.linear(edges, w[f"{p}._receive_attn.weight"],
+                                w[f"{p}._receive_attn.bias"])) * cut[:, None]
+    sa = torch.sigmoid(F.linear(edges, w[f"{p}._send_attn.weight"],
+                                w[f"{p}._send_attn.bias"])) * cut[:, None]
+    e_in = torch.cat([edges, nodes[senders], nodes[receivers]], 1)
+    ue = mlp_norm(e_in, w, f"{p}._edge_mlp")
+    sent = torch.zeros(N, ue.shape[1], dtype=ue.dtype).index_add(0, senders, ue * sa)
+    recv = torch.zeros(N, ue.shape[1], dtype=ue.dtype).index_add(0, receivers, ue * ra)
+    un = mlp_norm(torch.cat([nodes, recv, sent], 1), w, f"{p}._node_mlp")
+    return nodes + un, edges + ue
+
+
+def energy_forces(w, cfg, pos, Z, edge_index, shift=None, compute_stress=False):
+    """Raw (normalised-space) energy, forces = -dE/dpos and virial dE/dstrain. ``edge_index``
+    is the UMA-convention graph [src, tgt]; Orb uses senders = tgt, receivers = src."""
+    src, tgt = edge_index[0], edge_index[1]
+    senders, receivers = tgt, src
+    pos = pos.detach().clone().requires_grad_(True)
+    vec = pos[receivers] - pos[senders]
+    if shift is not None:
+        vec = vec + shift
+    strain = None
+    if compute_stress:
+        strain = torch.zeros(3, 3, requires_grad=True)
+        vec = vec + vec @ (0.5 * (strain + strain.T))
+    feat, cut = edge_features(vec, cfg["cutoff"], cfg["num_bases"])
+    nodes = mlp_norm(w["atom_emb.embeddings.weight"][Z], w, "_encoder._node_fn")
+    edges = mlp_norm(feat, w, "_encoder._edge_fn")
+    for i in range(cfg["num_message_passing_steps"]):
+        nodes, edges = interaction(nodes, edges, w, f"gnn_stacks.{i}", senders, receivers, cut)
+    mean = nodes.mean(0, keepdim=True)
+    h = F.silu(F.linear(mean, w["energy_head.mlp.NN-0.weight"], w["energy_head.mlp.NN-0.bias"]))
+    E = F.linear(h, w["energy_head.mlp.NN-1.weight"], w["energy_head.mlp.NN-1.bias"]).reshape(())
+    ins = [pos] if strain is None else [pos, strain]
+    g = torch.autograd.grad(E, ins)
+    return dict(energy=E.detach(), forces=-g[0], virial=g[1] if compute_stress else None)

@@ -23,7 +23,8 @@ class Fixture:
 
     def __init__(self, name):
         self.d = np.load(GOLDEN / name)
-        self.config = json.loads(bytes(self.d["config"]).decode())
+        self.config = (json.loads(bytes(self.d["config"]).decode())
+                       if "config" in self.d.files else {})
 
     def has(self, k):
         return k in self.d.files

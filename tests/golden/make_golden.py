@@ -92,6 +92,31 @@ def _run_reference(ref_root, out, cfg, w, tables, sysd, compute_stress):
     print("wrote", out, "N", len(sysd["Z"]), "E", ei.shape[1], "energy", E.item())
 
 
+def _orb_geometry(ref_root, out):
+    """Reference Orb edge features (tt_atom/orb_geometry.py:65-97) and their closed-form VJP
+    (:100-139) on a seeded periodic cell, from the reference's own code."""
+    for mod in [m for m in sys.modules if m == "tt_atom" or m.startswith("tt_atom.")]:
+        del sys.modules[mod]
+    sys.path[:] = [p for p in sys.path if not p.endswith("tt-atom_b200")]
+    sys.path.insert(0, str(ref_root))
+    from tt_atom.geometry import radius_graph
+    from tt_atom.orb_geometry import host_edge_features, host_edge_features_vjp
+    g = torch.Generator().manual_seed(5)
+    pos = torch.rand(40, 3, generator=g) * 7.0
+    cell = torch.diag(torch.tensor([7.0, 7.5, 8.0]))
+    ei, shift = radius_graph(pos, 4.0, cell=cell, pbc=[True] * 3)
+    senders, receivers = ei[1], ei[0]
+    feat, cut, vec = host_edge_features(pos, senders, receivers, shift, r_max=4.0, num_bases=8)
+    g_feat = torch.randn(feat.shape, generator=g)
+    g_cut = torch.randn(cut.shape, generator=g)
+    forces = host_edge_features_vjp(vec, senders, receivers, 40, g_feat, g_cut, r_max=4.0,
+                                    num_bases=8)
+    np.savez_compressed(HERE / out, pos=pos.numpy(), cell=cell.numpy(), edge_index=ei.numpy(),
+                        shift=shift.numpy(), feat=feat.numpy(), cut=cut.numpy(),
+                        g_feat=g_feat.numpy(), g_cut=g_cut.numpy(), forces=forces.numpy())
+    print("wrote", out, "E", ei.shape[1])
+
+
 def main(ref_root):
     ref_root = pathlib.Path(ref_root)
     _reduce_fairchem(ref_root, "golden_tiny.npz", "ref_golden_tiny.npz")
@@ -107,6 +132,7 @@ def main(ref_root):
     fcc = configs.fcc_alloy(reps=(2, 2, 2), seed=1)
     _run_reference(ref_root, "ref_run_tiny_molecule.npz", cfg, w, tables, mol, False)
     _run_reference(ref_root, "ref_run_tiny_fcc.npz", cfg, w, tables, fcc, True)
+    _orb_geometry(ref_root, "ref_orb_geometry.npz")
 
 
 if __name__ == "__main__":

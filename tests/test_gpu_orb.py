@@ -1,0 +1,75 @@
+"""Orb-v3 conservative path on the GPU against the CPU oracle and the reference's geometry."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import orb as OB
+from oracle import uma as O
+from tt_atom import _lib as L
+from tt_atom import configs
+from tt_atom._lib import call, ptr
+from tt_atom.graph import build_graph
+from tt_atom.orb import OrbCalculator
+
+pytestmark = pytest.mark.gpu
+E_REL, F_ABS, S_ABS = 1e-5, 1e-4, 1e-5
+
+
+def test_orb_edge_features_and_vjp_vs_reference(fx):
+    d = fx("ref_orb_geometry.npz").d
+    pos = torch.from_numpy(d["pos"]).cuda()
+    g = build_graph(d["pos"], np.zeros(40, np.int64), 4.0, d["cell"], [True] * 3)
+    ei, _, perm = g.reference_order()
+    assert torch.equal(ei.cpu(), torch.from_numpy(d["edge_index"]).long())
+    E = g.E
+    feat, cut, ev = torch.empty(E, 128).cuda(), torch.empty(E).cuda(), torch.empty(E, 3).cuda()
+    s = L.stream_ptr()
+    call("atom_orb_edge_features", ptr(pos), ptr(g.src), ptr(g.tgt), ptr(g.img), ptr(g.shifts),
+         E, 4.0, 8, ptr(feat), ptr(cut), ptr(ev), s)
+    assert (feat[perm].cpu() - torch.from_numpy(d["feat"])).abs().max() < 1e-5
+    # the p = 4 polynomial cancels near r_max: compare to fp32 rounding of its terms
+    assert (cut[perm].cpu() - torch.from_numpy(d["cut"]).reshape(-1)).abs().max() < 1e-5
+    # VJP: feed the reference's random adjoints (in reference order) and reduce to forces
+    gf, gc = torch.empty(E, 128), torch.empty(E)
+    gf[perm.cpu()] = torch.from_numpy(d["g_feat"])
+    gc[perm.cpu()] = torch.from_numpy(d["g_cut"]).reshape(-1)
+    gf, gc = gf.cuda(), gc.cuda()
+    gev = torch.empty(E, 3).cuda()
+    call("atom_orb_edge_features_bwd", ptr(pos), ptr(g.src), ptr(g.tgt), ptr(g.img),
+         ptr(g.shifts), E, 4.0, 8, ptr(gf), ptr(gc), ptr(gev), s)
+    F = torch.empty(40, 3).cuda()
+    call("atom_forces_virial", ptr(gev), ptr(ev), E, 40, ptr(g.recv_ptr), ptr(g.send_ptr),
+         ptr(g.send_eid), ptr(F), None, None, s)
+    assert (F.cpu() - torch.from_numpy(d["forces"])).abs().max() < 1e-4
+
+
+def _run(shape, sysd, precision):
+    cfg = configs.orb_config(shape)
+    w = configs.orb_random_weights(cfg, seed=0)
+    calc = OrbCalculator(w, cfg, precision=precision)
+    periodic = sysd["pbc"]
+    E, F, V = calc._evaluate(sysd["pos"], sysd["Z"], sysd["cell"] if periodic else None,
+                             [True] * 3 if periodic else None, True, periodic)
+    pos = torch.from_numpy(sysd["pos"])
+    cell = torch.from_numpy(sysd["cell"]) if periodic else None
+    ei, sh = O.neighbor_list(pos, cfg["cutoff"], cell, [True] * 3 if periodic else None,
+                             cfg["max_num_neighbors"])
+    r = OB.energy_forces(w, cfg, pos, torch.from_numpy(sysd["Z"]), ei,
+                         sh if periodic else None, compute_stress=periodic)
+    return E, F, V, r
+
+
+@pytest.mark.parametrize("precision", ["fp32", "3xtf32"])
+@pytest.mark.parametrize("shape,sysname", [("orb-tiny", "mol"), ("orb-v3", "sio2")])
+def test_orb_energy_forces_stress_vs_oracle(shape, sysname, precision):
+    if sysname == "mol":
+        sysd = configs.tiny_molecule()
+    else:
+        sysd = configs.amorphous_sio2(n_si=20, n_o=40, seed=2)
+    E, F, V, r = _run(shape, sysd, precision)
+    E_ref = float(r["energy"])
+    assert abs(E - E_ref) <= E_REL * max(abs(E_ref), 1.0), (E, E_ref)
+    assert (F.float() - r["forces"]).abs().max() <= F_ABS
+    if V is not None:
+        vol = abs(np.linalg.det(sysd["cell"].astype(np.float64)))
+        assert (V.float() - r["virial"]).abs().max() / vol <= S_ABS

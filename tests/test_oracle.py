@@ -110,3 +110,35 @@ def test_cap_rule_keeps_nearest_per_receiver():
         assert kd.numel() == min(5, int(sel.sum()))
         if dropped.numel():
             assert kd.max() <= dropped.min()
+
+
+def test_orb_oracle_geometry_matches_reference(fx):
+    """Orb edge features of the oracle equal the reference's host_edge_features; the autograd
+    VJP equals the reference's closed-form host_edge_features_vjp."""
+    from oracle import orb as OB
+    d = fx("ref_orb_geometry.npz").d
+    pos = torch.from_numpy(d["pos"]).requires_grad_(True)
+    ei = torch.from_numpy(d["edge_index"]).long()
+    vec = pos[ei[0]] - pos[ei[1]] + torch.from_numpy(d["shift"])
+    feat, cut = OB.edge_features(vec, 4.0, 8)
+    assert (feat - torch.from_numpy(d["feat"])).abs().max() < 1e-5
+    assert (cut - torch.from_numpy(d["cut"]).reshape(-1)).abs().max() < 1e-6
+    (g,) = torch.autograd.grad([feat, cut], [pos], [torch.from_numpy(d["g_feat"]),
+                                                   torch.from_numpy(d["g_cut"]).reshape(-1)])
+    assert (-g - torch.from_numpy(d["forces"])).abs().max() < 1e-4
+
+
+def test_orb_oracle_runs_tiny():
+    import sys
+    from oracle import orb as OB
+    from tt_atom import configs
+    cfg = configs.orb_config("orb-tiny")
+    w = configs.orb_random_weights(cfg)
+    s = configs.tiny_molecule()
+    pos = torch.from_numpy(s["pos"])
+    from oracle import uma as O
+    ei, _ = O.neighbor_list(pos, cfg["cutoff"], max_neighbors=cfg["max_num_neighbors"])
+    r = OB.energy_forces(w, cfg, pos, torch.from_numpy(s["Z"]), ei)
+    assert torch.isfinite(r["energy"]) and torch.isfinite(r["forces"]).all()
+    # net force of a conservative, translation-invariant model vanishes
+    assert r["forces"].sum(0).abs().max() < 1e-4

@@ -9,10 +9,11 @@
 //      weights are constant); A's split is made in shared memory by the epilogue warps, which are
 //      otherwise idle during the main loop.
 //
-// CTA layout (192 threads): warp 0 issues TMA loads, warp 1 allocates tensor memory and issues
-// the MMAs (one elected lane), warps 2-5 split A (mode 2) and run the epilogue; warp w reads
-// tensor-memory lanes 32 * (w % 4) .. + 31, i.e. output rows of that quarter. One CTA computes a
-// 128 x BN tile; K advances in 32-element (128-byte) stages through an S-deep mbarrier ring.
+// Persistent CTAs (one per SM, 320 threads): warp 0 issues TMA loads, warp 1 allocates tensor
+// memory and issues the MMAs (one elected lane), warps 2-5 run the epilogue (warp w reads
+// tensor-memory lanes 32 * (w % 4) .. + 31, i.e. output rows of that quarter), warps 6-9 split
+// A (mode 2). A tile is 128 x BN; K advances in 32-element (128-byte) stages through an S-deep
+// mbarrier ring that runs on across tiles.
 //
 // Every wait is bounded: on expiry the CTA records an error code in g_tc_error, abandons the
 // tile and still releases its tensor memory.
@@ -20,6 +21,14 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+
+// Pipeline depth (shared-memory stages) per precision mode; overridable at build time.
+#ifndef ATOM_TC_STAGES_3X
+#define ATOM_TC_STAGES_3X 3
+#endif
+#ifndef ATOM_TC_STAGES_1X
+#define ATOM_TC_STAGES_1X 5
+#endif
 
 namespace atom {
 
@@ -152,8 +161,9 @@ struct Cfg {
     static constexpr uint32_t kTileB = BN * BK * 4;
     static constexpr uint32_t kStage = kTileA + kTileB + (MODE == 2 ? kTileA + kTileB : 0);
     static constexpr uint32_t kLoadBytes = kTileA + kTileB * (MODE == 2 ? 2 : 1);  // TMA bytes
-    static constexpr int kStages = MODE == 2 ? 3 : 5;
+    static constexpr int kStages = MODE == 2 ? ATOM_TC_STAGES_3X : ATOM_TC_STAGES_1X;
     static constexpr uint32_t kSmem = kStages * kStage + 1024 + 256;
+    static_assert(4 * BN <= 512, "accumulators must fit tensor memory");
     static constexpr uint32_t kTmemCols = 4 * BN;   // up to 4 accumulators of BN columns
 };
 
@@ -164,9 +174,35 @@ struct Maps {
     CUtensorMap l[8];
 };
 
+// Tile t of the launch -> (group, first row, first column, K stages).
+struct TileInfo {
+    int grp, n0, nk;
+    long long m0;
+};
+template <int BN>
+__device__ __forceinline__ TileInfo tile_info(const Args& p, int ntn, int t) {
+    TileInfo ti;
+    int mt = t / ntn, tn = t - mt * ntn;
+    int grp = 0;
+    while (grp + 1 < p.g.ngroups && tn >= p.g.tile_start[grp + 1]) ++grp;
+    ti.grp = grp;
+    ti.n0 = (tn - p.g.tile_start[grp]) * BN;
+    ti.m0 = (long long)mt * BM;
+    ti.nk = p.g.K[grp] / BK;
+    return ti;
+}
+
+// Persistent kernel: each CTA walks tiles blockIdx.x, blockIdx.x + gridDim.x, ... (column
+// tiles of one row block are adjacent, so concurrently running CTAs share A rows in L2).
+// Warps: 0 TMA producer, 1 TMEM allocator + MMA issuer, 2-5 epilogue, 6-9 A splitters (mode 2).
+// The epilogue drains the accumulators into registers and releases tensor memory before it
+// computes and stores, so the next tile's MMAs overlap the previous tile's stores.
+constexpr int kThreads = 320;
+
 template <int BN, int MODE>
-__global__ void __launch_bounds__(192, 1)
-    gemm_tc_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Args p) {
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Args p, int ntn,
+                   int ntiles) {
     using CF = Cfg<BN, MODE>;
     constexpr int S = CF::kStages;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -175,27 +211,20 @@ __global__ void __launch_bounds__(192, 1)
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * CF::kStage);
     uint64_t* conv = full + S;
     uint64_t* empty = conv + S;
-    uint64_t* accum = empty + S;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+    uint64_t* accf = empty + S;
+    uint64_t* acce = accf + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 1);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int tn = blockIdx.x, grp = 0;
-    while (grp + 1 < p.g.ngroups && tn >= p.g.tile_start[grp + 1]) ++grp;
-    const int n0 = (tn - p.g.tile_start[grp]) * BN;
-    const long long m0 = (long long)blockIdx.y * BM;
-    const int K = p.g.K[grp], N = p.g.N[grp];
-    const int nk = K / BK;
-    const CUtensorMap* mB = &maps.b[grp];
-    const CUtensorMap* mL = &maps.l[grp];
-
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&conv[s], 128);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accum, 1);
+        mbar_init(accf, 1);
+        mbar_init(acce, 128);
         // a CTA that failed earlier in this grid (or an earlier launch) stops the rest here
         *abort_flag = *(volatile int*)&g_tc_error != 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -216,126 +245,154 @@ __global__ void __launch_bounds__(192, 1)
     auto stB = [&](int s) { return smem + s * CF::kStage + kTileA; };
     auto stAL = [&](int s) { return smem + s * CF::kStage + kTileA + CF::kTileB; };
     auto stBL = [&](int s) { return smem + s * CF::kStage + 2 * kTileA + CF::kTileB; };
+    auto aborted = [&]() { return *(volatile int*)abort_flag != 0; };
 
     if (warp == 0) {
         // ------------------------------------------------------------- TMA producer
         if (lane == 0) {
-            const int a_x0 = p.g.a_col[grp];
-            for (int kt = 0; kt < nk; ++kt) {
-                int s = kt % S;
-                uint32_t ph = (uint32_t)(kt / S) & 1u;
-                if (!mbar_wait(&empty[s], ph ^ 1u, 1) || *(volatile int*)abort_flag) {
-                    *(volatile int*)abort_flag = 1;
-                    break;
+            uint32_t it = 0;
+            for (int t = blockIdx.x; t < ntiles && !aborted(); t += gridDim.x) {
+                TileInfo ti = tile_info<BN>(p, ntn, t);
+                const int a_x0 = p.g.a_col[ti.grp];
+                for (int kt = 0; kt < ti.nk; ++kt, ++it) {
+                    int s = it % S;
+                    uint32_t ph = (it / S) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, 1) || aborted()) {
+                        *(volatile int*)abort_flag = 1;
+                        break;
+                    }
+                    mbar_expect_tx(&full[s], CF::kLoadBytes);
+                    tma_load_2d(stA(s), &maps.a, a_x0 + kt * BK, (int)ti.m0, &full[s]);
+                    tma_load_2d(stB(s), &maps.b[ti.grp], kt * BK, ti.n0, &full[s]);
+                    if (MODE == 2) tma_load_2d(stBL(s), &maps.l[ti.grp], kt * BK, ti.n0, &full[s]);
                 }
-                mbar_expect_tx(&full[s], CF::kLoadBytes);
-                tma_load_2d(stA(s), &maps.a, a_x0 + kt * BK, (int)m0, &full[s]);
-                tma_load_2d(stB(s), mB, kt * BK, n0, &full[s]);
-                if (MODE == 2) tma_load_2d(stBL(s), mL, kt * BK, n0, &full[s]);
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------- MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_tf32<BN>();
-            bool ok = true;
-            for (int kt = 0; kt < nk; ++kt) {
-                int s = kt % S;
-                uint32_t ph = (uint32_t)(kt / S) & 1u;
-                if (!mbar_wait(MODE == 2 ? &conv[s] : &full[s], ph, 2) ||
-                    *(volatile int*)abort_flag) {
+            uint32_t it = 0, j = 0;
+            for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++j) {
+                TileInfo ti = tile_info<BN>(p, ntn, t);
+                bool ok = !aborted() && mbar_wait(acce, (j & 1u) ^ 1u, 5);
+                if (ok) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                for (int kt = 0; ok && kt < ti.nk; ++kt, ++it) {
+                    int s = it % S;
+                    uint32_t ph = (it / S) & 1u;
+                    if (!mbar_wait(MODE == 2 ? &conv[s] : &full[s], ph, 2) || aborted()) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    uint32_t a = smem_u32(stA(s)), b = smem_u32(stB(s));
+                    // stage kt accumulates into accumulator kt % nacc (fp32 columns BN apart)
+                    const uint32_t dacc = tmem + (uint32_t)((kt % p.nacc) * BN);
+                    const bool first = kt < p.nacc;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; ++kk) {
+                        uint32_t acc = (!first || kk > 0) ? 1u : 0u;
+                        mma_tf32(dacc, sdesc(a + kk * 32), sdesc(b + kk * 32), idesc, acc);
+                        if (MODE == 2) {
+                            uint32_t al = smem_u32(stAL(s)), bl = smem_u32(stBL(s));
+                            mma_tf32(dacc, sdesc(a + kk * 32), sdesc(bl + kk * 32), idesc, 1u);
+                            mma_tf32(dacc, sdesc(al + kk * 32), sdesc(b + kk * 32), idesc, 1u);
+                        }
+                    }
+                    mma_commit(&empty[s]);
+                }
+                if (ok) {
+                    mma_commit(accf);
+                } else {
                     *(volatile int*)abort_flag = 1;
-                    ok = false;
+                    mbar_arrive(accf);
                     break;
                 }
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                uint32_t a = smem_u32(stA(s)), b = smem_u32(stB(s));
-                // stage kt accumulates into accumulator kt % nacc (fp32 columns BN apart)
-                const uint32_t dacc = tmem + (uint32_t)((kt % p.nacc) * BN);
-                const bool first = kt < p.nacc;
-#pragma unroll
-                for (int kk = 0; kk < BK / 8; ++kk) {
-                    uint32_t acc = (!first || kk > 0) ? 1u : 0u;
-                    mma_tf32(dacc, sdesc(a + kk * 32), sdesc(b + kk * 32), idesc, acc);
-                    if (MODE == 2) {
-                        uint32_t al = smem_u32(stAL(s)), bl = smem_u32(stBL(s));
-                        mma_tf32(dacc, sdesc(a + kk * 32), sdesc(bl + kk * 32), idesc, 1u);
-                        mma_tf32(dacc, sdesc(al + kk * 32), sdesc(b + kk * 32), idesc, 1u);
-                    }
-                }
-                mma_commit(&empty[s]);
             }
-            if (ok) mma_commit(accum);
-            else mbar_arrive(accum);
+        }
+    } else if (warp >= 6) {
+        // ------------------------------------------------------ A split (3xTF32 only)
+        if (MODE == 2) {
+            const int ct = threadIdx.x - 192;      // 0..127
+            uint32_t it = 0;
+            for (int t = blockIdx.x; t < ntiles && !aborted(); t += gridDim.x) {
+                TileInfo ti = tile_info<BN>(p, ntn, t);
+                for (int kt = 0; kt < ti.nk; ++kt, ++it) {
+                    int s = it % S;
+                    uint32_t ph = (it / S) & 1u;
+                    if (!mbar_wait(&full[s], ph, 3) || aborted()) {
+                        *(volatile int*)abort_flag = 1;
+                        break;
+                    }
+                    float4* hi = reinterpret_cast<float4*>(stA(s));
+                    float4* lo = reinterpret_cast<float4*>(stAL(s));
+#pragma unroll
+                    for (int i = 0; i < (int)(kTileA / 16) / 128; ++i) {
+                        int q = ct + 128 * i;
+                        float4 x = hi[q], h, l;
+                        h.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u); l.x = x.x - h.x;
+                        h.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u); l.y = x.y - h.y;
+                        h.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u); l.z = x.z - h.z;
+                        h.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u); l.w = x.w - h.w;
+                        hi[q] = h;
+                        lo[q] = l;
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mbar_arrive(&conv[s]);
+                }
+            }
         }
     } else {
-        // ------------------------------------------- A split (mode 2) and the epilogue
-        const int et = threadIdx.x - 64;     // 0..127
-        if (MODE == 2) {
-            for (int kt = 0; kt < nk; ++kt) {
-                int s = kt % S;
-                uint32_t ph = (uint32_t)(kt / S) & 1u;
-                if (!mbar_wait(&full[s], ph, 3) || *(volatile int*)abort_flag) {
-                    *(volatile int*)abort_flag = 1;
-                    break;
-                }
-                float4* hi = reinterpret_cast<float4*>(stA(s));
-                float4* lo = reinterpret_cast<float4*>(stAL(s));
+        // ------------------------------------------------------------------ epilogue
+        const int quarter = warp & 3;
+        uint32_t j = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++j) {
+            TileInfo ti = tile_info<BN>(p, ntn, t);
+            bool ok = mbar_wait(accf, j & 1u, 4) && !aborted();
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            // drain the accumulators into registers (partial sums added with round-to-nearest)
+            const int nused = ti.nk < p.nacc ? ti.nk : p.nacc;
+            float v[BN];
+            const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll
-                for (int i = 0; i < (int)(kTileA / 16) / 128; ++i) {
-                    int q = et + 128 * i;
-                    float4 x = hi[q], h, l;
-                    h.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u); l.x = x.x - h.x;
-                    h.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u); l.y = x.y - h.y;
-                    h.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u); l.z = x.z - h.z;
-                    h.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u); l.w = x.w - h.w;
-                    hi[q] = h;
-                    lo[q] = l;
-                }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive(&conv[s]);
-            }
-        }
-        bool ok = mbar_wait(accum, 0, 4) && !*(volatile int*)abort_flag;
-        ok = __all_sync(0xffffffffu, ok);
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (ok) {
-            const int quarter = warp & 3;
-            const long long m = m0 + quarter * 32 + lane;
-            const float* bias = p.g.bias[grp];
-            const int ccol = p.g.c_col[grp], tcol = p.g.t_col[grp];
-            const int nused = nk < p.nacc ? nk : p.nacc;
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                float v[16];
-                const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0;
-                tmem_ld16(lane_base, v);
-                for (int q = 1; q < nused; ++q) {   // partial sums added with round-to-nearest
+            for (int c0 = 0; c0 < BN; c0 += 16) tmem_ld16(lane_base + (uint32_t)c0, v + c0);
+            for (int q = 1; q < nused; ++q) {
+#pragma unroll
+                for (int c0 = 0; c0 < BN; c0 += 16) {
                     float w[16];
-                    tmem_ld16(lane_base + (uint32_t)(q * BN), w);
+                    tmem_ld16(lane_base + (uint32_t)(q * BN + c0), w);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] += w[j];
+                    for (int jj = 0; jj < 16; ++jj) v[c0 + jj] += w[jj];
                 }
-                if (m >= p.M || n0 + c0 >= N) continue;
-                const long long row = m * p.ldc + ccol + n0 + c0;
-                const float* t1 = p.T1 ? p.T1 + (long long)p.idx1[m] * p.ldt + tcol + n0 + c0 : nullptr;
-                const float* t2 = p.T2 ? p.T2 + (long long)p.idx2[m] * p.ldt + tcol + n0 + c0 : nullptr;
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            mbar_arrive(acce);                  // tensor memory may take the next tile now
+            const long long m = ti.m0 + quarter * 32 + lane;
+            const int N = p.g.N[ti.grp];
+            if (m >= p.M) continue;
+            const float* bias = p.g.bias[ti.grp];
+            const int ccol = p.g.c_col[ti.grp], tcol = p.g.t_col[ti.grp];
+            const long long row = m * p.ldc + ccol + ti.n0;
+            const float* t1 = p.T1 ? p.T1 + (long long)p.idx1[m] * p.ldt + tcol + ti.n0 : nullptr;
+            const float* t2 = p.T2 ? p.T2 + (long long)p.idx2[m] * p.ldt + tcol + ti.n0 : nullptr;
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    int n = n0 + c0 + j;
-                    if (n >= N) break;
-                    float x = v[j];
+            for (int c = 0; c < BN; ++c) {
+                const int n = ti.n0 + c;
+                if (n < N) {
+                    float x = v[c];
                     if (bias) x += bias[n];
-                    if (t1) x += t1[j];
-                    if (t2) x += t2[j];
+                    if (t1) x += t1[c];
+                    if (t2) x += t2[c];
                     if (p.act == 1) {
-                        if (p.Cpre) p.Cpre[row + j] = x;
+                        if (p.Cpre) p.Cpre[row + c] = x;
                         x = silu_f(x);
                     }
-                    p.C[row + j] = p.accumulate ? p.C[row + j] + x : x;
+                    p.C[row + c] = p.accumulate ? p.C[row + c] + x : x;
                 }
             }
         }
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     }
     __syncthreads();
     if (warp == 1) {
@@ -430,8 +487,16 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
             if (int s = make_map(&maps.l[i], g->Bt_lo[i], g->K[i], g->N[i], g->K[i], BN)) return s;
     }
     p.g.tile_start[g->ngroups] = tiles;
-    dim3 grid(tiles, ceil_div(M, BM));
-    gemm_tc_kernel<BN, MODE><<<grid, 192, CF::kSmem, st>>>(maps, p);
+    const long long ntiles = (long long)tiles * ceil_div(M, BM);
+    if (ntiles >= (1LL << 31)) {
+        set_error("gemm_tc: too many tiles");
+        return ATOM_ERR_ARG;
+    }
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = (int)(ntiles < nsm ? ntiles : nsm);
+    gemm_tc_kernel<BN, MODE><<<grid, kThreads, CF::kSmem, st>>>(maps, p, tiles, (int)ntiles);
     return check_launch("gemm_tc");
 }
 

@@ -85,6 +85,24 @@ _SIGS = {
     "atom_segment_sum": (c_void_p, c_int64, c_void_p, c_int, c_void_p, c_void_p),
     "atom_node_embed": (c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p,
                         c_void_p),
+    "atom_orb_edge_features": (c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                               c_float, c_int, c_void_p, c_void_p, c_void_p, c_void_p),
+    "atom_orb_edge_features_bwd": (c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                                   c_float, c_int, c_void_p, c_void_p, c_void_p, c_void_p),
+    "atom_rmsnorm_rows": (c_void_p, c_int64, c_int64, c_int, c_void_p, c_float, c_void_p,
+                          c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p),
+    "atom_rmsnorm_rows_bwd": (c_void_p, c_void_p, c_int64, c_int, c_void_p, c_float, c_void_p,
+                              c_void_p),
+    "atom_orb_attention": (c_void_p, c_int64, c_int, c_void_p, c_float, c_void_p, c_float,
+                           c_void_p, c_void_p, c_void_p, c_void_p),
+    "atom_csr_sum": (c_void_p, c_int64, c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int,
+                     c_void_p, c_int64, c_int, c_void_p),
+    "atom_orb_messages_bwd": (c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                              c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p,
+                              c_void_p, c_void_p, c_void_p),
+    "atom_col_mean": (c_void_p, c_int64, c_int64, c_int, c_float, c_void_p, c_void_p),
+    "atom_row_broadcast": (c_void_p, c_int64, c_int, c_float, c_void_p, c_int64, c_int,
+                           c_void_p),
     "atom_edge_species": (c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p),
 }
 

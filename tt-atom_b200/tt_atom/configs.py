@@ -223,3 +223,69 @@ def system(name):
     if name == "bcc-fe":
         return bcc_iron()
     raise KeyError(name)
+
+
+# ------------------------------------------------------------------------------- Orb-v3 shape
+
+ORB_SHAPES = {
+    # config 3: Orb-v3-conservative shape (random init)
+    "orb-v3": dict(latent_dim=256, hidden_dim=1024, node_embed_size=256, edge_embed_size=128,
+                   num_bases=8, num_message_passing_steps=5, cutoff=6.0, max_num_neighbors=20,
+                   head_hidden=256),
+    # CPU-sized variant for tests
+    "orb-tiny": dict(latent_dim=32, hidden_dim=64, node_embed_size=32, edge_embed_size=128,
+                     num_bases=8, num_message_passing_steps=2, cutoff=6.0, max_num_neighbors=20,
+                     head_hidden=32),
+}
+
+
+def orb_config(name):
+    cfg = dict(ORB_SHAPES[name])
+    cfg.update(family="orb", task="omat")
+    return cfg
+
+
+def orb_random_weights(cfg, seed=0):
+    """Random-init Orb weights with the reference's key names (gns.MoleculeGNS naming as read by
+    tt_atom/orb_model.py:127-338 in the reference)."""
+    g = torch.Generator().manual_seed(seed)
+    C, Hd, L = cfg["latent_dim"], cfg["hidden_dim"], cfg["num_message_passing_steps"]
+    w = {}
+
+    def lin(name, fo, fi):
+        b = 1.0 / math.sqrt(fi)
+        w[f"{name}.weight"] = (torch.rand(fo, fi, generator=g) * 2 - 1) * b
+        w[f"{name}.bias"] = (torch.rand(fo, generator=g) * 2 - 1) * b
+
+    def mlpnorm(p, fi):
+        lin(f"{p}.mlp.NN-0", Hd, fi)
+        lin(f"{p}.mlp.NN-1", Hd, Hd)
+        lin(f"{p}.mlp.NN-2", C, Hd)
+        w[f"{p}.layer_norm.weight"] = 1.0 + 0.1 * torch.randn(C, generator=g)
+
+    w["atom_emb.embeddings.weight"] = torch.randn(119, cfg["node_embed_size"], generator=g)
+    mlpnorm("_encoder._node_fn", cfg["node_embed_size"])
+    mlpnorm("_encoder._edge_fn", cfg["edge_embed_size"])
+    for i in range(L):
+        p = f"gnn_stacks.{i}"
+        mlpnorm(f"{p}._edge_mlp", 3 * C)
+        mlpnorm(f"{p}._node_mlp", 3 * C)
+        lin(f"{p}._receive_attn", 1, C)
+        lin(f"{p}._send_attn", 1, C)
+    lin("energy_head.mlp.NN-0", cfg["head_hidden"], C)
+    lin("energy_head.mlp.NN-1", 1, cfg["head_hidden"])
+    return {k: v.float().contiguous() for k, v in w.items()}
+
+
+def amorphous_sio2(n_si=334, n_o=668, density=2.2, min_dist=1.4, seed=2):
+    """Config 3: amorphous SiO2, uniform random positions at ``density`` g/cm^3 in a cubic box,
+    rejection-sampled to ``min_dist`` A."""
+    rng = np.random.default_rng(seed)
+    mass = n_si * 28.0855 + n_o * 15.999                        # amu
+    vol = mass * 1.66053906660e-24 / density * 1e24             # A^3
+    side = vol ** (1.0 / 3.0)
+    Z = np.array([14] * n_si + [8] * n_o, dtype=np.int64)
+    Z = Z[rng.permutation(len(Z))]
+    pos = _reject_uniform(rng, len(Z), side, min_dist)
+    return dict(pos=pos.astype(np.float32), Z=Z,
+                cell=np.diag([side] * 3).astype(np.float32), pbc=True)

@@ -1,0 +1,345 @@
+"""Orb-v3 (conservative) energy + force + stress on the GPU, and its ASE calculator.
+
+Reference structure (tt-atom): tt_atom/orb_model.py:127-338 (MLPNorm, Encoder,
+AttentionInteractionLayer, EnergyHead), tt_atom/orb_forces.py:82-378 (their VJPs),
+tt_atom/orb_geometry.py:65-139 (edge features and VJP), tt_atom/orb_calculator.py:89-215.
+
+The edge MLP of every interaction layer is the dominant contraction. Its first linear acts on
+[edges | nodes[sender] | nodes[receiver]]; here it is split: the node parts are one node-level
+GEMM ``P = nodes @ [W_s; W_r]^T`` ([N, 2 hidden]) whose rows are gathered and added in the edge
+GEMM's epilogue, so the gathered [E, 3C] input is never built (K drops from 3C to C). Its
+reverse pass likewise sums the first-layer adjoint per node (CSR) before one node-level GEMM.
+SiLU is fused into the GEMM epilogues (pre-activations kept for the reverse pass); RMSNorm and
+the residual update are one kernel.
+
+Not on the GPU: the energy normaliser / per-element references (applied on the host when the
+weights carry them) and the ZBL pair term (host glue in the reference; not implemented here).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from ._lib import ptr
+from .ase_compat import _AseCalculator, all_changes, atoms_volume, voigt_6
+from .engine import PRECISIONS, _Groups, _dev, call
+from .graph import build_graph
+
+
+class OrbEngine:
+    def __init__(self, weights, cfg, device="cuda", precision="3xtf32"):
+        L.lib()
+        self.device = torch.device(device)
+        self.cfg = dict(cfg)
+        self.precision = PRECISIONS[precision]
+        C, Hd = cfg["latent_dim"], cfg["hidden_dim"]
+        self.C, self.Hd, self.NL = C, Hd, cfg["num_message_passing_steps"]
+        self.nb, self.rmax = cfg["num_bases"], float(cfg["cutoff"])
+        self.D0 = cfg["node_embed_size"]
+        w = {k: v.float() for k, v in weights.items()}
+        d = lambda t: _dev(t, self.device)  # noqa: E731
+
+        def lin_groups(W, b=None, a_col=0, c_col=0):
+            return _Groups([dict(a_col=a_col, K=W.shape[1], c_col=c_col, N=W.shape[0],
+                                 B=d(W.t()), bias=b)])
+
+        def bw_groups(W):       # g_in = g_out @ W
+            return _Groups([dict(a_col=0, K=W.shape[0], c_col=0, N=W.shape[1], B=d(W))])
+
+        def mlpnorm(p):
+            (W0, b0), (W1, b1), (W2, b2) = [(w[f"{p}.mlp.NN-{i}.weight"],
+                                            w[f"{p}.mlp.NN-{i}.bias"]) for i in range(3)]
+            return dict(f0=lin_groups(W0, d(b0)), f1=lin_groups(W1, d(b1)),
+                        f2=lin_groups(W2, d(b2)), b0=bw_groups(W0), b1=bw_groups(W1),
+                        b2=bw_groups(W2), nw=d(w[f"{p}.layer_norm.weight"]), W0=W0, b0v=d(b0))
+
+        self.emb = d(w["atom_emb.embeddings.weight"])
+        self.zero_row = torch.zeros(1, self.D0, device=self.device)
+        self.enc_n = mlpnorm("_encoder._node_fn")
+        self.enc_e = mlpnorm("_encoder._edge_fn")
+        self.layers = []
+        for i in range(self.NL):
+            p = f"gnn_stacks.{i}"
+            em, nm = mlpnorm(f"{p}._edge_mlp"), mlpnorm(f"{p}._node_mlp")
+            W0 = em["W0"]                               # [Hd, 3C]: edges | sender | receiver
+            Wa, Ws, Wr = W0[:, :C], W0[:, C:2 * C], W0[:, 2 * C:]
+            em["f0"] = _Groups([dict(a_col=0, K=C, c_col=0, N=Hd, B=d(Wa.t()), bias=em["b0v"])])
+            em["proj"] = _Groups([dict(a_col=0, K=C, c_col=0, N=Hd, B=d(Ws.t())),
+                                  dict(a_col=0, K=C, c_col=Hd, N=Hd, B=d(Wr.t()))])
+            em["b0a"] = _Groups([dict(a_col=0, K=Hd, c_col=0, N=C, B=d(Wa))])
+            em["b0sr"] = _Groups([dict(a_col=0, K=2 * Hd, c_col=0, N=C,
+                                       B=d(torch.cat([Ws, Wr], 0)))])
+            nW0 = nm["W0"]
+            nm["b0n"] = _Groups([dict(a_col=0, K=Hd, c_col=0, N=C, B=d(nW0[:, :C]))])
+            nm["b0agg"] = _Groups([dict(a_col=0, K=Hd, c_col=0, N=2 * C, B=d(nW0[:, C:]))])
+            self.layers.append(dict(
+                em=em, nm=nm,
+                wr=d(w[f"{p}._receive_attn.weight"].reshape(-1)),
+                br=float(w[f"{p}._receive_attn.bias"].reshape(-1)[0]),
+                ws=d(w[f"{p}._send_attn.weight"].reshape(-1)),
+                bs=float(w[f"{p}._send_attn.bias"].reshape(-1)[0])))
+        H0, Hb0 = w["energy_head.mlp.NN-0.weight"], w["energy_head.mlp.NN-0.bias"]
+        H1, Hb1 = w["energy_head.mlp.NN-1.weight"], w["energy_head.mlp.NN-1.bias"]
+        self.hh = H0.shape[0]
+        self.head0 = lin_groups(H0, d(Hb0))
+        self.head1 = lin_groups(H1, d(Hb1))
+        self.head1_row = d(H1.reshape(-1))
+        self.head0_bw = bw_groups(H0)
+
+    def _gemm(self, A, lda, M, groups, Cout, ldc, *, Cpre=None, T1=None, T2=None, idx1=None,
+              idx2=None, ldt=0, act=0, accumulate=0, s=0):
+        call("atom_gemm", ptr(A), lda, M, groups.struct, ptr(Cout), ldc, ptr(Cpre), ptr(T1),
+             ptr(T2), ptr(idx1), ptr(idx2), ldt, act, accumulate, self.precision, s)
+
+    def workspace(self, graph):
+        return OrbWorkspace(self, graph)
+
+    # ---------------------------------------------------------------------------- forward
+    def _mlpnorm_fwd(self, m, X, ldx, M, a0, a1, h2, tmp0, tmp1, s, first=None):
+        Hd = self.Hd
+        if first is None:
+            self._gemm(X, ldx, M, m["f0"], tmp0, Hd, Cpre=a0, act=1, s=s)
+        else:
+            first(tmp0, a0)
+        self._gemm(tmp0, Hd, M, m["f1"], tmp1, Hd, Cpre=a1, act=1, s=s)
+        self._gemm(tmp1, Hd, M, m["f2"], h2, self.C, s=s)
+
+    def launches_per_step(self, ws, forces=True, virial=True):
+        """Number of this library's kernels one ``run`` launches (counted)."""
+        from .engine import _counter
+        torch.cuda.synchronize()
+        c0 = _counter[0]
+        self.run(ws, forces=forces, virial=virial)
+        torch.cuda.synchronize()
+        return _counter[0] - c0
+
+    def time_kernels(self, ws, reps=5):
+        """Device time of the dominant kernel: the layer-0 edge-MLP hidden GEMM
+        ([E, hidden] x [hidden, hidden], SiLU epilogue), timed with CUDA events on its stream."""
+        st = torch.cuda.Stream(device=self.device)
+        st.wait_stream(torch.cuda.current_stream())
+        E, Hd = ws.graph.E, self.Hd
+        em = self.layers[0]["em"]
+        with torch.cuda.stream(st):
+            s = st.cuda_stream
+            self._gemm(ws.et0, Hd, E, em["f1"], ws.et1, Hd, Cpre=ws.ea1[0], act=1, s=s)
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record(st)
+            for _ in range(reps):
+                self._gemm(ws.et0, Hd, E, em["f1"], ws.et1, Hd, Cpre=ws.ea1[0], act=1, s=s)
+            t1.record(st)
+        st.synchronize()
+        torch.cuda.current_stream().wait_stream(st)
+        return dict(name="Orb edge-MLP hidden GEMM", ms=t0.elapsed_time(t1) / reps,
+                    flop=2.0 * E * Hd * Hd)
+
+    def run(self, ws, pos=None, forces=True, virial=False, stream=None):
+        """One E (+F, +virial) evaluation on ``ws``'s graph (``pos`` defaults to ws.pos)."""
+        if pos is not None and pos.data_ptr() != ws.pos.data_ptr():
+            ws.pos.copy_(pos)
+        s = L.stream_ptr(stream)
+        g = ws.graph
+        N, E, C, Hd = g.N, g.E, self.C, self.Hd
+        C3 = 3 * C
+        call("atom_orb_edge_features", ptr(ws.pos), ptr(g.src), ptr(g.tgt), ptr(g.img),
+             ptr(g.shifts), E, self.rmax, self.nb, ptr(ws.feat), ptr(ws.cut), ptr(ws.ev), s)
+        # encoder: node features -> node_in[0][:, :C]; edge features -> edges[0]
+        self._mlpnorm_fwd(self.enc_n, ws.x0, self.D0, N, ws.na0[-1], ws.na1[-1], ws.nh2[-1],
+                          ws.nt0, ws.nt1, s)
+        call("atom_rmsnorm_rows", ptr(ws.nh2[-1]), C, N, C, ptr(self.enc_n["nw"]), 1e-6,
+             ptr(ws.node_in[0]), C3, None, 0, None, 0, s)
+        self._mlpnorm_fwd(self.enc_e, ws.feat, 16 * self.nb, E, ws.ea0[-1], ws.ea1[-1],
+                          ws.eh2[-1], ws.et0, ws.et1, s)
+        call("atom_rmsnorm_rows", ptr(ws.eh2[-1]), C, E, C, ptr(self.enc_e["nw"]), 1e-6,
+             ptr(ws.edges[0]), C, None, 0, None, 0, s)
+        for i, lay in enumerate(self.layers):
+            nodes, edges = ws.node_in[i], ws.edges[i]
+            call("atom_orb_attention", ptr(edges), E, C, ptr(lay["wr"]), lay["br"],
+                 ptr(lay["ws"]), lay["bs"], ptr(ws.cut), ptr(ws.lin[i]), ptr(ws.att[i]), s)
+            em, nm = lay["em"], lay["nm"]
+            # node projections for the gathered part of the edge MLP's first linear
+            self._gemm(nodes, C3, N, em["proj"], ws.P, 2 * Hd, s=s)
+
+            def first(out, pre, em=em, edges=edges):
+                self._gemm(edges, C, E, em["f0"], out, Hd, Cpre=pre, T1=ws.P, T2=ws.P[:, Hd:],
+                           idx1=g.tgt, idx2=g.src, ldt=2 * Hd, act=1, s=s)
+            self._mlpnorm_fwd(em, None, 0, E, ws.ea0[i], ws.ea1[i], ws.eh2[i], ws.et0, ws.et1, s,
+                              first=first)
+            # ue = RMSNorm(h2); edges[i+1] = edges[i] + ue
+            call("atom_rmsnorm_rows", ptr(ws.eh2[i]), C, E, C, ptr(em["nw"]), 1e-6,
+                 ptr(ws.ue[i]), C, ptr(edges), C, ptr(ws.edges[i + 1]), C, s)
+            # aggregates into node_in[i][:, C:3C]: receivers (= src) then senders (= tgt)
+            call("atom_csr_sum", ptr(ws.ue[i]), C, ptr(ws.att[i]), 2, ptr(g.send_ptr),
+                 ptr(g.send_eid), N, C, ptr(nodes[:, C:]), C3, 0, s)
+            call("atom_csr_sum", ptr(ws.ue[i]), C, ptr(ws.att[i][:, 1:]), 2, ptr(g.recv_ptr),
+                 None, N, C, ptr(nodes[:, 2 * C:]), C3, 0, s)
+            self._mlpnorm_fwd(nm, nodes, C3, N, ws.na0[i], ws.na1[i], ws.nh2[i], ws.nt0, ws.nt1,
+                              s)
+            call("atom_rmsnorm_rows", ptr(ws.nh2[i]), C, N, C, ptr(nm["nw"]), 1e-6, None, 0,
+                 ptr(nodes), C3, ptr(ws.node_in[i + 1]), C3, s)
+        # energy head on the node mean
+        call("atom_col_mean", ptr(ws.node_in[self.NL]), C3, N, C, 1.0 / N, ptr(ws.mean), s)
+        self._gemm(ws.mean, C, 1, self.head0, ws.hh, self.hh, Cpre=ws.hhp, act=1, s=s)
+        self._gemm(ws.hh, self.hh, 1, self.head1, ws.energy, 1, s=s)
+        if forces:
+            self._backward(ws, virial, s)
+
+    # --------------------------------------------------------------------------- reverse
+    def _mlpnorm_bwd(self, m, h2, gY, M, a0, a1, tmp0, tmp1, g_a0, s):
+        """gY: adjoint of the normalised output [M, C] (overwritten with the h2 adjoint);
+        returns the first layer's pre-activation adjoint in g_a0 [M, Hd]."""
+        C, Hd = self.C, self.Hd
+        call("atom_rmsnorm_rows_bwd", ptr(h2), ptr(gY), M, C, ptr(m["nw"]), 1e-6, ptr(gY), s)
+        self._gemm(gY, C, M, m["b2"], tmp1, Hd, s=s)
+        call("atom_silu_bwd", ptr(tmp1), ptr(a1), M * Hd, ptr(tmp1), s)
+        self._gemm(tmp1, Hd, M, m["b1"], tmp0, Hd, s=s)
+        call("atom_silu_bwd", ptr(tmp0), ptr(a0), M * Hd, ptr(g_a0), s)
+
+    def _backward(self, ws, virial, s):
+        g = ws.graph
+        N, E, C, Hd = g.N, g.E, self.C, self.Hd
+        ws.g_cut.zero_()
+        # head: dE/dmean, broadcast / N to every node
+        call("atom_silu_bwd", ptr(self.head1_row), ptr(ws.hhp), self.hh, ptr(ws.ghh), s)
+        self._gemm(ws.ghh, self.hh, 1, self.head0_bw, ws.gmean, C, s=s)
+        call("atom_row_broadcast", ptr(ws.gmean), N, C, 1.0 / N, ptr(ws.gN), C, 0, s)
+        ws.gE.zero_()
+        for i in reversed(range(self.NL)):
+            lay = self.layers[i]
+            em, nm = lay["em"], lay["nm"]
+            # node MLP: its output adds to nodes -> adjoint gN
+            ws.gtmpN.copy_(ws.gN)
+            self._mlpnorm_bwd(nm, ws.nh2[i], ws.gtmpN, N, ws.na0[i], ws.na1[i], ws.nt0, ws.nt1,
+                              ws.nt0, s)
+            self._gemm(ws.nt0, Hd, N, nm["b0n"], ws.gN, C, accumulate=1, s=s)
+            self._gemm(ws.nt0, Hd, N, nm["b0agg"], ws.gagg, 2 * C, s=s)
+            # aggregates + attention gates -> g_ue, gE (+gate part), g_cut
+            call("atom_orb_messages_bwd", ptr(ws.gagg), ptr(ws.gE), ptr(ws.ue[i]),
+                 ptr(ws.lin[i]), ptr(ws.att[i]), ptr(ws.cut), ptr(g.src), ptr(g.tgt), E, C,
+                 ptr(lay["wr"]), ptr(lay["ws"]), ptr(ws.gue), ptr(ws.gE), ptr(ws.g_cut), s)
+            # edge MLP
+            self._mlpnorm_bwd(em, ws.eh2[i], ws.gue, E, ws.ea0[i], ws.ea1[i], ws.et0, ws.et1,
+                              ws.et0, s)
+            self._gemm(ws.et0, Hd, E, em["b0a"], ws.gE, C, accumulate=1, s=s)
+            call("atom_csr_sum", ptr(ws.et0), Hd, None, 0, ptr(g.recv_ptr), None, N, Hd,
+                 ptr(ws.gP), 2 * Hd, 0, s)
+            call("atom_csr_sum", ptr(ws.et0), Hd, None, 0, ptr(g.send_ptr), ptr(g.send_eid), N,
+                 Hd, ptr(ws.gP[:, Hd:]), 2 * Hd, 0, s)
+            self._gemm(ws.gP, 2 * Hd, N, em["b0sr"], ws.gN, C, accumulate=1, s=s)
+        # edge encoder -> edge-feature adjoint
+        self._mlpnorm_bwd(self.enc_e, ws.eh2[-1], ws.gE, E, ws.ea0[-1], ws.ea1[-1], ws.et0,
+                          ws.et1, ws.et0, s)
+        self._gemm(ws.et0, Hd, E, self.enc_e["b0"], ws.gfeat, 16 * self.nb, s=s)
+        call("atom_orb_edge_features_bwd", ptr(ws.pos), ptr(g.src), ptr(g.tgt), ptr(g.img),
+             ptr(g.shifts), E, self.rmax, self.nb, ptr(ws.gfeat), ptr(ws.g_cut), ptr(ws.g_ev), s)
+        call("atom_forces_virial", ptr(ws.g_ev), ptr(ws.ev), E, N, ptr(g.recv_ptr),
+             ptr(g.send_ptr), ptr(g.send_eid), ptr(ws.forces),
+             ptr(ws.virial) if virial else None, ptr(ws.vscratch), s)
+
+
+class OrbWorkspace:
+    def __init__(self, eng, graph):
+        self.graph = graph
+        dev = eng.device
+        N, E, C, Hd, NL = graph.N, graph.E, eng.C, eng.Hd, eng.NL
+        f = lambda *sh: torch.empty(*sh, device=dev, dtype=torch.float32)  # noqa: E731
+        self.pos = f(N, 3)
+        self.feat, self.cut, self.ev = f(E, 16 * eng.nb), f(E), f(E, 3)
+        self.x0 = f(N, eng.D0)
+        self._eng = eng
+        self.rebind(graph)
+        # per layer (+1 slot at the end for the encoder)
+        self.ea0 = [f(E, Hd) for _ in range(NL + 1)]
+        self.ea1 = [f(E, Hd) for _ in range(NL + 1)]
+        self.eh2 = [f(E, C) for _ in range(NL + 1)]
+        self.na0 = [f(N, Hd) for _ in range(NL + 1)]
+        self.na1 = [f(N, Hd) for _ in range(NL + 1)]
+        self.nh2 = [f(N, C) for _ in range(NL + 1)]
+        self.ue = [f(E, C) for _ in range(NL)]
+        self.lin = [f(E, 2) for _ in range(NL)]
+        self.att = [f(E, 2) for _ in range(NL)]
+        self.edges = [f(E, C) for _ in range(NL + 1)]
+        self.node_in = [f(N, 3 * C) for _ in range(NL + 1)]
+        self.et0, self.et1 = f(E, Hd), f(E, Hd)
+        self.nt0, self.nt1 = f(N, Hd), f(N, Hd)
+        self.P = f(N, 2 * Hd)
+        self.mean, self.hh, self.hhp = f(1, C), f(1, eng.hh), f(1, eng.hh)
+        self.energy = f(1)
+        self.ghh, self.gmean = f(1, eng.hh), f(1, C)
+        self.gN, self.gtmpN, self.gagg = f(N, C), f(N, C), f(N, 2 * C)
+        self.gE, self.gue, self.gP = f(E, C), f(E, C), f(N, 2 * Hd)
+        self.gfeat, self.g_cut, self.g_ev = f(E, 16 * eng.nb), f(E), f(E, 3)
+        self.forces, self.virial, self.vscratch = f(N, 3), f(3, 3), f(9 * 1024)
+
+
+    def rebind(self, graph):
+        """Point the workspace at a graph of the same sizes; recompute the node input rows
+        (the species embedding lookup)."""
+        self.graph = graph
+        eng = self._eng
+        call("atom_node_embed", ptr(graph.Z), None, ptr(eng.emb), ptr(eng.zero_row), graph.N,
+             eng.D0, ptr(self.x0), L.stream_ptr())
+
+
+class OrbCalculator(_AseCalculator):
+    """ASE calculator for Orb-v3 conservative bundles (tt_atom/orb_calculator.py:28-215):
+    energy, forces = -dE/dpos and stress from the strain virial. Energies are the raw model
+    output, denormalised on the host when the weights carry ``energy_head.normalizer`` /
+    ``energy_head.reference`` entries; the ZBL pair term is not included."""
+
+    implemented_properties = ["energy", "free_energy", "energies", "forces", "stress"]
+
+    def __init__(self, weights, cfg=None, device=None, device_id=0, precision="3xtf32",
+                 max_num_neighbors="config", **kwargs):
+        super().__init__(**kwargs)
+        if cfg is None:
+            from .weights import WeightBundle
+            b = WeightBundle.load(weights) if isinstance(weights, str) else weights
+            cfg, weights = b.config, b.weights
+        self.cfg = cfg
+        self._w = weights
+        self.device = torch.device(device) if device is not None else torch.device("cuda",
+                                                                                    device_id)
+        self.engine = OrbEngine(weights, cfg, self.device, precision)
+        self.max_nbrs = cfg.get("max_num_neighbors") if max_num_neighbors == "config" \
+            else max_num_neighbors
+        self._ws = None
+
+    def _evaluate(self, pos, Z, cell, pbc, forces=True, stress=False):
+        g = build_graph(pos, Z, self.cfg["cutoff"], cell, pbc, max_neighbors=self.max_nbrs,
+                        device=self.device)
+        if g.E == 0:
+            raise ValueError("no edges within cutoff — system too sparse for this model")
+        if self._ws is None or self._ws.graph.N != g.N or self._ws.graph.E != g.E:
+            self._ws = self.engine.workspace(g)
+        else:
+            self._ws.rebind(g)                  # same sizes: reuse the buffers
+        ws = self._ws
+        ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))
+        self.engine.run(ws, forces=forces, virial=stress)
+        E = float(ws.energy.double().cpu()[0])
+        return E, ws.forces.double().cpu(), (ws.virial.double().cpu() if stress else None)
+
+    def calculate(self, atoms=None, properties=("energy", "forces"), system_changes=all_changes):
+        super().calculate(atoms, properties, system_changes)
+        pos = np.asarray(atoms.get_positions(), np.float32)
+        Z = np.asarray(atoms.get_atomic_numbers(), np.int64)
+        pbc = np.asarray(atoms.get_pbc())
+        cell = np.asarray(atoms.get_cell(), np.float32) if pbc.any() else None
+        want_stress = cell is not None and ("stress" in properties or bool(pbc.all()))
+        E, F, V = self._evaluate(pos, Z, cell, pbc if pbc.any() else None, True, want_stress)
+        n = len(Z)
+        w = self._w
+        scale = 1.0
+        if "energy_head.normalizer.bn.running_var" in w:
+            sigma = float(w["energy_head.normalizer.bn.running_var"].double().sqrt())
+            E = (E * sigma + float(w["energy_head.normalizer.bn.running_mean"])) * n
+            E += float(w["energy_head.reference.linear.weight"].double().reshape(-1)[Z].sum())
+            scale = sigma * n
+        self.results["energy"] = self.results["free_energy"] = E
+        self.results["energies"] = np.full(n, E / n)
+        self.results["forces"] = (scale * F).numpy()
+        if V is not None:
+            self.results["stress"] = voigt_6(scale * V.numpy() / atoms_volume(atoms))
