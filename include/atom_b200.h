@@ -95,6 +95,9 @@ int atom_fused_ln_bw(const float* g, const float* x, const float* n, const float
  *   recv_cnt [N]         edges per receiver (device, written)
  *   cand_idx, cand_d     scratch of N * max_cand int32 / fp32 each (device; pass 1 writes,
  *                        pass 2 reads)
+ *   bbox_host            HOST [6] = (min xyz, max xyz) of all positions, or NULL: images
+ *                        whose shifted box lies beyond the cutoff of a receiver are skipped
+ *                        (exact; only speeds up large cells). At most 255 images.
  *   small_scratch        8 * (nsys + 2) bytes of device scratch, 8-byte aligned
  * Pass 1 (edges == NULL): fills recv_cnt, returns ATOM_ERR_CAPACITY (with the needed max_cand
  * in *need) if a receiver has more than max_cand candidates.
@@ -104,7 +107,8 @@ int atom_neighbor_list(const float* pos, int64_t N, const int64_t* sys_ptr_host,
                        const float* shifts, int nshift, float cutoff, int periodic, int max_nbrs,
                        int max_cand, int* cand_idx, float* cand_d, int* recv_cnt,
                        const int* recv_ptr, int* edge_src, int* edge_tgt, int* edge_img,
-                       void* small_scratch, int* need_host, void* stream);
+                       const float* bbox_host, void* small_scratch, int* need_host,
+                       void* stream);
 
 /* Exclusive prefix sum of n int32 counts: ptr[0] = 0, ptr[i+1] = ptr[i] + cnt[i]; also copies
  * the total to *total_host (synchronous on `stream`) when total_host is not NULL. */

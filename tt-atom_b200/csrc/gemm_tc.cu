@@ -162,7 +162,8 @@ struct Cfg {
     static constexpr uint32_t kStage = kTileA + kTileB + (MODE == 2 ? kTileA + kTileB : 0);
     static constexpr uint32_t kLoadBytes = kTileA + kTileB * (MODE == 2 ? 2 : 1);  // TMA bytes
     static constexpr int kStages = MODE == 2 ? ATOM_TC_STAGES_3X : ATOM_TC_STAGES_1X;
-    static constexpr uint32_t kSmem = kStages * kStage + 1024 + 256;
+    static constexpr uint32_t kStageOut = 4 * 32 * 33 * 4;   // per-warp 32 x 33 store tiles
+    static constexpr uint32_t kSmem = kStages * kStage + 1024 + 256 + kStageOut;
     static_assert(4 * BN <= 512, "accumulators must fit tensor memory");
     static constexpr uint32_t kTmemCols = 4 * BN;   // up to 4 accumulators of BN columns
 };
@@ -215,6 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* acce = accf + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 1);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+    float* stage_out = reinterpret_cast<float*>(smem + S * CF::kStage + 256);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -369,28 +371,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             mbar_arrive(acce);                  // tensor memory may take the next tile now
-            const long long m = ti.m0 + quarter * 32 + lane;
+            // stores: each 32 x 32 block goes through this warp's shared tile, so that a warp
+            // writes 32 consecutive columns of one row per instruction (and reads bias and
+            // table entries coalesced)
             const int N = p.g.N[ti.grp];
-            if (m >= p.M) continue;
             const float* bias = p.g.bias[ti.grp];
             const int ccol = p.g.c_col[ti.grp], tcol = p.g.t_col[ti.grp];
-            const long long row = m * p.ldc + ccol + ti.n0;
-            const float* t1 = p.T1 ? p.T1 + (long long)p.idx1[m] * p.ldt + tcol + ti.n0 : nullptr;
-            const float* t2 = p.T2 ? p.T2 + (long long)p.idx2[m] * p.ldt + tcol + ti.n0 : nullptr;
+            float* st = stage_out + (warp - 2) * 32 * 33;
+            const long long mrow0 = ti.m0 + quarter * 32;
 #pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                const int n = ti.n0 + c;
-                if (n < N) {
-                    float x = v[c];
-                    if (bias) x += bias[n];
-                    if (t1) x += t1[c];
-                    if (t2) x += t2[c];
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) st[lane * 33 + jj] = v[c0 + jj];
+                __syncwarp();
+                const int n = ti.n0 + c0 + lane;
+                const bool nok = n < N;
+                const float bn = (bias && nok) ? bias[n] : 0.f;
+                for (int r = 0; r < 32; ++r) {
+                    const long long m = mrow0 + r;
+                    if (m >= p.M) break;
+                    if (!nok) continue;
+                    float x = st[r * 33 + lane] + bn;
+                    if (p.T1) x += p.T1[(long long)p.idx1[m] * p.ldt + tcol + n];
+                    if (p.T2) x += p.T2[(long long)p.idx2[m] * p.ldt + tcol + n];
+                    const long long off = m * p.ldc + ccol + n;
                     if (p.act == 1) {
-                        if (p.Cpre) p.Cpre[row + c] = x;
+                        if (p.Cpre) p.Cpre[off] = x;
                         x = silu_f(x);
                     }
-                    p.C[row + c] = p.accumulate ? p.C[row + c] + x : x;
+                    p.C[off] = p.accumulate ? p.C[off] + x : x;
                 }
+                __syncwarp();
             }
         }
     }

@@ -37,19 +37,42 @@ __device__ __forceinline__ int find_sys(const long long* sp, int nsys, long long
 
 // Pass 1: one warp per receiver, candidates in (j, c) order tested 32 at a time; the survivors
 // are appended in order (ballot + popc) to the receiver's candidate slots.
+// Images that cannot hold a neighbour of receiver i are skipped: image c is kept only if the
+// bounding box of all positions, shifted by shift[c], comes within the cutoff of pos[i] (with
+// a relative slack far above fp32 rounding, so no pair that passes the exact test is skipped).
+// Candidates stay in (j, c) order.
+struct BBox {
+    float lo[3], hi[3];
+};
+
 __global__ void nl_collect_kernel(const float* __restrict__ pos, long long N,
                                   const long long* __restrict__ sys_ptr, int nsys,
                                   const float* __restrict__ shifts, int S, float cutoff,
                                   float cut2, int periodic, int max_nbrs, int max_cand,
-                                  int* __restrict__ cand_idx, float* __restrict__ cand_d,
-                                  int* __restrict__ recv_cnt, int* __restrict__ need) {
+                                  BBox box, int* __restrict__ cand_idx,
+                                  float* __restrict__ cand_d, int* __restrict__ recv_cnt,
+                                  int* __restrict__ need) {
     long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
     if (i >= N) return;
     int k = find_sys(sys_ptr, nsys, i);
     long long lo = sys_ptr[k], hi = sys_ptr[k + 1];
     float pix = pos[i * 3 + 0], piy = pos[i * 3 + 1], piz = pos[i * 3 + 2];
-    long long total = (hi - lo) * (long long)S;
+    // surviving images for this receiver (all lanes compute the same list)
+    unsigned char surv[256];
+    int ns = 0;
+    for (int c = 0; c < S; ++c) {
+        if (!periodic) { surv[ns++] = (unsigned char)c; continue; }
+        float d2 = 0.f;
+        const float p[3] = {pix, piy, piz};
+        for (int k = 0; k < 3; ++k) {
+            float a = box.lo[k] + shifts[c * 3 + k], b = box.hi[k] + shifts[c * 3 + k];
+            float d = p[k] < a ? a - p[k] : (p[k] > b ? p[k] - b : 0.f);
+            d2 += d * d;
+        }
+        if (d2 <= cut2 * 1.0001f + 1e-3f) surv[ns++] = (unsigned char)c;
+    }
+    long long total = (hi - lo) * (long long)ns;
     int cnt = 0;
     int* ci = cand_idx + i * (long long)max_cand;
     float* cd = cand_d + i * (long long)max_cand;
@@ -58,9 +81,11 @@ __global__ void nl_collect_kernel(const float* __restrict__ pos, long long N,
         long long t = base + lane;
         bool keep = false;
         float key = 0.f;
+        int tidx = 0;
         if (t < total) {
-            long long j = lo + t / S;
-            int c = (int)(t % S);
+            long long j = lo + t / ns;
+            int c = surv[t % ns];
+            tidx = (int)((j - lo) * S + c);
             float pjx = pos[j * 3 + 0], pjy = pos[j * 3 + 1], pjz = pos[j * 3 + 2];
             if (periodic) {
                 float qx = __fadd_rn(pjx, shifts[c * 3 + 0]);
@@ -83,7 +108,7 @@ __global__ void nl_collect_kernel(const float* __restrict__ pos, long long N,
         if (keep) {
             int slot = cnt + __popc(m & ((1u << lane) - 1u));
             if (slot < max_cand) {
-                ci[slot] = (int)t;
+                ci[slot] = tidx;
                 cd[slot] = key;
             }
         }
@@ -227,9 +252,11 @@ extern "C" int atom_neighbor_list(const float* pos, int64_t N, const int64_t* sy
                                   int periodic, int max_nbrs, int max_cand, int* cand_idx,
                                   float* cand_d, int* recv_cnt, const int* recv_ptr,
                                   int* edge_src, int* edge_tgt, int* edge_img,
-                                  void* small_scratch, int* need_host, void* stream) {
+                                  const float* bbox_host, void* small_scratch, int* need_host,
+                                  void* stream) {
     ATOM_REQUIRE(nsys >= 1 && nsys <= 1 << 20, "nsys out of range");
     ATOM_REQUIRE(nshift >= 1 && max_cand >= 1, "nshift and max_cand must be positive");
+    ATOM_REQUIRE(nshift <= 255, "at most 255 periodic images (cell too small for the cutoff)");
     ATOM_REQUIRE(sys_ptr_host[0] == 0 && sys_ptr_host[nsys] == N, "sys_ptr must span [0, N)");
     ATOM_REQUIRE(N * (long long)nshift < (1LL << 31), "N * nshift too large for this kernel");
     cudaStream_t st = (cudaStream_t)stream;
@@ -248,8 +275,13 @@ extern "C" int atom_neighbor_list(const float* pos, int64_t N, const int64_t* sy
         int* dneed = reinterpret_cast<int*>(sp + nsys + 1);
         cudaMemsetAsync(dneed, 0, sizeof(int), st);
         float cut2 = (float)((double)cutoff * (double)cutoff);
+        BBox box;
+        for (int k = 0; k < 3; ++k) {
+            box.lo[k] = bbox_host ? bbox_host[k] : -3.0e38f;
+            box.hi[k] = bbox_host ? bbox_host[3 + k] : 3.0e38f;
+        }
         nl_collect_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(
-            pos, N, sp, nsys, shifts, nshift, cutoff, cut2, periodic, max_nbrs, max_cand,
+            pos, N, sp, nsys, shifts, nshift, cutoff, cut2, periodic, max_nbrs, max_cand, box,
             cand_idx, cand_d, recv_cnt, dneed);
         ATOM_CHECK_LAUNCH("neighbor_list collect");
         int h = 0;

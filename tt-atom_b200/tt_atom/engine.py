@@ -232,8 +232,8 @@ class UMAEngine:
         call("atom_gemm", ptr(A), lda, M, groups.struct, ptr(Cout), ldc, ptr(Cpre), ptr(T1),
              ptr(T2), ptr(idx1), ptr(idx2), ldt, act, accumulate, self.precision, stream)
 
-    def workspace(self, graph, sys_emb):
-        return Workspace(self, graph, sys_emb)
+    def workspace(self, graph, sys_emb, lean=False):
+        return Workspace(self, graph, sys_emb, lean)
 
     def launches_per_step(self, ws, forces=True, virial=True):
         """Number of this library's kernels one ``run`` launches (counted, not estimated)."""
@@ -274,6 +274,15 @@ class UMAEngine:
     def run(self, ws, pos, forces=True, virial=False, stream=None):
         """One E (+F, +virial) evaluation for ``pos`` [N, 3] (device fp32) on ``ws``'s graph.
         Results land in ``ws.energy`` [nsys], ``ws.forces`` [N, 3], ``ws.virial`` [3, 3]."""
+        for _ in self.steps(ws, pos, forces, virial, stream):
+            pass
+
+    def steps(self, ws, pos, forces=True, virial=False, stream=None):
+        """``run`` as a generator that pauses where a spatially partitioned caller must
+        exchange halo rows: ("x", i) after layer i's input features x[i] are computed (halo
+        rows must then be overwritten by their owners' values), ("gx", i) after the adjoint of
+        x[i] is complete (halo rows must be sent to and added by their owners, then zeroed),
+        and ("forces", None) after the forces (halo rows' partial forces belong to owners)."""
         s = L.stream_ptr(stream)
         g = ws.graph
         N, E = g.N, g.E
@@ -297,6 +306,7 @@ class UMAEngine:
         ede = ws.RAD[:, self.rad_off[self.NL]:]
         call("atom_edge_degree_fwd", ptr(ede), self.ldr, ptr(ws.coef), ptr(ws.env), ptr(ws.l0),
              N, C, ptr(g.recv_ptr), 5.0, ptr(ws.x[0]), s)
+        yield ("x", 0)
         # ---------------- blocks
         for i, b in enumerate(self.blocks):
             x, nb = ws.x[i], ws.nb[i]
@@ -320,6 +330,8 @@ class UMAEngine:
             ws.x[i + 1].copy_(ws.xm[i])
             call("atom_node_project", ptr(ws.h1), N, P, C, ptr(self.FG), 9, 1, 1,
                  ptr(ws.x[i + 1]), s)
+            if i + 1 < self.NL:
+                yield ("x", i + 1)
         # ---------------- final norm + energy head
         call("atom_rmsnorm_sh_fwd", ptr(ws.x[self.NL]), N, C, ptr(self.nfw), ptr(self.nfb), None,
              1e-5, ptr(ws.ne), s)
@@ -329,7 +341,7 @@ class UMAEngine:
         call("atom_segment_sum", ptr(ws.enode), N, ptr(g.sys_ptr), g.nsys, ptr(ws.energy), s)
         if not forces:
             return
-        self._backward(ws, virial, s)
+        yield from self._backward(ws, virial, s)
 
     def _backward(self, ws, virial, s):
         g = ws.graph
@@ -349,6 +361,9 @@ class UMAEngine:
         # ---------------- blocks, reversed
         for i in reversed(range(NL)):
             b = self.blocks[i]
+            if ws.lean:       # the rotated inputs were not kept: recompute them
+                call("atom_rotate_in", ptr(ws.nb[i]), ptr(g.src), ptr(g.tgt), ptr(ws.coef), E,
+                     C, ptr(ws.RAD), self.ldr, self.rad_off[i], ptr(ws.rot[i]), ptr(ws.A1), s)
             # atomwise (grid) VJP
             call("atom_node_project", ptr(ws.gx), N, 9, C, ptr(self.FG), P, 0, 0, ptr(ws.h1), s)
             self._gemm(ws.h1, C, N * P, b["gc_bw"], ws.h2, C, stream=s)
@@ -372,6 +387,7 @@ class UMAEngine:
                  ptr(g.send_ptr), ptr(g.send_eid), 0, ptr(ws.gn), s)
             call("atom_rmsnorm_sh_bwd", ptr(ws.x[i]), ptr(ws.gn), N, C, ptr(b["n1w"]), 1e-5, 1,
                  ptr(ws.gx), s)
+            yield ("gx", i)
         # ---------------- edge-degree VJP (gx = dE/dx_init)
         ede_off = self.rad_off[NL]
         call("atom_edge_degree_bwd", ptr(ws.gx), ptr(g.tgt), ptr(ws.RAD[:, ede_off:]), self.ldr,
@@ -393,12 +409,13 @@ class UMAEngine:
         call("atom_forces_virial", ptr(ws.g_ev), ptr(ws.ev), E, N, ptr(g.recv_ptr),
              ptr(g.send_ptr), ptr(g.send_eid), ptr(ws.forces),
              ptr(ws.virial) if virial else None, ptr(ws.vscratch), s)
+        yield ("forces", None)
 
 
 class Workspace:
     """Every device buffer of one step for one graph topology."""
 
-    def __init__(self, eng, graph, sys_emb):
+    def __init__(self, eng, graph, sys_emb, lean=False):
         self.graph = graph
         dev = eng.device
         N, E = graph.N, graph.E
@@ -412,7 +429,10 @@ class Workspace:
         self.x = [f(N, 9, C) for _ in range(NL + 1)]
         self.nb = [f(N, 9, C) for _ in range(NL)]
         self.xm = [f(N, 9, C) for _ in range(NL)]
-        self.rot = [f(E, 18 * C) for _ in range(NL)]
+        # lean: one rotated-input buffer, recomputed in the reverse pass (-18 C floats per edge
+        # per layer); otherwise one per layer
+        self.lean = lean
+        self.rot = [f(E, 18 * C)] * NL if lean else [f(E, 18 * C) for _ in range(NL)]
         self.Y1 = [f(E, 11 * H) for _ in range(NL)]
         self.Y2 = [f(E, 9 * C) for _ in range(NL)]
         self.G0 = f(N * P, C)
@@ -454,12 +474,12 @@ class Workspace:
              eng_C, ptr(self.l0), s)
 
     def nbytes(self):
-        tot = 0
+        seen, tot = set(), 0
         for v in self.__dict__.values():
-            if torch.is_tensor(v):
-                tot += v.numel() * v.element_size()
-            elif isinstance(v, list):
-                tot += sum(t.numel() * t.element_size() for t in v if torch.is_tensor(t))
+            for t in (v if isinstance(v, list) else [v]):
+                if torch.is_tensor(t) and t.data_ptr() not in seen:
+                    seen.add(t.data_ptr())
+                    tot += t.numel() * t.element_size()
         return tot
 
 

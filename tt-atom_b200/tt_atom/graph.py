@@ -117,13 +117,16 @@ def build_graph(pos, Z, cutoff, cell=None, pbc=None, max_neighbors=None, sys_ptr
     small = torch.empty(nsys + 2, dtype=torch.int64, device=dev)
     sp_host = L.host_i64(sys_ptr)
     need = ctypes.c_int(0)
+    pos_np = pos.detach().cpu().numpy() if periodic else None
+    bbox = (L.host_f32(list(pos_np.min(0)) + list(pos_np.max(0)))
+            if periodic and N > 0 else None)
     while True:
         cand_idx = torch.empty(max(N * max_cand, 1), dtype=torch.int32, device=dev)
         cand_d = torch.empty(max(N * max_cand, 1), dtype=torch.float32, device=dev)
         rc = L.lib().atom_neighbor_list(ptr(pos), N, sp_host, nsys, ptr(shifts), S, float(cutoff),
                                         int(periodic), cap, max_cand, ptr(cand_idx), ptr(cand_d),
-                                        ptr(recv_cnt), None, None, None, None, ptr(small),
-                                        ctypes.byref(need), s)
+                                        ptr(recv_cnt), None, None, None, None, bbox,
+                                        ptr(small), ctypes.byref(need), s)
         if rc == L.ATOM_ERR_CAPACITY:
             max_cand = int(need.value * 1.25) + 32
             continue
@@ -139,7 +142,7 @@ def build_graph(pos, Z, cutoff, cell=None, pbc=None, max_neighbors=None, sys_ptr
     img = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
     call("atom_neighbor_list", ptr(pos), N, sp_host, nsys, ptr(shifts), S, float(cutoff),
          int(periodic), cap, max_cand, ptr(cand_idx), ptr(cand_d), ptr(recv_cnt), ptr(recv_ptr),
-         ptr(src), ptr(tgt), ptr(img), ptr(small), None, s)
+         ptr(src), ptr(tgt), ptr(img), bbox, ptr(small), None, s)
     src, tgt, img = src[:E], tgt[:E], img[:E]
     send_ptr = torch.empty(N + 1, dtype=torch.int32, device=dev)
     send_eid = torch.empty(max(E, 1), dtype=torch.int32, device=dev)

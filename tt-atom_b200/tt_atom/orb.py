@@ -274,6 +274,10 @@ class OrbWorkspace:
         self.forces, self.virial, self.vscratch = f(N, 3), f(3, 3), f(9 * 1024)
 
 
+    def nbytes(self):
+        from .engine import Workspace
+        return Workspace.nbytes(self)
+
     def rebind(self, graph):
         """Point the workspace at a graph of the same sizes; recompute the node input rows
         (the species embedding lookup)."""
