@@ -448,7 +448,7 @@ class Workspace:
         self.g_coef, self.g_env, self.g_gauss, self.g_ev = f(E, 35), f(E), f(E, NB), f(E, 3)
         self.gx, self.gn, self.gne = f(N, 9, C), f(N, 9, C), f(N, 9, C)
         self.ge1, self.ge2 = f(N, H), f(N, H)
-        self.eh4_rows = eng.eh4_row.reshape(1, H).expand(N, H).contiguous()
+        self.eh4_rows = f(N, H)
         self.forces, self.virial, self.vscratch = f(N, 3), f(3, 3), f(9 * 1024)
         self.sysn, self.l0 = f(N, C), f(N, C)
         self._zero_sphere = torch.zeros_like(eng.sphere)
@@ -466,6 +466,11 @@ class Workspace:
         assert graph.N == self.pos.shape[0]
         self.graph = graph
         eng, N, eng_C = self._eng, graph.N, self._eng.C
+        # energy seed: dE/d(node energy) = 1 for the atoms the energy counts (rows past the
+        # last segment are a partition's halo copies and get 0)
+        n_count = graph.sys_ptr_host[-1]
+        self.eh4_rows[:n_count] = eng.eh4_row.reshape(1, -1)
+        self.eh4_rows[n_count:] = 0
         se = sys_emb.to(eng.device, torch.float32).contiguous()    # [nsys, C]
         s = L.stream_ptr()
         call("atom_node_embed", ptr(graph.Z), ptr(graph.sys_id), ptr(self._zero_sphere), ptr(se),
