@@ -138,7 +138,7 @@ def run_slab(args):
     del g
     eng = UMAEngine(b.weights, cfg, b.tables(), device=device, precision=args.precision)
     se = csd_embedding(b.weights, [0.0], [0.0], cfg["sphere_channels"])
-    ws = eng.workspace(lg, se, lean=True)
+    ws = eng.workspace(lg, se)
     ws.pos.copy_(pos[plan.global_ids.to(device)])
     exch = DistExchange(plan)
     red = torch.zeros(10, device=device, dtype=torch.float64)

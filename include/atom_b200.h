@@ -284,6 +284,15 @@ int atom_rmsnorm_sh_bwd(const float* x, const float* gout, int64_t N, int C,
 int atom_node_project(const float* in, int64_t N, int P, int C, const float* M, int Q,
                       int trans, int accumulate, float* out, void* stream);
 
+/* Spectral feed-forward gate (tt_atom/spectral.py:168-188), natural (l, m) order, lmax = 2:
+ * out[n, 0] = silu(h[n, 0]), out[n, j] = h[n, j] * sigmoid(gat[n, (l(j)-1) H : l(j) H]) for
+ * j >= 1; h, out [N, 9, H], gat [N, 2H] the post-SiLU scalar gating. */
+int atom_spectral_gate_fwd(const float* h, const float* gat, int64_t N, int H, float* out,
+                           void* stream);
+/* VJP (tt_atom/forces.py:307-346): g_h [N, 9, H] and g_gat [N, 2H] from g_out [N, 9, H]. */
+int atom_spectral_gate_bwd(const float* h, const float* gat, const float* g_out, int64_t N,
+                           int H, float* g_h, float* g_gat, void* stream);
+
 /* Elementwise: out = g * silu'(pre) (n values). */
 int atom_silu_bwd(const float* g, const float* pre, int64_t n, float* out, void* stream);
 

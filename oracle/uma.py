@@ -334,6 +334,25 @@ def grid_ff(x, w, p, to_grid, from_grid):
     return torch.einsum("pi,npc->nic", fg, g)
 
 
+def spectral_ff(x, w, p, lmax):
+    """Spectral feed-forward (tt_atom/spectral.py:168-188, fairchem SpectralAtomwise): gating =
+    SiLU(scalar MLP on l = 0); per-degree SO3 linear (one weight per l, bias on l = 0); SiLU on
+    l = 0 and sigmoid(gating[degree]) on l >= 1; second SO3 linear."""
+    N, nsph, _ = x.shape
+    lc = torch.tensor(_l_of(lmax))
+    gating = F.silu(F.linear(x[:, 0], w[f"{p}.scalar_mlp.0.weight"], w[f"{p}.scalar_mlp.0.bias"]))
+    W1, b1 = w[f"{p}.so3_linear_1.weight"], w[f"{p}.so3_linear_1.bias"]
+    h = torch.einsum("nic,ihc->nih", x, W1[lc])
+    h = torch.cat([h[:, :1] + b1, h[:, 1:]], 1)
+    H = h.shape[2]
+    sg = torch.sigmoid(gating).view(N, lmax, H)
+    g = torch.cat([F.silu(h[:, :1])] + [h[:, l * l:(l + 1) ** 2] * sg[:, l - 1:l]
+                                         for l in range(1, lmax + 1)], 1)
+    W2, b2 = w[f"{p}.so3_linear_2.weight"], w[f"{p}.so3_linear_2.bias"]
+    out = torch.einsum("nih,ich->nic", g, W2[lc])
+    return torch.cat([out[:, :1] + b2, out[:, 1:]], 1)
+
+
 def edgewise(x, w, p, cfg, wig, x_edge, env, edge_index, N):
     """Edgewise message block (tests/mirror.py:95-109)."""
     C, H, lmax, mmax = cfg["sphere_channels"], cfg["hidden_channels"], cfg["lmax"], cfg["mmax"]
@@ -357,7 +376,10 @@ def backbone(w, cfg, tables, x_init, wig, x_edge, env, sys_emb, edge_index):
         n = torch.cat([n[:, :1, :] + sys_emb[:, None, :], n[:, 1:, :]], 1)
         x = edgewise(n, w, f"{p}.edge_wise", cfg, wig, x_edge, env, edge_index, N) + x
         n = rms_norm_sh(x, w, f"{p}.norm_2", lmax)
-        x = grid_ff(n, w, f"{p}.atom_wise", tables["to_grid_mat"], tables["from_grid_mat"]) + x
+        if cfg.get("ff_type", "grid") == "spectral":
+            x = spectral_ff(n, w, f"{p}.atom_wise", lmax) + x
+        else:
+            x = grid_ff(n, w, f"{p}.atom_wise", tables["to_grid_mat"], tables["from_grid_mat"]) + x
     return rms_norm_sh(x, w, "norm", lmax)
 
 

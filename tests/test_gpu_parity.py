@@ -133,9 +133,12 @@ def _tables(cfg):
 
 
 @pytest.mark.parametrize("precision", PRECISIONS)
-@pytest.mark.parametrize("shape,sysname", [("tiny", "tiny"), ("uma-s-1", "fcc-small")])
-def test_configs_vs_oracle(shape, sysname, precision):
-    cfg = configs.model_config(shape)
+@pytest.mark.parametrize("shape,sysname,ff", [("tiny", "tiny", "grid"),
+                                              ("uma-s-1", "fcc-small", "grid"),
+                                              ("tiny", "tiny", "spectral"),
+                                              ("uma-s-1", "fcc-small", "spectral")])
+def test_configs_vs_oracle(shape, sysname, ff, precision):
+    cfg = configs.model_config(shape, ff_type=ff)
     arrs = configs.random_bundle_arrays(cfg, seed=0)
     b = WeightBundle.from_arrays(arrs)
     s = configs.system(sysname)

@@ -13,8 +13,8 @@ from tt_atom.weights import WeightBundle
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("shape,nparts,lean", [("tiny", 3, False), ("uma-s-1", 2, True)])
-def test_slab_lockstep_matches_single(shape, nparts, lean):
+@pytest.mark.parametrize("shape,nparts", [("tiny", 3), ("uma-s-1", 2)])
+def test_slab_lockstep_matches_single(shape, nparts):
     cfg = configs.model_config(shape)
     b = WeightBundle.from_arrays(configs.random_bundle_arrays(cfg, seed=0))
     s = configs.fcc_alloy(reps=(6, 3, 3), seed=3)          # 21.3 A along x: slabs >= 7.1 A
@@ -31,7 +31,7 @@ def test_slab_lockstep_matches_single(shape, nparts, lean):
     plans = plans_for(g, ranges)
     wss = []
     for p in plans:
-        ws = eng.workspace(local_graph(g, p), se, lean=lean)
+        ws = eng.workspace(local_graph(g, p), se)
         ws.pos.copy_(pos[p.global_ids.cuda()])       # owned atoms, then halo atoms
         wss.append(ws)
     run_lockstep(eng, wss, LockstepGroup(plans))

@@ -46,6 +46,43 @@ __device__ __forceinline__ float4 wrow(const float* w, const float4* v) {
     return acc;
 }
 
+// Reduce-scatter across a warp: on return, lane l's v[0] holds the warp-wide sum of v[l]
+// (31 shuffles for 32 sums instead of 32 x 5). v[] is clobbered.
+__device__ __forceinline__ float warp_reduce_scatter32(float* v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) {
+        const bool upper = (lane & s) != 0;
+#pragma unroll
+        for (int i = 0; i < s; ++i) {
+            float send = upper ? v[i] : v[i + s];
+            float keep = upper ? v[i + s] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+        }
+    }
+    return v[0];
+}
+
+// Sums over the warp of pc[0..34] written by lane 0..34 mapping: lanes 0-31 own entries 0-31,
+// entries 32..34 are reduced with plain butterflies; returns lane-owned total for entry `lane`
+// (and fills tail[3] on every lane).
+__device__ __forceinline__ float warp_sum35(float* pc, float* tail) {
+    tail[0] = warp_sum(pc[32]);
+    tail[1] = warp_sum(pc[33]);
+    tail[2] = warp_sum(pc[34]);
+    return warp_reduce_scatter32(pc);
+}
+
+// wrow<R> for a row index known only after unrolling
+__device__ __forceinline__ float4 wrow_rt(const float* w, const float4* v, int r) {
+    const int l = row_deg(r), o = row_off(r), c0 = deg_col0(l);
+    float4 acc = f4(0.f);
+#pragma unroll
+    for (int jj = 0; jj < 5; ++jj)
+        if (jj < 2 * l + 1) fma4(acc, w[o + jj], v[c0 + jj]);
+    return acc;
+}
+
 __device__ __forceinline__ void load_coef(const float* __restrict__ coef, long long e, float* w) {
 #pragma unroll
     for (int k = 0; k < kNnz; ++k) w[k] = __ldg(coef + e * kNnz + k);
@@ -67,36 +104,22 @@ __global__ void __launch_bounds__(256) rotate_in_kernel(
     float* rowA = A + e * kNsph * W2;
     float* rowR = rot ? rot + e * kNsph * W2 : nullptr;
     const float* rr = rad ? rad + e * ldr + rad_col : nullptr;
-    for (int c = lane * 4; c < C; c += 128) {
-        float4 vs[kNsph], vt[kNsph];
+    // source-channel half, then target-channel half of every row
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+        const float* xh = half ? xt : xs;
+        const int ho = half * C;
+        for (int c = lane * 4; c < C; c += 128) {
+            float4 v[kNsph];
 #pragma unroll
-        for (int j = 0; j < kNsph; ++j) {
-            vs[j] = ld4(xs + j * C + c);
-            vt[j] = ld4(xt + j * C + c);
-        }
-        float4 os[kNsph], ot[kNsph];
-        os[0] = wrow<0>(w, vs); ot[0] = wrow<0>(w, vt);
-        os[1] = wrow<1>(w, vs); ot[1] = wrow<1>(w, vt);
-        os[2] = wrow<2>(w, vs); ot[2] = wrow<2>(w, vt);
-        os[3] = wrow<3>(w, vs); ot[3] = wrow<3>(w, vt);
-        os[4] = wrow<4>(w, vs); ot[4] = wrow<4>(w, vt);
-        os[5] = wrow<5>(w, vs); ot[5] = wrow<5>(w, vt);
-        os[6] = wrow<6>(w, vs); ot[6] = wrow<6>(w, vt);
-        os[7] = wrow<7>(w, vs); ot[7] = wrow<7>(w, vt);
-        os[8] = wrow<8>(w, vs); ot[8] = wrow<8>(w, vt);
+            for (int j = 0; j < kNsph; ++j) v[j] = ld4(xh + j * C + c);
 #pragma unroll
-        for (int r = 0; r < kNsph; ++r) {
-            if (rowR) {
-                st4(rowR + r * W2 + c, os[r]);
-                st4(rowR + r * W2 + C + c, ot[r]);
+            for (int r = 0; r < kNsph; ++r) {
+                float4 o = wrow_rt(w, v, r);
+                if (rowR) st4(rowR + r * W2 + ho + c, o);
+                if (rr) o = mul4(o, ld4(rr + rad_slice(r) * W2 + ho + c));
+                st4(rowA + r * W2 + ho + c, o);
             }
-            float4 a = os[r], b = ot[r];
-            if (rr) {
-                a = mul4(a, ld4(rr + rad_slice(r) * W2 + c));
-                b = mul4(b, ld4(rr + rad_slice(r) * W2 + C + c));
-            }
-            st4(rowA + r * W2 + c, a);
-            st4(rowA + r * W2 + C + c, b);
         }
     }
 }
@@ -241,13 +264,11 @@ __global__ void __launch_bounds__(256) rotate_back_bwd_kernel(
         }
     }
     penv = warp_sum(penv);
-#pragma unroll
-    for (int k = 0; k < kNnz; ++k) pc[k] = warp_sum(pc[k]);
-    if (lane == 0) {
-        g_env[e] += penv;
-#pragma unroll
-        for (int k = 0; k < kNnz; ++k) g_coef[e * kNnz + k] += s * pc[k];
-    }
+    float tail[3];
+    const float mine = warp_sum35(pc, tail);
+    g_coef[e * kNnz + lane] += s * mine;
+    if (lane < 3) g_coef[e * kNnz + 32 + lane] += s * tail[lane];
+    if (lane == 0) g_env[e] += penv;
 }
 
 // ------------------------------------------------------------ rotate-in VJP (edge part)
@@ -260,8 +281,9 @@ __global__ void __launch_bounds__(256) rotate_in_bwd_edge_kernel(
     int lane = threadIdx.x & 31;
     if (e >= E) return;
     const int W2 = 2 * C;
+    float w[kNnz];
+    load_coef(coef, e, w);
     const float* ga = gA + e * kNsph * W2;
-    const float* ro = rot + e * kNsph * W2;
     const float* rr = rad + e * ldr + rad_col;
     float* gr = g_rot + e * kNsph * W2;
     float* grd = g_rad + e * ldr + rad_col;
@@ -270,46 +292,41 @@ __global__ void __launch_bounds__(256) rotate_in_bwd_edge_kernel(
     float pc[kNnz];
 #pragma unroll
     for (int k = 0; k < kNnz; ++k) pc[k] = 0.f;
-    for (int c = lane * 4; c < C; c += 128) {
-        float4 vs[kNsph], vt[kNsph];
+    // the source-channel half and the target-channel half of every row, one after the other
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+        const float* xh = half ? xt : xs;
+        const int ho = half * C;
+        for (int c = lane * 4; c < C; c += 128) {
+            float4 v[kNsph];
 #pragma unroll
-        for (int j = 0; j < kNsph; ++j) {
-            vs[j] = ld4(xs + j * C + c);
-            vt[j] = ld4(xt + j * C + c);
-        }
-        // the two halves (source channels, target channels) of every row
-        float4 gsl[6], gtl[6];   // radial-slice adjoints
+            for (int j = 0; j < kNsph; ++j) v[j] = ld4(xh + j * C + c);
+            float4 gsl[6];   // radial-slice adjoints
 #pragma unroll
-        for (int q = 0; q < 6; ++q) gsl[q] = gtl[q] = f4(0.f);
+            for (int q = 0; q < 6; ++q) gsl[q] = f4(0.f);
 #pragma unroll
-        for (int r = 0; r < kNsph; ++r) {
-            const int q = rad_slice(r);
-            float4 gas = ld4(ga + r * W2 + c), gat = ld4(ga + r * W2 + C + c);
-            float4 ms = ld4(rr + q * W2 + c), mt = ld4(rr + q * W2 + C + c);
-            float4 rs = ld4(ro + r * W2 + c), rt = ld4(ro + r * W2 + C + c);
-            float4 gs = mul4(gas, ms), gt = mul4(gat, mt);
-            st4(gr + r * W2 + c, gs);
-            st4(gr + r * W2 + C + c, gt);
-            float4 ps = mul4(gas, rs), pt = mul4(gat, rt);
-            gsl[q].x += ps.x; gsl[q].y += ps.y; gsl[q].z += ps.z; gsl[q].w += ps.w;
-            gtl[q].x += pt.x; gtl[q].y += pt.y; gtl[q].z += pt.z; gtl[q].w += pt.w;
-            const int l = row_deg(r), o = row_off(r), c0 = deg_col0(l);
+            for (int r = 0; r < kNsph; ++r) {
+                const int q = rad_slice(r);
+                float4 gav = ld4(ga + r * W2 + ho + c);
+                float4 g = mul4(gav, ld4(rr + q * W2 + ho + c));
+                st4(gr + r * W2 + ho + c, g);
+                // the rotated input of this row (before the radial multiplier): stored, or
+                // recomputed from the node rows already in registers
+                float4 rv = rot ? ld4(rot + e * kNsph * W2 + r * W2 + ho + c) : wrow_rt(w, v, r);
+                float4 p = mul4(gav, rv);
+                gsl[q].x += p.x; gsl[q].y += p.y; gsl[q].z += p.z; gsl[q].w += p.w;
+                const int l = row_deg(r), o = row_off(r), c0 = deg_col0(l);
 #pragma unroll
-            for (int jj = 0; jj < 2 * l + 1; ++jj)
-                pc[o + jj] += dot4(gs, vs[c0 + jj]) + dot4(gt, vt[c0 + jj]);
-        }
+                for (int jj = 0; jj < 2 * l + 1; ++jj) pc[o + jj] += dot4(g, v[c0 + jj]);
+            }
 #pragma unroll
-        for (int q = 0; q < 6; ++q) {
-            st4(grd + q * W2 + c, gsl[q]);
-            st4(grd + q * W2 + C + c, gtl[q]);
+            for (int q = 0; q < 6; ++q) st4(grd + q * W2 + ho + c, gsl[q]);
         }
     }
-#pragma unroll
-    for (int k = 0; k < kNnz; ++k) pc[k] = warp_sum(pc[k]);
-    if (lane == 0) {
-#pragma unroll
-        for (int k = 0; k < kNnz; ++k) g_coef[e * kNnz + k] += pc[k];
-    }
+    float tail[3];
+    const float mine = warp_sum35(pc, tail);
+    g_coef[e * kNnz + lane] += mine;
+    if (lane < 3) g_coef[e * kNnz + 32 + lane] += tail[lane];
 }
 
 // acc[j] += sum over rows r of degree l(j) of W[r][j - l^2] * g[r]   (Wig^T g)
@@ -330,26 +347,38 @@ __global__ void __launch_bounds__(256) rotate_in_bwd_node_kernel(
         float4 acc[kNsph];
 #pragma unroll
         for (int j = 0; j < kNsph; ++j) acc[j] = accumulate ? ld4(gx + (n * kNsph + j) * C + c) : f4(0.f);
-        // this node as receiver: target half of the rotated rows
-        for (int e = recv_ptr[n]; e < recv_ptr[n + 1]; ++e) {
-            float w[kNnz];
-            load_coef(coef, e, w);
-            float4 g[kNsph];
-            const float* ge = g_rot + (long long)e * kNsph * W2 + C;
+        // this node as receiver (target half of the rotated rows), then as sender (source
+        // half); two edges are loaded per iteration to keep more loads in flight
+        const int r0 = recv_ptr[n], r1 = recv_ptr[n + 1];
+        const int s0 = send_ptr[n], s1 = send_ptr[n + 1];
+        const int nr = r1 - r0, total = nr + (s1 - s0);
+        int k = 0;
+        for (; k + 1 < total; k += 2) {
+            const int ea = k < nr ? r0 + k : send_eid[s0 + k - nr];
+            const int eb = k + 1 < nr ? r0 + k + 1 : send_eid[s0 + k + 1 - nr];
+            const float* ga = g_rot + (long long)ea * kNsph * W2 + (k < nr ? C : 0);
+            const float* gb = g_rot + (long long)eb * kNsph * W2 + (k + 1 < nr ? C : 0);
+            float wa[kNnz], wb[kNnz];
+            load_coef(coef, ea, wa);
+            load_coef(coef, eb, wb);
+            float4 g1[kNsph], g2[kNsph];
 #pragma unroll
-            for (int r = 0; r < kNsph; ++r) g[r] = ld4(ge + r * W2 + c);
-            wig_t_acc(w, g, acc);
+            for (int r = 0; r < kNsph; ++r) {
+                g1[r] = ld4(ga + r * W2 + c);
+                g2[r] = ld4(gb + r * W2 + c);
+            }
+            wig_t_acc(wa, g1, acc);
+            wig_t_acc(wb, g2, acc);
         }
-        // this node as sender: source half
-        for (int k = send_ptr[n]; k < send_ptr[n + 1]; ++k) {
-            int e = send_eid[k];
-            float w[kNnz];
-            load_coef(coef, e, w);
-            float4 g[kNsph];
-            const float* ge = g_rot + (long long)e * kNsph * W2;
+        if (k < total) {
+            const int ea = k < nr ? r0 + k : send_eid[s0 + k - nr];
+            const float* ga = g_rot + (long long)ea * kNsph * W2 + (k < nr ? C : 0);
+            float wa[kNnz];
+            load_coef(coef, ea, wa);
+            float4 g1[kNsph];
 #pragma unroll
-            for (int r = 0; r < kNsph; ++r) g[r] = ld4(ge + r * W2 + c);
-            wig_t_acc(w, g, acc);
+            for (int r = 0; r < kNsph; ++r) g1[r] = ld4(ga + r * W2 + c);
+            wig_t_acc(wa, g1, acc);
         }
 #pragma unroll
         for (int j = 0; j < kNsph; ++j) st4(gx + (n * kNsph + j) * C + c, acc[j]);

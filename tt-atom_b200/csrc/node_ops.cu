@@ -381,3 +381,74 @@ extern "C" int atom_edge_species(const int* Z, const int* src, const int* tgt, i
     ATOM_CHECK_LAUNCH("edge_species");
     return ATOM_OK;
 }
+
+// ------------------------------------------------------------ spectral feed-forward gate
+// Natural (l, m) coefficient order, lmax = 2 (tt_atom/spectral.py:168-188):
+//   out[n, 0] = silu(h[n, 0]);  out[n, j] = h[n, j] * sigmoid(gat[n, (l(j) - 1) H + c]), j >= 1,
+// where gat is the post-SiLU scalar gating [N, 2H]. One thread per (n, c).
+namespace atom {
+
+__global__ void spectral_gate_fwd_kernel(const float* __restrict__ h,
+                                         const float* __restrict__ gat, long long N, int H,
+                                         float* __restrict__ out) {
+    long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= N * H) return;
+    long long n = t / H;
+    int c = (int)(t - n * H);
+    const float* hn = h + n * 9LL * H;
+    float* on = out + n * 9LL * H;
+    float s1 = sigmoid_f(gat[n * 2 * H + c]), s2 = sigmoid_f(gat[n * 2 * H + H + c]);
+    on[c] = silu_f(hn[c]);
+#pragma unroll
+    for (int j = 1; j < 9; ++j) on[j * H + c] = hn[j * H + c] * (j < 4 ? s1 : s2);
+}
+
+// VJP: g_h [N, 9H] and g_gat [N, 2H] (adjoint of the post-SiLU gating) from g_out.
+__global__ void spectral_gate_bwd_kernel(const float* __restrict__ h,
+                                         const float* __restrict__ gat,
+                                         const float* __restrict__ g_out, long long N, int H,
+                                         float* __restrict__ g_h, float* __restrict__ g_gat) {
+    long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= N * H) return;
+    long long n = t / H;
+    int c = (int)(t - n * H);
+    const float* hn = h + n * 9LL * H;
+    const float* gn = g_out + n * 9LL * H;
+    float* ghn = g_h + n * 9LL * H;
+    float s1 = sigmoid_f(gat[n * 2 * H + c]), s2 = sigmoid_f(gat[n * 2 * H + H + c]);
+    ghn[c] = gn[c] * dsilu_f(hn[c]);
+    float a1 = 0.f, a2 = 0.f;
+#pragma unroll
+    for (int j = 1; j < 9; ++j) {
+        float g = gn[j * H + c];
+        if (j < 4) {
+            ghn[j * H + c] = g * s1;
+            a1 = fmaf(g, hn[j * H + c], a1);
+        } else {
+            ghn[j * H + c] = g * s2;
+            a2 = fmaf(g, hn[j * H + c], a2);
+        }
+    }
+    g_gat[n * 2 * H + c] = a1 * s1 * (1.f - s1);
+    g_gat[n * 2 * H + H + c] = a2 * s2 * (1.f - s2);
+}
+
+}  // namespace atom
+
+extern "C" int atom_spectral_gate_fwd(const float* h, const float* gat, int64_t N, int H,
+                                      float* out, void* stream) {
+    if (N == 0) return ATOM_OK;
+    spectral_gate_fwd_kernel<<<ceil_div(N * H, 256), 256, 0, (cudaStream_t)stream>>>(h, gat, N,
+                                                                                   H, out);
+    ATOM_CHECK_LAUNCH("spectral_gate_fwd");
+    return ATOM_OK;
+}
+
+extern "C" int atom_spectral_gate_bwd(const float* h, const float* gat, const float* g_out,
+                                      int64_t N, int H, float* g_h, float* g_gat, void* stream) {
+    if (N == 0) return ATOM_OK;
+    spectral_gate_bwd_kernel<<<ceil_div(N * H, 256), 256, 0, (cudaStream_t)stream>>>(
+        h, gat, g_out, N, H, g_h, g_gat);
+    ATOM_CHECK_LAUNCH("spectral_gate_bwd");
+    return ATOM_OK;
+}

@@ -81,6 +81,9 @@ _SIGS = {
                             c_void_p, c_void_p),
     "atom_node_project": (c_void_p, c_int64, c_int, c_int, c_void_p, c_int, c_int, c_int,
                           c_void_p, c_void_p),
+    "atom_spectral_gate_fwd": (c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p),
+    "atom_spectral_gate_bwd": (c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p,
+                               c_void_p),
     "atom_silu_bwd": (c_void_p, c_void_p, c_int64, c_void_p, c_void_p),
     "atom_segment_sum": (c_void_p, c_int64, c_void_p, c_int, c_void_p, c_void_p),
     "atom_node_embed": (c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p,

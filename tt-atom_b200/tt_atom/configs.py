@@ -36,9 +36,10 @@ MODEL_SHAPES = {
 }
 
 
-def model_config(name):
+def model_config(name, ff_type="grid"):
+    """``ff_type``: "grid" (the reference's mirror and goldens) or "spectral" (real uma-s-1)."""
     cfg = dict(MODEL_SHAPES[name])
-    cfg.update(norm_type="rms_norm_sh", act_type="gate", ff_type="grid", task="omat",
+    cfg.update(norm_type="rms_norm_sh", act_type="gate", ff_type=ff_type, task="omat",
                max_num_elements=100)
     return cfg
 
@@ -113,8 +114,16 @@ def random_weights(cfg, seed=0):
         for m in range(1, mmax + 1):
             lin(f"{p}.edge_wise.so2_conv_2.so2_m_conv.{m-1}.fc", 2 * ncoef[m] * C,
                 ncoef[m] * H, bias=False)
-        for gi in (0, 2, 4):
-            lin(f"{p}.atom_wise.grid_mlp.{gi}", C, C, bias=False)
+        if cfg.get("ff_type", "grid") == "spectral":
+            lin(f"{p}.atom_wise.scalar_mlp.0", lmax * H, C)
+            for name, fo, fi in (("so3_linear_1", H, C), ("so3_linear_2", C, H)):
+                b = 1.0 / math.sqrt(fi)
+                w[f"{p}.atom_wise.{name}.weight"] = \
+                    (torch.rand(lmax + 1, fo, fi, generator=g) * 2 - 1) * b
+                w[f"{p}.atom_wise.{name}.bias"] = (torch.rand(fo, generator=g) * 2 - 1) * b
+        else:
+            for gi in (0, 2, 4):
+                lin(f"{p}.atom_wise.grid_mlp.{gi}", C, C, bias=False)
     w["norm.affine_weight"] = 1.0 + 0.1 * torch.randn(lmax + 1, C, generator=g)
     w["norm.affine_bias"] = 0.1 * torch.randn(C, generator=g)
     lin("energy_block.0", H, C)

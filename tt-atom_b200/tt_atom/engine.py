@@ -114,8 +114,9 @@ class UMAEngine:
     def __init__(self, weights, cfg, tables, device="cuda", precision="fp32"):
         if cfg.get("lmax", 2) != 2 or cfg.get("mmax", 2) != 2:
             raise RuntimeError("this build implements lmax = mmax = 2 (uma-s shape) only")
-        if cfg.get("ff_type", "grid") != "grid":
-            raise RuntimeError("only the grid feed-forward is implemented")
+        self.ff = cfg.get("ff_type", "grid")
+        if self.ff not in ("grid", "spectral"):
+            raise RuntimeError(f"feed-forward type {self.ff!r} is not implemented")
         L.lib()
         self.device = torch.device(device)
         self.cfg = dict(cfg)
@@ -195,23 +196,19 @@ class UMAEngine:
             f2_, b2_ = _so2_blocks(d(w[f"{e2}.fc_m0.weight"]), d(w[f"{e2}.fc_m0.bias"]),
                                    [d(w[f"{e2}.so2_m_conv.{m}.fc.weight"]) for m in range(2)],
                                    H, C, 0)
-            self.blocks.append(dict(
+            blk = dict(
                 n1w=d(w[f"{p}.norm_1.affine_weight"]), n1b=d(w[f"{p}.norm_1.affine_bias"]),
                 n2w=d(w[f"{p}.norm_2.affine_weight"]), n2b=d(w[f"{p}.norm_2.affine_bias"]),
-                so2_1=_Groups(f1), so2_1_bw=_Groups(b1), so2_2=_Groups(f2_), so2_2_bw=_Groups(b2_),
-                ga=_Groups([dict(a_col=0, K=C, c_col=0, N=C,
-                                 B=d(w[f"{p}.atom_wise.grid_mlp.0.weight"].t()))]),
-                gb=_Groups([dict(a_col=0, K=C, c_col=0, N=C,
-                                 B=d(w[f"{p}.atom_wise.grid_mlp.2.weight"].t()))]),
-                gc=_Groups([dict(a_col=0, K=C, c_col=0, N=C,
-                                 B=d(w[f"{p}.atom_wise.grid_mlp.4.weight"].t()))]),
-                ga_bw=_Groups([dict(a_col=0, K=C, c_col=0, N=C,
-                                    B=d(w[f"{p}.atom_wise.grid_mlp.0.weight"]))]),
-                gb_bw=_Groups([dict(a_col=0, K=C, c_col=0, N=C,
-                                    B=d(w[f"{p}.atom_wise.grid_mlp.2.weight"]))]),
-                gc_bw=_Groups([dict(a_col=0, K=C, c_col=0, N=C,
-                                    B=d(w[f"{p}.atom_wise.grid_mlp.4.weight"]))]),
-            ))
+                so2_1=_Groups(f1), so2_1_bw=_Groups(b1), so2_2=_Groups(f2_), so2_2_bw=_Groups(b2_))
+            a = f"{p}.atom_wise"
+            if self.ff == "grid":
+                for key, gi in (("ga", 0), ("gb", 2), ("gc", 4)):
+                    W = w[f"{a}.grid_mlp.{gi}.weight"]
+                    blk[key] = _Groups([dict(a_col=0, K=C, c_col=0, N=C, B=d(W.t()))])
+                    blk[key + "_bw"] = _Groups([dict(a_col=0, K=C, c_col=0, N=C, B=d(W))])
+            else:
+                blk.update(self._spectral_weights(w, a, d))
+            self.blocks.append(blk)
         self.nfw, self.nfb = d(w["norm.affine_weight"]), d(w["norm.affine_bias"])
         E0, E2, E4 = w["energy_block.0.weight"], w["energy_block.2.weight"], w["energy_block.4.weight"]
         self.eh0 = _Groups([dict(a_col=0, K=C, c_col=0, N=H, B=d(E0.t()),
@@ -226,14 +223,39 @@ class UMAEngine:
         self.sphere = d(w["sphere_embedding.weight"])
         self._w_host = w
 
+    def _spectral_weights(self, w, a, d):
+        """Grouped-GEMM weights of one spectral feed-forward (tt_atom/spectral.py:41-188): the
+        scalar MLP on l = 0 and the two SO3 linears as one group per coefficient (weight of the
+        coefficient's degree, bias on coefficient 0), split into launches of at most 8 groups."""
+        C, H = self.C, self.H
+        lc = [0, 1, 1, 1, 2, 2, 2, 2, 2]
+        Ws, bs = w[f"{a}.scalar_mlp.0.weight"], w[f"{a}.scalar_mlp.0.bias"]
+        W1, b1 = w[f"{a}.so3_linear_1.weight"], w[f"{a}.so3_linear_1.bias"]
+        W2, b2 = w[f"{a}.so3_linear_2.weight"], w[f"{a}.so3_linear_2.bias"]
+        bias1, bias2 = d(b1), d(b2)
+
+        def split(gs):
+            return [_Groups(gs[:5]), _Groups(gs[5:])]
+        return dict(
+            sm=_Groups([dict(a_col=0, K=C, c_col=0, N=Ws.shape[0], B=d(Ws.t()), bias=d(bs))]),
+            sm_bw=_Groups([dict(a_col=0, K=Ws.shape[0], c_col=0, N=C, B=d(Ws))]),
+            so3_1=split([dict(a_col=c * C, K=C, c_col=c * H, N=H, B=d(W1[lc[c]].t()),
+                              bias=bias1 if c == 0 else None) for c in range(9)]),
+            so3_1_bw=split([dict(a_col=c * H, K=H, c_col=c * C, N=C, B=d(W1[lc[c]]))
+                            for c in range(9)]),
+            so3_2=split([dict(a_col=c * H, K=H, c_col=c * C, N=C, B=d(W2[lc[c]].t()),
+                              bias=bias2 if c == 0 else None) for c in range(9)]),
+            so3_2_bw=split([dict(a_col=c * C, K=C, c_col=c * H, N=H, B=d(W2[lc[c]]))
+                            for c in range(9)]))
+
     # ------------------------------------------------------------------------------ helpers
     def _gemm(self, A, lda, M, groups, Cout, ldc, *, Cpre=None, T1=None, T2=None, idx1=None,
               idx2=None, ldt=0, act=0, accumulate=0, stream=0):
         call("atom_gemm", ptr(A), lda, M, groups.struct, ptr(Cout), ldc, ptr(Cpre), ptr(T1),
              ptr(T2), ptr(idx1), ptr(idx2), ldt, act, accumulate, self.precision, stream)
 
-    def workspace(self, graph, sys_emb, lean=False):
-        return Workspace(self, graph, sys_emb, lean)
+    def workspace(self, graph, sys_emb):
+        return Workspace(self, graph, sys_emb)
 
     def launches_per_step(self, ws, forces=True, virial=True):
         """Number of this library's kernels one ``run`` launches (counted, not estimated)."""
@@ -313,7 +335,7 @@ class UMAEngine:
             call("atom_rmsnorm_sh_fwd", ptr(x), N, C, ptr(b["n1w"]), ptr(b["n1b"]),
                  ptr(ws.sysn), 1e-5, ptr(nb), s)
             call("atom_rotate_in", ptr(nb), ptr(g.src), ptr(g.tgt), ptr(ws.coef), E, C,
-                 ptr(ws.RAD), self.ldr, self.rad_off[i], ptr(ws.rot[i]), ptr(ws.A1), s)
+                 ptr(ws.RAD), self.ldr, self.rad_off[i], None, ptr(ws.A1), s)
             self._gemm(ws.A1, 18 * C, E, b["so2_1"], ws.Y1[i], 11 * H, stream=s)
             call("atom_gate_fwd", ptr(ws.Y1[i]), E, H, ptr(ws.Gt), s)
             self._gemm(ws.Gt, 9 * H, E, b["so2_2"], ws.Y2[i], 9 * C, stream=s)
@@ -321,15 +343,27 @@ class UMAEngine:
                  ptr(g.recv_ptr), ptr(x), ptr(ws.xm[i]), s)
             call("atom_rmsnorm_sh_fwd", ptr(ws.xm[i]), N, C, ptr(b["n2w"]), ptr(b["n2b"]), None,
                  1e-5, ptr(ws.n2), s)
-            P = self.npts
-            call("atom_node_project", ptr(ws.n2), N, 9, C, ptr(self.TG), P, 0, 0,
-                 ptr(ws.G0), s)
-            self._gemm(ws.G0, C, N * P, b["ga"], ws.h1, C, Cpre=ws.P1[i], act=1, stream=s)
-            self._gemm(ws.h1, C, N * P, b["gb"], ws.h2, C, Cpre=ws.P2[i], act=1, stream=s)
-            self._gemm(ws.h2, C, N * P, b["gc"], ws.h1, C, stream=s)
-            ws.x[i + 1].copy_(ws.xm[i])
-            call("atom_node_project", ptr(ws.h1), N, P, C, ptr(self.FG), 9, 1, 1,
-                 ptr(ws.x[i + 1]), s)
+            if self.ff == "grid":
+                P = self.npts
+                call("atom_node_project", ptr(ws.n2), N, 9, C, ptr(self.TG), P, 0, 0,
+                     ptr(ws.G0), s)
+                self._gemm(ws.G0, C, N * P, b["ga"], ws.h1, C, Cpre=ws.P1[i], act=1, stream=s)
+                self._gemm(ws.h1, C, N * P, b["gb"], ws.h2, C, Cpre=ws.P2[i], act=1, stream=s)
+                self._gemm(ws.h2, C, N * P, b["gc"], ws.h1, C, stream=s)
+                ws.x[i + 1].copy_(ws.xm[i])
+                call("atom_node_project", ptr(ws.h1), N, P, C, ptr(self.FG), 9, 1, 1,
+                     ptr(ws.x[i + 1]), s)
+            else:
+                self._gemm(ws.n2, 9 * C, N, b["sm"], ws.GAT[i], 2 * H, Cpre=ws.S1[i], act=1,
+                           stream=s)
+                for grp in b["so3_1"]:
+                    self._gemm(ws.n2, 9 * C, N, grp, ws.HS[i], 9 * H, stream=s)
+                call("atom_spectral_gate_fwd", ptr(ws.HS[i]), ptr(ws.GAT[i]), N, H,
+                     ptr(ws.sgg), s)
+                ws.x[i + 1].copy_(ws.xm[i])
+                for grp in b["so3_2"]:
+                    self._gemm(ws.sgg, 9 * H, N, grp, ws.x[i + 1], 9 * C, accumulate=1,
+                               stream=s)
             if i + 1 < self.NL:
                 yield ("x", i + 1)
         # ---------------- final norm + energy head
@@ -361,17 +395,27 @@ class UMAEngine:
         # ---------------- blocks, reversed
         for i in reversed(range(NL)):
             b = self.blocks[i]
-            if ws.lean:       # the rotated inputs were not kept: recompute them
-                call("atom_rotate_in", ptr(ws.nb[i]), ptr(g.src), ptr(g.tgt), ptr(ws.coef), E,
-                     C, ptr(ws.RAD), self.ldr, self.rad_off[i], ptr(ws.rot[i]), ptr(ws.A1), s)
-            # atomwise (grid) VJP
-            call("atom_node_project", ptr(ws.gx), N, 9, C, ptr(self.FG), P, 0, 0, ptr(ws.h1), s)
-            self._gemm(ws.h1, C, N * P, b["gc_bw"], ws.h2, C, stream=s)
-            call("atom_silu_bwd", ptr(ws.h2), ptr(ws.P2[i]), N * P * C, ptr(ws.h2), s)
-            self._gemm(ws.h2, C, N * P, b["gb_bw"], ws.h1, C, stream=s)
-            call("atom_silu_bwd", ptr(ws.h1), ptr(ws.P1[i]), N * P * C, ptr(ws.h1), s)
-            self._gemm(ws.h1, C, N * P, b["ga_bw"], ws.h2, C, stream=s)
-            call("atom_node_project", ptr(ws.h2), N, P, C, ptr(self.TG), 9, 1, 0, ptr(ws.gn), s)
+            if self.ff == "grid":
+                # atomwise (grid) VJP
+                call("atom_node_project", ptr(ws.gx), N, 9, C, ptr(self.FG), P, 0, 0,
+                     ptr(ws.h1), s)
+                self._gemm(ws.h1, C, N * P, b["gc_bw"], ws.h2, C, stream=s)
+                call("atom_silu_bwd", ptr(ws.h2), ptr(ws.P2[i]), N * P * C, ptr(ws.h2), s)
+                self._gemm(ws.h2, C, N * P, b["gb_bw"], ws.h1, C, stream=s)
+                call("atom_silu_bwd", ptr(ws.h1), ptr(ws.P1[i]), N * P * C, ptr(ws.h1), s)
+                self._gemm(ws.h1, C, N * P, b["ga_bw"], ws.h2, C, stream=s)
+                call("atom_node_project", ptr(ws.h2), N, P, C, ptr(self.TG), 9, 1, 0,
+                     ptr(ws.gn), s)
+            else:
+                # atomwise (spectral) VJP (tt_atom/forces.py:307-346)
+                for grp in b["so3_2_bw"]:
+                    self._gemm(ws.gx, 9 * C, N, grp, ws.sgg, 9 * H, stream=s)
+                call("atom_spectral_gate_bwd", ptr(ws.HS[i]), ptr(ws.GAT[i]), ptr(ws.sgg), N, H,
+                     ptr(ws.sgh), ptr(ws.sgat), s)
+                call("atom_silu_bwd", ptr(ws.sgat), ptr(ws.S1[i]), N * 2 * H, ptr(ws.sgat), s)
+                for grp in b["so3_1_bw"]:
+                    self._gemm(ws.sgh, 9 * H, N, grp, ws.gn, 9 * C, stream=s)
+                self._gemm(ws.sgat, 2 * H, N, b["sm_bw"], ws.gn, 9 * C, accumulate=1, stream=s)
             call("atom_rmsnorm_sh_bwd", ptr(ws.xm[i]), ptr(ws.gn), N, C, ptr(b["n2w"]), 1e-5, 1,
                  ptr(ws.gx), s)
             # edgewise VJP (gx now holds the adjoint of the block's mid point)
@@ -380,7 +424,8 @@ class UMAEngine:
             self._gemm(ws.gY2, 9 * C, E, b["so2_2_bw"], ws.Gt, 9 * H, stream=s)
             call("atom_gate_bwd", ptr(ws.Y1[i]), ptr(ws.Gt), E, H, ptr(ws.gY1), s)
             self._gemm(ws.gY1, 11 * H, E, b["so2_1_bw"], ws.A1, 18 * C, stream=s)
-            call("atom_rotate_in_bwd_edge", ptr(ws.A1), ptr(ws.rot[i]), ptr(ws.RAD), self.ldr,
+            # the rotated inputs are not stored: the kernel recomputes them from nb[i]
+            call("atom_rotate_in_bwd_edge", ptr(ws.A1), None, ptr(ws.RAD), self.ldr,
                  self.rad_off[i], ptr(ws.nb[i]), ptr(g.src), ptr(g.tgt), ptr(ws.coef), E, C,
                  ptr(ws.grot), ptr(ws.gRAD), ptr(ws.g_coef), s)
             call("atom_rotate_in_bwd_node", ptr(ws.grot), ptr(ws.coef), N, C, ptr(g.recv_ptr),
@@ -415,7 +460,7 @@ class UMAEngine:
 class Workspace:
     """Every device buffer of one step for one graph topology."""
 
-    def __init__(self, eng, graph, sys_emb, lean=False):
+    def __init__(self, eng, graph, sys_emb):
         self.graph = graph
         dev = eng.device
         N, E = graph.N, graph.E
@@ -429,17 +474,20 @@ class Workspace:
         self.x = [f(N, 9, C) for _ in range(NL + 1)]
         self.nb = [f(N, 9, C) for _ in range(NL)]
         self.xm = [f(N, 9, C) for _ in range(NL)]
-        # lean: one rotated-input buffer, recomputed in the reverse pass (-18 C floats per edge
-        # per layer); otherwise one per layer
-        self.lean = lean
-        self.rot = [f(E, 18 * C)] * NL if lean else [f(E, 18 * C) for _ in range(NL)]
         self.Y1 = [f(E, 11 * H) for _ in range(NL)]
         self.Y2 = [f(E, 9 * C) for _ in range(NL)]
-        self.G0 = f(N * P, C)
-        self.P1 = [f(N * P, C) for _ in range(NL)]
-        self.P2 = [f(N * P, C) for _ in range(NL)]
+        self.G0 = f(N * P, C) if eng.ff == "grid" else None
+        if eng.ff == "spectral":
+            self.S1 = [f(N, 2 * H) for _ in range(NL)]
+            self.GAT = [f(N, 2 * H) for _ in range(NL)]
+            self.HS = [f(N, 9 * H) for _ in range(NL)]
+            self.sgg, self.sgh, self.sgat = f(N, 9 * H), f(N, 9 * H), f(N, 2 * H)
+        grid = eng.ff == "grid"
+        self.P1 = [f(N * P, C) for _ in range(NL)] if grid else None
+        self.P2 = [f(N * P, C) for _ in range(NL)] if grid else None
         self.A1, self.Gt = f(E, 18 * C), f(E, 9 * H)
-        self.n2, self.h1, self.h2 = f(N, 9, C), f(N * P, C), f(N * P, C)
+        self.n2 = f(N, 9, C)
+        self.h1, self.h2 = (f(N * P, C), f(N * P, C)) if grid else (None, None)
         self.ne, self.e1, self.e1p, self.e2, self.e2p = f(N, 9, C), f(N, H), f(N, H), f(N, H), f(N, H)
         self.enode = f(N)
         self.energy = f(graph.nsys)
