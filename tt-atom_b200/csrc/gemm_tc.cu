@@ -57,6 +57,7 @@ struct Args {
     const int* idx1;
     const int* idx2;
     int act, accumulate;
+    int tma_out;         // epilogue writes C (and Cpre) with TMA stores / reduce-adds
     int nacc;            // tensor-memory accumulators the K stages are spread over (1 or 4)
     Groups g;
 };
@@ -107,6 +108,24 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
+}
+
+// TMA store (or fp32 reduce-add) of one 32 x 32 box from shared memory, bulk-group completion.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y,
+                                             bool add) {
+    if (add)
+        asm volatile(
+            "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group"
+            " [%0, {%1, %2}], [%3];" ::"l"(reinterpret_cast<uint64_t>(map)),
+            "r"(x), "r"(y), "r"(smem_u32(src))
+            : "memory");
+    else
+        asm volatile(
+            "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                reinterpret_cast<uint64_t>(map)),
+            "r"(x), "r"(y), "r"(smem_u32(src))
+            : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 bytes apart.
@@ -162,8 +181,12 @@ struct Cfg {
     static constexpr uint32_t kStage = kTileA + kTileB + (MODE == 2 ? kTileA + kTileB : 0);
     static constexpr uint32_t kLoadBytes = kTileA + kTileB * (MODE == 2 ? 2 : 1);  // TMA bytes
     static constexpr int kStages = MODE == 2 ? ATOM_TC_STAGES_3X : ATOM_TC_STAGES_1X;
-    static constexpr uint32_t kStageOut = 4 * 32 * 33 * 4;   // per-warp 32 x 33 store tiles
-    static constexpr uint32_t kSmem = kStages * kStage + 1024 + 256 + kStageOut;
+    // output staging: per epilogue warp two 32 x 32 fp32 buffers (128-byte swizzled) for the
+    // TMA stores; the row-store path of gathered-table launches reuses them as 32 x 33 tiles
+    static constexpr uint32_t kOutBuf = 32 * 32 * 4;
+    static constexpr uint32_t kStageOut = 4 * 2 * kOutBuf;
+    static_assert(32 * 33 * 4 <= 2 * kOutBuf, "row-store tile fits a warp's buffers");
+    static constexpr uint32_t kSmem = kStages * kStage + kStageOut + 256 + 1024;
     static_assert(4 * BN <= 512, "accumulators must fit tensor memory");
     static constexpr uint32_t kTmemCols = 4 * BN;   // up to 4 accumulators of BN columns
 };
@@ -173,6 +196,8 @@ struct Maps {
     CUtensorMap a;
     CUtensorMap b[8];
     CUtensorMap l[8];
+    CUtensorMap c[8];     // per group: C columns c_col .. c_col + N (TMA-store epilogue)
+    CUtensorMap cp[8];    // per group: the same columns of Cpre
 };
 
 // Tile t of the launch -> (group, first row, first column, K stages).
@@ -209,14 +234,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * CF::kStage);
+    uint8_t* outbuf = smem + S * CF::kStage;                      // 1024-byte aligned
+    uint64_t* full = reinterpret_cast<uint64_t*>(outbuf + CF::kStageOut);
     uint64_t* conv = full + S;
     uint64_t* empty = conv + S;
     uint64_t* accf = empty + S;
     uint64_t* acce = accf + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 1);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
-    float* stage_out = reinterpret_cast<float*>(smem + S * CF::kStage + 256);
+    float* stage_out = reinterpret_cast<float*>(outbuf);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -347,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ------------------------------------------------------------------ epilogue
         const int quarter = warp & 3;
-        uint32_t j = 0;
+        uint32_t j = 0, ring = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++j) {
             TileInfo ti = tile_info<BN>(p, ntn, t);
             bool ok = mbar_wait(accf, j & 1u, 4) && !aborted();
@@ -371,6 +397,49 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             mbar_arrive(acce);                  // tensor memory may take the next tile now
+            if (p.tma_out) {
+                // each 32 x 32 block: bias (+ SiLU) applied in registers, written 128-byte
+                // swizzled into one of this warp's two buffers, stored by one lane with TMA
+                // (reduce-add when accumulating); the tensor map clips rows >= M, cols >= N
+                const int N = p.g.N[ti.grp];
+                const float* bias = p.g.bias[ti.grp];
+                const int y0 = (int)(ti.m0 + quarter * 32);
+                if (y0 >= p.M) continue;
+#pragma unroll
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    const int x0 = ti.n0 + c0;
+                    if (x0 >= N) break;
+#pragma unroll
+                    for (int pass = 0; pass < 2; ++pass) {
+                        // pass 0: pre-activation to Cpre (SiLU launches that keep it)
+                        if (pass == 0 && !(p.act == 1 && p.Cpre)) continue;
+                        const bool silu = pass == 1 && p.act == 1;
+                        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                        __syncwarp();
+                        float4* buf = reinterpret_cast<float4*>(
+                            outbuf + ((warp - 2) * 2 + (ring & 1)) * CF::kOutBuf);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            float e[4];
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const int jj = 4 * q + k;
+                                const float b = (bias && x0 + jj < N) ? bias[x0 + jj] : 0.f;
+                                const float y = v[c0 + jj] + b;
+                                e[k] = silu ? silu_f(y) : y;
+                            }
+                            buf[lane * 8 + (q ^ (lane & 7))] = make_float4(e[0], e[1], e[2], e[3]);
+                        }
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0)
+                            tma_store_2d(pass == 0 ? &maps.cp[ti.grp] : &maps.c[ti.grp], buf, x0,
+                                         y0, pass == 1 && p.accumulate);
+                        ++ring;
+                    }
+                }
+                continue;
+            }
             // stores: each 32 x 32 block goes through this warp's shared tile, so that a warp
             // writes 32 consecutive columns of one row per instruction (and reads bias and
             // table entries coalesced)
@@ -405,6 +474,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     }
+    // TMA stores issued by this thread must finish before the CTA (and its shared memory) ends
+    if (warp >= 2 && warp < 6 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     __syncthreads();
     if (warp == 1) {
         __syncwarp();
@@ -498,6 +569,19 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
             if (int s = make_map(&maps.l[i], g->Bt_lo[i], g->K[i], g->N[i], g->K[i], BN)) return s;
     }
     p.g.tile_start[g->ngroups] = tiles;
+    // TMA-store epilogue: no gathered tables, 16-byte aligned column blocks and rows
+    bool tma_out = !T1 && !T2 && ldc % 4 == 0 && aligned16(C) && (!Cpre || aligned16(Cpre));
+    for (int i = 0; i < g->ngroups; ++i)
+        tma_out = tma_out && g->c_col[i] % 4 == 0 && g->N[i] >= 32;
+    p.tma_out = tma_out ? 1 : 0;
+    if (tma_out) {
+        for (int i = 0; i < g->ngroups; ++i) {
+            if (int s = make_map(&maps.c[i], C + g->c_col[i], g->N[i], M, ldc, 32)) return s;
+            if (act == 1 && Cpre)
+                if (int s = make_map(&maps.cp[i], Cpre + g->c_col[i], g->N[i], M, ldc, 32))
+                    return s;
+        }
+    }
     const long long ntiles = (long long)tiles * ceil_div(M, BM);
     if (ntiles >= (1LL << 31)) {
         set_error("gemm_tc: too many tiles");
