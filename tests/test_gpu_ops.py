@@ -122,6 +122,60 @@ def test_grouped_gemm_with_epilogues(M, precision):
 
 
 @pytest.mark.parametrize("precision", [1, 2])
+@pytest.mark.parametrize("M", [1, 129, 1000])
+@pytest.mark.parametrize("N2", [132, 130])
+def test_gemm_tma_store_epilogue(M, precision, N2):
+    """Launches without gathered tables take the TMA-store epilogue: bias + SiLU with the
+    pre-activation kept, then an accumulating launch (TMA reduce-add); N2 = 132 and the row
+    counts leave ragged tile edges that the tensor maps must clip. N2 = 130 (not a multiple of
+    4 columns) takes the row-store path instead; both must leave the columns around the groups
+    untouched."""
+    from tt_atom.engine import _Groups
+    K1, N1, K2 = 96, 160, 64
+    A = rnd(M, K1 + K2)
+    B1, B2 = rnd(K1, N1, seed=1), rnd(K2, N2, seed=2)
+    bias1 = rnd(N1, seed=3)
+    g = _Groups([dict(a_col=0, K=K1, c_col=0, N=N1, B=B1, bias=bias1),
+                 dict(a_col=K1, K=K2, c_col=N1 + 4, N=N2, B=B2)])
+    ldc = N1 + 4 + N2 + 2
+    C = torch.full((M, ldc), 7.0, device=dev)
+    Cpre = torch.full((M, ldc), 7.0, device=dev)
+    call("atom_gemm", ptr(A), K1 + K2, M, ctypes.byref(g.struct), ptr(C), ldc, ptr(Cpre),
+         None, None, None, None, 0, 1, 0, precision, s())
+    Ad = A.double()
+    pre = torch.cat([Ad[:, :K1] @ B1.double() + bias1.double(), Ad[:, K1:] @ B2.double()], 1)
+    cols = torch.cat([torch.arange(N1), torch.arange(N1 + 4, N1 + 4 + N2)]).to(dev)
+    close(Cpre[:, cols], pre, TOL[precision])
+    close(C[:, cols], F.silu(pre), TOL[precision])
+    gap = torch.ones(ldc, dtype=torch.bool, device=dev)
+    gap[cols] = False
+    assert (C[:, gap] == 7.0).all() and (Cpre[:, gap] == 7.0).all()   # nothing outside the groups
+    C2 = C.clone()
+    call("atom_gemm", ptr(A), K1 + K2, M, ctypes.byref(g.struct), ptr(C2), ldc, None,
+         None, None, None, None, 0, 0, 1, precision, s())
+    close(C2[:, cols], C[:, cols].double() + pre, TOL[precision])
+    assert (C2[:, gap] == 7.0).all()
+
+
+def test_gemm_3xtf32_split_is_exact_for_truncating_tensor_cores():
+    """3xTF32 leaves A in shared memory as loaded and relies on the tensor core reading an fp32
+    operand as TF32 by dropping its low 13 mantissa bits (truncation); A_lo = A - trunc(A) is
+    exact. A = 1 + 3 * 2^-12 lies 0.75 TF32 ulp above 1: truncation gives 1 and the product
+    with B = 1 comes out exact; a rounding tensor core would give 1 + 2^-10 + 3 * 2^-12."""
+    from tt_atom.engine import _Groups
+    M, K, N = 128, 32, 32
+    A = torch.zeros(M, K, device=dev)
+    A[:, 0] = 1.0 + 3.0 * 2.0 ** -12
+    B = torch.zeros(K, N, device=dev)
+    B[0, :] = 1.0
+    g = _Groups([dict(a_col=0, K=K, c_col=0, N=N, B=B)])
+    C = torch.empty(M, N, device=dev)
+    call("atom_gemm", ptr(A), K, M, ctypes.byref(g.struct), ptr(C), N, None, None, None, None,
+         None, 0, 0, 0, 2, s())
+    assert (C == 1.0 + 3.0 * 2.0 ** -12).all()
+
+
+@pytest.mark.parametrize("precision", [1, 2])
 def test_tensor_core_gemm_so2_shapes_many_groups(precision):
     """The so2_conv_1 block layout (K = 768, 1024, 512) and an 8-group radial-style layout."""
     from tt_atom.engine import _Groups

@@ -6,8 +6,9 @@
 //   2  3xTF32: each fp32 operand x is split into hi = x with the low 13 mantissa bits cleared and
 //      lo = x - hi (exact); C += A_hi B_hi + A_hi B_lo + A_lo B_hi, which carries fp32-level
 //      accuracy (the dropped A_lo B_lo term is ~2^-22 relative). B's split is precomputed (the
-//      weights are constant); A's split is made in shared memory by the epilogue warps, which are
-//      otherwise idle during the main loop.
+//      weights are constant); A's split is made in shared memory by four split warps. Only A_lo
+//      is written: the tensor core reads an fp32 operand as TF32 by dropping its low 13 mantissa
+//      bits, so the A tile as loaded already acts as A_hi (a known-answer test checks this).
 //
 // Persistent CTAs (one per SM, 320 threads): warp 0 issues TMA loads, warp 1 allocates tensor
 // memory and issues the MMAs (one elected lane), warps 2-5 run the epilogue (warp w reads
@@ -24,7 +25,7 @@
 
 // Pipeline depth (shared-memory stages) per precision mode; overridable at build time.
 #ifndef ATOM_TC_STAGES_3X
-#define ATOM_TC_STAGES_3X 3
+#define ATOM_TC_STAGES_3X 4
 #endif
 #ifndef ATOM_TC_STAGES_1X
 #define ATOM_TC_STAGES_1X 5
@@ -154,6 +155,22 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
 }
+// Same, with A read from tensor memory (lane = row, one column per K element).
+__device__ __forceinline__ void mma_tf32_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t b,
+                                            uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+// 32 consecutive tensor-memory columns of this thread's lane <- r[0..31].
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile(
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -178,7 +195,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
 template <int BN, int MODE>
 struct Cfg {
     static constexpr uint32_t kTileB = BN * BK * 4;
-    static constexpr uint32_t kStage = kTileA + kTileB + (MODE == 2 ? kTileA + kTileB : 0);
+    // mode 2 keeps no A_lo tile in shared memory: the split writes A_hi / A_lo to tensor memory
+    static constexpr uint32_t kStage = kTileA + kTileB + (MODE == 2 ? kTileB : 0);
     static constexpr uint32_t kLoadBytes = kTileA + kTileB * (MODE == 2 ? 2 : 1);  // TMA bytes
     static constexpr int kStages = MODE == 2 ? ATOM_TC_STAGES_3X : ATOM_TC_STAGES_1X;
     // output staging: per epilogue warp two 32 x 32 fp32 buffers (128-byte swizzled) for the
@@ -224,6 +242,10 @@ __device__ __forceinline__ TileInfo tile_info(const Args& p, int ntn, int t) {
 // The epilogue drains the accumulators into registers and releases tensor memory before it
 // computes and stores, so the next tile's MMAs overlap the previous tile's stores.
 constexpr int kThreads = 320;
+// mode 2 tensor memory: main accumulators at columns 0 and 2 BN, corrections at BN, then two
+// A slots of 2 x BK columns (A_hi, A_lo) at kSlot0
+constexpr uint32_t kSlot0 = 3 * 128;
+static_assert(kSlot0 + 2 * 2 * BK <= 512, "tensor-memory columns");
 
 template <int BN, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -240,7 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* empty = conv + S;
     uint64_t* accf = empty + S;
     uint64_t* acce = accf + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 1);
+    uint64_t* afree = acce + 1;          // mode 2: tensor-memory A slot 0 / 1 free again
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(afree + 2);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
     float* stage_out = reinterpret_cast<float*>(outbuf);
 
@@ -253,6 +276,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(accf, 1);
         mbar_init(acce, 128);
+        mbar_init(&afree[0], 1);
+        mbar_init(&afree[1], 1);
         // a CTA that failed earlier in this grid (or an earlier launch) stops the rest here
         *abort_flag = *(volatile int*)&g_tc_error != 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -271,8 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     auto stA = [&](int s) { return smem + s * CF::kStage; };
     auto stB = [&](int s) { return smem + s * CF::kStage + kTileA; };
-    auto stAL = [&](int s) { return smem + s * CF::kStage + kTileA + CF::kTileB; };
-    auto stBL = [&](int s) { return smem + s * CF::kStage + 2 * kTileA + CF::kTileB; };
+    auto stBL = [&](int s) { return smem + s * CF::kStage + kTileA + CF::kTileB; };
     auto aborted = [&]() { return *(volatile int*)abort_flag != 0; };
 
     if (warp == 0) {
@@ -313,21 +337,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    uint32_t a = smem_u32(stA(s)), b = smem_u32(stB(s));
-                    // stage kt accumulates into accumulator kt % nacc (fp32 columns BN apart)
-                    const uint32_t dacc = tmem + (uint32_t)((kt % p.nacc) * BN);
-                    const bool first = kt < p.nacc;
+                    const uint32_t a = smem_u32(stA(s)), b = smem_u32(stB(s));
+                    if constexpr (MODE == 2) {
+                        // A_hi / A_lo from tensor-memory slot it % 2; A_hi B_hi into main
+                        // accumulator kt % 2 (columns 0 / 2 BN), both corrections into columns BN
+                        const uint32_t slot = tmem + kSlot0 + (it & 1u) * 2 * BK;
+                        const uint32_t bl = smem_u32(stBL(s));
+                        const uint32_t dmain = tmem + (uint32_t)((kt & 1) * 2 * BN);
+                        const uint32_t dcorr = tmem + BN;
 #pragma unroll
-                    for (int kk = 0; kk < BK / 8; ++kk) {
-                        uint32_t acc = (!first || kk > 0) ? 1u : 0u;
-                        mma_tf32(dacc, sdesc(a + kk * 32), sdesc(b + kk * 32), idesc, acc);
-                        if (MODE == 2) {
-                            uint32_t al = smem_u32(stAL(s)), bl = smem_u32(stBL(s));
-                            mma_tf32(dacc, sdesc(a + kk * 32), sdesc(bl + kk * 32), idesc, 1u);
-                            mma_tf32(dacc, sdesc(al + kk * 32), sdesc(b + kk * 32), idesc, 1u);
+                        for (int kk = 0; kk < BK / 8; ++kk) {
+                            const uint32_t am = (kt > 1 || kk > 0) ? 1u : 0u;
+                            const uint32_t ac = (kt > 0 || kk > 0) ? 1u : 0u;
+                            mma_tf32_ta(dmain, slot + kk * 8, sdesc(b + kk * 32), idesc, am);
+                            mma_tf32_ta(dcorr, slot + kk * 8, sdesc(bl + kk * 32), idesc, ac);
+                            mma_tf32_ta(dcorr, slot + BK + kk * 8, sdesc(b + kk * 32), idesc, 1u);
                         }
+                        mma_commit(&empty[s]);
+                        mma_commit(&afree[it & 1u]);
+                    } else {
+                        // stage kt accumulates into accumulator kt % nacc (columns BN apart)
+                        const uint32_t dacc = tmem + (uint32_t)((kt % p.nacc) * BN);
+                        const bool first = kt < p.nacc;
+#pragma unroll
+                        for (int kk = 0; kk < BK / 8; ++kk) {
+                            uint32_t acc = (!first || kk > 0) ? 1u : 0u;
+                            mma_tf32(dacc, sdesc(a + kk * 32), sdesc(b + kk * 32), idesc, acc);
+                        }
+                        mma_commit(&empty[s]);
                     }
-                    mma_commit(&empty[s]);
                 }
                 if (ok) {
                     mma_commit(accf);
@@ -340,32 +378,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 6) {
         // ------------------------------------------------------ A split (3xTF32 only)
+        // Thread = tile row (warp w owns tensor-memory lanes 32 * (w % 4) ..): reads its row of
+        // the swizzled A stage, writes A_hi (low 13 mantissa bits cleared) and A_lo = A - A_hi
+        // to 2 x BK columns of tensor-memory slot it % 2, once the MMAs that read that slot two
+        // stages earlier have completed.
         if (MODE == 2) {
-            const int ct = threadIdx.x - 192;      // 0..127
+            const int quarter = warp & 3;
+            const int r = quarter * 32 + lane;
+            const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
             uint32_t it = 0;
-            for (int t = blockIdx.x; t < ntiles && !aborted(); t += gridDim.x) {
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < ntiles && !aborted(); t += gridDim.x) {
                 TileInfo ti = tile_info<BN>(p, ntn, t);
                 for (int kt = 0; kt < ti.nk; ++kt, ++it) {
                     int s = it % S;
                     uint32_t ph = (it / S) & 1u;
-                    if (!mbar_wait(&full[s], ph, 3) || aborted()) {
+                    ok = mbar_wait(&full[s], ph, 3) &&
+                         mbar_wait(&afree[it & 1u], ((it >> 1) & 1u) ^ 1u, 6) && !aborted();
+                    ok = __all_sync(0xffffffffu, ok);
+                    if (!ok) {
                         *(volatile int*)abort_flag = 1;
                         break;
                     }
-                    float4* hi = reinterpret_cast<float4*>(stA(s));
-                    float4* lo = reinterpret_cast<float4*>(stAL(s));
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint8_t* row = stA(s) + (r >> 3) * 1024 + (r & 7) * 128;
+                    uint32_t hi[BK], lo[BK];
 #pragma unroll
-                    for (int i = 0; i < (int)(kTileA / 16) / 128; ++i) {
-                        int q = ct + 128 * i;
-                        float4 x = hi[q], h, l;
-                        h.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u); l.x = x.x - h.x;
-                        h.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u); l.y = x.y - h.y;
-                        h.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u); l.z = x.z - h.z;
-                        h.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u); l.w = x.w - h.w;
-                        hi[q] = h;
-                        lo[q] = l;
+                    for (int c = 0; c < BK / 4; ++c) {
+                        const float4 x =
+                            *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) << 4));
+                        const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const uint32_t h = __float_as_uint(xs[k]) & 0xFFFFE000u;
+                            hi[4 * c + k] = h;
+                            lo[4 * c + k] = __float_as_uint(xs[k] - __uint_as_float(h));
+                        }
                     }
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    const uint32_t slot = lane_base + kSlot0 + (it & 1u) * 2 * BK;
+                    tmem_st32(slot, hi);
+                    tmem_st32(slot + BK, lo);
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                     mbar_arrive(&conv[s]);
                 }
             }
@@ -381,11 +435,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             // drain the accumulators into registers (partial sums added with round-to-nearest)
-            const int nused = ti.nk < p.nacc ? ti.nk : p.nacc;
+            // mode 2: main accumulator 0, the corrections, main accumulator 1 (when nk > 1)
+            const int nuse0 = ti.nk + (MODE == 2 ? 1 : 0);
+            const int nused = nuse0 < p.nacc ? nuse0 : p.nacc;
             float v[BN];
             const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll
             for (int c0 = 0; c0 < BN; c0 += 16) tmem_ld16(lane_base + (uint32_t)c0, v + c0);
+#pragma unroll 1
             for (int q = 1; q < nused; ++q) {
 #pragma unroll
                 for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -525,7 +582,10 @@ static int make_map(CUtensorMap* m, const float* base, long long inner, long lon
 // zero, so its error grows with the number of steps in one accumulator; spreading the stages
 // over 4 accumulators (summed in the epilogue with round-to-nearest) divides that by 4.
 // Measured on B200 (K = 1024, all-positive operands, 3xTF32): mean relative bias -2.1e-5 with
-// one accumulator, -5.3e-6 with four.
+// one accumulator (all three products in it), -5.3e-6 with four. TF32 uses four; 3xTF32
+// uses two main accumulators for A_hi B_hi (alternate stages) plus one for the two small
+// correction products, whose rounding is negligible against the total, so each main
+// accumulator takes K / 16 steps.
 constexpr int g_nacc = 4;
 
 template <int BN, int MODE>
@@ -552,7 +612,7 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
     Args p;
     p.M = M; p.ldc = ldc; p.ldt = ldt; p.C = C; p.Cpre = Cpre; p.T1 = T1; p.T2 = T2;
     p.idx1 = idx1; p.idx2 = idx2; p.act = act; p.accumulate = accumulate;
-    p.nacc = g_nacc;
+    p.nacc = MODE == 2 ? 3 : g_nacc;
     p.g.ngroups = g->ngroups;
     int tiles = 0;
     for (int i = 0; i < g->ngroups; ++i) {
@@ -569,10 +629,12 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
             if (int s = make_map(&maps.l[i], g->Bt_lo[i], g->K[i], g->N[i], g->K[i], BN)) return s;
     }
     p.g.tile_start[g->ngroups] = tiles;
-    // TMA-store epilogue: no gathered tables, 16-byte aligned column blocks and rows
+    // TMA-store epilogue: no gathered tables, 16-byte aligned column blocks and rows. A group's
+    // width must be a multiple of 4 columns too: the store clips at 16-byte granularity, so a
+    // 130-column group would also get columns 130 and 131 written (measured on B200).
     bool tma_out = !T1 && !T2 && ldc % 4 == 0 && aligned16(C) && (!Cpre || aligned16(Cpre));
     for (int i = 0; i < g->ngroups; ++i)
-        tma_out = tma_out && g->c_col[i] % 4 == 0 && g->N[i] >= 32;
+        tma_out = tma_out && g->c_col[i] % 4 == 0 && g->N[i] % 4 == 0 && g->N[i] >= 32;
     p.tma_out = tma_out ? 1 : 0;
     if (tma_out) {
         for (int i = 0; i < g->ngroups; ++i) {
