@@ -3,18 +3,21 @@
 //
 // Precision modes
 //   1  TF32: one MMA per k-step on the operands as stored (about 1e-3 relative per product).
+//      Tiles 128 x 128, A and B from shared memory, K stages spread over 4 accumulators.
 //   2  3xTF32: each fp32 operand x is split into hi = x with the low 13 mantissa bits cleared and
 //      lo = x - hi (exact); C += A_hi B_hi + A_hi B_lo + A_lo B_hi, which carries fp32-level
 //      accuracy (the dropped A_lo B_lo term is ~2^-22 relative). B's split is precomputed (the
-//      weights are constant); A's split is made in shared memory by four split warps. Only A_lo
-//      is written: the tensor core reads an fp32 operand as TF32 by dropping its low 13 mantissa
-//      bits, so the A tile as loaded already acts as A_hi (a known-answer test checks this).
+//      weights are constant). Four split warps write A_hi / A_lo of each stage into tensor
+//      memory and the MMAs read A from there, so shared memory only feeds B. Tiles are
+//      128 x 192: 192 columns for A_hi B_hi, 192 for the corrections and two 64-column A slots
+//      fill the 512 tensor-memory columns (wider MMAs run faster per product: N = 256 took only
+//      ~13% longer than N = 128 on B200).
 //
-// Persistent CTAs (one per SM, 320 threads): warp 0 issues TMA loads, warp 1 allocates tensor
-// memory and issues the MMAs (one elected lane), warps 2-5 run the epilogue (warp w reads
-// tensor-memory lanes 32 * (w % 4) .. + 31, i.e. output rows of that quarter), warps 6-9 split
-// A (mode 2). A tile is 128 x BN; K advances in 32-element (128-byte) stages through an S-deep
-// mbarrier ring that runs on across tiles.
+// Persistent CTAs (one per SM, 448 threads): warp 0 issues TMA loads, warp 1 allocates tensor
+// memory and issues the MMAs (one elected lane), warps 2-9 run the epilogue (warp w reads
+// tensor-memory lanes 32 * (w % 4) .. + 31, i.e. output rows of that quarter, and one column
+// half of the tile), warps 10-13 split A (mode 2). K advances in 32-element (128-byte) stages
+// through an S-deep mbarrier ring that runs on across tiles.
 //
 // Every wait is bounded: on expiry the CTA records an error code in g_tc_error, abandons the
 // tile and still releases its tensor memory.
@@ -25,7 +28,7 @@
 
 // Pipeline depth (shared-memory stages) per precision mode; overridable at build time.
 #ifndef ATOM_TC_STAGES_3X
-#define ATOM_TC_STAGES_3X 4
+#define ATOM_TC_STAGES_3X 3
 #endif
 #ifndef ATOM_TC_STAGES_1X
 #define ATOM_TC_STAGES_1X 5
@@ -140,12 +143,18 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
     return d;
 }
 
-template <int BN>
-__host__ __device__ constexpr uint32_t idesc_tf32() {
+// Instruction descriptor: D fp32, A and B tf32, both K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t idesc_tf32(int n) {
     return (1u << 4)                    // D: fp32
            | (2u << 7) | (2u << 10)     // A, B: tf32
-           | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+           | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
+
+// Warp roles: 0 TMA producer, 1 TMEM allocator + MMA issuer, 2-9 epilogue, 10-13 A split.
+constexpr int kEpiWarps = 8;
+constexpr int kSplitWarps = 4;
+constexpr int kThreads = 32 * (2 + kEpiWarps + kSplitWarps);   // 448
+constexpr uint32_t kTmemCols = 512;
 
 __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
                                          uint32_t accumulate) {
@@ -192,6 +201,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+    uint32_t r[8];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 template <int BN, int MODE>
 struct Cfg {
     static constexpr uint32_t kTileB = BN * BK * 4;
@@ -199,14 +220,16 @@ struct Cfg {
     static constexpr uint32_t kStage = kTileA + kTileB + (MODE == 2 ? kTileB : 0);
     static constexpr uint32_t kLoadBytes = kTileA + kTileB * (MODE == 2 ? 2 : 1);  // TMA bytes
     static constexpr int kStages = MODE == 2 ? ATOM_TC_STAGES_3X : ATOM_TC_STAGES_1X;
-    // output staging: per epilogue warp two 32 x 32 fp32 buffers (128-byte swizzled) for the
-    // TMA stores; the row-store path of gathered-table launches reuses them as 32 x 33 tiles
+    static constexpr int kEpiCols = BN / 2;        // columns per epilogue warp
+    // output staging: one 32 x 32 fp32 buffer (128-byte swizzled) per epilogue warp for the TMA
+    // stores; the row-store path of gathered-table launches uses it as an XOR-swizzled tile
     static constexpr uint32_t kOutBuf = 32 * 32 * 4;
-    static constexpr uint32_t kStageOut = 4 * 2 * kOutBuf;
-    static_assert(32 * 33 * 4 <= 2 * kOutBuf, "row-store tile fits a warp's buffers");
+    static constexpr uint32_t kStageOut = kEpiWarps * kOutBuf;
     static constexpr uint32_t kSmem = kStages * kStage + kStageOut + 256 + 1024;
-    static_assert(4 * BN <= 512, "accumulators must fit tensor memory");
-    static constexpr uint32_t kTmemCols = 4 * BN;   // up to 4 accumulators of BN columns
+    static_assert(kSmem <= 232448, "shared memory per CTA");
+    static_assert(kEpiCols % 32 == 0, "epilogue chunks");
+    // mode 1: 4 accumulators of BN columns; mode 2: main + corrections, then two A slots
+    static_assert(MODE == 2 ? 2 * BN + 4 * BK <= 512 : 4 * BN <= 512, "tensor-memory columns");
 };
 
 // Tensor maps of one launch: A, and per group the K-major weight (hi) and its lo part.
@@ -238,21 +261,16 @@ __device__ __forceinline__ TileInfo tile_info(const Args& p, int ntn, int t) {
 
 // Persistent kernel: each CTA walks tiles blockIdx.x, blockIdx.x + gridDim.x, ... (column
 // tiles of one row block are adjacent, so concurrently running CTAs share A rows in L2).
-// Warps: 0 TMA producer, 1 TMEM allocator + MMA issuer, 2-5 epilogue, 6-9 A splitters (mode 2).
 // The epilogue drains the accumulators into registers and releases tensor memory before it
 // computes and stores, so the next tile's MMAs overlap the previous tile's stores.
-constexpr int kThreads = 320;
-// mode 2 tensor memory: main accumulators at columns 0 and 2 BN, corrections at BN, then two
-// A slots of 2 x BK columns (A_hi, A_lo) at kSlot0
-constexpr uint32_t kSlot0 = 3 * 128;
-static_assert(kSlot0 + 2 * 2 * BK <= 512, "tensor-memory columns");
-
 template <int BN, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Args p, int ntn,
                    int ntiles) {
     using CF = Cfg<BN, MODE>;
     constexpr int S = CF::kStages;
+    constexpr int EC = CF::kEpiCols;
+    constexpr uint32_t kSlot0 = 2 * BN;   // mode 2: A slots after main and corrections
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -265,17 +283,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* afree = acce + 1;          // mode 2: tensor-memory A slot 0 / 1 free again
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(afree + 2);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
-    float* stage_out = reinterpret_cast<float*>(outbuf);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&conv[s], 128);
+            mbar_init(&conv[s], 32 * kSplitWarps);
             mbar_init(&empty[s], 1);
         }
         mbar_init(accf, 1);
-        mbar_init(acce, 128);
+        mbar_init(acce, 32 * kEpiWarps);
         mbar_init(&afree[0], 1);
         mbar_init(&afree[1], 1);
         // a CTA that failed earlier in this grid (or an earlier launch) stops the rest here
@@ -287,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
-                     "r"(CF::kTmemCols));
+                     "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     __syncthreads();
@@ -323,10 +340,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_tf32<BN>();
             uint32_t it = 0, j = 0;
             for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++j) {
                 TileInfo ti = tile_info<BN>(p, ntn, t);
+                // a group's last tile multiplies only the columns that remain (N multiple of 16)
+                const int rem = p.g.N[ti.grp] - ti.n0;
+                const uint32_t idesc = idesc_tf32(rem >= BN ? BN : (rem + 15) & ~15);
                 bool ok = !aborted() && mbar_wait(acce, (j & 1u) ^ 1u, 5);
                 if (ok) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 for (int kt = 0; ok && kt < ti.nk; ++kt, ++it) {
@@ -339,19 +358,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint32_t a = smem_u32(stA(s)), b = smem_u32(stB(s));
                     if constexpr (MODE == 2) {
-                        // A_hi / A_lo from tensor-memory slot it % 2; A_hi B_hi into main
-                        // accumulator kt % 2 (columns 0 / 2 BN), both corrections into columns BN
+                        // A_hi / A_lo from tensor-memory slot it % 2; A_hi B_hi into the main
+                        // accumulator (columns 0 ..), both corrections into columns BN ..
                         const uint32_t slot = tmem + kSlot0 + (it & 1u) * 2 * BK;
                         const uint32_t bl = smem_u32(stBL(s));
-                        const uint32_t dmain = tmem + (uint32_t)((kt & 1) * 2 * BN);
-                        const uint32_t dcorr = tmem + BN;
 #pragma unroll
                         for (int kk = 0; kk < BK / 8; ++kk) {
-                            const uint32_t am = (kt > 1 || kk > 0) ? 1u : 0u;
-                            const uint32_t ac = (kt > 0 || kk > 0) ? 1u : 0u;
-                            mma_tf32_ta(dmain, slot + kk * 8, sdesc(b + kk * 32), idesc, am);
-                            mma_tf32_ta(dcorr, slot + kk * 8, sdesc(bl + kk * 32), idesc, ac);
-                            mma_tf32_ta(dcorr, slot + BK + kk * 8, sdesc(b + kk * 32), idesc, 1u);
+                            const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
+                            mma_tf32_ta(tmem, slot + kk * 8, sdesc(b + kk * 32), idesc, acc);
+                            mma_tf32_ta(tmem + BN, slot + kk * 8, sdesc(bl + kk * 32), idesc,
+                                        acc);
+                            mma_tf32_ta(tmem + BN, slot + BK + kk * 8, sdesc(b + kk * 32), idesc,
+                                        1u);
                         }
                         mma_commit(&empty[s]);
                         mma_commit(&afree[it & 1u]);
@@ -376,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-    } else if (warp >= 6) {
+    } else if (warp >= 2 + kEpiWarps) {
         // ------------------------------------------------------ A split (3xTF32 only)
         // Thread = tile row (warp w owns tensor-memory lanes 32 * (w % 4) ..): reads its row of
         // the swizzled A stage, writes A_hi (low 13 mantissa bits cleared) and A_lo = A - A_hi
@@ -426,55 +444,62 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ------------------------------------------------------------------ epilogue
+        // warp w: output rows of lane quarter w % 4, columns half * EC .. + EC of the tile
         const int quarter = warp & 3;
-        uint32_t j = 0, ring = 0;
+        const int cbase = ((warp - 2) >> 2) * EC;
+        uint8_t* mybuf = outbuf + (warp - 2) * CF::kOutBuf;
+        uint32_t j = 0;
+        bool pending = false;            // a TMA store from this warp's buffer may be reading it
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++j) {
             TileInfo ti = tile_info<BN>(p, ntn, t);
             bool ok = mbar_wait(accf, j & 1u, 4) && !aborted();
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            // drain the accumulators into registers (partial sums added with round-to-nearest)
-            // mode 2: main accumulator 0, the corrections, main accumulator 1 (when nk > 1)
-            const int nuse0 = ti.nk + (MODE == 2 ? 1 : 0);
-            const int nused = nuse0 < p.nacc ? nuse0 : p.nacc;
-            float v[BN];
-            const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+            const int N = p.g.N[ti.grp];
+            const bool active = ti.n0 + cbase < N;
+            // drain the accumulators into registers (partial sums added with round-to-nearest):
+            // mode 1 the K-stage accumulators in use, mode 2 main + corrections
+            const int nused = MODE == 2 ? 2 : (ti.nk < p.nacc ? ti.nk : p.nacc);
+            float v[EC];
+            const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)cbase;
+            if (active) {
 #pragma unroll
-            for (int c0 = 0; c0 < BN; c0 += 16) tmem_ld16(lane_base + (uint32_t)c0, v + c0);
+                for (int c0 = 0; c0 < EC; c0 += 16) tmem_ld16(lane_base + (uint32_t)c0, v + c0);
 #pragma unroll 1
-            for (int q = 1; q < nused; ++q) {
+                for (int q = 1; q < nused; ++q) {
 #pragma unroll
-                for (int c0 = 0; c0 < BN; c0 += 16) {
-                    float w[16];
-                    tmem_ld16(lane_base + (uint32_t)(q * BN + c0), w);
+                    for (int c0 = 0; c0 < EC; c0 += 8) {
+                        float w[8];
+                        tmem_ld8(lane_base + (uint32_t)(q * BN + c0), w);
 #pragma unroll
-                    for (int jj = 0; jj < 16; ++jj) v[c0 + jj] += w[jj];
+                        for (int jj = 0; jj < 8; ++jj) v[c0 + jj] += w[jj];
+                    }
                 }
             }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             mbar_arrive(acce);                  // tensor memory may take the next tile now
+            if (!active) continue;
+            const float* bias = p.g.bias[ti.grp];
             if (p.tma_out) {
                 // each 32 x 32 block: bias (+ SiLU) applied in registers, written 128-byte
-                // swizzled into one of this warp's two buffers, stored by one lane with TMA
-                // (reduce-add when accumulating); the tensor map clips rows >= M, cols >= N
-                const int N = p.g.N[ti.grp];
-                const float* bias = p.g.bias[ti.grp];
+                // swizzled into this warp's buffer, stored by one lane with TMA (reduce-add when
+                // accumulating); the tensor map clips rows >= M, cols >= N
                 const int y0 = (int)(ti.m0 + quarter * 32);
                 if (y0 >= p.M) continue;
 #pragma unroll
-                for (int c0 = 0; c0 < BN; c0 += 32) {
-                    const int x0 = ti.n0 + c0;
+                for (int c0 = 0; c0 < EC; c0 += 32) {
+                    const int x0 = ti.n0 + cbase + c0;
                     if (x0 >= N) break;
-#pragma unroll
+#pragma unroll 1
                     for (int pass = 0; pass < 2; ++pass) {
                         // pass 0: pre-activation to Cpre (SiLU launches that keep it)
                         if (pass == 0 && !(p.act == 1 && p.Cpre)) continue;
                         const bool silu = pass == 1 && p.act == 1;
-                        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                        if (pending && lane == 0)
+                            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
                         __syncwarp();
-                        float4* buf = reinterpret_cast<float4*>(
-                            outbuf + ((warp - 2) * 2 + (ring & 1)) * CF::kOutBuf);
+                        float4* buf = reinterpret_cast<float4*>(mybuf);
 #pragma unroll
                         for (int q = 0; q < 8; ++q) {
                             float e[4];
@@ -492,32 +517,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (lane == 0)
                             tma_store_2d(pass == 0 ? &maps.cp[ti.grp] : &maps.c[ti.grp], buf, x0,
                                          y0, pass == 1 && p.accumulate);
-                        ++ring;
+                        pending = true;
                     }
                 }
                 continue;
             }
-            // stores: each 32 x 32 block goes through this warp's shared tile, so that a warp
-            // writes 32 consecutive columns of one row per instruction (and reads bias and
-            // table entries coalesced)
-            const int N = p.g.N[ti.grp];
-            const float* bias = p.g.bias[ti.grp];
+            // row stores (gathered-table launches): each 32 x 32 block goes through this warp's
+            // XOR-swizzled shared tile, so that a warp writes 32 consecutive columns of one row
+            // per instruction (and reads bias and table entries coalesced)
             const int ccol = p.g.c_col[ti.grp], tcol = p.g.t_col[ti.grp];
-            float* st = stage_out + (warp - 2) * 32 * 33;
+            float* st = reinterpret_cast<float*>(mybuf);
             const long long mrow0 = ti.m0 + quarter * 32;
 #pragma unroll
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+            for (int c0 = 0; c0 < EC; c0 += 32) {
 #pragma unroll
-                for (int jj = 0; jj < 32; ++jj) st[lane * 33 + jj] = v[c0 + jj];
+                for (int jj = 0; jj < 32; ++jj) st[lane * 32 + (jj ^ lane)] = v[c0 + jj];
                 __syncwarp();
-                const int n = ti.n0 + c0 + lane;
+                const int n = ti.n0 + cbase + c0 + lane;
                 const bool nok = n < N;
                 const float bn = (bias && nok) ? bias[n] : 0.f;
                 for (int r = 0; r < 32; ++r) {
                     const long long m = mrow0 + r;
                     if (m >= p.M) break;
                     if (!nok) continue;
-                    float x = st[r * 33 + lane] + bn;
+                    float x = st[r * 32 + (lane ^ r)] + bn;
                     if (p.T1) x += p.T1[(long long)p.idx1[m] * p.ldt + tcol + n];
                     if (p.T2) x += p.T2[(long long)p.idx2[m] * p.ldt + tcol + n];
                     const long long off = m * p.ldc + ccol + n;
@@ -530,15 +553,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
             }
         }
+        // TMA stores issued by this warp must finish before the CTA (and its shared memory) ends
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
-    // TMA stores issued by this thread must finish before the CTA (and its shared memory) ends
-    if (warp >= 2 && warp < 6 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     __syncthreads();
     if (warp == 1) {
         __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(CF::kTmemCols));
+                     "r"(kTmemCols));
     }
 }
 
@@ -583,9 +606,8 @@ static int make_map(CUtensorMap* m, const float* base, long long inner, long lon
 // over 4 accumulators (summed in the epilogue with round-to-nearest) divides that by 4.
 // Measured on B200 (K = 1024, all-positive operands, 3xTF32): mean relative bias -2.1e-5 with
 // one accumulator (all three products in it), -5.3e-6 with four. TF32 uses four; 3xTF32
-// uses two main accumulators for A_hi B_hi (alternate stages) plus one for the two small
-// correction products, whose rounding is negligible against the total, so each main
-// accumulator takes K / 16 steps.
+// keeps A_hi B_hi in one accumulator (K / 8 steps instead of 3 K / 8) and the two small
+// correction products in another, whose rounding is negligible against the total.
 constexpr int g_nacc = 4;
 
 template <int BN, int MODE>
@@ -612,7 +634,7 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
     Args p;
     p.M = M; p.ldc = ldc; p.ldt = ldt; p.C = C; p.Cpre = Cpre; p.T1 = T1; p.T2 = T2;
     p.idx1 = idx1; p.idx2 = idx2; p.act = act; p.accumulate = accumulate;
-    p.nacc = MODE == 2 ? 3 : g_nacc;
+    p.nacc = MODE == 2 ? 2 : g_nacc;
     p.g.ngroups = g->ngroups;
     int tiles = 0;
     for (int i = 0; i < g->ngroups; ++i) {
@@ -678,7 +700,7 @@ int gemm_tc(const float* A, long long lda, long long M, const atom_gemm_groups* 
             cudaStream_t st) {
     if (int s = tc::encoder()) return s;
     if (precision == 2)
-        return tc::launch<128, 2>(A, lda, M, g, C, ldc, Cpre, T1, T2, idx1, idx2, ldt, act,
+        return tc::launch<192, 2>(A, lda, M, g, C, ldc, Cpre, T1, T2, idx1, idx2, ldt, act,
                                   accumulate, st);
     return tc::launch<128, 1>(A, lda, M, g, C, ldc, Cpre, T1, T2, idx1, idx2, ldt, act,
                               accumulate, st);
