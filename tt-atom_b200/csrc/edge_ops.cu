@@ -196,30 +196,56 @@ __device__ __forceinline__ void rotate_back_acc(const float* w, const float4* y,
     }
 }
 
-__global__ void __launch_bounds__(256) rotate_back_reduce_kernel(
+// Channel-parallel receiver reduction: one block of kCP = 128 threads per node, one channel per
+// thread (looping when C > 128). Each output keeps the fma order of the warp-per-node float4
+// form (edges in CSR order), so results are identical, but four times as many warps stay in
+// flight, which this gather-bound reduction over ~30 edges per node needs at a few thousand
+// nodes.
+constexpr int kCP = 128;
+
+// acc[j] += s * sum over rows r of degree l(j) of W[r][j - l^2] * y[r], one channel
+__device__ __forceinline__ void rotate_back_acc_s(const float* w, const float* y, float s,
+                                                  float* acc) {
+    acc[0] = fmaf(s * w[row_off(0)], y[0], acc[0]);
+#pragma unroll
+    for (int jj = 0; jj < 3; ++jj) {
+        acc[1 + jj] = fmaf(s * w[row_off(1) + jj], y[1], acc[1 + jj]);
+        acc[1 + jj] = fmaf(s * w[row_off(3) + jj], y[3], acc[1 + jj]);
+        acc[1 + jj] = fmaf(s * w[row_off(5) + jj], y[5], acc[1 + jj]);
+    }
+#pragma unroll
+    for (int jj = 0; jj < 5; ++jj) {
+        acc[4 + jj] = fmaf(s * w[row_off(2) + jj], y[2], acc[4 + jj]);
+        acc[4 + jj] = fmaf(s * w[row_off(4) + jj], y[4], acc[4 + jj]);
+        acc[4 + jj] = fmaf(s * w[row_off(6) + jj], y[6], acc[4 + jj]);
+        acc[4 + jj] = fmaf(s * w[row_off(7) + jj], y[7], acc[4 + jj]);
+        acc[4 + jj] = fmaf(s * w[row_off(8) + jj], y[8], acc[4 + jj]);
+    }
+}
+
+// out[n] = resid[n] + sum over edges e received by n (CSR order) of env[e] * Wig(e)^T Y[e]
+__global__ void __launch_bounds__(kCP) rotate_back_reduce_kernel(
     const float* __restrict__ Y, const float* __restrict__ coef, const float* __restrict__ env,
     long long N, int C, const int* __restrict__ recv_ptr, const float* __restrict__ resid,
     float* __restrict__ out) {
-    long long n = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    int lane = threadIdx.x & 31;
-    if (n >= N) return;
-    int e0 = recv_ptr[n], e1 = recv_ptr[n + 1];
-    for (int c = lane * 4; c < C; c += 128) {
-        float4 acc[kNsph];
+    const long long n = blockIdx.x;
+    const int e0 = recv_ptr[n], e1 = recv_ptr[n + 1];
+    for (int c = threadIdx.x; c < C; c += kCP) {
+        float acc[kNsph];
 #pragma unroll
-        for (int j = 0; j < kNsph; ++j) acc[j] = resid ? ld4(resid + (n * kNsph + j) * C + c) : f4(0.f);
+        for (int j = 0; j < kNsph; ++j) acc[j] = resid ? resid[(n * kNsph + j) * C + c] : 0.f;
         for (int e = e0; e < e1; ++e) {
             float w[kNnz];
             load_coef(coef, e, w);
-            float s = __ldg(env + e);
-            float4 y[kNsph];
+            const float s = __ldg(env + e);
+            float y[kNsph];
             const float* ye = Y + (long long)e * kNsph * C;
 #pragma unroll
-            for (int r = 0; r < kNsph; ++r) y[r] = ld4(ye + r * C + c);
-            rotate_back_acc(w, y, s, acc);
+            for (int r = 0; r < kNsph; ++r) y[r] = ye[r * C + c];
+            rotate_back_acc_s(w, y, s, acc);
         }
 #pragma unroll
-        for (int j = 0; j < kNsph; ++j) st4(out + (n * kNsph + j) * C + c, acc[j]);
+        for (int j = 0; j < kNsph; ++j) out[(n * kNsph + j) * C + c] = acc[j];
     }
 }
 
@@ -476,6 +502,7 @@ static int check_c(int C) {
 using namespace atom;
 
 #define WARP_GRID(n) ceil_div((long long)(n) * 32, 256), 256, 0, (cudaStream_t)stream
+#define CP_GRID(n) (unsigned)(n), kCP, 0, (cudaStream_t)stream
 
 extern "C" int atom_rotate_in(const float* x, const int* src, const int* tgt, const float* coef,
                               int64_t E, int C, const float* rad, int64_t ldr, int rad_col,
@@ -510,7 +537,7 @@ extern "C" int atom_rotate_back_reduce(const float* Y, const float* coef, const 
                                        const float* resid, float* out, void* stream) {
     if (int s = check_c(C)) return s;
     if (N == 0) return ATOM_OK;
-    rotate_back_reduce_kernel<<<WARP_GRID(N)>>>(Y, coef, env, N, C, recv_ptr, resid, out);
+    rotate_back_reduce_kernel<<<CP_GRID(N)>>>(Y, coef, env, N, C, recv_ptr, resid, out);
     ATOM_CHECK_LAUNCH("rotate_back_reduce");
     return ATOM_OK;
 }
