@@ -238,8 +238,11 @@ def test_rmsnorm_sh_fwd_bwd(C):
     close(gx, gref + 1, 1e-4)
 
 
-def test_ln_silu_groups_and_projection():
-    E, G, W = 777, 5, 32
+@pytest.mark.parametrize("W", [32, 128, 256])
+def test_ln_silu_groups_and_projection(W):
+    """W = 32 takes the general warp loop, W = 128 / 256 the register-resident float4 forms
+    (the backward also in place, dX aliasing gY)."""
+    E, G = 777, 5
     X = rnd(E, G * W).requires_grad_()
     gam, bet, gY = 1 + 0.1 * rnd(G * W, seed=1), rnd(G * W, seed=2), rnd(E, G * W, seed=3)
     ref = torch.cat([F.silu(F.layer_norm(X[:, g * W:(g + 1) * W], (W,), gam[g * W:(g + 1) * W],
@@ -252,6 +255,10 @@ def test_ln_silu_groups_and_projection():
     call("atom_ln_silu_bwd", ptr(X.detach()), ptr(gY), E, G * W, G, W, ptr(gam), ptr(bet), 1e-5,
          ptr(dX), s())
     close(dX, gref, 1e-4)
+    gY2 = gY.clone()
+    call("atom_ln_silu_bwd", ptr(X.detach()), ptr(gY2), E, G * W, G, W, ptr(gam), ptr(bet), 1e-5,
+         ptr(gY2), s())
+    close(gY2, gref, 1e-4)
     N, P, C, Q = 50, 9, 64, 42
     inp, M = rnd(N, P, C), rnd(Q, P, seed=6)
     out = torch.empty(N, Q, C, device=dev)

@@ -161,6 +161,110 @@ __global__ void ln_silu_fwd_kernel(const float* __restrict__ X, long long rows, 
     for (int c = lane; c < W; c += 32) yr[c] = silu_f((xr[c] - mean) * rstd * ga[c] + be[c]);
 }
 
+// Register-resident forms for W = 128 * NV: each lane holds its 4 * NV elements of the row as
+// float4s, so X, gY, gamma and beta are each read once (the loops above re-read the row per
+// pass).
+__device__ __forceinline__ float4 ldv4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float f4get(const float4& v, int k) {
+    return k == 0 ? v.x : (k == 1 ? v.y : (k == 2 ? v.z : v.w));
+}
+
+template <int NV>
+__global__ void ln_silu_fwd_v_kernel(const float* __restrict__ X, long long rows, long long ld,
+                                     int groups, const float* __restrict__ gamma,
+                                     const float* __restrict__ beta, float eps,
+                                     float* __restrict__ Y) {
+    constexpr int W = 128 * NV;
+    long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (wid >= rows * groups) return;
+    long long row = wid / groups;
+    int g = (int)(wid - row * groups);
+    const float* xr = X + row * ld + (long long)g * W;
+    float* yr = Y + row * ld + (long long)g * W;
+    float x[NV][4];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const float4 t = ldv4(xr + 128 * i + 4 * lane);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) { x[i][k] = f4get(t, k); s += x[i][k]; }
+    }
+    const float mean = warp_sum(s) / W;
+    float v = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) { const float d = x[i][k] - mean; v = fmaf(d, d, v); }
+    const float rstd = rsqrtf(warp_sum(v) / W + eps);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int c = 128 * i + 4 * lane;
+        const float4 ga = ldv4(gamma + g * W + c), be = ldv4(beta + g * W + c);
+        float o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            o[k] = silu_f((x[i][k] - mean) * rstd * f4get(ga, k) + f4get(be, k));
+        *reinterpret_cast<float4*>(yr + c) = make_float4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// gY and dX may alias (in-place): all of a row is read before any of it is written
+template <int NV>
+__global__ void ln_silu_bwd_v_kernel(const float* __restrict__ X, const float* gY,
+                                     long long rows, long long ld, int groups,
+                                     const float* __restrict__ gamma,
+                                     const float* __restrict__ beta, float eps, float* dX) {
+    constexpr int W = 128 * NV;
+    long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (wid >= rows * groups) return;
+    long long row = wid / groups;
+    int g = (int)(wid - row * groups);
+    const float* xr = X + row * ld + (long long)g * W;
+    const float* gr = gY + row * ld + (long long)g * W;
+    float* dr = dX + row * ld + (long long)g * W;
+    float x[NV][4], gy[NV][4];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int c = 128 * i + 4 * lane;
+        const float4 t = ldv4(xr + c), u = ldv4(gr + c);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) { x[i][k] = f4get(t, k); gy[i][k] = f4get(u, k); s += x[i][k]; }
+    }
+    const float mean = warp_sum(s) / W;
+    float v = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) { const float d = x[i][k] - mean; v = fmaf(d, d, v); }
+    const float rstd = rsqrtf(warp_sum(v) / W + eps);
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int c = 128 * i + 4 * lane;
+        const float4 ga = ldv4(gamma + g * W + c), be = ldv4(beta + g * W + c);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            x[i][k] = (x[i][k] - mean) * rstd;                     // now x-hat
+            const float gk = f4get(ga, k);
+            gy[i][k] = gy[i][k] * dsilu_f(x[i][k] * gk + f4get(be, k)) * gk;
+            s1 += gy[i][k];
+            s2 = fmaf(gy[i][k], x[i][k], s2);
+        }
+    }
+    s1 = warp_sum(s1) / W;
+    s2 = warp_sum(s2) / W;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        float o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[k] = rstd * (gy[i][k] - s1 - x[i][k] * s2);
+        *reinterpret_cast<float4*>(dr + 128 * i + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
+    }
+}
+
 // gY and dX may alias (in-place)
 __global__ void ln_silu_bwd_kernel(const float* __restrict__ X, const float* gY,
                                    long long rows, long long ld, int groups, int W,
@@ -298,7 +402,17 @@ extern "C" int atom_ln_silu_fwd(const float* X, int64_t rows, int64_t ld, int gr
                                 void* stream) {
     ATOM_REQUIRE(groups > 0 && W > 0 && ld >= (int64_t)groups * W, "ln_silu: bad shape");
     if (rows == 0) return ATOM_OK;
-    ln_silu_fwd_kernel<<<WARP_GRID(rows * groups)>>>(X, rows, ld, groups, W, gamma, beta, eps, Y);
+    const bool v4 = ld % 4 == 0 && aligned16(X) && aligned16(Y) && aligned16(gamma) &&
+                    aligned16(beta);
+    if (v4 && W == 128)
+        ln_silu_fwd_v_kernel<1><<<WARP_GRID(rows * groups)>>>(X, rows, ld, groups, gamma, beta,
+                                                              eps, Y);
+    else if (v4 && W == 256)
+        ln_silu_fwd_v_kernel<2><<<WARP_GRID(rows * groups)>>>(X, rows, ld, groups, gamma, beta,
+                                                              eps, Y);
+    else
+        ln_silu_fwd_kernel<<<WARP_GRID(rows * groups)>>>(X, rows, ld, groups, W, gamma, beta,
+                                                         eps, Y);
     ATOM_CHECK_LAUNCH("ln_silu_fwd");
     return ATOM_OK;
 }
@@ -308,8 +422,17 @@ extern "C" int atom_ln_silu_bwd(const float* X, const float* gY, int64_t rows, i
                                 float eps, float* dX, void* stream) {
     ATOM_REQUIRE(groups > 0 && W > 0 && ld >= (int64_t)groups * W, "ln_silu: bad shape");
     if (rows == 0) return ATOM_OK;
-    ln_silu_bwd_kernel<<<WARP_GRID(rows * groups)>>>(X, gY, rows, ld, groups, W, gamma, beta,
-                                                     eps, dX);
+    const bool v4 = ld % 4 == 0 && aligned16(X) && aligned16(gY) && aligned16(dX) &&
+                    aligned16(gamma) && aligned16(beta);
+    if (v4 && W == 128)
+        ln_silu_bwd_v_kernel<1><<<WARP_GRID(rows * groups)>>>(X, gY, rows, ld, groups, gamma,
+                                                              beta, eps, dX);
+    else if (v4 && W == 256)
+        ln_silu_bwd_v_kernel<2><<<WARP_GRID(rows * groups)>>>(X, gY, rows, ld, groups, gamma,
+                                                              beta, eps, dX);
+    else
+        ln_silu_bwd_kernel<<<WARP_GRID(rows * groups)>>>(X, gY, rows, ld, groups, W, gamma,
+                                                         beta, eps, dX);
     ATOM_CHECK_LAUNCH("ln_silu_bwd");
     return ATOM_OK;
 }

@@ -292,6 +292,33 @@ class UMAEngine:
         return dict(name="so2_conv_1 grouped GEMM", ms=t0.elapsed_time(t1) / reps,
                     flop=self.so2_flop(E))
 
+    def time_edge_kernel(self, ws, reps=5):
+        """Average device time of the layer-0 rotate-in edge kernel (Wigner rotation of both
+        node rows times the radial slices, HBM-bound) with its algorithmic bytes per launch:
+        node rows read once, radial slices, coefficients and indices read, A written."""
+        st = torch.cuda.Stream(device=self.device)
+        st.wait_stream(torch.cuda.current_stream())
+        s = st.cuda_stream
+        g = ws.graph
+        E, N, C = g.E, g.N, self.C
+
+        def launch():
+            call("atom_rotate_in", ptr(ws.nb[0]), ptr(g.src), ptr(g.tgt), ptr(ws.coef), E, C,
+                 ptr(ws.RAD), self.ldr, self.rad_off[0], None, ptr(ws.A1), s)
+        with torch.cuda.stream(st):
+            launch()
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record(st)
+            for _ in range(reps):
+                launch()
+            t1.record(st)
+        st.synchronize()
+        torch.cuda.current_stream().wait_stream(st)
+        nbytes = 4 * (N * 9 * C + E * (6 * 2 * C + 35 + 2 + 9 * 2 * C))
+        return dict(name="rotate_in (Wigner rotation x radial)", ms=t0.elapsed_time(t1) / reps,
+                    bytes=nbytes)
+
     # --------------------------------------------------------------------------------- step
     def run(self, ws, pos, forces=True, virial=False, stream=None):
         """One E (+F, +virial) evaluation for ``pos`` [N, 3] (device fp32) on ``ws``'s graph.
