@@ -269,6 +269,25 @@ def test_ln_silu_groups_and_projection(W):
     close(back, torch.einsum("qp,nqc->npc", M, out), 1e-5)
 
 
+def test_node_project_any_width_and_silu_bwd():
+    """node_project with a P that has no compiled specialisation; silu_bwd on a multiple of 4
+    (float4 path), an odd length (scalar path) and in place."""
+    N, P, C, Q = 31, 7, 40, 5
+    inp, M = rnd(N, P, C), rnd(Q, P, seed=6)
+    out = torch.empty(N, Q, C, device=dev)
+    call("atom_node_project", ptr(inp), N, P, C, ptr(M), Q, 0, 0, ptr(out), s())
+    close(out, torch.einsum("qp,npc->nqc", M, inp), 1e-5)
+    for n in (4096, 1001):
+        g, pre = rnd(n, seed=7), rnd(n, seed=8)
+        x = pre.clone().requires_grad_()
+        (ref,) = torch.autograd.grad(F.silu(x), x, g)
+        o = torch.empty(n, device=dev)
+        call("atom_silu_bwd", ptr(g), ptr(pre), n, ptr(o), s())
+        close(o, ref, 1e-5)
+        call("atom_silu_bwd", ptr(g), ptr(pre), n, ptr(g), s())
+        close(g, ref, 1e-5)
+
+
 def test_segment_sum_deterministic():
     v = rnd(100003)
     sp = torch.tensor([0, 5, 5, 70000, 100003], dtype=torch.int32, device=dev)

@@ -307,9 +307,13 @@ __global__ void ln_silu_bwd_kernel(const float* __restrict__ X, const float* gY,
 
 // ------------------------------------------------------------------- per-node projection
 // out[n, q, c] (+)= sum_p M[q, p] in[n, p, c]; one thread per (n, c); M staged in shared memory.
-__global__ void node_project_kernel(const float* __restrict__ in, long long N, int P, int C,
+// PT > 0: P known at compile time, so the P inputs of a thread stay in registers (PT = 0: any
+// P <= 64, runtime loop).
+template <int PT>
+__global__ void node_project_kernel(const float* __restrict__ in, long long N, int Pr, int C,
                                     const float* __restrict__ M, int Q, int trans,
                                     int accumulate, float* __restrict__ out) {
+    const int P = PT > 0 ? PT : Pr;
     extern __shared__ float sm[];   // [Q * P]
     for (int i = threadIdx.x; i < Q * P; i += blockDim.x) {
         int q = i / P, p = i - q * P;
@@ -322,12 +326,16 @@ __global__ void node_project_kernel(const float* __restrict__ in, long long N, i
     int c = (int)(t - n * C);
     const float* xin = in + n * (long long)P * C + c;
     float* o = out + n * (long long)Q * C + c;
-    float v[64];
-    for (int p = 0; p < P; ++p) v[p] = xin[(long long)p * C];
+    float v[PT > 0 ? PT : 64];
+#pragma unroll
+    for (int p = 0; p < (PT > 0 ? PT : 64); ++p)
+        if (PT > 0 || p < P) v[p] = xin[(long long)p * C];
     for (int q = 0; q < Q; ++q) {
         float acc = 0.f;
         const float* mr = sm + q * P;
-        for (int p = 0; p < P; ++p) acc = fmaf(mr[p], v[p], acc);
+#pragma unroll
+        for (int p = 0; p < (PT > 0 ? PT : 64); ++p)
+            if (PT > 0 || p < P) acc = fmaf(mr[p], v[p], acc);
         o[(long long)q * C] = accumulate ? o[(long long)q * C] + acc : acc;
     }
 }
@@ -337,6 +345,16 @@ __global__ void silu_bwd_kernel(const float* g, const float* __restrict__ pre, l
                                 float* out) {
     long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (t < n) out[t] = g[t] * dsilu_f(pre[t]);
+}
+
+// four elements per thread (16-byte aligned arrays, n a multiple of 4); g and out may alias
+__global__ void silu_bwd4_kernel(const float4* g, const float4* __restrict__ pre, long long n4,
+                                 float4* out) {
+    long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n4) return;
+    const float4 a = g[t], b = pre[t];
+    out[t] = make_float4(a.x * dsilu_f(b.x), a.y * dsilu_f(b.y), a.z * dsilu_f(b.z),
+                         a.w * dsilu_f(b.w));
 }
 
 // Deterministic segmented sum: one 256-thread block per segment, strided partials then a
@@ -441,8 +459,15 @@ extern "C" int atom_node_project(const float* in, int64_t N, int P, int C, const
                                  int Q, int trans, int accumulate, float* out, void* stream) {
     ATOM_REQUIRE(P > 0 && P <= 64 && Q > 0 && Q <= 64 && C > 0, "node_project: bad shape");
     if (N == 0) return ATOM_OK;
-    node_project_kernel<<<ceil_div(N * C, 128), 128, Q * P * sizeof(float),
-                          (cudaStream_t)stream>>>(in, N, P, C, M, Q, trans, accumulate, out);
+    const unsigned grid = ceil_div(N * C, 128);
+    const size_t sh = Q * P * sizeof(float);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (P == 9)
+        node_project_kernel<9><<<grid, 128, sh, st>>>(in, N, P, C, M, Q, trans, accumulate, out);
+    else if (P == 42)
+        node_project_kernel<42><<<grid, 128, sh, st>>>(in, N, P, C, M, Q, trans, accumulate, out);
+    else
+        node_project_kernel<0><<<grid, 128, sh, st>>>(in, N, P, C, M, Q, trans, accumulate, out);
     ATOM_CHECK_LAUNCH("node_project");
     return ATOM_OK;
 }
@@ -450,7 +475,12 @@ extern "C" int atom_node_project(const float* in, int64_t N, int P, int C, const
 extern "C" int atom_silu_bwd(const float* g, const float* pre, int64_t n, float* out,
                              void* stream) {
     if (n == 0) return ATOM_OK;
-    silu_bwd_kernel<<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(g, pre, n, out);
+    if (n % 4 == 0 && aligned16(g) && aligned16(pre) && aligned16(out))
+        silu_bwd4_kernel<<<ceil_div(n / 4, 256), 256, 0, (cudaStream_t)stream>>>(
+            reinterpret_cast<const float4*>(g), reinterpret_cast<const float4*>(pre), n / 4,
+            reinterpret_cast<float4*>(out));
+    else
+        silu_bwd_kernel<<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(g, pre, n, out);
     ATOM_CHECK_LAUNCH("silu_bwd");
     return ATOM_OK;
 }
