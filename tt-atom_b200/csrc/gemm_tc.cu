@@ -61,6 +61,7 @@ struct Args {
     const int* idx1;
     const int* idx2;
     int act, accumulate;
+    int bn;              // column-tile width of this launch (multiple of 32, <= the kernel's BN)
     int tma_out;         // epilogue writes C (and Cpre) with TMA stores / reduce-adds
     int nacc;            // tensor-memory accumulators the K stages are spread over (1 or 4)
     Groups g;
@@ -187,6 +188,10 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
         : "memory");
 }
 
+__device__ __forceinline__ float4 ldg4(const float* q) {
+    return *reinterpret_cast<const float4*>(q);
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
     uint32_t r[16];
     asm volatile(
@@ -246,14 +251,13 @@ struct TileInfo {
     int grp, n0, nk;
     long long m0;
 };
-template <int BN>
 __device__ __forceinline__ TileInfo tile_info(const Args& p, int ntn, int t) {
     TileInfo ti;
     int mt = t / ntn, tn = t - mt * ntn;
     int grp = 0;
     while (grp + 1 < p.g.ngroups && tn >= p.g.tile_start[grp + 1]) ++grp;
     ti.grp = grp;
-    ti.n0 = (tn - p.g.tile_start[grp]) * BN;
+    ti.n0 = (tn - p.g.tile_start[grp]) * p.bn;
     ti.m0 = (long long)mt * BM;
     ti.nk = p.g.K[grp] / BK;
     return ti;
@@ -263,7 +267,9 @@ __device__ __forceinline__ TileInfo tile_info(const Args& p, int ntn, int t) {
 // tiles of one row block are adjacent, so concurrently running CTAs share A rows in L2).
 // The epilogue drains the accumulators into registers and releases tensor memory before it
 // computes and stores, so the next tile's MMAs overlap the previous tile's stores.
-template <int BN, int MODE>
+// TAB: the launch adds gathered table rows (T1 / T2) in the TMA-store epilogue; a separate
+// instantiation so that launches without tables keep the lighter epilogue.
+template <int BN, int MODE, bool TAB>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Args p, int ntn,
                    int ntiles) {
@@ -321,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             uint32_t it = 0;
             for (int t = blockIdx.x; t < ntiles && !aborted(); t += gridDim.x) {
-                TileInfo ti = tile_info<BN>(p, ntn, t);
+                TileInfo ti = tile_info(p, ntn, t);
                 const int a_x0 = p.g.a_col[ti.grp];
                 for (int kt = 0; kt < ti.nk; ++kt, ++it) {
                     int s = it % S;
@@ -342,10 +348,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             uint32_t it = 0, j = 0;
             for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++j) {
-                TileInfo ti = tile_info<BN>(p, ntn, t);
+                TileInfo ti = tile_info(p, ntn, t);
                 // a group's last tile multiplies only the columns that remain (N multiple of 16)
                 const int rem = p.g.N[ti.grp] - ti.n0;
-                const uint32_t idesc = idesc_tf32(rem >= BN ? BN : (rem + 15) & ~15);
+                const uint32_t idesc = idesc_tf32(rem >= p.bn ? p.bn : (rem + 15) & ~15);
                 bool ok = !aborted() && mbar_wait(acce, (j & 1u) ^ 1u, 5);
                 if (ok) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 for (int kt = 0; ok && kt < ti.nk; ++kt, ++it) {
@@ -407,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t it = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < ntiles && !aborted(); t += gridDim.x) {
-                TileInfo ti = tile_info<BN>(p, ntn, t);
+                TileInfo ti = tile_info(p, ntn, t);
                 for (int kt = 0; kt < ti.nk; ++kt, ++it) {
                     int s = it % S;
                     uint32_t ph = (it / S) & 1u;
@@ -451,13 +457,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t j = 0;
         bool pending = false;            // a TMA store from this warp's buffer may be reading it
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++j) {
-            TileInfo ti = tile_info<BN>(p, ntn, t);
+            TileInfo ti = tile_info(p, ntn, t);
             bool ok = mbar_wait(accf, j & 1u, 4) && !aborted();
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const int N = p.g.N[ti.grp];
-            const bool active = ti.n0 + cbase < N;
+            const bool active = ti.n0 + cbase < N && cbase < p.bn;
             // drain the accumulators into registers (partial sums added with round-to-nearest):
             // mode 1 the K-stage accumulators in use, mode 2 main + corrections
             const int nused = MODE == 2 ? 2 : (ti.nk < p.nacc ? ti.nk : p.nacc);
@@ -482,15 +488,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!active) continue;
             const float* bias = p.g.bias[ti.grp];
             if (p.tma_out) {
-                // each 32 x 32 block: bias (+ SiLU) applied in registers, written 128-byte
-                // swizzled into this warp's buffer, stored by one lane with TMA (reduce-add when
-                // accumulating); the tensor map clips rows >= M, cols >= N
+                // each 32 x 32 block: bias (+ gathered table rows) (+ SiLU) applied in registers,
+                // written 128-byte swizzled into this warp's buffer, stored by one lane with TMA
+                // (reduce-add when accumulating); the tensor map clips rows >= M, cols >= N
                 const int y0 = (int)(ti.m0 + quarter * 32);
                 if (y0 >= p.M) continue;
+                // this thread's output row and its rows of the gathered tables (one per lane)
+                const long long row = (long long)y0 + lane;
+                const float* t1row = nullptr;
+                const float* t2row = nullptr;
+                if (TAB && row < p.M) {
+                    const int tc = p.g.t_col[ti.grp];
+                    if (p.T1) t1row = p.T1 + (long long)p.idx1[row] * p.ldt + tc;
+                    if (p.T2) t2row = p.T2 + (long long)p.idx2[row] * p.ldt + tc;
+                }
 #pragma unroll
                 for (int c0 = 0; c0 < EC; c0 += 32) {
                     const int x0 = ti.n0 + cbase + c0;
-                    if (x0 >= N) break;
+                    if (x0 >= N || cbase + c0 >= p.bn) break;
 #pragma unroll 1
                     for (int pass = 0; pass < 2; ++pass) {
                         // pass 0: pre-activation to Cpre (SiLU launches that keep it)
@@ -500,17 +515,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                             asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
                         __syncwarp();
                         float4* buf = reinterpret_cast<float4*>(mybuf);
+                        if (TAB) {
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) {
-                            float e[4];
+                            for (int q = 0; q < 8; ++q) {
+                                // columns x0 + 4q .. + 3 are all inside or all outside the group
+                                // (N is a multiple of 4 on this path)
+                                const bool in = x0 + 4 * q < N;
+                                float4 a1 = make_float4(0.f, 0.f, 0.f, 0.f), a2 = a1;
+                                if (t1row && in) a1 = ldg4(t1row + x0 + 4 * q);
+                                if (t2row && in) a2 = ldg4(t2row + x0 + 4 * q);
+                                const float t1v[4] = {a1.x, a1.y, a1.z, a1.w};
+                                const float t2v[4] = {a2.x, a2.y, a2.z, a2.w};
+                                float e[4];
 #pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                const int jj = 4 * q + k;
-                                const float b = (bias && x0 + jj < N) ? bias[x0 + jj] : 0.f;
-                                const float y = v[c0 + jj] + b;
-                                e[k] = silu ? silu_f(y) : y;
+                                for (int k = 0; k < 4; ++k) {
+                                    const int jj = 4 * q + k;
+                                    const float b = (bias && in) ? bias[x0 + jj] : 0.f;
+                                    const float y = (v[c0 + jj] + b + t1v[k]) + t2v[k];
+                                    e[k] = silu ? silu_f(y) : y;
+                                }
+                                buf[lane * 8 + (q ^ (lane & 7))] =
+                                    make_float4(e[0], e[1], e[2], e[3]);
                             }
-                            buf[lane * 8 + (q ^ (lane & 7))] = make_float4(e[0], e[1], e[2], e[3]);
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                float e[4];
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) {
+                                    const int jj = 4 * q + k;
+                                    const float b = (bias && x0 + jj < N) ? bias[x0 + jj] : 0.f;
+                                    const float y = v[c0 + jj] + b;
+                                    e[k] = silu ? silu_f(y) : y;
+                                }
+                                buf[lane * 8 + (q ^ (lane & 7))] =
+                                    make_float4(e[0], e[1], e[2], e[3]);
+                            }
                         }
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                         __syncwarp();
@@ -534,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int jj = 0; jj < 32; ++jj) st[lane * 32 + (jj ^ lane)] = v[c0 + jj];
                 __syncwarp();
                 const int n = ti.n0 + cbase + c0 + lane;
-                const bool nok = n < N;
+                const bool nok = n < N && cbase + c0 + lane < p.bn;
                 const float bn = (bias && nok) ? bias[n] : 0.f;
                 for (int r = 0; r < 32; ++r) {
                     const long long m = mrow0 + r;
@@ -618,9 +658,12 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
     using CF = Cfg<BN, MODE>;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, MODE>,
+        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, MODE, false>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)CF::kSmem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_tc_kernel<BN, MODE, true>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)CF::kSmem);
         if (e != cudaSuccess) {
             set_error("gemm_tc: cannot reserve %u bytes of shared memory: %s", CF::kSmem,
                       cudaGetErrorString(e));
@@ -636,6 +679,24 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
     p.idx1 = idx1; p.idx2 = idx2; p.act = act; p.accumulate = accumulate;
     p.nacc = MODE == 2 ? 2 : g_nacc;
     p.g.ngroups = g->ngroups;
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    // column-tile width: the full BN unless that leaves SMs without a tile (few rows, e.g.
+    // node-level GEMMs); then the widest multiple of 32 (down to 64) that gives every SM one
+    const long long mblocks = ceil_div(M, BM);
+    auto count_tiles = [&](int w) {
+        long long t = 0;
+        for (int i = 0; i < g->ngroups; ++i) t += ceil_div(g->N[i], w);
+        return t * mblocks;
+    };
+    int bn = BN;
+    if (count_tiles(BN) < nsm)
+        for (int w = BN - 32; w >= 64; w -= 32) {
+            bn = w;
+            if (count_tiles(w) >= nsm) break;
+        }
+    p.bn = bn;
     int tiles = 0;
     for (int i = 0; i < g->ngroups; ++i) {
         p.g.a_col[i] = g->a_col[i];
@@ -645,18 +706,21 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
         p.g.t_col[i] = g->t_col[i];
         p.g.bias[i] = g->bias[i];
         p.g.tile_start[i] = tiles;
-        tiles += ceil_div(g->N[i], BN);
+        tiles += ceil_div(g->N[i], bn);
         if (int s = make_map(&maps.b[i], g->Bt[i], g->K[i], g->N[i], g->K[i], BN)) return s;
         if (MODE == 2)
             if (int s = make_map(&maps.l[i], g->Bt_lo[i], g->K[i], g->N[i], g->K[i], BN)) return s;
     }
     p.g.tile_start[g->ngroups] = tiles;
-    // TMA-store epilogue: no gathered tables, 16-byte aligned column blocks and rows. A group's
-    // width must be a multiple of 4 columns too: the store clips at 16-byte granularity, so a
-    // 130-column group would also get columns 130 and 131 written (measured on B200).
-    bool tma_out = !T1 && !T2 && ldc % 4 == 0 && aligned16(C) && (!Cpre || aligned16(Cpre));
+    // TMA-store epilogue: 16-byte aligned column blocks, rows and gathered-table rows. A
+    // group's width must be a multiple of 4 columns too: the store clips at 16-byte granularity,
+    // so a 130-column group would also get columns 130 and 131 written (measured on B200).
+    bool tma_out = ldc % 4 == 0 && aligned16(C) && (!Cpre || aligned16(Cpre)) &&
+                   ((!T1 && !T2) || ldt % 4 == 0) && (!T1 || aligned16(T1)) &&
+                   (!T2 || aligned16(T2));
     for (int i = 0; i < g->ngroups; ++i)
-        tma_out = tma_out && g->c_col[i] % 4 == 0 && g->N[i] % 4 == 0 && g->N[i] >= 32;
+        tma_out = tma_out && g->c_col[i] % 4 == 0 && g->N[i] % 4 == 0 && g->N[i] >= 32 &&
+                  ((!T1 && !T2) || g->t_col[i] % 4 == 0);
     p.tma_out = tma_out ? 1 : 0;
     if (tma_out) {
         for (int i = 0; i < g->ngroups; ++i) {
@@ -671,11 +735,13 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
         set_error("gemm_tc: too many tiles");
         return ATOM_ERR_ARG;
     }
-    int dev = 0, nsm = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     const int grid = (int)(ntiles < nsm ? ntiles : nsm);
-    gemm_tc_kernel<BN, MODE><<<grid, kThreads, CF::kSmem, st>>>(maps, p, tiles, (int)ntiles);
+    if (tma_out && (T1 || T2))
+        gemm_tc_kernel<BN, MODE, true><<<grid, kThreads, CF::kSmem, st>>>(maps, p, tiles,
+                                                                         (int)ntiles);
+    else
+        gemm_tc_kernel<BN, MODE, false><<<grid, kThreads, CF::kSmem, st>>>(maps, p, tiles,
+                                                                          (int)ntiles);
     return check_launch("gemm_tc");
 }
 

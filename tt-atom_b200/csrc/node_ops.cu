@@ -75,7 +75,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
     if (n >= N) return;
     const float* xn = x + n * kNsph * C;
     const float* gn = g + n * kNsph * C;
-    float v[kNsph][CPL];
+    // x, the adjoint and the affine weights are all loaded up front (one memory round trip)
+    float v[kNsph][CPL], u[kNsph][CPL];
     float s0 = 0.f;
 #pragma unroll
     for (int j = 0; j < kNsph; ++j)
@@ -83,6 +84,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
         for (int q = 0; q < CPL; ++q) {
             int c = lane + 32 * q;
             v[j][q] = c < C ? xn[j * C + c] : 0.f;
+            u[j][q] = c < C ? gn[j * C + c] * aw[coef_deg(j) * C + c] : 0.f;
         }
 #pragma unroll
     for (int q = 0; q < CPL; ++q) s0 += v[0][q];
@@ -98,7 +100,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
         for (int q = 0; q < CPL; ++q) {
             int c = lane + 32 * q;
             t = fmaf(v[j][q], v[j][q], t);
-            if (c < C) S = fmaf(gn[j * C + c] * aw[coef_deg(j) * C + c], v[j][q], S);
+            if (c < C) S = fmaf(u[j][q], v[j][q], S);
         }
         ss = fmaf(bal_w(j), t, ss);
     }
@@ -117,8 +119,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
                 if (j == 0) gr0[q] = 0.f;
                 continue;
             }
-            float u = gn[j * C + c] * aw[coef_deg(j) * C + c];
-            float r = fn * u - k3 * bal_w(j) * v[j][q];
+            float r = fn * u[j][q] - k3 * bal_w(j) * v[j][q];
             if (j == 0) {
                 gr0[q] = r;
                 gsum0 += r;
