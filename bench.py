@@ -60,8 +60,8 @@ def dist_env():
     return ws, rank, local
 
 
-class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+class _SmiSampler:
+    """nvidia-smi clock / throttle sampling (fallback when NVML bindings are missing)."""
 
     def __init__(self, index):
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
@@ -97,7 +97,67 @@ class ClockSampler:
                 if v.lower().startswith("active"):
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi"}
+
+
+class ClockSampler:
+    """SM clock, max clock and clock-event (throttle) reasons of this rank's GPU, polled every
+    10 ms through NVML (read-only queries) in a background thread while the timed region runs.
+    The constructor returns once the first sample is taken, so even a short timed region is
+    covered; ``stop`` adds a final sample."""
+
+    _REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown", 0x8),
+                ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+                ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+                ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap", 0x4))
+
+    def __new__(cls, index):
+        try:
+            import pynvml  # noqa: F401
+        except ImportError:
+            return _SmiSampler(index)
+        return super().__new__(cls)
+
+    def __init__(self, index):
+        import threading
+
+        import pynvml as nv
+        self.nv = nv
+        nv.nvmlInit()
+        try:
+            uuid = str(torch.cuda.get_device_properties(index).uuid)
+            self.h = nv.nvmlDeviceGetHandleByUUID(("GPU-" + uuid).encode())
+        except Exception:
+            self.h = nv.nvmlDeviceGetHandleByIndex(index)
+        self.bits = [(nm, getattr(nv, attr, val)) for nm, attr, val in self._REASONS]
+        self.sm, self.reasons = [], set()
+        self.mx = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+        self.done = threading.Event()
+        self._sample()
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+
+    def _sample(self):
+        nv = self.nv
+        self.sm.append(float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)))
+        try:
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except AttributeError:
+            r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+        for nm, bit in self.bits:
+            if r & bit:
+                self.reasons.add(nm)
+
+    def _run(self):
+        while not self.done.wait(0.01):
+            self._sample()
+
+    def stop(self):
+        self._sample()
+        self.done.set()
+        self.t.join()
+        return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": float(self.mx),
+                "reasons": sorted(self.reasons), "samples": len(self.sm), "source": "nvml"}
 
 
 def make_workload(device, cells=(10, 10, 5), precision="3xtf32"):
@@ -213,12 +273,14 @@ def run_screen(args):
     torch.cuda.synchronize()
     if ws_n > 1:
         dist.barrier()
+    clk = ClockSampler(local)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(args.steps):
         step()
     t1.record()
     torch.cuda.synchronize()
+    clocks = clk.stop()
     ms = torch.tensor([t0.elapsed_time(t1)], device=device)
     if ws_n > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
@@ -235,7 +297,8 @@ def run_screen(args):
                        "batch": bs, "precision": args.precision,
                        "parallelism": f"partition x{ws_n}, no collectives",
                        "timing": "end to end through evaluate_batch (host inputs, GPU "
-                                 "neighbour lists, host results)"}}))
+                                 "neighbour lists, host results)"},
+            "clocks": clocks}))
     if ws_n > 1:
         dist.destroy_process_group()
 
