@@ -25,6 +25,8 @@ from __future__ import annotations
 
 import math
 
+import numpy as np
+
 import torch
 
 from . import _lib as L
@@ -180,6 +182,19 @@ class UMAEngine:
         self.rad3_bw = _Groups([dict(a_col=self.rad_off[g], K=r_out[g], c_col=g * EC, N=EC,
                                      B=d(f3[g])) for g in range(G)])
         self.rad1_bw = _Groups([dict(a_col=0, K=G * EC, c_col=0, N=NB, B=self.W0g_cat)])
+        # one group at a time, for receiver-chunked execution (a layer's radial function is
+        # recomputed per chunk instead of storing [E, 6528] radial outputs and their adjoint)
+        self.radg = []
+        for g in range(G):
+            self.radg.append(dict(
+                r1=_Groups([dict(a_col=0, K=NB, c_col=0, N=EC, B=d(w0g[g].t()), t_col=g * EC)]),
+                r2=_Groups([dict(a_col=0, K=EC, c_col=0, N=EC, B=d(f2[g].t()), bias=d(f2b[g]))]),
+                r3=_Groups([dict(a_col=0, K=EC, c_col=0, N=r_out[g], B=d(f3[g].t()),
+                                 bias=d(f3b[g]))]),
+                r3_bw=_Groups([dict(a_col=0, K=r_out[g], c_col=0, N=EC, B=d(f3[g]))]),
+                r2_bw=_Groups([dict(a_col=0, K=EC, c_col=0, N=EC, B=d(f2[g]))]),
+                r1_bw=_Groups([dict(a_col=0, K=EC, c_col=0, N=NB, B=d(w0g[g]))]),
+                width=r_out[g]))
         for i in range(NL):
             assert r_out[i] == 12 * C, "so2_conv_1 radial output must be 6 * 2C"
         assert r_out[NL] == 3 * C, "edge-degree radial output must be 3C"
@@ -254,8 +269,11 @@ class UMAEngine:
         call("atom_gemm", ptr(A), lda, M, groups.struct, ptr(Cout), ldc, ptr(Cpre), ptr(T1),
              ptr(T2), ptr(idx1), ptr(idx2), ldt, act, accumulate, self.precision, stream)
 
-    def workspace(self, graph, sys_emb):
-        return Workspace(self, graph, sys_emb)
+    def workspace(self, graph, sys_emb, chunk_edges=None):
+        """Device buffers for one topology. With ``chunk_edges`` the edge stages run over
+        contiguous receiver chunks of at most that many edges (recomputed in the reverse
+        pass), so per-edge storage is the geometry only; see ``Workspace``."""
+        return Workspace(self, graph, sys_emb, chunk_edges=chunk_edges)
 
     def launches_per_step(self, ws, forces=True, virial=True):
         """Number of this library's kernels one ``run`` launches (counted, not estimated)."""
@@ -342,32 +360,46 @@ class UMAEngine:
         call("atom_edge_geometry", ptr(ws.pos), ptr(g.src), ptr(g.tgt), ptr(g.img),
              ptr(g.shifts), E, self.jd1, self.jd2, self.perm9, ptr(self.offset), NB, self.coeff,
              self.cutoff, ptr(ws.coef), ptr(ws.gauss), ptr(ws.env), ptr(ws.ev), None, s)
-        # ---------------- radial MLPs (all groups at once)
-        self._gemm(ws.gauss, NB, E, self.rad1, ws.R0, G * EC, T1=self.Tsrc, T2=self.Ttgt,
-                   idx1=g.zs, idx2=g.zt, ldt=G * EC, stream=s)
-        call("atom_ln_silu_fwd", ptr(ws.R0), E, G * EC, G, EC, ptr(self.ln1g), ptr(self.ln1b),
-             1e-5, ptr(ws.H1), s)
-        self._gemm(ws.H1, G * EC, E, self.rad2, ws.R1, G * EC, stream=s)
-        call("atom_ln_silu_fwd", ptr(ws.R1), E, G * EC, G, EC, ptr(self.ln2g), ptr(self.ln2b),
-             1e-5, ptr(ws.H2), s)
-        self._gemm(ws.H2, G * EC, E, self.rad3, ws.RAD, self.ldr, stream=s)
-        # ---------------- edge-degree node init
-        ede = ws.RAD[:, self.rad_off[self.NL]:]
-        call("atom_edge_degree_fwd", ptr(ede), self.ldr, ptr(ws.coef), ptr(ws.env), ptr(ws.l0),
-             N, C, ptr(g.recv_ptr), 5.0, ptr(ws.x[0]), s)
+        if ws.chunks is None:
+            # ---------------- radial MLPs (all groups at once)
+            self._gemm(ws.gauss, NB, E, self.rad1, ws.R0, G * EC, T1=self.Tsrc, T2=self.Ttgt,
+                       idx1=g.zs, idx2=g.zt, ldt=G * EC, stream=s)
+            call("atom_ln_silu_fwd", ptr(ws.R0), E, G * EC, G, EC, ptr(self.ln1g),
+                 ptr(self.ln1b), 1e-5, ptr(ws.H1), s)
+            self._gemm(ws.H1, G * EC, E, self.rad2, ws.R1, G * EC, stream=s)
+            call("atom_ln_silu_fwd", ptr(ws.R1), E, G * EC, G, EC, ptr(self.ln2g),
+                 ptr(self.ln2b), 1e-5, ptr(ws.H2), s)
+            self._gemm(ws.H2, G * EC, E, self.rad3, ws.RAD, self.ldr, stream=s)
+            # ---------------- edge-degree node init
+            ede = ws.RAD[:, self.rad_off[self.NL]:]
+            call("atom_edge_degree_fwd", ptr(ede), self.ldr, ptr(ws.coef), ptr(ws.env),
+                 ptr(ws.l0), N, C, ptr(g.recv_ptr), 5.0, ptr(ws.x[0]), s)
+        else:
+            for ch in ws.chunks:
+                self._radial_group_fwd(ws, self.NL, ch, s)
+                call("atom_edge_degree_fwd", ptr(ws.RAD), ws.RAD.shape[1],
+                     ptr(ws.coef[ch.e0:]), ptr(ws.env[ch.e0:]), ptr(ws.l0[ch.n0:]),
+                     ch.n1 - ch.n0, C, ptr(ch.rp_local), 5.0, ptr(ws.x[0][ch.n0:]), s)
         yield ("x", 0)
         # ---------------- blocks
         for i, b in enumerate(self.blocks):
             x, nb = ws.x[i], ws.nb[i]
             call("atom_rmsnorm_sh_fwd", ptr(x), N, C, ptr(b["n1w"]), ptr(b["n1b"]),
                  ptr(ws.sysn), 1e-5, ptr(nb), s)
-            call("atom_rotate_in", ptr(nb), ptr(g.src), ptr(g.tgt), ptr(ws.coef), E, C,
-                 ptr(ws.RAD), self.ldr, self.rad_off[i], None, ptr(ws.A1), s)
-            self._gemm(ws.A1, 18 * C, E, b["so2_1"], ws.Y1[i], 11 * H, stream=s)
-            call("atom_gate_fwd", ptr(ws.Y1[i]), E, H, ptr(ws.Gt), s)
-            self._gemm(ws.Gt, 9 * H, E, b["so2_2"], ws.Y2[i], 9 * C, stream=s)
-            call("atom_rotate_back_reduce", ptr(ws.Y2[i]), ptr(ws.coef), ptr(ws.env), N, C,
-                 ptr(g.recv_ptr), ptr(x), ptr(ws.xm[i]), s)
+            if ws.chunks is None:
+                call("atom_rotate_in", ptr(nb), ptr(g.src), ptr(g.tgt), ptr(ws.coef), E, C,
+                     ptr(ws.RAD), self.ldr, self.rad_off[i], None, ptr(ws.A1), s)
+                self._gemm(ws.A1, 18 * C, E, b["so2_1"], ws.Y1[i], 11 * H, stream=s)
+                call("atom_gate_fwd", ptr(ws.Y1[i]), E, H, ptr(ws.Gt), s)
+                self._gemm(ws.Gt, 9 * H, E, b["so2_2"], ws.Y2[i], 9 * C, stream=s)
+                call("atom_rotate_back_reduce", ptr(ws.Y2[i]), ptr(ws.coef), ptr(ws.env), N, C,
+                     ptr(g.recv_ptr), ptr(x), ptr(ws.xm[i]), s)
+            else:
+                for ch in ws.chunks:
+                    self._chunk_edge_fwd(ws, i, ch, s)
+                    call("atom_rotate_back_reduce", ptr(ws.Y2[0]), ptr(ws.coef[ch.e0:]),
+                         ptr(ws.env[ch.e0:]), ch.n1 - ch.n0, C, ptr(ch.rp_local),
+                         ptr(x[ch.n0:]), ptr(ws.xm[i][ch.n0:]), s)
             call("atom_rmsnorm_sh_fwd", ptr(ws.xm[i]), N, C, ptr(b["n2w"]), ptr(b["n2b"]), None,
                  1e-5, ptr(ws.n2), s)
             if self.ff == "grid":
@@ -411,6 +443,8 @@ class UMAEngine:
         P = self.npts
         ws.g_coef.zero_()
         ws.g_env.zero_()
+        if ws.chunks is not None:
+            ws.g_gauss.zero_()          # accumulated group by group, chunk by chunk
         # ---------------- energy head (seed dE/d e_node = 1)
         call("atom_silu_bwd", ptr(ws.eh4_rows), ptr(ws.e2p), N * H, ptr(ws.ge2), s)
         self._gemm(ws.ge2, H, N, self.eh2_bw, ws.ge1, H, stream=s)
@@ -446,6 +480,12 @@ class UMAEngine:
             call("atom_rmsnorm_sh_bwd", ptr(ws.xm[i]), ptr(ws.gn), N, C, ptr(b["n2w"]), 1e-5, 1,
                  ptr(ws.gx), s)
             # edgewise VJP (gx now holds the adjoint of the block's mid point)
+            if ws.chunks is not None:
+                self._chunked_edge_bwd(ws, i, s)
+                call("atom_rmsnorm_sh_bwd", ptr(ws.x[i]), ptr(ws.gn), N, C, ptr(b["n1w"]), 1e-5,
+                     1, ptr(ws.gx), s)
+                yield ("gx", i)
+                continue
             call("atom_rotate_back_bwd", ptr(ws.gx), ptr(g.tgt), ptr(ws.coef), ptr(ws.env),
                  ptr(ws.Y2[i]), E, C, ptr(ws.gY2), ptr(ws.g_env), ptr(ws.g_coef), s)
             self._gemm(ws.gY2, 9 * C, E, b["so2_2_bw"], ws.Gt, 9 * H, stream=s)
@@ -460,6 +500,25 @@ class UMAEngine:
             call("atom_rmsnorm_sh_bwd", ptr(ws.x[i]), ptr(ws.gn), N, C, ptr(b["n1w"]), 1e-5, 1,
                  ptr(ws.gx), s)
             yield ("gx", i)
+        if ws.chunks is not None:
+            # edge-degree VJP and its radial group, chunk by chunk (the layers' radial groups
+            # were back-propagated inside their blocks)
+            for ch in ws.chunks:
+                Ec = ch.e1 - ch.e0
+                self._radial_group_fwd(ws, NL, ch, s)
+                call("atom_edge_degree_bwd", ptr(ws.gx), ptr(g.tgt[ch.e0:]), ptr(ws.RAD),
+                     ws.RAD.shape[1], ptr(ws.coef[ch.e0:]), ptr(ws.env[ch.e0:]), Ec, C, 5.0,
+                     ptr(ws.gRAD), ws.gRAD.shape[1], ptr(ws.g_env[ch.e0:]),
+                     ptr(ws.g_coef[ch.e0:]), s)
+                self._radial_group_bwd(ws, NL, ch, s)
+        else:
+            self._radial_bwd_all(ws, s)
+        # ---------------- geometry VJP, forces, virial
+        yield from self._geometry_bwd(ws, virial, s)
+
+    def _radial_bwd_all(self, ws, s):
+        g = ws.graph
+        E, C, EC, NB, G, NL = g.E, self.C, self.EC, self.NB, self.G, self.NL
         # ---------------- edge-degree VJP (gx = dE/dx_init)
         ede_off = self.rad_off[NL]
         call("atom_edge_degree_bwd", ptr(ws.gx), ptr(g.tgt), ptr(ws.RAD[:, ede_off:]), self.ldr,
@@ -473,7 +532,72 @@ class UMAEngine:
         call("atom_ln_silu_bwd", ptr(ws.R0), ptr(ws.H1), E, G * EC, G, EC, ptr(self.ln1g),
              ptr(self.ln1b), 1e-5, ptr(ws.H1), s)
         self._gemm(ws.H1, G * EC, E, self.rad1_bw, ws.g_gauss, NB, stream=s)
-        # ---------------- geometry VJP, forces, virial
+
+    # ------------------------------------------------------- receiver-chunked edge stages
+    def _radial_group_fwd(self, ws, grp, ch, s):
+        """Radial function of group ``grp`` (layer grp, or the edge-degree group) for the edges
+        of chunk ``ch``: R0 -> LN+SiLU -> R1 -> LN+SiLU -> ws.RAD[:Ec, :width]."""
+        g, EC, NB = ws.graph, self.EC, self.NB
+        rg, Ec, lo = self.radg[grp], ch.e1 - ch.e0, grp * EC
+        self._gemm(ws.gauss[ch.e0:], NB, Ec, rg["r1"], ws.R0, EC, T1=self.Tsrc, T2=self.Ttgt,
+                   idx1=g.zs[ch.e0:], idx2=g.zt[ch.e0:], ldt=self.G * EC, stream=s)
+        call("atom_ln_silu_fwd", ptr(ws.R0), Ec, EC, 1, EC, ptr(self.ln1g[lo:]),
+             ptr(self.ln1b[lo:]), 1e-5, ptr(ws.H1), s)
+        self._gemm(ws.H1, EC, Ec, rg["r2"], ws.R1, EC, stream=s)
+        call("atom_ln_silu_fwd", ptr(ws.R1), Ec, EC, 1, EC, ptr(self.ln2g[lo:]),
+             ptr(self.ln2b[lo:]), 1e-5, ptr(ws.H2), s)
+        self._gemm(ws.H2, EC, Ec, rg["r3"], ws.RAD, ws.RAD.shape[1], stream=s)
+
+    def _radial_group_bwd(self, ws, grp, ch, s):
+        """Adjoint of ``_radial_group_fwd`` (run just before, same chunk) from ws.gRAD down
+        to the Gaussian basis, added into g_gauss of the chunk's edges."""
+        EC, NB = self.EC, self.NB
+        rg, Ec, lo = self.radg[grp], ch.e1 - ch.e0, grp * EC
+        self._gemm(ws.gRAD, ws.gRAD.shape[1], Ec, rg["r3_bw"], ws.H2, EC, stream=s)
+        call("atom_ln_silu_bwd", ptr(ws.R1), ptr(ws.H2), Ec, EC, 1, EC, ptr(self.ln2g[lo:]),
+             ptr(self.ln2b[lo:]), 1e-5, ptr(ws.H2), s)
+        self._gemm(ws.H2, EC, Ec, rg["r2_bw"], ws.H1, EC, stream=s)
+        call("atom_ln_silu_bwd", ptr(ws.R0), ptr(ws.H1), Ec, EC, 1, EC, ptr(self.ln1g[lo:]),
+             ptr(self.ln1b[lo:]), 1e-5, ptr(ws.H1), s)
+        self._gemm(ws.H1, EC, Ec, rg["r1_bw"], ws.g_gauss[ch.e0:], NB, accumulate=1, stream=s)
+
+    def _chunk_edge_fwd(self, ws, i, ch, s):
+        """Layer i's edge chain for chunk ch up to the rotate-back input ws.Y2[0] (rows of
+        the chunk's edges): radial group, rotate-in, so2_1, gate, so2_2."""
+        g, C, H, b = ws.graph, self.C, self.H, self.blocks[i]
+        Ec = ch.e1 - ch.e0
+        self._radial_group_fwd(ws, i, ch, s)
+        call("atom_rotate_in", ptr(ws.nb[i]), ptr(g.src[ch.e0:]), ptr(g.tgt[ch.e0:]),
+             ptr(ws.coef[ch.e0:]), Ec, C, ptr(ws.RAD), ws.RAD.shape[1], 0, None, ptr(ws.A1), s)
+        self._gemm(ws.A1, 18 * C, Ec, b["so2_1"], ws.Y1[0], 11 * H, stream=s)
+        call("atom_gate_fwd", ptr(ws.Y1[0]), Ec, H, ptr(ws.Gt), s)
+        self._gemm(ws.Gt, 9 * H, Ec, b["so2_2"], ws.Y2[0], 9 * C, stream=s)
+
+    def _chunked_edge_bwd(self, ws, i, s):
+        """Edgewise VJP of layer i, chunk by chunk (each chunk's forward chain recomputed):
+        ws.gx (adjoint of the block's mid point) -> ws.gn (adjoint of nb[i], accumulated over
+        chunks in chunk order), and the chunk's coefficient, envelope and Gaussian adjoints."""
+        g, N, C, H, b = ws.graph, ws.graph.N, self.C, self.H, self.blocks[i]
+        ws.gn.zero_()
+        for ch in ws.chunks:
+            Ec = ch.e1 - ch.e0
+            self._chunk_edge_fwd(ws, i, ch, s)
+            call("atom_rotate_back_bwd", ptr(ws.gx), ptr(g.tgt[ch.e0:]), ptr(ws.coef[ch.e0:]),
+                 ptr(ws.env[ch.e0:]), ptr(ws.Y2[0]), Ec, C, ptr(ws.gY2), ptr(ws.g_env[ch.e0:]),
+                 ptr(ws.g_coef[ch.e0:]), s)
+            self._gemm(ws.gY2, 9 * C, Ec, b["so2_2_bw"], ws.Gt, 9 * H, stream=s)
+            call("atom_gate_bwd", ptr(ws.Y1[0]), ptr(ws.Gt), Ec, H, ptr(ws.gY1), s)
+            self._gemm(ws.gY1, 11 * H, Ec, b["so2_1_bw"], ws.A1, 18 * C, stream=s)
+            call("atom_rotate_in_bwd_edge", ptr(ws.A1), None, ptr(ws.RAD), ws.RAD.shape[1], 0,
+                 ptr(ws.nb[i]), ptr(g.src[ch.e0:]), ptr(g.tgt[ch.e0:]), ptr(ws.coef[ch.e0:]),
+                 Ec, C, ptr(ws.grot), ptr(ws.gRAD), ptr(ws.g_coef[ch.e0:]), s)
+            call("atom_rotate_in_bwd_node", ptr(ws.grot), ptr(ws.coef[ch.e0:]), N, C,
+                 ptr(ch.rp_full), ptr(ch.send_ptr), ptr(ch.send_eid), 1, ptr(ws.gn), s)
+            self._radial_group_bwd(ws, i, ch, s)
+
+    def _geometry_bwd(self, ws, virial, s):
+        g = ws.graph
+        N, E, NB = g.N, g.E, self.NB
         call("atom_edge_geometry_bwd", ptr(ws.pos), ptr(g.src), ptr(g.tgt), ptr(g.img),
              ptr(g.shifts), E, self.jd1, self.jd2, self.perm9, ptr(self.offset), NB, self.coeff,
              self.cutoff, ptr(ws.g_coef), ptr(ws.gauss), ptr(ws.g_gauss), ptr(ws.g_env),
@@ -484,25 +608,77 @@ class UMAEngine:
         yield ("forces", None)
 
 
-class Workspace:
-    """Every device buffer of one step for one graph topology."""
+class _Chunk:
+    """One receiver chunk: nodes [n0, n1) and their received edges [e0, e1) (edges are
+    receiver-major), the chunk's receiver CSR relative to e0 (local: nodes n0..n1; full: all
+    N nodes, empty outside the chunk) and its sender CSR over chunk-local edge ids."""
 
-    def __init__(self, eng, graph, sys_emb):
+    def __init__(self, n0, n1, e0, e1):
+        self.n0, self.n1, self.e0, self.e1 = n0, n1, e0, e1
+
+
+def _plan_chunks(graph, chunk_edges, stream):
+    """Split the receivers into contiguous node ranges of at most ``chunk_edges`` received
+    edges each (a node is never split)."""
+    N = graph.N
+    rp = graph.recv_ptr.long().cpu().numpy()
+    dev = graph.src.device
+    rp_dev = graph.recv_ptr.long()
+    chunks, n0 = [], 0
+    while n0 < N:
+        n1 = int(np.searchsorted(rp, rp[n0] + chunk_edges, side="right")) - 1
+        n1 = min(max(n1, n0 + 1), N)
+        e0, e1 = int(rp[n0]), int(rp[n1])
+        if e1 - e0 > chunk_edges:
+            raise ValueError(f"node {n0} receives {e1 - e0} edges, more than chunk_edges "
+                             f"= {chunk_edges}")
+        ch = _Chunk(n0, n1, e0, e1)
+        Ec = e1 - e0
+        ch.rp_local = (rp_dev[n0:n1 + 1] - e0).to(torch.int32).contiguous()
+        ch.rp_full = (rp_dev - e0).clamp(0, Ec).to(torch.int32).contiguous()
+        ch.send_ptr = torch.empty(N + 1, dtype=torch.int32, device=dev)
+        ch.send_eid = torch.empty(max(Ec, 1), dtype=torch.int32, device=dev)
+        scratch = torch.empty(max(N, 1), dtype=torch.int32, device=dev)
+        call("atom_sender_csr", ptr(graph.src[e0:]), Ec, N, ptr(scratch), ptr(ch.send_ptr),
+             ptr(ch.send_eid), stream)
+        chunks.append(ch)
+        n0 = n1
+    return chunks
+
+
+class Workspace:
+    """Every device buffer of one step for one graph topology.
+
+    With ``chunk_edges`` the edge stages (radial function, rotate-in, SO(2) convolutions,
+    gate, rotate-back and their adjoints) run over contiguous receiver chunks of at most that
+    many edges, and their buffers are chunk-sized: per-edge storage is then the geometry
+    (Wigner coefficients, Gaussian basis, envelope, edge vectors) and its adjoint only, and the
+    reverse pass recomputes each chunk's forward chain. This is how a cell whose full per-edge
+    workspace exceeds device memory runs on one GPU."""
+
+    def __init__(self, eng, graph, sys_emb, chunk_edges=None):
         self.graph = graph
         dev = eng.device
         N, E = graph.N, graph.E
         C, H, EC, NB, G, NL = eng.C, eng.H, eng.EC, eng.NB, eng.G, eng.NL
         P = eng.npts
         f = lambda *shape: torch.empty(*shape, device=dev, dtype=torch.float32)  # noqa: E731
+        self.chunk_edges = chunk_edges
+        self.chunks = None
         self.pos = f(N, 3)
         self.coef, self.gauss, self.env, self.ev = f(E, 35), f(E, NB), f(E), f(E, 3)
-        self.R0, self.H1, self.R1, self.H2 = f(E, G * EC), f(E, G * EC), f(E, G * EC), f(E, G * EC)
-        self.RAD = f(E, eng.ldr)
+        if chunk_edges is None:
+            Eb, RW, nY, GW = E, eng.ldr, NL, G * EC
+        else:
+            Eb, RW, nY, GW = max(1, min(chunk_edges, E)), max(eng.radg[g]["width"]
+                                                               for g in range(G)), 1, EC
+        self.R0, self.H1, self.R1, self.H2 = f(Eb, GW), f(Eb, GW), f(Eb, GW), f(Eb, GW)
+        self.RAD = f(Eb, RW)
         self.x = [f(N, 9, C) for _ in range(NL + 1)]
         self.nb = [f(N, 9, C) for _ in range(NL)]
         self.xm = [f(N, 9, C) for _ in range(NL)]
-        self.Y1 = [f(E, 11 * H) for _ in range(NL)]
-        self.Y2 = [f(E, 9 * C) for _ in range(NL)]
+        self.Y1 = [f(Eb, 11 * H) for _ in range(nY)]
+        self.Y2 = [f(Eb, 9 * C) for _ in range(nY)]
         self.G0 = f(N * P, C) if eng.ff == "grid" else None
         if eng.ff == "spectral":
             self.S1 = [f(N, 2 * H) for _ in range(NL)]
@@ -512,14 +688,14 @@ class Workspace:
         grid = eng.ff == "grid"
         self.P1 = [f(N * P, C) for _ in range(NL)] if grid else None
         self.P2 = [f(N * P, C) for _ in range(NL)] if grid else None
-        self.A1, self.Gt = f(E, 18 * C), f(E, 9 * H)
+        self.A1, self.Gt = f(Eb, 18 * C), f(Eb, 9 * H)
         self.n2 = f(N, 9, C)
         self.h1, self.h2 = (f(N * P, C), f(N * P, C)) if grid else (None, None)
         self.ne, self.e1, self.e1p, self.e2, self.e2p = f(N, 9, C), f(N, H), f(N, H), f(N, H), f(N, H)
         self.enode = f(N)
         self.energy = f(graph.nsys)
         # reverse pass
-        self.gY2, self.gY1, self.grot, self.gRAD = f(E, 9 * C), f(E, 11 * H), f(E, 18 * C), f(E, eng.ldr)
+        self.gY2, self.gY1, self.grot, self.gRAD = f(Eb, 9 * C), f(Eb, 11 * H), f(Eb, 18 * C), f(Eb, RW)
         self.g_coef, self.g_env, self.g_gauss, self.g_ev = f(E, 35), f(E), f(E, NB), f(E, 3)
         self.gx, self.gn, self.gne = f(N, 9, C), f(N, 9, C), f(N, 9, C)
         self.ge1, self.ge2 = f(N, H), f(N, H)
@@ -541,6 +717,8 @@ class Workspace:
         assert graph.N == self.pos.shape[0]
         self.graph = graph
         eng, N, eng_C = self._eng, graph.N, self._eng.C
+        if self.chunk_edges is not None:
+            self.chunks = _plan_chunks(graph, self.chunk_edges, L.stream_ptr())
         # energy seed: dE/d(node energy) = 1 for the atoms the energy counts (rows past the
         # last segment are a partition's halo copies and get 0)
         n_count = graph.sys_ptr_host[-1]
