@@ -198,7 +198,10 @@ def run_slab(args):
     del g
     eng = UMAEngine(b.weights, cfg, b.tables(), device=device, precision=args.precision)
     se = csd_embedding(b.weights, [0.0], [0.0], cfg["sphere_channels"])
-    ws = eng.workspace(lg, se)
+    # one GPU cannot hold the full per-edge workspace of 1.97M edges: run the edge stages over
+    # receiver chunks (recomputed in the reverse pass); ranks of a partitioned run fit whole
+    chunk = args.chunk_edges if args.chunk_edges > 0 else (262144 if ws_n == 1 else None)
+    ws = eng.workspace(lg, se, chunk_edges=chunk)
     ws.pos.copy_(pos[plan.global_ids.to(device)])
     exch = DistExchange(plan)
     red = torch.zeros(10, device=device, dtype=torch.float64)
@@ -237,6 +240,8 @@ def run_slab(args):
                "config": {"workload": WORKLOADS["fe65k"], "atoms": N, "edges": E_total,
                           "edges_rank0": lg.E, "halo_rank0": plan.n_halo,
                           "precision": args.precision, "parallelism": f"slab x{ws_n}",
+                          "chunk_edges": chunk,
+                          "chunks": len(ws.chunks) if ws.chunks else None,
                           "workspace_GB_rank0": round(ws.nbytes() / 1e9, 1)},
                "energy": float(red[0]), "clocks": clocks}
         print(json.dumps(out))
@@ -519,6 +524,9 @@ def main():
     ap.add_argument("--cells", default="10,10,5", help="fcc cells (profiling uses a smaller cell)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "fp32", "tf32"])
+    ap.add_argument("--chunk-edges", type=int, default=0,
+                    help="fe65k: receiver-chunk size of the edge stages (0: automatic, chunked "
+                         "on one GPU only)")
     ap.add_argument("--workload", default="uma", choices=sorted(WORKLOADS),
                     help="uma: config 2 (the headline); orb: config 3; fe65k: config 5; screen: config 4")
     args = ap.parse_args()
