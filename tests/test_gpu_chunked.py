@@ -39,3 +39,43 @@ def test_chunked_matches_unchunked(shape, ff, nchunks):
     vol = abs(np.linalg.det(s["cell"].astype(np.float64)))
     assert (ws.virial - ref.virial).abs().max().item() / vol <= 1e-6
     assert ws.nbytes() < ref.nbytes()
+
+
+def test_workspace_size_estimate_and_chunk_choice():
+    cfg = configs.model_config("uma-s-1")
+    b = WeightBundle.from_arrays(configs.random_bundle_arrays(cfg, seed=0))
+    s = configs.fcc_alloy(reps=(4, 3, 3), seed=5)
+    eng = UMAEngine(b.weights, cfg, b.tables(), precision="3xtf32")
+    se = csd_embedding(b.weights, [0.0], [0.0], cfg["sphere_channels"])
+    g = build_graph(torch.from_numpy(s["pos"]).cuda(), s["Z"], cfg["cutoff"], s["cell"],
+                    [True] * 3, max_neighbors=cfg["max_neighbors"])
+    for k in (None, 2000):
+        ws = eng.workspace(g, se, chunk_edges=k)
+        est = eng.workspace_bytes(g.N, g.E, chunk_edges=k)
+        assert 0.75 * ws.nbytes() <= est <= 1.25 * ws.nbytes()
+        del ws
+    full = eng.workspace_bytes(g.N, g.E)
+    assert eng.choose_chunk_edges(g, budget_bytes=2 * full) is None
+    # halfway between the chunked workspace's fixed part and one chunk of all edges
+    budget = 0.5 * (eng.workspace_bytes(g.N, g.E, chunk_edges=0)
+                    + eng.workspace_bytes(g.N, g.E, chunk_edges=g.E))
+    k = eng.choose_chunk_edges(g, budget_bytes=budget)
+    assert k is not None and 0 < k < g.E
+    assert eng.workspace_bytes(g.N, g.E, chunk_edges=k) <= budget
+    with pytest.raises(MemoryError):
+        eng.choose_chunk_edges(g, budget_bytes=1e3)
+
+
+def test_calculator_with_chunks_matches_default():
+    from tt_atom.calculator import TTAtomCalculator
+    cfg = configs.model_config("uma-s-1")
+    b = WeightBundle.from_arrays(configs.random_bundle_arrays(cfg, seed=0))
+    s = configs.fcc_alloy(reps=(4, 3, 3), seed=5)
+    args = (s["pos"], s["Z"], s["cell"], [True] * 3, [0.0], [0.0])
+    E0, F0, V0 = TTAtomCalculator(b)._evaluate(*args, forces=True, stress=True)
+    c = TTAtomCalculator(b, chunk_edges=1500)
+    E1, F1, V1 = c._evaluate(*args, forces=True, stress=True)
+    assert c._ws.chunks is not None and len(c._ws.chunks) > 1
+    assert abs(float(E1[0] - E0[0])) <= 1e-6 * abs(float(E0[0]))
+    assert (F1 - F0).abs().max().item() <= 1e-5
+    assert (V1 - V0).abs().max().item() <= 1e-4

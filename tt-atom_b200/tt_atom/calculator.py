@@ -43,8 +43,12 @@ class TTAtomCalculator(_AseCalculator):
     implemented_properties = ["energy", "energies", "free_energy", "forces", "stress"]
 
     def __init__(self, bundle, task_name=None, device=None, device_id=0, gamma=0.0, fast=False,
-                 trace=False, precision="3xtf32", max_neighbors="config", **kwargs):
+                 trace=False, precision="3xtf32", max_neighbors="config", chunk_edges="auto",
+                 **kwargs):
         super().__init__(**kwargs)
+        # receiver-chunked edge stages: "auto" (only when the whole workspace would not fit in
+        # free device memory), None (never) or a chunk size in edges
+        self.chunk_edges = chunk_edges
         if isinstance(bundle, str):
             bundle = WeightBundle.load(bundle)
         if gamma != 0.0:
@@ -96,7 +100,11 @@ class TTAtomCalculator(_AseCalculator):
             if self._ws is not None and self._ws.fits(g):
                 self._ws.rebind(g, se)              # same sizes: reuse the buffers
             else:
-                self._ws = self.engine.workspace(g, se)
+                self._ws = self._step = None        # free the old buffers first
+                chunk = self.chunk_edges
+                if chunk == "auto":
+                    chunk = self.engine.choose_chunk_edges(g)
+                self._ws = self.engine.workspace(g, se, chunk_edges=chunk)
             self._ws_key, self._se, self._step = key, se, None
         ws = self._ws
         ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))

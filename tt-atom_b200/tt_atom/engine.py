@@ -269,6 +269,36 @@ class UMAEngine:
         call("atom_gemm", ptr(A), lda, M, groups.struct, ptr(Cout), ldc, ptr(Cpre), ptr(T1),
              ptr(T2), ptr(idx1), ptr(idx2), ldt, act, accumulate, self.precision, stream)
 
+    def workspace_bytes(self, N, E, chunk_edges=None):
+        """Approximate device bytes of a workspace for N atoms and E edges (unchunked, or
+        with receiver chunks of ``chunk_edges`` edges)."""
+        C, H, EC, NB, G, NL, P = self.C, self.H, self.EC, self.NB, self.G, self.NL, self.npts
+        node = N * (9 * C * (3 * NL + 9) + (2 * NL + 3) * P * C + 8 * H + 2 * C)
+        geo = E * 2 * (NB + 39)
+        if chunk_edges is None:
+            edge = E * (4 * G * EC + 2 * self.ldr + NL * (11 * H + 9 * C) + 45 * C + 20 * H)
+        else:
+            RW = max(r["width"] for r in self.radg)
+            edge = min(chunk_edges, E) * (4 * EC + 2 * RW + 31 * H + 54 * C)
+        return 4 * (node + geo + edge)
+
+    def choose_chunk_edges(self, graph, budget_bytes=None):
+        """None when the unchunked workspace fits ``budget_bytes`` (default: 85 % of the
+        device's free memory), else the largest receiver-chunk size that does."""
+        N, E = graph.N, graph.E
+        if budget_bytes is None:
+            budget_bytes = 0.85 * torch.cuda.mem_get_info(self.device)[0]
+        if self.workspace_bytes(N, E) <= budget_bytes:
+            return None
+        fixed = self.workspace_bytes(N, E, chunk_edges=0)
+        per_edge = self.workspace_bytes(N, E, chunk_edges=1) - fixed
+        max_in = int((graph.recv_ptr[1:] - graph.recv_ptr[:-1]).max()) if N else 1
+        k = int((budget_bytes - fixed) // per_edge)
+        if k < max(max_in, 1):
+            raise MemoryError(f"{N} atoms / {E} edges do not fit in {budget_bytes / 1e9:.1f} GB "
+                              f"even in receiver chunks (fixed part {fixed / 1e9:.1f} GB)")
+        return min(k, E)
+
     def workspace(self, graph, sys_emb, chunk_edges=None):
         """Device buffers for one topology. With ``chunk_edges`` the edge stages run over
         contiguous receiver chunks of at most that many edges (recomputed in the reverse
