@@ -122,9 +122,8 @@ def _sim_worker(device_id, model, task, trace, sim_params, in_q, out_q):
                            forces=np.asarray(atoms.get_forces(), dtype=np.float64),
                            fmax=None, nsteps=0, converged=None)
             else:
-                if not HAVE_ASE:
-                    raise RuntimeError(f"mode {mode!r} runs ASE's optimiser / integrator, and ASE "
-                                       "is not installed")
+                # ASE's optimiser / integrator when ASE is installed, else the GPU-resident
+                # loops of tt_atom.dynamics
                 from .simulate import md_atoms, relax_atoms
                 if mode == "relax":
                     res = relax_atoms(atoms, fmax=sim_params["fmax"], steps=sim_params["steps"])

@@ -87,8 +87,11 @@ class TTAtomCalculator(_AseCalculator):
                            max_neighbors=self.max_neighbors, sys_ptr=sys_ptr, device=self.device)
 
     def _evaluate(self, pos, Z, cell, pbc, charges, spins, sys_ptr=None, forces=True,
-                  stress=False, trace=False):
-        """Raw (unnormalised) per-system energies [nsys], forces [N, 3], virial [3, 3]|None."""
+                  stress=False, trace=False, device_out=False):
+        """Raw (unnormalised) per-system energies [nsys], forces [N, 3], virial [3, 3]|None,
+        as float64 host tensors, or (``device_out``) as float32 device tensors that the next
+        call overwrites (``pos`` may then be a device tensor too: nothing crosses to the host
+        but the neighbour-list size)."""
         g = self._graph(pos, Z, cell, pbc, sys_ptr)
         if g.E == 0:
             raise ValueError("no edges within cutoff — system too sparse for this model")
@@ -114,6 +117,8 @@ class TTAtomCalculator(_AseCalculator):
             self._step()
         else:
             self.engine.run(ws, ws.pos, forces=forces, virial=stress)
+        if device_out:
+            return ws.energy, ws.forces if forces else None, ws.virial if stress else None
         E = ws.energy.double().cpu()
         F = ws.forces.double().cpu() if forces else None
         V = ws.virial.double().cpu() if stress else None
