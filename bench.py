@@ -9,7 +9,7 @@ cutoff 6 A, at most 30 neighbours), random-init fp32 weights (seed 0).
 * ``value``: atom-steps/s of the device step (geometry -> forward -> hand-written backward ->
   forces + virial) replayed from a CUDA graph with positions resident in HBM; timed with CUDA
   events over exactly K steps; the per-step working set (~10 GB) is far larger than L2.
-* ``e2e``: the same metric through the public API (``TTAtomCalculator.calculate``): host
+* ``e2e``: the same metric through the public API (``TTAtomCalculator.calculate``, trace=True): host
   positions -> H2D copy -> GPU neighbour list -> step -> D2H of energy, forces, stress.
 * Multi-GPU (torchrun, N ranks): each rank runs its own replica structure (independent
   systems, no collective on the data path); value = all ranks' atoms x steps / max-over-ranks
@@ -358,6 +358,9 @@ def run_ours(args):
     edge = eng.time_edge_kernel(ws, reps=3) if hasattr(eng, "time_edge_kernel") else None
     # ---- end to end through the public API (host positions in, host results out)
     atoms = SimpleAtoms(s["Z"], s["pos"], cell, True)
+    # the calculator's trace option (the reference's Calculator(trace=True)): the step is
+    # captured as a CUDA graph per topology and replayed while the neighbour list is unchanged
+    calc.trace = True
     atoms.calc = calc
     for _ in range(max(1, args.warmup)):
         calc.calculate(atoms, ("energy", "forces", "stress"))

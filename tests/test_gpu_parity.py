@@ -171,6 +171,28 @@ def test_batch_equals_single_and_trace_is_bit_exact():
     assert torch.equal(F0, F1) and torch.equal(F1, F2)
 
 
+
+def test_traced_calculate_with_stress_is_bit_exact():
+    """Calculator(trace=True) replays the captured step (virial included) and gives the eager
+    results bit for bit, also after the positions move within the same topology."""
+    from tt_atom.ase_compat import SimpleAtoms
+    cfg = configs.model_config("uma-s-1")
+    b = WeightBundle.from_arrays(configs.random_bundle_arrays(cfg, seed=0))
+    s = configs.fcc_alloy(reps=(3, 3, 3), seed=2)
+    res = {}
+    for trace in (False, True):
+        calc = TTAtomCalculator(b, trace=trace)
+        out = []
+        for dx in (0.0, 0.001, 0.0):
+            a = SimpleAtoms(s["Z"], s["pos"] + dx, s["cell"], True)
+            calc.calculate(a, ("energy", "forces", "stress"))
+            out.append((calc.results["energy"], calc.results["forces"].copy(),
+                        calc.results["stress"].copy()))
+        res[trace] = out
+    for (e0, f0, s0), (e1, f1, s1) in zip(res[False], res[True]):
+        assert e0 == e1 and np.array_equal(f0, f1) and np.array_equal(s0, s1)
+
+
 def test_calculator_api_and_errors():
     from tt_atom.ase_compat import SimpleAtoms
     cfg = configs.model_config("tiny")

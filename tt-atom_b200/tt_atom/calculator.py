@@ -130,7 +130,7 @@ class TTAtomCalculator(_AseCalculator):
         pos, Z, charge, spin, cell, pbc = _fields(atoms)
         want_stress = cell is not None and ("stress" in properties or bool(np.all(pbc)))
         E, F, V = self._evaluate(pos, Z, cell, pbc, [charge], [spin], forces=True,
-                                 stress=want_stress, trace=self.trace and "stress" not in properties)
+                                 stress=want_stress, trace=self.trace)
         e = self.scale_rmsd * float(E[0]) + self.scale_mean
         if self.elem_refs is not None:
             e += float(self.elem_refs[torch.as_tensor(Z)].sum())
