@@ -302,3 +302,32 @@ def test_segment_sum_deterministic():
     out2 = torch.empty(4, device=dev)
     call("atom_segment_sum", ptr(v), v.numel(), ptr(sp), 4, ptr(out2), s())
     assert torch.equal(out, out2)
+
+
+@pytest.mark.parametrize("W", [256, 1024])
+def test_csr_sum_orders_and_scales(W):
+    """Orb's segmented sums: out[n] (+)= sum over the CSR rows of node n (optionally through an
+    edge-id list, optionally scaled per edge), as the plain sum in CSR order."""
+    g = torch.Generator().manual_seed(3)
+    N = 37
+    deg = torch.randint(0, 10, (N,), generator=g)
+    ptr_ = torch.cat([torch.zeros(1, dtype=torch.long), deg.cumsum(0)])
+    E = int(ptr_[-1])
+    X = rnd(E, W + 8, seed=4)
+    sc = rnd(E, 2, seed=5)
+    eid = torch.randperm(E, generator=g)
+    ptr_d, eid_d = ptr_.to(dev, torch.int32), eid.to(dev, torch.int32)   # kept alive
+    for use_eid in (False, True):
+        for use_scale in (False, True):
+            out = rnd(N, W, seed=6)
+            base = out.clone()
+            call("atom_csr_sum", ptr(X), W + 8, ptr(sc) if use_scale else None, 2,
+                 ptr(ptr_d), ptr(eid_d) if use_eid else None,
+                 N, W, ptr(out), W, 1, s())
+            ref = base.double().clone()
+            for n in range(N):
+                for k in range(int(ptr_[n]), int(ptr_[n + 1])):
+                    e = int(eid[k]) if use_eid else k
+                    w = float(sc[e, 0]) if use_scale else 1.0
+                    ref[n] += w * X[e, :W].double()
+            close(out, ref, 1e-5)

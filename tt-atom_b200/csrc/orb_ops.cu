@@ -244,21 +244,42 @@ __global__ void orb_attention_kernel(const float* __restrict__ edges, long long 
 
 // ------------------------------------------------------------------------ CSR sums
 // out[n, :W] (+)= sum_{k in [ptr[n], ptr[n+1])} scale[e] X[e, :W], e = eid ? eid[k] : k.
+// One block per node, one float4 of channels per thread: the loads of four edges are issued
+// before their multiply-adds, which still run in CSR order (the same sums as one edge at a
+// time).
 __global__ void csr_sum_kernel(const float* __restrict__ X, long long ldx,
                                const float* __restrict__ scale, int sstride,
                                const int* __restrict__ ptr, const int* __restrict__ eid,
                                long long N, int W, float* __restrict__ out, long long ldo,
                                int accumulate) {
-    long long n = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    int lane = threadIdx.x & 31;
-    if (n >= N) return;
+    const long long n = blockIdx.x;
     const int k0 = ptr[n], k1 = ptr[n + 1];
-    for (int c = lane * 4; c < W; c += 128) {
+    for (int c = threadIdx.x * 4; c < W; c += blockDim.x * 4) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int k = k0; k < k1; ++k) {
-            int e = eid ? eid[k] : k;
-            float s = scale ? scale[(long long)e * sstride] : 1.f;
-            float4 v = *reinterpret_cast<const float4*>(X + (long long)e * ldx + c);
+        int k = k0;
+        for (; k + 3 < k1; k += 4) {
+            int e[4];
+            float s[4];
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) e[u] = eid ? eid[k + u] : k + u;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                s[u] = scale ? scale[(long long)e[u] * sstride] : 1.f;
+                v[u] = *reinterpret_cast<const float4*>(X + (long long)e[u] * ldx + c);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                acc.x = fmaf(s[u], v[u].x, acc.x);
+                acc.y = fmaf(s[u], v[u].y, acc.y);
+                acc.z = fmaf(s[u], v[u].z, acc.z);
+                acc.w = fmaf(s[u], v[u].w, acc.w);
+            }
+        }
+        for (; k < k1; ++k) {
+            const int e = eid ? eid[k] : k;
+            const float s = scale ? scale[(long long)e * sstride] : 1.f;
+            const float4 v = *reinterpret_cast<const float4*>(X + (long long)e * ldx + c);
             acc.x = fmaf(s, v.x, acc.x);
             acc.y = fmaf(s, v.y, acc.y);
             acc.z = fmaf(s, v.z, acc.z);
@@ -401,7 +422,10 @@ extern "C" int atom_csr_sum(const float* X, int64_t ldx, const float* scale, int
     ATOM_REQUIRE(W % 4 == 0 && ldx % 4 == 0 && ldo % 4 == 0 && aligned16(X) && aligned16(out),
                  "csr_sum: W, ldx, ldo must be multiples of 4 and X, out 16-byte aligned");
     if (N == 0) return ATOM_OK;
-    csr_sum_kernel<<<WARPS(N)>>>(X, ldx, scale, sstride, ptr, eid, N, W, out, ldo, accumulate);
+    const int threads = W / 4 < 32 ? 32 : (W / 4 > 256 ? 256 : (W / 4 + 31) / 32 * 32);
+    csr_sum_kernel<<<(unsigned)N, threads, 0, (cudaStream_t)stream>>>(X, ldx, scale, sstride,
+                                                                      ptr, eid, N, W, out, ldo,
+                                                                      accumulate);
     ATOM_CHECK_LAUNCH("csr_sum");
     return ATOM_OK;
 }
