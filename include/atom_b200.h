@@ -361,6 +361,16 @@ int atom_col_mean(const float* X, int64_t ld, int64_t N, int C, float scale, flo
 int atom_row_broadcast(const float* v, int64_t N, int C, float scale, float* out, int64_t ld,
                        int accumulate, void* stream);
 
+/* ZBL pair repulsion of Orb (replaces the host closed form of tt_atom/orb_model.py:491-587:
+ * host_zbl_energy / host_zbl_forces / host_zbl_stress), fp64 per edge. ev [E,3] edge vectors
+ * (pos[src] - pos[tgt] + shift), Z [N] atomic numbers, src / tgt [E] (Orb senders = tgt),
+ * rcov [nrad] covalent radii (A) indexed by Z + 1, scale = 1 / N (per-node mean) or 1 (sum).
+ * Writes g_ev [E,3] = dE_zbl/d(ev) (feed atom_forces_virial for forces and virial),
+ * partials [1024] (scratch) and energy [1] = scale * sum of pair terms. */
+int atom_orb_zbl(const float* ev, const int* Z, const int* src, const int* tgt, int64_t E,
+                 const double* rcov, int nrad, double scale, float* g_ev, double* partials,
+                 double* energy, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,8 +15,12 @@ restates, in fp32 torch on the CPU, the reference's Orb port:
 * forces / stress -- autograd of the raw (normalised-space) energy w.r.t. positions and a
                      symmetric strain leaf on the edge vectors (tt_atom/orb_geometry.py:83-88)
 
-Not restated: the energy normaliser / per-element references and the ZBL pair term, which are
-host-side scalar glue outside the GPU path (tt_atom/orb_model.py:491-600). Parity is unpinned by
+* ZBL repulsion   -- tt_atom/orb_model.py:491-587 (host_zbl_energy and its autograd forces /
+                     strain virial), in float64; covalent radii passed in (the reference reads
+                     ase.data.covalent_radii, absent here)
+
+Not restated: the energy normaliser / per-element references (host-side scalar glue,
+tt_atom/orb_model.py:588-600). Parity is unpinned by
 any committed Orb golden (the reference has none); it rests on this restatement of the
 reference's own Orb code.
 """
@@ -115,3 +119,34 @@ def energy_forces(w, cfg, pos, Z, edge_index, shift=None, compute_stress=False):
     ins = [pos] if strain is None else [pos, strain]
     g = torch.autograd.grad(E, ins)
     return dict(energy=E.detach(), forces=-g[0], virial=g[1] if compute_stress else None)
+
+
+def zbl_energy_forces_virial(Z, src, tgt, pos, shift, rcov, node_aggregation="mean", p=6):
+    """ZBL pair repulsion of tt_atom/orb_model.py:491-537 in float64 with its forces
+    (-dE/dpos) and strain virial (dE/dstrain) by autograd. Orb senders = tgt, receivers = src;
+    atomic numbers enter as Z + 1 (the upstream embedding-index convention kept by the
+    reference)."""
+    c = torch.tensor([0.1818, 0.5099, 0.2802, 0.02817], dtype=torch.float64).unsqueeze(1)
+    d = torch.tensor([3.2, 0.9423, 0.4028, 0.2016], dtype=torch.float64).unsqueeze(1)
+    rcov = torch.as_tensor(rcov, dtype=torch.float64)
+    senders, receivers = tgt.long(), src.long()
+    pos = pos.detach().double().clone().requires_grad_(True)
+    strain = torch.zeros(3, 3, dtype=torch.float64, requires_grad=True)
+    vec = pos[receivers] - pos[senders]
+    if shift is not None:
+        vec = vec + shift.double()
+    vec = vec @ (torch.eye(3, dtype=torch.float64) + 0.5 * (strain + strain.T))
+    Zu = Z[senders].double() + 1
+    Zv = Z[receivers].double() + 1
+    a = 0.4543 * 0.529 / (Zu.pow(0.300) + Zv.pow(0.300))
+    x = vec.norm(dim=1)
+    phi = (c * torch.exp(-d * (x / a).unsqueeze(0))).sum(dim=0)
+    v_raw = 14.3996 * Zu * Zv / x * phi
+    r_max = rcov[Zu.long()] + rcov[Zv.long()]
+    t = x / r_max
+    env = (1.0 - ((p + 1.0) * (p + 2.0) / 2.0) * t.pow(p) + p * (p + 2.0) * t.pow(p + 1)
+           - (p * (p + 1.0) / 2.0) * t.pow(p + 2)) * (x < r_max).double()
+    V = torch.zeros(Z.shape[0], dtype=torch.float64).index_add(0, senders, 0.5 * v_raw * env)
+    E = V.mean() if node_aggregation == "mean" else V.sum()
+    gp, gs = torch.autograd.grad(E, [pos, strain])
+    return float(E.detach()), -gp, gs

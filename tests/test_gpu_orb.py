@@ -73,3 +73,36 @@ def test_orb_energy_forces_stress_vs_oracle(shape, sysname, precision):
     if V is not None:
         vol = abs(np.linalg.det(sysd["cell"].astype(np.float64)))
         assert (V.float() - r["virial"]).abs().max() / vol <= S_ABS
+
+
+def test_zbl_pair_repulsion_vs_oracle():
+    """calculate() with zbl=True minus zbl=False is the ZBL term: energy, forces and stress
+    against the float64 oracle restatement on the same edges (a compressed SiO2 cell, so many
+    pairs sit inside r_cov(Z+1) sums)."""
+    from tt_atom.ase_compat import SimpleAtoms
+    from tt_atom.orb import COVALENT_RADII
+    cfg = configs.orb_config("orb-tiny")
+    w = configs.orb_random_weights(cfg, seed=0)
+    s = configs.amorphous_sio2(n_si=20, n_o=40, seed=4)
+    pos, cell = 0.85 * s["pos"], 0.85 * s["cell"]
+    res = {}
+    for zbl in (False, True):
+        calc = OrbCalculator(w, cfg, zbl=zbl, max_num_neighbors=None)
+        a = SimpleAtoms(s["Z"], pos, cell, True)
+        calc.calculate(a, ("energy", "forces", "stress"))
+        res[zbl] = (calc.results["energy"], calc.results["forces"], calc.results["stress"], calc)
+    g = res[True][3]._ws.graph
+    shift = g.shifts.double().cpu()[g.img.long().cpu()]
+    Ez, Fz, Vz = OB.zbl_energy_forces_virial(torch.from_numpy(s["Z"]), g.src.cpu(), g.tgt.cpu(),
+                                             torch.from_numpy(pos), shift, COVALENT_RADII)
+    assert abs(Ez) > 1e-3                                    # the term is exercised
+    dE = res[True][0] - res[False][0]
+    assert abs(dE - Ez) <= 1e-6 * max(1.0, abs(Ez))
+    dF = res[True][1] - res[False][1]
+    assert np.abs(dF - Fz.numpy()).max() <= 1e-4 * max(1.0, np.abs(Fz.numpy()).max())
+    vol = abs(np.linalg.det(cell.astype(np.float64)))
+    S = Vz.numpy() / vol
+    voigt = np.array([S[0, 0], S[1, 1], S[2, 2], 0.5 * (S[1, 2] + S[2, 1]),
+                      0.5 * (S[0, 2] + S[2, 0]), 0.5 * (S[0, 1] + S[1, 0])])
+    dS = res[True][2] - res[False][2]
+    assert np.abs(dS - voigt).max() <= 1e-4 * max(1e-3, np.abs(voigt).max())

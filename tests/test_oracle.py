@@ -142,3 +142,12 @@ def test_orb_oracle_runs_tiny():
     assert torch.isfinite(r["energy"]) and torch.isfinite(r["forces"]).all()
     # net force of a conservative, translation-invariant model vanishes
     assert r["forces"].sum(0).abs().max() < 1e-4
+
+
+def test_covalent_radii_table_matches_ase_when_available():
+    """The ZBL term's covalent radii are ASE's table (Cordero et al. 2008); checked against
+    ase.data where ASE is installed (it is not in every environment)."""
+    from tt_atom.orb import COVALENT_RADII
+    assert len(COVALENT_RADII) == 119 and COVALENT_RADII[14] == 1.11 and COVALENT_RADII[8] == 0.66
+    ase_data = pytest.importorskip("ase.data")
+    assert np.allclose(np.asarray(ase_data.covalent_radii), np.asarray(COVALENT_RADII))

@@ -357,6 +357,82 @@ __global__ void row_broadcast_kernel(const float* __restrict__ v, long long N, i
     out[n * ld + c] = accumulate ? out[n * ld + c] + x : x;
 }
 
+// ------------------------------------------------------------- ZBL pair repulsion (fp64)
+// Ziegler-Biersack-Littmark screened Coulomb repulsion of Orb's pair_repulsion.ZBLBasis as
+// the reference evaluates it on the host (tt_atom/orb_model.py:491-537): per edge, with
+// Zu / Zv the sender / receiver atomic numbers plus one (the upstream indexing convention),
+//   a   = 0.4543 * 0.529 / (Zu^0.3 + Zv^0.3)
+//   phi = sum_k c_k exp(-d_k x / a)          (c, d: the 4-term universal screening function)
+//   v   = 0.5 * 14.3996 Zu Zv / x * phi * env(x / (r_cov[Zu] + r_cov[Zv])),
+//   env(t) = 1 - (p+1)(p+2)/2 t^p + p(p+2) t^(p+1) - p(p+1)/2 t^(p+2) for t < 1, else 0 (p = 6)
+// and the total is scale * sum_e v_e (scale = 1 / N for the per-node mean). Each thread also
+// writes dE/d(edge vector) = scale dv/dx vec / x, from which the force / virial reduction
+// follows; per-block partial energies (fixed grid, fixed tree) make the sum deterministic.
+constexpr int kZblBlocks = 1024;
+
+__global__ void __launch_bounds__(256) zbl_kernel(
+    const float* __restrict__ ev, const int* __restrict__ Z, const int* __restrict__ src,
+    const int* __restrict__ tgt, long long E, const double* __restrict__ rcov, int nrad,
+    double scale, float* __restrict__ g_ev, double* __restrict__ part) {
+    __shared__ double red[256];
+    const double c[4] = {0.1818, 0.5099, 0.2802, 0.02817};
+    const double d[4] = {3.2, 0.9423, 0.4028, 0.2016};
+    const double p = 6.0;
+    double acc = 0.0;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < E;
+         e += (long long)gridDim.x * blockDim.x) {
+        const double vx = ev[3 * e], vy = ev[3 * e + 1], vz = ev[3 * e + 2];
+        const double x = sqrt(vx * vx + vy * vy + vz * vz);
+        const int iu = Z[tgt[e]] + 1, iv = Z[src[e]] + 1;     // Orb: senders = tgt
+        const double Zu = iu, Zv = iv;
+        const double a = 0.4543 * 0.529 / (pow(Zu, 0.3) + pow(Zv, 0.3));
+        double phi = 0.0, dphi = 0.0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const double t = c[k] * exp(-d[k] * x / a);
+            phi += t;
+            dphi -= t * d[k] / a;
+        }
+        const double q = 0.5 * 14.3996 * Zu * Zv;
+        const double rmax = (iu < nrad ? rcov[iu] : 0.0) + (iv < nrad ? rcov[iv] : 0.0);
+        double env = 0.0, denv = 0.0;
+        if (x < rmax) {
+            const double t = x / rmax;
+            const double tp = pow(t, p - 1.0);
+            env = 1.0 - (p + 1.0) * (p + 2.0) / 2.0 * tp * t + p * (p + 2.0) * tp * t * t -
+                  p * (p + 1.0) / 2.0 * tp * t * t * t;
+            denv = (-(p + 1.0) * (p + 2.0) / 2.0 * p * tp + p * (p + 2.0) * (p + 1.0) * tp * t -
+                    p * (p + 1.0) / 2.0 * (p + 2.0) * tp * t * t) / rmax;
+        }
+        const double v = q / x * phi * env;
+        const double dvdx = q * ((dphi * x - phi) / (x * x) * env + phi / x * denv);
+        acc += v;
+        const double gs = scale * dvdx / x;
+        g_ev[3 * e] = (float)(gs * vx);
+        g_ev[3 * e + 1] = (float)(gs * vy);
+        g_ev[3 * e + 2] = (float)(gs * vz);
+    }
+    red[threadIdx.x] = acc;
+    __syncthreads();
+    for (int w = 128; w > 0; w >>= 1) {
+        if ((int)threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) part[blockIdx.x] = red[0];
+}
+
+__global__ void zbl_total_kernel(const double* __restrict__ part, double scale,
+                                 double* __restrict__ energy) {
+    __shared__ double red[kZblBlocks];
+    for (int i = threadIdx.x; i < kZblBlocks; i += blockDim.x) red[i] = part[i];
+    __syncthreads();
+    for (int w = kZblBlocks / 2; w > 0; w >>= 1) {
+        for (int i = threadIdx.x; i < w; i += blockDim.x) red[i] += red[i + w];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) energy[0] = scale * red[0];
+}
+
 }  // namespace atom
 
 using namespace atom;
@@ -455,5 +531,18 @@ extern "C" int atom_row_broadcast(const float* v, int64_t N, int C, float scale,
     row_broadcast_kernel<<<ceil_div(N * C, 256), 256, 0, (cudaStream_t)stream>>>(
         v, N, C, scale, out, ld, accumulate);
     ATOM_CHECK_LAUNCH("row_broadcast");
+    return ATOM_OK;
+}
+
+extern "C" int atom_orb_zbl(const float* ev, const int* Z, const int* src, const int* tgt,
+                            int64_t E, const double* rcov, int nrad, double scale, float* g_ev,
+                            double* partials, double* energy, void* stream) {
+    ATOM_REQUIRE(E >= 0 && nrad > 0, "orb_zbl: bad sizes");
+    cudaStream_t st = (cudaStream_t)stream;
+    zbl_kernel<<<kZblBlocks, 256, 0, st>>>(ev, Z, src, tgt, E, rcov, nrad, scale, g_ev,
+                                          partials);
+    ATOM_CHECK_LAUNCH("orb_zbl");
+    zbl_total_kernel<<<1, 256, 0, st>>>(partials, scale, energy);
+    ATOM_CHECK_LAUNCH("orb_zbl_total");
     return ATOM_OK;
 }

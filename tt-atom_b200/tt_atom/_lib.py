@@ -16,6 +16,7 @@ _lib = None
 ATOM_ERR_CAPACITY = 3
 
 c_void_p, c_int, c_int64, c_float = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+c_double = ctypes.c_double
 
 
 class GemmGroups(ctypes.Structure):
@@ -104,6 +105,8 @@ _SIGS = {
                               c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p,
                               c_void_p, c_void_p, c_void_p),
     "atom_col_mean": (c_void_p, c_int64, c_int64, c_int, c_float, c_void_p, c_void_p),
+    "atom_orb_zbl": (c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int, c_double,
+                     c_void_p, c_void_p, c_void_p, c_void_p),
     "atom_row_broadcast": (c_void_p, c_int64, c_int, c_float, c_void_p, c_int64, c_int,
                            c_void_p),
     "atom_edge_species": (c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p),

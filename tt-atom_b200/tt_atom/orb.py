@@ -12,8 +12,8 @@ reverse pass likewise sums the first-layer adjoint per node (CSR) before one nod
 SiLU is fused into the GEMM epilogues (pre-activations kept for the reverse pass); RMSNorm and
 the residual update are one kernel.
 
-Not on the GPU: the energy normaliser / per-element references (applied on the host when the
-weights carry them) and the ZBL pair term (host glue in the reference; not implemented here).
+Not on the GPU: the energy normaliser / per-element references (a few scalars applied on the
+host when the weights carry them). The ZBL pair repulsion runs on the GPU (``atom_orb_zbl``).
 """
 from __future__ import annotations
 
@@ -287,17 +287,33 @@ class OrbWorkspace:
              eng.D0, ptr(self.x0), L.stream_ptr())
 
 
+# Covalent radii (Angstrom) indexed by atomic number, Cordero et al., Dalton Trans. 2008,
+# 2832-2838 (low-spin values for Mn, Fe, Co; sp3 carbon), the table ASE ships as
+# ase.data.covalent_radii (index 0 and elements past Cm: 0.2). The reference's ZBL term looks
+# it up at Z + 1 (tt_atom/orb_model.py:507-523).
+COVALENT_RADII = (
+    0.20, 0.31, 0.28, 1.28, 0.96, 0.84, 0.76, 0.71, 0.66, 0.57, 0.58, 1.66, 1.41, 1.21, 1.11,
+    1.07, 1.05, 1.02, 1.06, 2.03, 1.76, 1.70, 1.60, 1.53, 1.39, 1.39, 1.32, 1.26, 1.24, 1.32,
+    1.22, 1.22, 1.20, 1.19, 1.20, 1.20, 1.16, 2.20, 1.95, 1.90, 1.75, 1.64, 1.54, 1.47, 1.46,
+    1.42, 1.39, 1.45, 1.44, 1.42, 1.39, 1.39, 1.38, 1.39, 1.40, 2.44, 2.15, 2.07, 2.04, 2.03,
+    2.01, 1.99, 1.98, 1.98, 1.96, 1.94, 1.92, 1.92, 1.89, 1.90, 1.87, 1.87, 1.75, 1.70, 1.62,
+    1.51, 1.44, 1.41, 1.36, 1.36, 1.32, 1.45, 1.46, 1.48, 1.40, 1.50, 1.50, 2.60, 2.21, 2.15,
+    2.06, 2.00, 1.96, 1.90, 1.87, 1.80, 1.69) + (0.20,) * 22
+
+
 class OrbCalculator(_AseCalculator):
     """ASE calculator for Orb-v3 conservative bundles (tt_atom/orb_calculator.py:28-215):
     energy, forces = -dE/dpos and stress from the strain virial. Energies are the raw model
     output, denormalised on the host when the weights carry ``energy_head.normalizer`` /
-    ``energy_head.reference`` entries; the ZBL pair term is not included."""
+    ``energy_head.reference`` entries, plus (``zbl=True``, the reference's behaviour) the ZBL
+    pair repulsion computed on the GPU (``atom_orb_zbl``, per-node mean)."""
 
     implemented_properties = ["energy", "free_energy", "energies", "forces", "stress"]
 
     def __init__(self, weights, cfg=None, device=None, device_id=0, precision="3xtf32",
-                 max_num_neighbors="config", **kwargs):
+                 max_num_neighbors="config", zbl=True, **kwargs):
         super().__init__(**kwargs)
+        self.zbl = zbl
         if cfg is None:
             from .weights import WeightBundle
             b = WeightBundle.load(weights) if isinstance(weights, str) else weights
@@ -310,6 +326,25 @@ class OrbCalculator(_AseCalculator):
         self.max_nbrs = cfg.get("max_num_neighbors") if max_num_neighbors == "config" \
             else max_num_neighbors
         self._ws = None
+        self._rcov = torch.tensor(COVALENT_RADII, dtype=torch.float64, device=self.device)
+
+    def _zbl(self, ws, stress):
+        """ZBL energy (scale 1 / N), forces and virial on ``ws``'s graph (its edge vectors
+        ``ws.ev`` are those of the last ``engine.run``)."""
+        g, N, E = ws.graph, ws.graph.N, ws.graph.E
+        if getattr(ws, "zbl_gev", None) is None or ws.zbl_gev.shape[0] != max(E, 1):
+            f = lambda *sh, dt=torch.float32: torch.empty(*sh, device=self.device, dtype=dt)  # noqa: E731
+            ws.zbl_gev, ws.zbl_F, ws.zbl_V = f(max(E, 1), 3), f(N, 3), f(3, 3)
+            ws.zbl_part = f(1024, dt=torch.float64)
+            ws.zbl_E = f(1, dt=torch.float64)
+        s = L.stream_ptr()
+        call("atom_orb_zbl", ptr(ws.ev), ptr(g.Z), ptr(g.src), ptr(g.tgt), E, ptr(self._rcov),
+             len(COVALENT_RADII), 1.0 / N, ptr(ws.zbl_gev), ptr(ws.zbl_part), ptr(ws.zbl_E), s)
+        call("atom_forces_virial", ptr(ws.zbl_gev), ptr(ws.ev), E, N, ptr(g.recv_ptr),
+             ptr(g.send_ptr), ptr(g.send_eid), ptr(ws.zbl_F),
+             ptr(ws.zbl_V) if stress else None, ptr(ws.vscratch), s)
+        return (float(ws.zbl_E.cpu()[0]), ws.zbl_F.double().cpu(),
+                ws.zbl_V.double().cpu() if stress else None)
 
     def _evaluate(self, pos, Z, cell, pbc, forces=True, stress=False):
         g = build_graph(pos, Z, self.cfg["cutoff"], cell, pbc, max_neighbors=self.max_nbrs,
@@ -346,4 +381,13 @@ class OrbCalculator(_AseCalculator):
         self.results["energies"] = np.full(n, E / n)
         self.results["forces"] = (scale * F).numpy()
         if V is not None:
-            self.results["stress"] = voigt_6(scale * V.numpy() / atoms_volume(atoms))
+            V = scale * V
+        if self.zbl:
+            Ez, Fz, Vz = self._zbl(self._ws, V is not None)
+            self.results["energy"] = self.results["free_energy"] = E = E + Ez
+            self.results["energies"] = np.full(n, E / n)
+            self.results["forces"] = self.results["forces"] + Fz.numpy()
+            if V is not None:
+                V = V + Vz
+        if V is not None:
+            self.results["stress"] = voigt_6(V.numpy() / atoms_volume(atoms))
