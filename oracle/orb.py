@@ -150,3 +150,31 @@ def zbl_energy_forces_virial(Z, src, tgt, pos, shift, rcov, node_aggregation="me
     E = V.mean() if node_aggregation == "mean" else V.sum()
     gp, gs = torch.autograd.grad(E, [pos, strain])
     return float(E.detach()), -gp, gs
+
+
+def direct_predict(w, cfg, pos, Z, edge_index, shift=None):
+    """Direct checkpoints: raw energy, raw per-atom forces with the net force removed and raw
+    Voigt-6 stress from the final node features (tt_atom/orb_model.py:307-436: EnergyHead,
+    ForceHead, StressHead), one forward pass without autograd."""
+    src, tgt = edge_index[0], edge_index[1]
+    senders, receivers = tgt, src
+    with torch.no_grad():
+        vec = pos[receivers] - pos[senders]
+        if shift is not None:
+            vec = vec + shift
+        feat, cut = edge_features(vec, cfg["cutoff"], cfg["num_bases"])
+        nodes = mlp_norm(w["atom_emb.embeddings.weight"][Z], w, "_encoder._node_fn")
+        edges = mlp_norm(feat, w, "_encoder._edge_fn")
+        for i in range(cfg["num_message_passing_steps"]):
+            nodes, edges = interaction(nodes, edges, w, f"gnn_stacks.{i}", senders, receivers,
+                                       cut)
+        mean = nodes.mean(0, keepdim=True)
+
+        def head(x, p):
+            h = F.silu(F.linear(x, w[f"{p}.mlp.NN-0.weight"], w[f"{p}.mlp.NN-0.bias"]))
+            return F.linear(h, w[f"{p}.mlp.NN-1.weight"], w[f"{p}.mlp.NN-1.bias"])
+        E = head(mean, "energy_head").reshape(())
+        fr = head(nodes, "forces_head")
+        fr = fr - fr.mean(0, keepdim=True)
+        sr = head(mean, "stress_head").reshape(6)
+    return dict(energy=E, forces=fr, stress=sr)

@@ -106,3 +106,32 @@ def test_zbl_pair_repulsion_vs_oracle():
                       0.5 * (S[0, 2] + S[2, 0]), 0.5 * (S[0, 1] + S[1, 0])])
     dS = res[True][2] - res[False][2]
     assert np.abs(dS - voigt).max() <= 1e-4 * max(1e-3, np.abs(voigt).max())
+
+
+def test_direct_checkpoint_heads_vs_oracle():
+    """A direct checkpoint (force and stress heads, no backward pass): the calculator's
+    energy / forces / stress without ZBL equal the oracle's head outputs through the
+    normalisers."""
+    from tt_atom.ase_compat import SimpleAtoms
+    cfg = configs.orb_config("orb-tiny")
+    w = configs.orb_random_weights(cfg, seed=1, direct=True)
+    s = configs.amorphous_sio2(n_si=20, n_o=40, seed=4)
+    calc = OrbCalculator(w, cfg, zbl=False, max_num_neighbors=None)
+    assert calc.engine.direct and calc.engine.has_stress_head
+    a = SimpleAtoms(s["Z"], s["pos"], s["cell"], True)
+    calc.calculate(a, ("energy", "forces", "stress"))
+    pos = torch.from_numpy(s["pos"])
+    ei, sh = O.neighbor_list(pos, cfg["cutoff"], torch.from_numpy(s["cell"]), [True] * 3, None)
+    r = OB.direct_predict(w, cfg, pos, torch.from_numpy(s["Z"]), ei, sh)
+    assert abs(calc.results["energy"] - float(r["energy"])) <= 1e-5 * max(1.0, abs(float(r["energy"])))
+    fs = float(w["forces_head.normalizer.bn.running_var"].sqrt())
+    fm = float(w["forces_head.normalizer.bn.running_mean"])
+    assert np.abs(calc.results["forces"] - (r["forces"].numpy() * fs + fm)).max() <= 1e-4
+    ds = float(w["stress_head.diag_normalizer.bn.running_var"].sqrt())
+    dm = float(w["stress_head.diag_normalizer.bn.running_mean"])
+    os_ = float(w["stress_head.offdiag_normalizer.bn.running_var"].sqrt())
+    om = float(w["stress_head.offdiag_normalizer.bn.running_mean"])
+    ref_s = np.concatenate([r["stress"][:3].numpy() * ds + dm, r["stress"][3:].numpy() * os_ + om])
+    assert np.abs(calc.results["stress"] - ref_s).max() <= 1e-6
+    # net force removed (before the per-component normaliser's mean is added back)
+    assert np.abs((calc.results["forces"] - fm).sum(0)).max() <= 1e-3 * fs

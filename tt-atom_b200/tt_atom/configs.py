@@ -254,9 +254,10 @@ def orb_config(name):
     return cfg
 
 
-def orb_random_weights(cfg, seed=0):
+def orb_random_weights(cfg, seed=0, direct=False):
     """Random-init Orb weights with the reference's key names (gns.MoleculeGNS naming as read by
-    tt_atom/orb_model.py:127-338 in the reference)."""
+    tt_atom/orb_model.py:127-338 in the reference); ``direct`` adds the force and stress heads
+    and their normalisers of direct checkpoints (tt_atom/orb_model.py:358-457)."""
     g = torch.Generator().manual_seed(seed)
     C, Hd, L = cfg["latent_dim"], cfg["hidden_dim"], cfg["num_message_passing_steps"]
     w = {}
@@ -283,6 +284,16 @@ def orb_random_weights(cfg, seed=0):
         lin(f"{p}._send_attn", 1, C)
     lin("energy_head.mlp.NN-0", cfg["head_hidden"], C)
     lin("energy_head.mlp.NN-1", 1, cfg["head_hidden"])
+    if direct:
+        lin("forces_head.mlp.NN-0", cfg["head_hidden"], C)
+        lin("forces_head.mlp.NN-1", 3, cfg["head_hidden"])
+        lin("stress_head.mlp.NN-0", cfg["head_hidden"], C)
+        lin("stress_head.mlp.NN-1", 6, cfg["head_hidden"])
+        for p_, mu, var in (("forces_head.normalizer", 0.01, 0.3),
+                            ("stress_head.diag_normalizer", -0.002, 0.0004),
+                            ("stress_head.offdiag_normalizer", 0.0, 0.0001)):
+            w[f"{p_}.bn.running_mean"] = torch.tensor([mu])
+            w[f"{p_}.bn.running_var"] = torch.tensor([var])
     return {k: v.float().contiguous() for k, v in w.items()}
 
 

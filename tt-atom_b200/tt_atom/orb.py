@@ -86,6 +86,19 @@ class OrbEngine:
         self.head1 = lin_groups(H1, d(Hb1))
         self.head1_row = d(H1.reshape(-1))
         self.head0_bw = bw_groups(H0)
+        # direct checkpoints (orb-v3-direct-*): per-node force head and node-mean stress head
+        self.direct = "forces_head.mlp.NN-0.weight" in w
+        self.has_stress_head = "stress_head.mlp.NN-0.weight" in w
+        if self.direct:
+            F0, F1 = w["forces_head.mlp.NN-0.weight"], w["forces_head.mlp.NN-1.weight"]
+            self.fh = F0.shape[0]
+            self.fhead0 = lin_groups(F0, d(w["forces_head.mlp.NN-0.bias"]))
+            self.fhead1 = lin_groups(F1, d(w["forces_head.mlp.NN-1.bias"]))
+        if self.has_stress_head:
+            S0, S1 = w["stress_head.mlp.NN-0.weight"], w["stress_head.mlp.NN-1.weight"]
+            self.sh = S0.shape[0]
+            self.shead0 = lin_groups(S0, d(w["stress_head.mlp.NN-0.bias"]))
+            self.shead1 = lin_groups(S1, d(w["stress_head.mlp.NN-1.bias"]))
 
     def _gemm(self, A, lda, M, groups, Cout, ldc, *, Cpre=None, T1=None, T2=None, idx1=None,
               idx2=None, ldt=0, act=0, accumulate=0, s=0):
@@ -186,6 +199,25 @@ class OrbEngine:
         if forces:
             self._backward(ws, virial, s)
 
+    def direct_heads(self, ws, stress=False, stream=None):
+        """Direct checkpoints, after a forward ``run(ws, forces=False)``: raw (normalised
+        space) per-atom forces with the net force removed -> ws.fraw[:, :3]
+        (tt_atom/orb_model.py:358-388) and the raw Voigt-6 stress of the node mean -> ws.sraw
+        (tt_atom/orb_model.py:407-436)."""
+        s = L.stream_ptr(stream)
+        N, C = ws.graph.N, self.C
+        nodes = ws.node_in[self.NL]                     # [N, 3C], latent in the first C
+        self._gemm(nodes, 3 * C, N, self.fhead0, ws.fhid, self.fh, act=1, s=s)
+        self._gemm(ws.fhid, self.fh, N, self.fhead1, ws.fraw, 4, s=s)
+        call("atom_col_mean", ptr(ws.fraw), 4, N, 4, 1.0 / N, ptr(ws.fmean), s)
+        call("atom_row_broadcast", ptr(ws.fmean), N, 4, -1.0, ptr(ws.fraw), 4, 1, s)
+        if stress:
+            if not self.has_stress_head:
+                raise ValueError("stress requested but this direct checkpoint carries no "
+                                 "stress_head weights")
+            self._gemm(ws.mean, C, 1, self.shead0, ws.shid, self.sh, act=1, s=s)
+            self._gemm(ws.shid, self.sh, 1, self.shead1, ws.sraw, 8, s=s)
+
     # --------------------------------------------------------------------------- reverse
     def _mlpnorm_bwd(self, m, h2, gY, M, a0, a1, tmp0, tmp1, g_a0, s):
         """gY: adjoint of the normalised output [M, C] (overwritten with the h2 adjoint);
@@ -266,6 +298,10 @@ class OrbWorkspace:
         self.nt0, self.nt1 = f(N, Hd), f(N, Hd)
         self.P = f(N, 2 * Hd)
         self.mean, self.hh, self.hhp = f(1, C), f(1, eng.hh), f(1, eng.hh)
+        if eng.direct:
+            self.fhid, self.fraw, self.fmean = f(N, eng.fh), torch.zeros(N, 4, device=dev), f(4)
+        if eng.has_stress_head:
+            self.shid, self.sraw = f(1, eng.sh), torch.zeros(1, 8, device=dev)
         self.energy = f(1)
         self.ghh, self.gmean = f(1, eng.hh), f(1, C)
         self.gN, self.gtmpN, self.gagg = f(N, C), f(N, C), f(N, 2 * C)
@@ -328,9 +364,10 @@ class OrbCalculator(_AseCalculator):
         self._ws = None
         self._rcov = torch.tensor(COVALENT_RADII, dtype=torch.float64, device=self.device)
 
-    def _zbl(self, ws, stress):
-        """ZBL energy (scale 1 / N), forces and virial on ``ws``'s graph (its edge vectors
-        ``ws.ev`` are those of the last ``engine.run``)."""
+    def _zbl(self, ws, stress, scale=None):
+        """ZBL energy (``scale`` times the pair sum: 1 / N, the per-node mean, by default),
+        forces and virial on ``ws``'s graph (its edge vectors ``ws.ev`` are those of the last
+        ``engine.run``)."""
         g, N, E = ws.graph, ws.graph.N, ws.graph.E
         if getattr(ws, "zbl_gev", None) is None or ws.zbl_gev.shape[0] != max(E, 1):
             f = lambda *sh, dt=torch.float32: torch.empty(*sh, device=self.device, dtype=dt)  # noqa: E731
@@ -339,12 +376,24 @@ class OrbCalculator(_AseCalculator):
             ws.zbl_E = f(1, dt=torch.float64)
         s = L.stream_ptr()
         call("atom_orb_zbl", ptr(ws.ev), ptr(g.Z), ptr(g.src), ptr(g.tgt), E, ptr(self._rcov),
-             len(COVALENT_RADII), 1.0 / N, ptr(ws.zbl_gev), ptr(ws.zbl_part), ptr(ws.zbl_E), s)
+             len(COVALENT_RADII), 1.0 / N if scale is None else scale, ptr(ws.zbl_gev),
+             ptr(ws.zbl_part), ptr(ws.zbl_E), s)
         call("atom_forces_virial", ptr(ws.zbl_gev), ptr(ws.ev), E, N, ptr(g.recv_ptr),
              ptr(g.send_ptr), ptr(g.send_eid), ptr(ws.zbl_F),
              ptr(ws.zbl_V) if stress else None, ptr(ws.vscratch), s)
         return (float(ws.zbl_E.cpu()[0]), ws.zbl_F.double().cpu(),
                 ws.zbl_V.double().cpu() if stress else None)
+
+    def _evaluate_direct(self, pos, Z, cell, pbc, stress=False):
+        """Direct checkpoints: raw energy, raw per-atom forces [N, 3] (net force removed) and
+        raw Voigt-6 stress (or None) from one forward pass and the heads."""
+        self._evaluate(pos, Z, cell, pbc, forces=False, stress=False)
+        ws = self._ws
+        self.engine.direct_heads(ws, stress=stress)
+        E = float(ws.energy.double().cpu()[0])
+        F = ws.fraw[:, :3].double().cpu()
+        S = ws.sraw[0, :6].double().cpu() if stress else None
+        return E, F, S
 
     def _evaluate(self, pos, Z, cell, pbc, forces=True, stress=False):
         g = build_graph(pos, Z, self.cfg["cutoff"], cell, pbc, max_neighbors=self.max_nbrs,
@@ -368,6 +417,8 @@ class OrbCalculator(_AseCalculator):
         pbc = np.asarray(atoms.get_pbc())
         cell = np.asarray(atoms.get_cell(), np.float32) if pbc.any() else None
         want_stress = cell is not None and ("stress" in properties or bool(pbc.all()))
+        if self.engine.direct:
+            return self._calculate_direct(atoms, pos, Z, cell, pbc, properties, want_stress)
         E, F, V = self._evaluate(pos, Z, cell, pbc if pbc.any() else None, True, want_stress)
         n = len(Z)
         w = self._w
@@ -391,3 +442,40 @@ class OrbCalculator(_AseCalculator):
                 V = V + Vz
         if V is not None:
             self.results["stress"] = voigt_6(V.numpy() / atoms_volume(atoms))
+
+    def _calculate_direct(self, atoms, pos, Z, cell, pbc, properties, want_stress):
+        """Direct checkpoints (tt_atom/orb_calculator.py:137-186): energy through the energy
+        head's normaliser, forces and stress from their heads through their own normalisers,
+        each plus the ZBL term summed over atoms."""
+        if "stress" in properties and cell is not None and not self.engine.has_stress_head:
+            raise ValueError("stress requested but this direct checkpoint carries no "
+                             "stress_head weights.")
+        want_stress = want_stress and self.engine.has_stress_head
+        E, F, S = self._evaluate_direct(pos, Z, cell, pbc if pbc.any() else None, want_stress)
+        n = len(Z)
+        w = self._w
+
+        def aff(x, p):
+            mu = w.get(f"{p}.running_mean")
+            var = w.get(f"{p}.running_var")
+            if var is None:
+                return x
+            return x * float(var.double().sqrt()) + (float(mu) if mu is not None else 0.0)
+        if "energy_head.normalizer.bn.running_var" in w:
+            E = aff(E, "energy_head.normalizer.bn") * n
+            E += float(w["energy_head.reference.linear.weight"].double().reshape(-1)[Z].sum())
+        F = aff(F, "forces_head.normalizer.bn")
+        if S is not None:
+            S = torch.cat([aff(S[:3], "stress_head.diag_normalizer.bn"),
+                           aff(S[3:], "stress_head.offdiag_normalizer.bn")])
+        if self.zbl:
+            Ez, Fz, Vz = self._zbl(self._ws, S is not None, scale=1.0)
+            E = E + Ez
+            F = F + Fz
+            if S is not None:
+                S = S + torch.as_tensor(voigt_6(Vz.numpy() / atoms_volume(atoms)))
+        self.results["energy"] = self.results["free_energy"] = E
+        self.results["energies"] = np.full(n, E / n)
+        self.results["forces"] = F.numpy()
+        if S is not None:
+            self.results["stress"] = S.numpy()
