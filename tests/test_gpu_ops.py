@@ -331,3 +331,15 @@ def test_csr_sum_orders_and_scales(W):
                     w = float(sc[e, 0]) if use_scale else 1.0
                     ref[n] += w * X[e, :W].double()
             close(out, ref, 1e-5)
+
+
+@pytest.mark.parametrize("N,C", [(1, 4), (1002, 256), (37, 70)])
+def test_col_mean_fixed_order(N, C):
+    """out[c] = scale * sum_n X[n, c] over a padded row stride; the same result twice."""
+    X = rnd(N, C + 12, seed=9)
+    out = torch.empty(C, device=dev)
+    call("atom_col_mean", ptr(X), C + 12, N, C, 1.0 / N, ptr(out), s())
+    close(out, X[:, :C].double().sum(0) / N, 1e-6)
+    out2 = torch.empty(C, device=dev)
+    call("atom_col_mean", ptr(X), C + 12, N, C, 1.0 / N, ptr(out2), s())
+    assert torch.equal(out, out2)

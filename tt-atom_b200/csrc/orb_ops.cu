@@ -337,13 +337,24 @@ __global__ void orb_messages_bwd_kernel(const float* __restrict__ g_agg, const f
 
 // --------------------------------------------------------------- node mean / broadcast
 // out[c] = scale * sum_n X[n, c] in a fixed order (one thread per column, rows in order).
-__global__ void col_mean_kernel(const float* __restrict__ X, long long ld, long long N, int C,
-                                float scale, float* __restrict__ out) {
-    int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= C) return;
+// 32 columns per block, 32 row groups (rows r, r + 32, ...) per column, then a fixed-order tree
+// over the groups: deterministic, and the rows are read by 1,024 threads instead of 32.
+__global__ void __launch_bounds__(1024) col_mean_kernel(const float* __restrict__ X, long long ld,
+                                                        long long N, int C, float scale,
+                                                        float* __restrict__ out) {
+    __shared__ float part[32][33];
+    const int cx = threadIdx.x, ry = threadIdx.y;
+    const int c = blockIdx.x * 32 + cx;
     float s = 0.f;
-    for (long long n = 0; n < N; ++n) s += X[n * ld + c];
-    out[c] = s * scale;
+    if (c < C)
+        for (long long n = ry; n < N; n += 32) s += X[n * ld + c];
+    part[ry][cx] = s;
+    __syncthreads();
+    for (int w = 16; w > 0; w >>= 1) {
+        if (ry < w) part[ry][cx] += part[ry + w][cx];
+        __syncthreads();
+    }
+    if (ry == 0 && c < C) out[c] = part[0][cx] * scale;
 }
 
 __global__ void row_broadcast_kernel(const float* __restrict__ v, long long N, int C,
@@ -520,7 +531,8 @@ extern "C" int atom_orb_messages_bwd(const float* g_agg, const float* gE_in, con
 
 extern "C" int atom_col_mean(const float* X, int64_t ld, int64_t N, int C, float scale,
                              float* out, void* stream) {
-    col_mean_kernel<<<ceil_div(C, 128), 128, 0, (cudaStream_t)stream>>>(X, ld, N, C, scale, out);
+    col_mean_kernel<<<ceil_div(C, 32), dim3(32, 32), 0, (cudaStream_t)stream>>>(X, ld, N, C,
+                                                                              scale, out);
     ATOM_CHECK_LAUNCH("col_mean");
     return ATOM_OK;
 }
