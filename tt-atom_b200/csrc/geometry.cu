@@ -179,6 +179,25 @@ __global__ void gauss_kernel(const float* __restrict__ pos, const int* __restric
     gauss[t] = expf(coeff * (d * d));
 }
 
+// The same, one block per edge (the edge vector computed once per block, not per element) and
+// four Gaussians per thread with a 16-byte store (NB a multiple of 4, gauss 16-byte aligned).
+__global__ void __launch_bounds__(128) gauss4_kernel(
+    const float* __restrict__ pos, const int* __restrict__ src, const int* __restrict__ tgt,
+    const int* __restrict__ img, const float* __restrict__ shifts, long long E,
+    const float* __restrict__ offset, int NB, float coeff, float* __restrict__ gauss) {
+    const long long e = blockIdx.x;
+    float v[3];
+    edge_vec(pos, src[e], tgt[e], shifts, img ? img[e] : 0, v);
+    const float nrm = norm3(v[0], v[1], v[2]);
+    for (int q = threadIdx.x; q < NB / 4; q += blockDim.x) {
+        const float4 o = *reinterpret_cast<const float4*>(offset + 4 * q);
+        const float d0 = nrm - o.x, d1 = nrm - o.y, d2 = nrm - o.z, d3 = nrm - o.w;
+        *reinterpret_cast<float4*>(gauss + e * NB + 4 * q) =
+            make_float4(expf(coeff * (d0 * d0)), expf(coeff * (d1 * d1)),
+                        expf(coeff * (d2 * d2)), expf(coeff * (d3 * d3)));
+    }
+}
+
 // <G, J Zb J Za> for given factor matrices
 template <int D>
 __device__ __forceinline__ float frob_chain(const float* G, const float* J, const float* Zb,
@@ -198,21 +217,34 @@ __global__ void __launch_bounds__(128) geometry_bwd_kernel(
     const float* __restrict__ offset, int NB, const float* __restrict__ g_coef,
     const float* __restrict__ gauss, const float* __restrict__ g_gauss,
     const float* __restrict__ g_env, float* __restrict__ g_ev) {
-    long long e = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    int lane = threadIdx.x & 31;
+    // a warp owns 32 edges: the Gaussian-basis adjoint of each is a warp reduction over the NB
+    // columns (one edge at a time, lane j keeps edge j's), then every lane runs the Wigner /
+    // angle chain of its own edge
+    const long long e0 = (((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 32;
+    const int lane = threadIdx.x & 31;
+    if (e0 >= E) return;
+    float gd = 0.f;   // dE/d dist of this lane's edge
+    if (g_gauss) {
+        const int nj = E - e0 < 32 ? (int)(E - e0) : 32;
+        for (int j = 0; j < nj; ++j) {
+            const long long ej = e0 + j;
+            float vj[3];
+            edge_vec(pos, src[ej], tgt[ej], shifts, img ? img[ej] : 0, vj);
+            const float nrm = angles(vj).nrm;
+            float t = 0.f;
+            for (int k = lane; k < NB; k += 32) {
+                float gk = gauss[ej * NB + k];
+                t = fmaf(g_gauss[ej * NB + k] * gk, 2.f * g.coeff * (nrm - offset[k]), t);
+            }
+            t = warp_sum(t);
+            if (lane == j) gd = t;
+        }
+    }
+    const long long e = e0 + lane;
     if (e >= E) return;
     float v[3];
     edge_vec(pos, src[e], tgt[e], shifts, img ? img[e] : 0, v);
     Angles a = angles(v);
-    float gd = 0.f;   // dE/d dist
-    if (g_gauss) {
-        for (int k = lane; k < NB; k += 32) {
-            float gk = gauss[e * NB + k];
-            gd = fmaf(g_gauss[e * NB + k] * gk, 2.f * g.coeff * (a.nrm - offset[k]), gd);
-        }
-        gd = warp_sum(gd);
-    }
-    if (lane != 0) return;
     float dv;
     envelope_val(a.nrm / g.cutoff, &dv);
     gd = fmaf(g_env[e], dv / g.cutoff, gd);
@@ -398,8 +430,12 @@ extern "C" int atom_edge_geometry(const float* pos, const int* src, const int* t
                                                          env, ev_out, dist_out);
     ATOM_CHECK_LAUNCH("edge_geometry");
     if (gauss && NB > 0) {
-        gauss_kernel<<<ceil_div(E * NB, 256), 256, 0, st>>>(pos, src, tgt, img, shifts, E, offset,
-                                                           NB, coeff, gauss);
+        if (NB % 4 == 0 && aligned16(gauss) && aligned16(offset))
+            gauss4_kernel<<<(unsigned)E, 128, 0, st>>>(pos, src, tgt, img, shifts, E, offset, NB,
+                                                      coeff, gauss);
+        else
+            gauss_kernel<<<ceil_div(E * NB, 256), 256, 0, st>>>(pos, src, tgt, img, shifts, E,
+                                                               offset, NB, coeff, gauss);
         ATOM_CHECK_LAUNCH("gauss");
     }
     return ATOM_OK;
@@ -416,7 +452,7 @@ extern "C" int atom_edge_geometry_bwd(const float* pos, const int* src, const in
     if (int s = make_geo(g, jd1, jd2, perm9, cutoff, coeff)) return s;
     ATOM_REQUIRE(!g_gauss || gauss, "g_gauss needs gauss");
     if (E == 0) return ATOM_OK;
-    geometry_bwd_kernel<<<ceil_div(E * 32, 128), 128, 0, (cudaStream_t)stream>>>(
+    geometry_bwd_kernel<<<ceil_div(E, 128), 128, 0, (cudaStream_t)stream>>>(
         pos, src, tgt, img, shifts, E, g, offset, NB, g_coef, gauss, g_gauss, g_env, g_ev);
     ATOM_CHECK_LAUNCH("edge_geometry_bwd");
     return ATOM_OK;
