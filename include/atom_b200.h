@@ -192,6 +192,17 @@ int atom_gemm(const float* A, int64_t lda, int64_t M, const atom_gemm_groups* gr
               const int* idx1, const int* idx2, int64_t ldt, int act, int accumulate,
               int precision, void* stream);
 
+/* atom_gemm with caller scratch (scratch_floats floats, stream-ordered, caller-owned): when a
+ * launch has too few output tiles to occupy the GPU (few rows, e.g. node-level layers), the
+ * tensor-core path splits each tile's K range over several CTAs, writes raw partial tiles to
+ * the scratch (splits x ceil(M / 128) * 128 rows of ldc floats) and adds them in split order
+ * (deterministic) before the bias / SiLU / accumulate epilogue. scratch NULL: as atom_gemm.
+ * No counterpart in the reference (its ttnn matmuls choose their own core split). */
+int atom_gemm_ex(const float* A, int64_t lda, int64_t M, const atom_gemm_groups* groups,
+                 float* C, int64_t ldc, float* Cpre, const float* T1, const float* T2,
+                 const int* idx1, const int* idx2, int64_t ldt, int act, int accumulate,
+                 int precision, float* scratch, int64_t scratch_floats, void* stream);
+
 /* Reads and clears the device-side error code of the tensor-core kernels (0 = none; a bounded
  * wait expired otherwise). Synchronises `stream`. */
 int atom_device_error(int* code_host, void* stream);

@@ -161,6 +161,52 @@ def test_gemm_tma_store_epilogue(M, precision, N2):
     assert (C2[:, gap] == 7.0).all()
 
 
+@pytest.mark.parametrize("precision", [1, 2])
+@pytest.mark.parametrize("M", [100, 1002])
+def test_gemm_split_k_with_scratch(M, precision):
+    """atom_gemm_ex with a scratch buffer: a launch with few row tiles splits K over more CTAs,
+    writes raw partial products to the scratch and sums them in a fixed order, then applies
+    bias, SiLU, the kept pre-activation and accumulation. Results match float64 within the
+    precision's tolerance, are bit-identical run to run, leave the columns around the groups
+    untouched, and a scratch too small to split gives the unsplit answer."""
+    from tt_atom.engine import _Groups
+    K1, N1, K2, N2 = 1024, 384, 512, 256
+    A = rnd(M, K1 + K2) * 0.1
+    B1, B2 = rnd(K1, N1, seed=1) * 0.1, rnd(K2, N2, seed=2) * 0.1
+    bias1, bias2 = rnd(N1, seed=3), rnd(N2, seed=4)
+    g = _Groups([dict(a_col=0, K=K1, c_col=0, N=N1, B=B1, bias=bias1),
+                 dict(a_col=K1, K=K2, c_col=N1 + 4, N=N2, B=B2, bias=bias2)])
+    ldc = N1 + 4 + N2 + 4
+    mpad = (M + 127) // 128 * 128
+    scratch = torch.empty(8 * mpad * ldc, device=dev)
+
+    def run(sc, n_sc, act=1, acc=0, C0=None):
+        C = torch.full((M, ldc), 7.0, device=dev) if C0 is None else C0.clone()
+        Cpre = torch.full((M, ldc), 7.0, device=dev)
+        call("atom_gemm_ex", ptr(A), K1 + K2, M, ctypes.byref(g.struct), ptr(C), ldc,
+             ptr(Cpre) if act else None, None, None, None, None, 0, act, acc, precision,
+             ptr(sc), n_sc, s())
+        return C, Cpre
+
+    Ad = A.double()
+    pre = torch.cat([Ad[:, :K1] @ B1.double() + bias1.double(),
+                     Ad[:, K1:] @ B2.double() + bias2.double()], 1)
+    cols = torch.cat([torch.arange(N1), torch.arange(N1 + 4, N1 + 4 + N2)]).to(dev)
+    gap = torch.ones(ldc, dtype=torch.bool, device=dev)
+    gap[cols] = False
+    C, Cpre = run(scratch, scratch.numel())
+    close(Cpre[:, cols], pre, TOL[precision])
+    close(C[:, cols], F.silu(pre), TOL[precision])
+    assert (C[:, gap] == 7.0).all() and (Cpre[:, gap] == 7.0).all()
+    C_again, _ = run(scratch, scratch.numel())
+    assert torch.equal(C, C_again)
+    C_small, _ = run(scratch, 1024)             # too small to split: the unsplit launch
+    close(C_small[:, cols], F.silu(pre), TOL[precision])
+    C_acc, _ = run(scratch, scratch.numel(), act=0, acc=1, C0=C)
+    close(C_acc[:, cols], C[:, cols].double() + pre, TOL[precision])
+    assert (C_acc[:, gap] == 7.0).all()
+
+
 def test_gemm_3xtf32_split_is_exact_for_truncating_tensor_cores():
     """3xTF32 leaves A in shared memory as loaded and relies on the tensor core reading an fp32
     operand as TF32 by dropping its low 13 mantissa bits (truncation); A_lo = A - trunc(A) is

@@ -18,7 +18,7 @@ bool gemm_tc_supported(const float* A, long long lda, const atom_gemm_groups* g,
 int gemm_tc(const float* A, long long lda, long long M, const atom_gemm_groups* g, float* C,
             long long ldc, float* Cpre, const float* T1, const float* T2, const int* idx1,
             const int* idx2, long long ldt, int act, int accumulate, int precision,
-            cudaStream_t st);
+            float* scratch, long long scratch_floats, cudaStream_t st);
 
 struct GemmArgs {
     const float* A;
@@ -138,10 +138,11 @@ __global__ void __launch_bounds__(256) gemm_fma_kernel(GemmArgs p) {
 
 using namespace atom;
 
-extern "C" int atom_gemm(const float* A, int64_t lda, int64_t M, const atom_gemm_groups* groups,
-                         float* Cout, int64_t ldc, float* C_pre, const float* T1, const float* T2,
-                         const int* idx1, const int* idx2, int64_t ldt, int act, int accumulate,
-                         int precision, void* stream) {
+extern "C" int atom_gemm_ex(const float* A, int64_t lda, int64_t M,
+                            const atom_gemm_groups* groups, float* Cout, int64_t ldc, float* C_pre,
+                            const float* T1, const float* T2, const int* idx1, const int* idx2,
+                            int64_t ldt, int act, int accumulate, int precision, float* scratch,
+                            int64_t scratch_floats, void* stream) {
     ATOM_REQUIRE(groups && groups->ngroups >= 1 && groups->ngroups <= 8, "1..8 groups");
     ATOM_REQUIRE(act == 0 || act == 1, "act must be 0 or 1");
     ATOM_REQUIRE(!T1 || idx1, "T1 needs idx1");
@@ -163,9 +164,17 @@ extern "C" int atom_gemm(const float* A, int64_t lda, int64_t M, const atom_gemm
     ATOM_REQUIRE(ceil_div(M, BM) < 65536, "M too large");
     if (gemm_tc_supported(A, lda, groups, precision))
         return gemm_tc(A, lda, M, groups, Cout, ldc, C_pre, T1, T2, idx1, idx2, ldt, act,
-                       accumulate, precision, (cudaStream_t)stream);
+                       accumulate, precision, scratch, scratch_floats, (cudaStream_t)stream);
     dim3 grid(tiles, ceil_div(M, BM));
     gemm_fma_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
     ATOM_CHECK_LAUNCH("gemm");
     return ATOM_OK;
+}
+
+extern "C" int atom_gemm(const float* A, int64_t lda, int64_t M, const atom_gemm_groups* groups,
+                         float* Cout, int64_t ldc, float* C_pre, const float* T1, const float* T2,
+                         const int* idx1, const int* idx2, int64_t ldt, int act, int accumulate,
+                         int precision, void* stream) {
+    return atom_gemm_ex(A, lda, M, groups, Cout, ldc, C_pre, T1, T2, idx1, idx2, ldt, act,
+                        accumulate, precision, nullptr, 0, stream);
 }

@@ -62,6 +62,8 @@ struct Args {
     const int* idx2;
     int act, accumulate;
     int bn;              // column-tile width of this launch (multiple of 32, <= the kernel's BN)
+    int ksplit;          // K splits per tile (> 1: raw partial tiles go to the scratch rows)
+    int mpad;            // rows per split in the partial buffer (a multiple of BM >= M)
     int tma_out;         // epilogue writes C (and Cpre) with TMA stores / reduce-adds
     int nacc;            // tensor-memory accumulators the K stages are spread over (1 or 4)
     Groups g;
@@ -244,22 +246,29 @@ struct Maps {
     CUtensorMap l[8];
     CUtensorMap c[8];     // per group: C columns c_col .. c_col + N (TMA-store epilogue)
     CUtensorMap cp[8];    // per group: the same columns of Cpre
+    CUtensorMap pm[8];    // per group: those columns of the split-K partial rows (ksplit x mpad)
 };
 
 // Tile t of the launch -> (group, first row, first column, K stages).
+// Work item t = tile * ksplit + split: the split's K stages are [kt0, kt1).
 struct TileInfo {
-    int grp, n0, nk;
+    int grp, n0, nk, kt0, kt1, ks;
     long long m0;
 };
 __device__ __forceinline__ TileInfo tile_info(const Args& p, int ntn, int t) {
     TileInfo ti;
+    ti.ks = t % p.ksplit;
+    t /= p.ksplit;
     int mt = t / ntn, tn = t - mt * ntn;
     int grp = 0;
     while (grp + 1 < p.g.ngroups && tn >= p.g.tile_start[grp + 1]) ++grp;
     ti.grp = grp;
     ti.n0 = (tn - p.g.tile_start[grp]) * p.bn;
     ti.m0 = (long long)mt * BM;
-    ti.nk = p.g.K[grp] / BK;
+    const int nk = p.g.K[grp] / BK;
+    ti.kt0 = ti.ks * nk / p.ksplit;
+    ti.kt1 = (ti.ks + 1) * nk / p.ksplit;
+    ti.nk = ti.kt1 - ti.kt0;
     return ti;
 }
 
@@ -329,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = blockIdx.x; t < ntiles && !aborted(); t += gridDim.x) {
                 TileInfo ti = tile_info(p, ntn, t);
                 const int a_x0 = p.g.a_col[ti.grp];
-                for (int kt = 0; kt < ti.nk; ++kt, ++it) {
+                for (int kt = ti.kt0; kt < ti.kt1; ++kt, ++it) {
                     int s = it % S;
                     uint32_t ph = (it / S) & 1u;
                     if (!mbar_wait(&empty[s], ph ^ 1u, 1) || aborted()) {
@@ -354,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t idesc = idesc_tf32(rem >= p.bn ? p.bn : (rem + 15) & ~15);
                 bool ok = !aborted() && mbar_wait(acce, (j & 1u) ^ 1u, 5);
                 if (ok) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                for (int kt = 0; ok && kt < ti.nk; ++kt, ++it) {
+                for (int kt = ti.kt0; ok && kt < ti.kt1; ++kt, ++it) {
                     int s = it % S;
                     uint32_t ph = (it / S) & 1u;
                     if (!mbar_wait(MODE == 2 ? &conv[s] : &full[s], ph, 2) || aborted()) {
@@ -370,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t bl = smem_u32(stBL(s));
 #pragma unroll
                         for (int kk = 0; kk < BK / 8; ++kk) {
-                            const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
+                            const uint32_t acc = (kt > ti.kt0 || kk > 0) ? 1u : 0u;
                             mma_tf32_ta(tmem, slot + kk * 8, sdesc(b + kk * 32), idesc, acc);
                             mma_tf32_ta(tmem + BN, slot + kk * 8, sdesc(bl + kk * 32), idesc,
                                         acc);
@@ -381,8 +390,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         mma_commit(&afree[it & 1u]);
                     } else {
                         // stage kt accumulates into accumulator kt % nacc (columns BN apart)
-                        const uint32_t dacc = tmem + (uint32_t)((kt % p.nacc) * BN);
-                        const bool first = kt < p.nacc;
+                        const uint32_t dacc = tmem + (uint32_t)(((kt - ti.kt0) % p.nacc) * BN);
+                        const bool first = kt - ti.kt0 < p.nacc;
 #pragma unroll
                         for (int kk = 0; kk < BK / 8; ++kk) {
                             uint32_t acc = (!first || kk > 0) ? 1u : 0u;
@@ -414,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int t = blockIdx.x; ok && t < ntiles && !aborted(); t += gridDim.x) {
                 TileInfo ti = tile_info(p, ntn, t);
-                for (int kt = 0; kt < ti.nk; ++kt, ++it) {
+                for (int kt = ti.kt0; kt < ti.kt1; ++kt, ++it) {
                     int s = it % S;
                     uint32_t ph = (it / S) & 1u;
                     ok = mbar_wait(&full[s], ph, 3) &&
@@ -486,7 +495,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             mbar_arrive(acce);                  // tensor memory may take the next tile now
             if (!active) continue;
-            const float* bias = p.g.bias[ti.grp];
+            // split-K work items store the raw partial sums (bias, tables and SiLU are applied
+            // when the partials are added)
+            const bool split = p.ksplit > 1;
+            const float* bias = split ? nullptr : p.g.bias[ti.grp];
             if (p.tma_out) {
                 // each 32 x 32 block: bias (+ gathered table rows) (+ SiLU) applied in registers,
                 // written 128-byte swizzled into this warp's buffer, stored by one lane with TMA
@@ -509,8 +521,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
                     for (int pass = 0; pass < 2; ++pass) {
                         // pass 0: pre-activation to Cpre (SiLU launches that keep it)
-                        if (pass == 0 && !(p.act == 1 && p.Cpre)) continue;
-                        const bool silu = pass == 1 && p.act == 1;
+                        if (pass == 0 && (split || !(p.act == 1 && p.Cpre))) continue;
+                        const bool silu = !split && pass == 1 && p.act == 1;
                         if (pending && lane == 0)
                             asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
                         __syncwarp();
@@ -554,9 +566,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                         __syncwarp();
-                        if (lane == 0)
-                            tma_store_2d(pass == 0 ? &maps.cp[ti.grp] : &maps.c[ti.grp], buf, x0,
-                                         y0, pass == 1 && p.accumulate);
+                        if (lane == 0) {
+                            if (split)
+                                tma_store_2d(&maps.pm[ti.grp], buf, x0, ti.ks * p.mpad + y0, false);
+                            else
+                                tma_store_2d(pass == 0 ? &maps.cp[ti.grp] : &maps.c[ti.grp], buf,
+                                             x0, y0, pass == 1 && p.accumulate);
+                        }
                         pending = true;
                     }
                 }
@@ -650,11 +666,40 @@ static int make_map(CUtensorMap* m, const float* base, long long inner, long lon
 // correction products in another, whose rounding is negligible against the total.
 constexpr int g_nacc = 4;
 
+// Split-K: C[m, c_col + n] (+)= act((sum over splits in order of P[s, m, c_col + n]) + bias[n]),
+// the pre-activation kept in Cpre when given; four columns per thread.
+__global__ void splitk_reduce_kernel(const float* __restrict__ P, int S, long long mpad,
+                                     long long ldc, long long M, int c_col, int N,
+                                     const float* __restrict__ bias, int act, float* Cpre,
+                                     int accumulate, float* C) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int nq = N / 4;
+    if (t >= M * nq) return;
+    const long long m = t / nq;
+    const int n = 4 * (int)(t - m * nq);
+    const long long off = m * ldc + c_col + n;
+    float4 acc = *reinterpret_cast<const float4*>(P + off);
+    for (int k = 1; k < S; ++k) {
+        const float4 q = *reinterpret_cast<const float4*>(P + k * mpad * ldc + off);
+        acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
+    }
+    float x[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        if (bias) x[k] += bias[n + k];
+        if (act == 1) {
+            if (Cpre) Cpre[off + k] = x[k];
+            x[k] = silu_f(x[k]);
+        }
+        C[off + k] = accumulate ? C[off + k] + x[k] : x[k];
+    }
+}
+
 template <int BN, int MODE>
 static int launch(const float* A, long long lda, long long M, const atom_gemm_groups* g,
                   float* C, long long ldc, float* Cpre, const float* T1, const float* T2,
                   const int* idx1, const int* idx2, long long ldt, int act, int accumulate,
-                  cudaStream_t st) {
+                  float* scratch, long long scratch_floats, cudaStream_t st) {
     using CF = Cfg<BN, MODE>;
     static bool attr_set = false;
     if (!attr_set) {
@@ -682,16 +727,44 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
     int dev = 0, nsm = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    // column-tile width: the full BN unless that leaves SMs without a tile (few rows, e.g.
-    // node-level GEMMs); then the widest multiple of 32 (down to 64) that gives every SM one
+    // TMA-store epilogue: 16-byte aligned column blocks, rows and gathered-table rows. A
+    // group's width must be a multiple of 4 columns too: the store clips at 16-byte granularity,
+    // so a 130-column group would also get columns 130 and 131 written (measured on B200).
+    bool tma_out = ldc % 4 == 0 && aligned16(C) && (!Cpre || aligned16(Cpre)) &&
+                   ((!T1 && !T2) || ldt % 4 == 0) && (!T1 || aligned16(T1)) &&
+                   (!T2 || aligned16(T2));
+    for (int i = 0; i < g->ngroups; ++i)
+        tma_out = tma_out && g->c_col[i] % 4 == 0 && g->N[i] % 4 == 0 && g->N[i] >= 32 &&
+                  ((!T1 && !T2) || g->t_col[i] % 4 == 0);
+    p.tma_out = tma_out ? 1 : 0;
     const long long mblocks = ceil_div(M, BM);
     auto count_tiles = [&](int w) {
         long long t = 0;
         for (int i = 0; i < g->ngroups; ++i) t += ceil_div(g->N[i], w);
         return t * mblocks;
     };
+    // split-K (caller scratch given, TMA epilogue, no gathered tables): when full-width tiles
+    // would leave at least half the SMs idle, each tile's K stages are split over up to 8 CTAs
+    // (>= 4 K stages each, and only for K >= 512: short-K launches lose more to the partial
+    // traffic than they gain); the raw partials are added in split order by a second kernel
+    int ksplit = 1;
+    const long long mpad = mblocks * BM;
+    if (scratch && tma_out && !T1 && !T2 && count_tiles(BN) * 2 <= nsm) {
+        int min_nk = 1 << 30;
+        for (int i = 0; i < g->ngroups; ++i) min_nk = min_nk < g->K[i] / BK ? min_nk : g->K[i] / BK;
+        int sk = (int)(nsm / count_tiles(BN));
+        sk = sk < 8 ? sk : 8;
+        sk = min_nk < 16 ? 1 : (sk < min_nk / 4 ? sk : min_nk / 4);
+        while (sk >= 2 && (long long)sk * mpad * ldc > scratch_floats) --sk;
+        if (sk >= 2) ksplit = sk;
+    }
+    p.ksplit = ksplit;
+    p.mpad = (int)mpad;
+    // column-tile width: the full BN unless that leaves SMs without a tile (few rows, e.g.
+    // node-level GEMMs without split-K); then the widest multiple of 32 (down to 64) that
+    // gives every SM one
     int bn = BN;
-    if (count_tiles(BN) < nsm)
+    if (ksplit == 1 && count_tiles(BN) < nsm)
         for (int w = BN - 32; w >= 64; w -= 32) {
             bn = w;
             if (count_tiles(w) >= nsm) break;
@@ -712,25 +785,19 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
             if (int s = make_map(&maps.l[i], g->Bt_lo[i], g->K[i], g->N[i], g->K[i], BN)) return s;
     }
     p.g.tile_start[g->ngroups] = tiles;
-    // TMA-store epilogue: 16-byte aligned column blocks, rows and gathered-table rows. A
-    // group's width must be a multiple of 4 columns too: the store clips at 16-byte granularity,
-    // so a 130-column group would also get columns 130 and 131 written (measured on B200).
-    bool tma_out = ldc % 4 == 0 && aligned16(C) && (!Cpre || aligned16(Cpre)) &&
-                   ((!T1 && !T2) || ldt % 4 == 0) && (!T1 || aligned16(T1)) &&
-                   (!T2 || aligned16(T2));
-    for (int i = 0; i < g->ngroups; ++i)
-        tma_out = tma_out && g->c_col[i] % 4 == 0 && g->N[i] % 4 == 0 && g->N[i] >= 32 &&
-                  ((!T1 && !T2) || g->t_col[i] % 4 == 0);
-    p.tma_out = tma_out ? 1 : 0;
     if (tma_out) {
         for (int i = 0; i < g->ngroups; ++i) {
             if (int s = make_map(&maps.c[i], C + g->c_col[i], g->N[i], M, ldc, 32)) return s;
             if (act == 1 && Cpre)
                 if (int s = make_map(&maps.cp[i], Cpre + g->c_col[i], g->N[i], M, ldc, 32))
                     return s;
+            if (ksplit > 1)
+                if (int s = make_map(&maps.pm[i], scratch + g->c_col[i], g->N[i],
+                                     ksplit * mpad, ldc, 32))
+                    return s;
         }
     }
-    const long long ntiles = (long long)tiles * ceil_div(M, BM);
+    const long long ntiles = (long long)tiles * ceil_div(M, BM) * ksplit;
     if (ntiles >= (1LL << 31)) {
         set_error("gemm_tc: too many tiles");
         return ATOM_ERR_ARG;
@@ -742,7 +809,17 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
     else
         gemm_tc_kernel<BN, MODE, false><<<grid, kThreads, CF::kSmem, st>>>(maps, p, tiles,
                                                                           (int)ntiles);
-    return check_launch("gemm_tc");
+    if (int s = check_launch("gemm_tc")) return s;
+    if (ksplit > 1) {
+        for (int i = 0; i < g->ngroups; ++i) {
+            const long long n4 = M * (g->N[i] / 4);
+            splitk_reduce_kernel<<<ceil_div(n4, 256), 256, 0, st>>>(
+                scratch, ksplit, mpad, ldc, M, g->c_col[i], g->N[i], g->bias[i], act, Cpre,
+                accumulate, C);
+        }
+        return check_launch("gemm_tc split-K reduce");
+    }
+    return ATOM_OK;
 }
 
 }  // namespace tc
@@ -763,13 +840,13 @@ bool gemm_tc_supported(const float* A, long long lda, const atom_gemm_groups* g,
 int gemm_tc(const float* A, long long lda, long long M, const atom_gemm_groups* g, float* C,
             long long ldc, float* Cpre, const float* T1, const float* T2, const int* idx1,
             const int* idx2, long long ldt, int act, int accumulate, int precision,
-            cudaStream_t st) {
+            float* scratch, long long scratch_floats, cudaStream_t st) {
     if (int s = tc::encoder()) return s;
     if (precision == 2)
         return tc::launch<192, 2>(A, lda, M, g, C, ldc, Cpre, T1, T2, idx1, idx2, ldt, act,
-                                  accumulate, st);
+                                  accumulate, scratch, scratch_floats, st);
     return tc::launch<128, 1>(A, lda, M, g, C, ldc, Cpre, T1, T2, idx1, idx2, ldt, act,
-                              accumulate, st);
+                              accumulate, scratch, scratch_floats, st);
 }
 
 }  // namespace atom

@@ -54,6 +54,9 @@ _SIGS = {
     "atom_gemm": (c_void_p, c_int64, c_int64, ctypes.POINTER(GemmGroups), c_void_p, c_int64,
                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int,
                   c_void_p),
+    "atom_gemm_ex": (c_void_p, c_int64, c_int64, ctypes.POINTER(GemmGroups), c_void_p, c_int64,
+                     c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int,
+                     c_int, c_void_p, c_int64, c_void_p),
     "atom_device_error": (c_void_p, c_void_p),
     "atom_rotate_in": (c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_int64,
                        c_int, c_void_p, c_void_p, c_void_p),

@@ -264,10 +264,15 @@ class UMAEngine:
                             for c in range(9)]))
 
     # ------------------------------------------------------------------------------ helpers
+    _scratch = None
+
     def _gemm(self, A, lda, M, groups, Cout, ldc, *, Cpre=None, T1=None, T2=None, idx1=None,
               idx2=None, ldt=0, act=0, accumulate=0, stream=0):
-        call("atom_gemm", ptr(A), lda, M, groups.struct, ptr(Cout), ldc, ptr(Cpre), ptr(T1),
-             ptr(T2), ptr(idx1), ptr(idx2), ldt, act, accumulate, self.precision, stream)
+        # the workspace's scratch lets node-level launches (few rows) split K over more CTAs
+        sc = self._scratch
+        call("atom_gemm_ex", ptr(A), lda, M, groups.struct, ptr(Cout), ldc, ptr(Cpre), ptr(T1),
+             ptr(T2), ptr(idx1), ptr(idx2), ldt, act, accumulate, self.precision, ptr(sc),
+             sc.numel() if sc is not None else 0, stream)
 
     def workspace_bytes(self, N, E, chunk_edges=None):
         """Approximate device bytes of a workspace for N atoms and E edges (unchunked, or
@@ -384,6 +389,7 @@ class UMAEngine:
         g = ws.graph
         N, E = g.N, g.E
         C, H, EC, NB, G = self.C, self.H, self.EC, self.NB, self.G
+        self._scratch = ws.gemm_scratch
         if pos.data_ptr() != ws.pos.data_ptr():
             ws.pos.copy_(pos)
         # ---------------- geometry
@@ -696,6 +702,9 @@ class Workspace:
         self.chunk_edges = chunk_edges
         self.chunks = None
         self.pos = f(N, 3)
+        # split-K scratch of node-level GEMMs (few rows): 8 splits x up to 4,096 padded rows x
+        # the widest node row; larger launches have enough tiles without splitting
+        self.gemm_scratch = f(8 * min(((N + 127) // 128) * 128, 4096) * 9 * max(C, H))
         self.coef, self.gauss, self.env, self.ev = f(E, 35), f(E, NB), f(E), f(E, 3)
         if chunk_edges is None:
             Eb, RW, nY, GW = E, eng.ldr, NL, G * EC

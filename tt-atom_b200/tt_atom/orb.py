@@ -102,8 +102,11 @@ class OrbEngine:
 
     def _gemm(self, A, lda, M, groups, Cout, ldc, *, Cpre=None, T1=None, T2=None, idx1=None,
               idx2=None, ldt=0, act=0, accumulate=0, s=0):
-        call("atom_gemm", ptr(A), lda, M, groups.struct, ptr(Cout), ldc, ptr(Cpre), ptr(T1),
-             ptr(T2), ptr(idx1), ptr(idx2), ldt, act, accumulate, self.precision, s)
+        # the workspace's scratch lets node-level launches (few rows) split K over more CTAs
+        sc = self._scratch
+        call("atom_gemm_ex", ptr(A), lda, M, groups.struct, ptr(Cout), ldc, ptr(Cpre), ptr(T1),
+             ptr(T2), ptr(idx1), ptr(idx2), ldt, act, accumulate, self.precision, ptr(sc),
+             sc.numel() if sc is not None else 0, s)
 
     def workspace(self, graph):
         return OrbWorkspace(self, graph)
@@ -148,8 +151,11 @@ class OrbEngine:
         return dict(name="Orb edge-MLP hidden GEMM", ms=t0.elapsed_time(t1) / reps,
                     flop=2.0 * E * Hd * Hd)
 
+    _scratch = None
+
     def run(self, ws, pos=None, forces=True, virial=False, stream=None):
         """One E (+F, +virial) evaluation on ``ws``'s graph (``pos`` defaults to ws.pos)."""
+        self._scratch = ws.gemm_scratch
         if pos is not None and pos.data_ptr() != ws.pos.data_ptr():
             ws.pos.copy_(pos)
         s = L.stream_ptr(stream)
@@ -278,6 +284,8 @@ class OrbWorkspace:
         N, E, C, Hd, NL = graph.N, graph.E, eng.C, eng.Hd, eng.NL
         f = lambda *sh: torch.empty(*sh, device=dev, dtype=torch.float32)  # noqa: E731
         self.pos = f(N, 3)
+        # split-K scratch of node-level GEMMs: 8 splits x padded rows x the widest node row
+        self.gemm_scratch = f(8 * ((N + 127) // 128) * 128 * max(2 * Hd, 3 * C))
         self.feat, self.cut, self.ev = f(E, 16 * eng.nb), f(E), f(E, 3)
         self.x0 = f(N, eng.D0)
         self._eng = eng
