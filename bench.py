@@ -380,7 +380,7 @@ def run_ours(args):
         if ws_n > 1:
             torch.distributed.destroy_process_group()
         return
-    eng_precision = {0: "fp32", 1: "tf32", 2: "3xtf32"}[eng.precision]
+    eng_precision = {0: "fp32", 1: "tf32", 2: "3xtf32", 3: "3xf16"}[eng.precision]
     ms_step = ms / args.steps
     value = N * ws_n * args.steps / (ms / 1e3)
     hbm, bf16, src = peaks()
@@ -526,7 +526,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cells", default="10,10,5", help="fcc cells (profiling uses a smaller cell)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "fp32", "tf32"])
+    ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "3xf16", "fp32", "tf32"])
     ap.add_argument("--chunk-edges", type=int, default=0,
                     help="fe65k: receiver-chunk size of the edge stages (0: automatic, chunked "
                          "on one GPU only)")

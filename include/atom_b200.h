@@ -41,6 +41,9 @@ enum {
 int atom_last_error(char* buf, size_t n);
 /* ABI version of this library. */
 int atom_abi_version(void);
+/* Number of kernels this library has launched since it was loaded (all threads). Launches
+ * replayed from a captured CUDA graph are not counted again. No counterpart in the reference. */
+int atom_launch_count(int64_t* n);
 
 /* ------------------------------------------------------------------------------------------
  * Reference-op equivalents. These four replace the nanobind ops of the reference's custom
@@ -175,9 +178,15 @@ int atom_forces_virial(const float* g_ev, const float* ev, int64_t E, int64_t N,
  * for m < M, n < N_g, k < K_g. bias/T1/T2 optional (NULL). act: 0 none, 1 SiLU (then
  * C_pre, when not NULL, receives the pre-activation). accumulate != 0 adds into C.
  * precision: 0 = fp32 FMA; 1 = TF32 tensor cores (tcgen05); 2 = 3xTF32 tensor cores (fp32-level
- * accuracy). Modes 1 and 2 read the K-major weight copies Bt[g] ([N_g, K_g] row-major, low 13
+ * accuracy); 3 = fp16-pair tensor cores (fp32-level accuracy at twice mode 2's MMA rate).
+ * Modes 1 and 2 read the K-major weight copies Bt[g] ([N_g, K_g] row-major, low 13
  * mantissa bits cleared) and, for mode 2, Bt_lo[g] = B^T - Bt; they need every K_g to be a
- * multiple of 32, lda % 4 == 0 and 16-byte aligned A / Bt, and otherwise run the fp32 kernel. */
+ * multiple of 32, lda % 4 == 0 and 16-byte aligned A / Bt, and otherwise run the fp32 kernel.
+ * Mode 3 reads, per group, s_n = 2^(14 - floor(log2 max_k |B[k, n]|)) (1 for a zero column),
+ * Bh[g] = fp16(B^T s) and Bh_lo[g] = fp16((B^T s - Bh) * 2^11) ([N_g, K_g] fp16 row-major) and
+ * Bh_inv[g] = 1 / s (N_g floats); it needs a scratch (atom_gemm_ex) of at least
+ * ceil(ngroups * ceil(M / 128) * 128 / 64) * 64 floats for its per-row scales of A, and runs
+ * as mode 2 without one. */
 typedef struct {
     int ngroups;
     int a_col[8], K[8], c_col[8], N[8], ldb[8], t_col[8];
@@ -185,6 +194,9 @@ typedef struct {
     const float* bias[8];
     const float* Bt[8];
     const float* Bt_lo[8];
+    const void* Bh[8];
+    const void* Bh_lo[8];
+    const float* Bh_inv[8];
 } atom_gemm_groups;
 
 int atom_gemm(const float* A, int64_t lda, int64_t M, const atom_gemm_groups* groups,

@@ -83,10 +83,21 @@ def test_fused_gate_and_ln_bw():
 
 # ------------------------------------------------------------------------------- GEMM
 
-TOL = {0: 1e-5, 1: 5e-3, 2: 1e-5}
+TOL = {0: 1e-5, 1: 5e-3, 2: 1e-5, 3: 1e-5}
 
 
-@pytest.mark.parametrize("precision", [0, 1, 2])
+def gemm(A, lda, M, groups, C, ldc, Cpre, T1, T2, i1, i2, ldt, act, acc, precision):
+    """atom_gemm_ex with a scratch large enough for the fp16-pair mode's row scales (and
+    split-K partials); other modes get no scratch (plain atom_gemm)."""
+    sc = None
+    if precision == 3:
+        sc = torch.empty(8 * ((M + 127) // 128 * 128) * max(ldc, 64) + 1024, device=dev)
+    call("atom_gemm_ex", ptr(A), lda, M, ctypes.byref(groups.struct), ptr(C), ldc, ptr(Cpre),
+         ptr(T1), ptr(T2), ptr(i1), ptr(i2), ldt, act, acc, precision, ptr(sc),
+         sc.numel() if sc is not None else 0, s())
+
+
+@pytest.mark.parametrize("precision", [0, 1, 2, 3])
 @pytest.mark.parametrize("M", [1, 129, 1000])
 @pytest.mark.parametrize("N2", [130, 132])
 def test_grouped_gemm_with_epilogues(M, precision, N2):
@@ -105,8 +116,7 @@ def test_grouped_gemm_with_epilogues(M, precision, N2):
                  dict(a_col=K1, K=K2, c_col=N1, N=N2, B=B2, t_col=200)])
     C = torch.empty(M, N1 + N2, device=dev)
     Cpre = torch.empty(M, N1 + N2, device=dev)
-    call("atom_gemm", ptr(A), K1 + K2, M, ctypes.byref(g.struct), ptr(C), N1 + N2, ptr(Cpre),
-         ptr(T1), ptr(T2), ptr(i1), ptr(i2), 400, 1, 0, precision, s())
+    gemm(A, K1 + K2, M, g, C, N1 + N2, Cpre, T1, T2, i1, i2, 400, 1, 0, precision)
     Ad = A.double()
     r1 = Ad[:, :K1] @ B1.double() + bias1.double() + T1.double()[i1.long(), :N1] + \
         T2.double()[i2.long(), :N1]
@@ -117,15 +127,14 @@ def test_grouped_gemm_with_epilogues(M, precision, N2):
     close(C, F.silu(pre), TOL[precision])
     # accumulate
     C2 = C.clone()
-    call("atom_gemm", ptr(A), K1 + K2, M, ctypes.byref(g.struct), ptr(C2), N1 + N2, None,
-         ptr(T1), ptr(T2), ptr(i1), ptr(i2), 400, 0, 1, precision, s())
+    gemm(A, K1 + K2, M, g, C2, N1 + N2, None, T1, T2, i1, i2, 400, 0, 1, precision)
     close(C2, C.double() + pre, TOL[precision])
     code = ctypes.c_int(-1)
     call("atom_device_error", ctypes.byref(code), s())
     assert code.value == 0
 
 
-@pytest.mark.parametrize("precision", [1, 2])
+@pytest.mark.parametrize("precision", [1, 2, 3])
 @pytest.mark.parametrize("M", [1, 129, 1000])
 @pytest.mark.parametrize("N2", [132, 130])
 def test_gemm_tma_store_epilogue(M, precision, N2):
@@ -144,8 +153,7 @@ def test_gemm_tma_store_epilogue(M, precision, N2):
     ldc = N1 + 4 + N2 + 2
     C = torch.full((M, ldc), 7.0, device=dev)
     Cpre = torch.full((M, ldc), 7.0, device=dev)
-    call("atom_gemm", ptr(A), K1 + K2, M, ctypes.byref(g.struct), ptr(C), ldc, ptr(Cpre),
-         None, None, None, None, 0, 1, 0, precision, s())
+    gemm(A, K1 + K2, M, g, C, ldc, Cpre, None, None, None, None, 0, 1, 0, precision)
     Ad = A.double()
     pre = torch.cat([Ad[:, :K1] @ B1.double() + bias1.double(), Ad[:, K1:] @ B2.double()], 1)
     cols = torch.cat([torch.arange(N1), torch.arange(N1 + 4, N1 + 4 + N2)]).to(dev)
@@ -155,13 +163,12 @@ def test_gemm_tma_store_epilogue(M, precision, N2):
     gap[cols] = False
     assert (C[:, gap] == 7.0).all() and (Cpre[:, gap] == 7.0).all()   # nothing outside the groups
     C2 = C.clone()
-    call("atom_gemm", ptr(A), K1 + K2, M, ctypes.byref(g.struct), ptr(C2), ldc, None,
-         None, None, None, None, 0, 0, 1, precision, s())
+    gemm(A, K1 + K2, M, g, C2, ldc, None, None, None, None, None, 0, 0, 1, precision)
     close(C2[:, cols], C[:, cols].double() + pre, TOL[precision])
     assert (C2[:, gap] == 7.0).all()
 
 
-@pytest.mark.parametrize("precision", [1, 2])
+@pytest.mark.parametrize("precision", [1, 2, 3])
 @pytest.mark.parametrize("M", [100, 1002])
 def test_gemm_split_k_with_scratch(M, precision):
     """atom_gemm_ex with a scratch buffer: a launch with few row tiles splits K over more CTAs,
@@ -225,7 +232,7 @@ def test_gemm_3xtf32_split_is_exact_for_truncating_tensor_cores():
     assert (C == 1.0 + 3.0 * 2.0 ** -12).all()
 
 
-@pytest.mark.parametrize("precision", [1, 2])
+@pytest.mark.parametrize("precision", [1, 2, 3])
 def test_tensor_core_gemm_so2_shapes_many_groups(precision):
     """The so2_conv_1 block layout (K = 768, 1024, 512) and an 8-group radial-style layout."""
     from tt_atom.engine import _Groups
@@ -237,8 +244,7 @@ def test_tensor_core_gemm_so2_shapes_many_groups(precision):
                  dict(a_col=768, K=1024, c_col=640, N=512, B=Bs[1]),
                  dict(a_col=1792, K=512, c_col=1152, N=256, B=Bs[2])])
     C = torch.empty(M, 1408, device=dev)
-    call("atom_gemm", ptr(A), 2304, M, ctypes.byref(g.struct), ptr(C), 1408, None, None, None,
-         None, None, 0, 0, 0, precision, s())
+    gemm(A, 2304, M, g, C, 1408, None, None, None, None, None, 0, 0, 0, precision)
     Ad = A.double()
     ref = torch.cat([Ad[:, :768] @ Bs[0].double() + bias0.double(),
                      Ad[:, 768:1792] @ Bs[1].double(), Ad[:, 1792:] @ Bs[2].double()], 1)
@@ -252,10 +258,82 @@ def test_tensor_core_gemm_so2_shapes_many_groups(precision):
     g = _Groups([dict(a_col=k * EC, K=EC, c_col=offs[k], N=Ws[k].shape[1], B=Ws[k])
                  for k in range(G)])
     C = torch.empty(M, offs[-1], device=dev)
-    call("atom_gemm", ptr(X), G * EC, M, ctypes.byref(g.struct), ptr(C), offs[-1], None, None,
-         None, None, None, 0, 0, 0, precision, s())
+    gemm(X, G * EC, M, g, C, offs[-1], None, None, None, None, None, 0, 0, 0, precision)
     ref = torch.cat([X[:, k * EC:(k + 1) * EC].double() @ Ws[k].double() for k in range(G)], 1)
     close(C, ref, TOL[precision])
+
+
+def test_gemm_f16_pair_exact_on_small_integers():
+    """Known answer for the fp16-pair mode's operand layout (two fp16 per tensor-memory column,
+    64-byte swizzled weights): small integers are exact in every split, so C must equal the
+    integer product exactly, for every row, column and K position."""
+    from tt_atom.engine import _Groups
+    M, K, N = 256, 96, 160
+    g0 = torch.Generator(device="cpu").manual_seed(5)
+    A = torch.randint(-8, 9, (M, K), generator=g0).float().to(dev)
+    B = torch.randint(-8, 9, (K, N), generator=g0).float().to(dev)
+    g = _Groups([dict(a_col=0, K=K, c_col=0, N=N, B=B)])
+    C = torch.empty(M, N, device=dev)
+    gemm(A, K, M, g, C, N, None, None, None, None, None, 0, 0, 0, 3)
+    assert torch.equal(C, (A.double() @ B.double()).float())
+
+
+def test_gemm_f16_pair_wide_magnitude_range():
+    """fp16 covers only ~2^-24 .. 2^16, so the fp16-pair mode scales every A row (per group)
+    and every B column by a power of two. Rows over 1e-15 .. 1e15 and columns over
+    1e-10 .. 1e10 (products stay inside fp32), an all-zero row and a row with one entry 1e9
+    times the others must still come out with fp32-level error relative to sum |a| |b|."""
+    from tt_atom.engine import _Groups
+    M, K, N = 300, 256, 192
+    A = rnd(M, K, seed=21)
+    g0 = torch.Generator(device="cpu").manual_seed(23)
+    rs = torch.logspace(-15, 15, M)[torch.randperm(M, generator=g0)].to(dev)
+    A = A * rs[:, None]
+    A[7] = 0.0
+    A[11] = A[11] / A[11].abs().max() * 1e-3
+    A[11, 5] = 1.0e6                     # one dominant entry in an otherwise small row
+    B = rnd(K, N, seed=22) * torch.logspace(-10, 10, N, device=dev)[None, :]
+    g = _Groups([dict(a_col=0, K=K, c_col=0, N=N, B=B)])
+    C = torch.empty(M, N, device=dev)
+    gemm(A, K, M, g, C, N, None, None, None, None, None, 0, 0, 0, 3)
+    Ad, Bd = A.double(), B.double()
+    ref = Ad @ Bd
+    bound = (Ad.abs() @ Bd.abs())              # sum_k |a_mk| |b_kn|
+    err = (C.double() - ref).abs()
+    assert torch.isfinite(C).all()
+    assert (err <= 2e-6 * bound + 1e-300).all(), float((err / (bound + 1e-300)).max())
+    assert (C[7] == 0).all()
+
+
+def test_gemm_f16_pair_without_scratch_runs_as_3xtf32():
+    """Mode 3 needs a scratch for its row scales; without one (plain atom_gemm) the launch
+    runs as 3xTF32 and gives exactly mode 2's result."""
+    from tt_atom.engine import _Groups
+    M, K, N = 500, 128, 192
+    A, B = rnd(M, K, seed=31), rnd(K, N, seed=32)
+    g = _Groups([dict(a_col=0, K=K, c_col=0, N=N, B=B)])
+    C2, C3 = torch.empty(M, N, device=dev), torch.empty(M, N, device=dev)
+    call("atom_gemm", ptr(A), K, M, ctypes.byref(g.struct), ptr(C2), N, None, None, None, None,
+         None, 0, 0, 0, 2, s())
+    call("atom_gemm", ptr(A), K, M, ctypes.byref(g.struct), ptr(C3), N, None, None, None, None,
+         None, 0, 0, 0, 3, s())
+    assert torch.equal(C2, C3)
+
+
+def test_library_counts_its_launches():
+    """atom_launch_count advances by the kernels one call launches: a mode-3 GEMM launches its
+    row-scale pass and the GEMM."""
+    from tt_atom.engine import _Groups, launch_count
+    M, K, N = 500, 128, 192
+    A, B = rnd(M, K, seed=31), rnd(K, N, seed=32)
+    g = _Groups([dict(a_col=0, K=K, c_col=0, N=N, B=B)])
+    C = torch.empty(M, N, device=dev)
+    n0 = launch_count()
+    gemm(A, K, M, g, C, N, None, None, None, None, None, 0, 0, 0, 3)
+    assert launch_count() - n0 == 2
+    n0 = launch_count()
+    gemm(A, K, M, g, C, N, None, None, None, None, None, 0, 0, 0, 2)
+    assert launch_count() - n0 == 1
 
 
 # --------------------------------------------------------------------- node-side kernels

@@ -4,6 +4,8 @@
 
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <atomic>
 #include <stdio.h>
 #include <string.h>
 
@@ -14,7 +16,12 @@ namespace atom {
 // Thread-local last error message read back through atom_last_error().
 void set_error(const char* fmt, ...);
 
-inline int check_launch(const char* what) {
+// Kernels this library has launched (read through atom_launch_count): every launch site is
+// followed by exactly one check_launch, told how many launches it covers.
+inline std::atomic<long long> g_launches{0};
+
+inline int check_launch(const char* what, int launches = 1) {
+    g_launches.fetch_add(launches, std::memory_order_relaxed);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_error("%s: CUDA launch error %s", what, cudaGetErrorString(e));
@@ -34,6 +41,11 @@ inline int check_launch(const char* what) {
 #define ATOM_CHECK_LAUNCH(name)                   \
     do {                                          \
         int _s = ::atom::check_launch(name);      \
+        if (_s != ATOM_OK) return _s;             \
+    } while (0)
+#define ATOM_CHECK_LAUNCHES(name, n)              \
+    do {                                          \
+        int _s = ::atom::check_launch(name, n);   \
         if (_s != ATOM_OK) return _s;             \
     } while (0)
 

@@ -7,9 +7,10 @@
 // [c_col, c_col + N) of C.
 //
 // precision 0: register-tiled FMA kernel (128 x 128 tile, 8 x 8 outputs per thread).
-// precision 1 / 2: the tcgen05 tensor-core kernel of gemm_tc.cu (TF32 / 3xTF32) when the shape
-// allows it (every K a multiple of 32, K-major weights given); otherwise the FMA kernel, which
-// is at least as accurate.
+// precision 1 / 2 / 3: the tcgen05 tensor-core kernel of gemm_tc.cu (TF32 / 3xTF32 / fp16 pair)
+// when the shape allows it (every K a multiple of 32, K-major weights given; mode 3 also needs
+// its fp16 weight halves and a scratch, else it runs as mode 2); otherwise the FMA kernel,
+// which is at least as accurate.
 #include "common.cuh"
 
 namespace atom {
@@ -147,7 +148,7 @@ extern "C" int atom_gemm_ex(const float* A, int64_t lda, int64_t M,
     ATOM_REQUIRE(act == 0 || act == 1, "act must be 0 or 1");
     ATOM_REQUIRE(!T1 || idx1, "T1 needs idx1");
     ATOM_REQUIRE(!T2 || idx2, "T2 needs idx2");
-    ATOM_REQUIRE(precision >= 0 && precision <= 2, "precision mode %d not available", precision);
+    ATOM_REQUIRE(precision >= 0 && precision <= 3, "precision mode %d not available", precision);
     GemmArgs p;
     p.A = A; p.lda = lda; p.M = M; p.C = Cout; p.Cpre = C_pre; p.ldc = ldc;
     p.T1 = T1; p.T2 = T2; p.idx1 = idx1; p.idx2 = idx2; p.ldt = ldt;

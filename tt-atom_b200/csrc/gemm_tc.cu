@@ -12,6 +12,15 @@
 //      128 x 192: 192 columns for A_hi B_hi, 192 for the corrections and two 64-column A slots
 //      fill the 512 tensor-memory columns (wider MMAs run faster per product: N = 256 took only
 //      ~13% longer than N = 128 on B200).
+//   3  fp16 pair: the same three products with 16-bit operands (kind::f16, twice the tf32
+//      rate). fp16 has 11 significant bits but a narrow exponent range, so every operand is
+//      first scaled by a power of two: A per (row, group) so that the row's largest magnitude
+//      lies in [2^14, 2^15) (a one-pass kernel writes the scales to the caller's scratch), B per
+//      output column (precomputed with the weights). x = hi + lo * 2^-11 with hi = fp16(x) and
+//      lo = fp16((x - hi) * 2^11) keeps 22 significant bits of x relative to its row's (column's)
+//      largest entry; lo is stored scaled so that it stays in fp16's normal range, and the
+//      correction accumulator is scaled back by 2^-11 in the epilogue, where the row and column
+//      scales are divided out again (all exact powers of two).
 //
 // Persistent CTAs (one per SM, 448 threads): warp 0 issues TMA loads, warp 1 allocates tensor
 // memory and issues the MMAs (one elected lane), warps 2-9 run the epilogue (warp w reads
@@ -24,6 +33,10 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cuda_fp16.h>
+
+#include <cstring>
+
 #include "common.cuh"
 
 // Pipeline depth (shared-memory stages) per precision mode; overridable at build time.
@@ -32,6 +45,9 @@
 #endif
 #ifndef ATOM_TC_STAGES_1X
 #define ATOM_TC_STAGES_1X 5
+#endif
+#ifndef ATOM_TC_STAGES_F16
+#define ATOM_TC_STAGES_F16 4
 #endif
 
 namespace atom {
@@ -49,6 +65,7 @@ struct Groups {
     int ngroups;
     int a_col[8], K[8], c_col[8], N[8], t_col[8];
     const float* bias[8];
+    const float* cinv[8];   // mode 3: per-column inverse scale of B (powers of two)
     int tile_start[9];
 };
 
@@ -66,6 +83,8 @@ struct Args {
     int mpad;            // rows per split in the partial buffer (a multiple of BM >= M)
     int tma_out;         // epilogue writes C (and Cpre) with TMA stores / reduce-adds
     int nacc;            // tensor-memory accumulators the K stages are spread over (1 or 4)
+    const float* rscale; // mode 3: power-of-two scale of A per (group, row), rows rs_ld apart
+    long long rs_ld;
     Groups g;
 };
 
@@ -146,6 +165,22 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
     return d;
 }
 
+// Same for 16-bit K-major operands with 64-byte swizzle (32 fp16 per row, atoms 512 bytes apart).
+__device__ __forceinline__ uint64_t sdesc64(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(512 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)4 << 61;                  // 64-byte swizzle
+    return d;
+}
+
+// Instruction descriptor (kind::f16): D fp32, A and B fp16, both K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t idesc_f16(int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
 // Instruction descriptor: D fp32, A and B tf32, both K-major, M = 128, N = n.
 __host__ __device__ constexpr uint32_t idesc_tf32(int n) {
     return (1u << 4)                    // D: fp32
@@ -175,6 +210,22 @@ __device__ __forceinline__ void mma_tf32_ta(uint32_t tmem_d, uint32_t tmem_a, ui
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
         "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+// kind::f16 with A (two fp16 per column, the even K element in the low half) from tensor memory.
+__device__ __forceinline__ void mma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t b,
+                                           uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+// 16 consecutive tensor-memory columns of this thread's lane <- r[0..15].
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
 }
 // 32 consecutive tensor-memory columns of this thread's lane <- r[0..31].
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
@@ -222,11 +273,16 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
 
 template <int BN, int MODE>
 struct Cfg {
-    static constexpr uint32_t kTileB = BN * BK * 4;
-    // mode 2 keeps no A_lo tile in shared memory: the split writes A_hi / A_lo to tensor memory
-    static constexpr uint32_t kStage = kTileA + kTileB + (MODE == 2 ? kTileB : 0);
-    static constexpr uint32_t kLoadBytes = kTileA + kTileB * (MODE == 2 ? 2 : 1);  // TMA bytes
-    static constexpr int kStages = MODE == 2 ? ATOM_TC_STAGES_3X : ATOM_TC_STAGES_1X;
+    // B is fp32 (modes 1, 2) or fp16 (mode 3) in shared memory; A always arrives as fp32
+    static constexpr uint32_t kTileB = BN * BK * (MODE == 3 ? 2 : 4);
+    // modes 2 and 3 keep no A_lo tile in shared memory: the split writes A_hi / A_lo to tensor
+    // memory; they load B's lo part beside B
+    static constexpr uint32_t kStage = kTileA + kTileB + (MODE >= 2 ? kTileB : 0);
+    static constexpr uint32_t kLoadBytes = kTileA + kTileB * (MODE >= 2 ? 2 : 1);  // TMA bytes
+    static constexpr int kStages =
+        MODE == 3 ? ATOM_TC_STAGES_F16 : MODE == 2 ? ATOM_TC_STAGES_3X : ATOM_TC_STAGES_1X;
+    // tensor-memory columns of one A slot (hi then lo): fp32 one K element per column, fp16 two
+    static constexpr uint32_t kSlotCols = MODE == 3 ? BK : 2 * BK;
     static constexpr int kEpiCols = BN / 2;        // columns per epilogue warp
     // output staging: one 32 x 32 fp32 buffer (128-byte swizzled) per epilogue warp for the TMA
     // stores; the row-store path of gathered-table launches uses it as an XOR-swizzled tile
@@ -235,9 +291,52 @@ struct Cfg {
     static constexpr uint32_t kSmem = kStages * kStage + kStageOut + 256 + 1024;
     static_assert(kSmem <= 232448, "shared memory per CTA");
     static_assert(kEpiCols % 32 == 0, "epilogue chunks");
-    // mode 1: 4 accumulators of BN columns; mode 2: main + corrections, then two A slots
-    static_assert(MODE == 2 ? 2 * BN + 4 * BK <= 512 : 4 * BN <= 512, "tensor-memory columns");
+    // mode 1: 4 accumulators of BN columns; modes 2, 3: main + corrections, then two A slots
+    static_assert(MODE >= 2 ? 2 * BN + 2 * kSlotCols <= 512 : 4 * BN <= 512,
+                  "tensor-memory columns");
 };
+
+// 1 / x for x = 2^s, |s| <= 126 (exact).
+__device__ __forceinline__ float pow2_inv(float x) {
+    return __uint_as_float((254u << 23) - (__float_as_uint(x) & 0x7F800000u));
+}
+
+// Power-of-two scale 2^(14 - e) for a row whose largest magnitude is mx in [2^e, 2^(e+1)), so
+// that the scaled row's largest entry lies in [2^14, 2^15); shift clamped to [-126, 126]. Zero,
+// infinite or NaN maxima get scale 1 (zeros stay zero, inf / NaN propagate).
+__host__ __device__ inline float pow2_scale(float mx) {
+    uint32_t u;
+    memcpy(&u, &mx, 4);
+    const int ex = (int)((u >> 23) & 0xFF);
+    if (mx == 0.f || ex == 0xFF) return 1.f;
+    int sh = 14 - (ex - 127);
+    sh = sh < -126 ? -126 : (sh > 126 ? 126 : sh);
+    const uint32_t o = (uint32_t)(sh + 127) << 23;
+    float f;
+    memcpy(&f, &o, 4);
+    return f;
+}
+
+// Mode-3 row scales: out[g * ld + m] = pow2_scale(max_k |A[m, a_col[g] + k]|), one warp per
+// row, float4 loads (a_col and K multiples of 4).
+__global__ void row_scale_kernel(const float* __restrict__ A, long long lda, long long M,
+                                 Groups g, long long ld, float* __restrict__ out) {
+    const long long m = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (m >= M) return;
+    const float* row = A + m * lda;
+    for (int i = 0; i < g.ngroups; ++i) {
+        const float* a = row + g.a_col[i];
+        float mx = 0.f;
+        for (int k = 4 * lane; k < g.K[i]; k += 128) {
+            const float4 x = *reinterpret_cast<const float4*>(a + k);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) out[i * ld + m] = pow2_scale(mx);
+    }
+}
 
 // Tensor maps of one launch: A, and per group the K-major weight (hi) and its lo part.
 struct Maps {
@@ -285,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     using CF = Cfg<BN, MODE>;
     constexpr int S = CF::kStages;
     constexpr int EC = CF::kEpiCols;
-    constexpr uint32_t kSlot0 = 2 * BN;   // mode 2: A slots after main and corrections
+    constexpr uint32_t kSlot0 = 2 * BN;   // modes 2, 3: A slots after main and corrections
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -348,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_expect_tx(&full[s], CF::kLoadBytes);
                     tma_load_2d(stA(s), &maps.a, a_x0 + kt * BK, (int)ti.m0, &full[s]);
                     tma_load_2d(stB(s), &maps.b[ti.grp], kt * BK, ti.n0, &full[s]);
-                    if (MODE == 2) tma_load_2d(stBL(s), &maps.l[ti.grp], kt * BK, ti.n0, &full[s]);
+                    if (MODE >= 2) tma_load_2d(stBL(s), &maps.l[ti.grp], kt * BK, ti.n0, &full[s]);
                 }
             }
         }
@@ -360,13 +459,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 TileInfo ti = tile_info(p, ntn, t);
                 // a group's last tile multiplies only the columns that remain (N multiple of 16)
                 const int rem = p.g.N[ti.grp] - ti.n0;
-                const uint32_t idesc = idesc_tf32(rem >= p.bn ? p.bn : (rem + 15) & ~15);
+                const int nmma = rem >= p.bn ? p.bn : (rem + 15) & ~15;
+                const uint32_t idesc = MODE == 3 ? idesc_f16(nmma) : idesc_tf32(nmma);
                 bool ok = !aborted() && mbar_wait(acce, (j & 1u) ^ 1u, 5);
                 if (ok) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 for (int kt = ti.kt0; ok && kt < ti.kt1; ++kt, ++it) {
                     int s = it % S;
                     uint32_t ph = (it / S) & 1u;
-                    if (!mbar_wait(MODE == 2 ? &conv[s] : &full[s], ph, 2) || aborted()) {
+                    if (!mbar_wait(MODE >= 2 ? &conv[s] : &full[s], ph, 2) || aborted()) {
                         ok = false;
                         break;
                     }
@@ -385,6 +485,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                                         acc);
                             mma_tf32_ta(tmem + BN, slot + BK + kk * 8, sdesc(b + kk * 32), idesc,
                                         1u);
+                        }
+                        mma_commit(&empty[s]);
+                        mma_commit(&afree[it & 1u]);
+                    } else if constexpr (MODE == 3) {
+                        // fp16 pair: per 16-element k-step, A_hi (slot columns 0..15) B_hi into
+                        // the main accumulator, A_hi B_lo and A_lo (columns 16..31) B_hi into the
+                        // corrections (lo parts carry a factor 2^11)
+                        const uint32_t slot = tmem + kSlot0 + (it & 1u) * CF::kSlotCols;
+                        const uint32_t bl = smem_u32(stBL(s));
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk) {
+                            const uint32_t acc = (kt > ti.kt0 || kk > 0) ? 1u : 0u;
+                            mma_f16_ta(tmem, slot + kk * 8, sdesc64(b + kk * 32), idesc, acc);
+                            mma_f16_ta(tmem + BN, slot + kk * 8, sdesc64(bl + kk * 32), idesc,
+                                       acc);
+                            mma_f16_ta(tmem + BN, slot + BK / 2 + kk * 8, sdesc64(b + kk * 32),
+                                       idesc, 1u);
                         }
                         mma_commit(&empty[s]);
                         mma_commit(&afree[it & 1u]);
@@ -410,12 +527,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp >= 2 + kEpiWarps) {
-        // ------------------------------------------------------ A split (3xTF32 only)
+        // ------------------------------------------------------ A split (modes 2 and 3)
         // Thread = tile row (warp w owns tensor-memory lanes 32 * (w % 4) ..): reads its row of
-        // the swizzled A stage, writes A_hi (low 13 mantissa bits cleared) and A_lo = A - A_hi
-        // to 2 x BK columns of tensor-memory slot it % 2, once the MMAs that read that slot two
-        // stages earlier have completed.
-        if (MODE == 2) {
+        // the swizzled A stage, writes A_hi and A_lo to tensor-memory slot it % 2, once the MMAs
+        // that read that slot two stages earlier have completed. Mode 2: A_hi = A with the low
+        // 13 mantissa bits cleared, A_lo = A - A_hi (fp32, 2 x BK columns). Mode 3: y = A times
+        // the row's power-of-two scale, A_hi = fp16(y), A_lo = fp16((y - A_hi) * 2^11), packed
+        // two per column (BK / 2 columns each).
+        if (MODE >= 2) {
             const int quarter = warp & 3;
             const int r = quarter * 32 + lane;
             const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
@@ -423,6 +542,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int t = blockIdx.x; ok && t < ntiles && !aborted(); t += gridDim.x) {
                 TileInfo ti = tile_info(p, ntn, t);
+                float rs = 1.f;
+                if (MODE == 3 && ti.m0 + r < p.M) rs = p.rscale[ti.grp * p.rs_ld + ti.m0 + r];
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt, ++it) {
                     int s = it % S;
                     uint32_t ph = (it / S) & 1u;
@@ -435,22 +556,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint8_t* row = stA(s) + (r >> 3) * 1024 + (r & 7) * 128;
-                    uint32_t hi[BK], lo[BK];
+                    const uint32_t slot = lane_base + kSlot0 + (it & 1u) * CF::kSlotCols;
+                    if constexpr (MODE == 3) {
+                        uint32_t hi[BK / 2], lo[BK / 2];
 #pragma unroll
-                    for (int c = 0; c < BK / 4; ++c) {
-                        const float4 x =
-                            *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) << 4));
-                        const float xs[4] = {x.x, x.y, x.z, x.w};
+                        for (int c = 0; c < BK / 4; ++c) {
+                            const float4 x =
+                                *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) << 4));
+                            const float y[4] = {x.x * rs, x.y * rs, x.z * rs, x.w * rs};
 #pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            const uint32_t h = __float_as_uint(xs[k]) & 0xFFFFE000u;
-                            hi[4 * c + k] = h;
-                            lo[4 * c + k] = __float_as_uint(xs[k] - __uint_as_float(h));
+                            for (int k = 0; k < 2; ++k) {
+                                const __half2 h = __floats2half2_rn(y[2 * k], y[2 * k + 1]);
+                                const float2 hb = __half22float2(h);
+                                const __half2 l = __floats2half2_rn((y[2 * k] - hb.x) * 2048.f,
+                                                                    (y[2 * k + 1] - hb.y) * 2048.f);
+                                hi[2 * c + k] = *reinterpret_cast<const uint32_t*>(&h);
+                                lo[2 * c + k] = *reinterpret_cast<const uint32_t*>(&l);
+                            }
                         }
+                        tmem_st16(slot, hi);
+                        tmem_st16(slot + BK / 2, lo);
+                    } else {
+                        uint32_t hi[BK], lo[BK];
+#pragma unroll
+                        for (int c = 0; c < BK / 4; ++c) {
+                            const float4 x =
+                                *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) << 4));
+                            const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const uint32_t h = __float_as_uint(xs[k]) & 0xFFFFE000u;
+                                hi[4 * c + k] = h;
+                                lo[4 * c + k] = __float_as_uint(xs[k] - __uint_as_float(h));
+                            }
+                        }
+                        tmem_st32(slot, hi);
+                        tmem_st32(slot + BK, lo);
                     }
-                    const uint32_t slot = lane_base + kSlot0 + (it & 1u) * 2 * BK;
-                    tmem_st32(slot, hi);
-                    tmem_st32(slot + BK, lo);
                     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                     mbar_arrive(&conv[s]);
@@ -474,8 +616,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int N = p.g.N[ti.grp];
             const bool active = ti.n0 + cbase < N && cbase < p.bn;
             // drain the accumulators into registers (partial sums added with round-to-nearest):
-            // mode 1 the K-stage accumulators in use, mode 2 main + corrections
-            const int nused = MODE == 2 ? 2 : (ti.nk < p.nacc ? ti.nk : p.nacc);
+            // mode 1 the K-stage accumulators in use, modes 2, 3 main + corrections (mode 3: the
+            // corrections carry 2^11, and the row and column scales are divided out)
+            const int nused = MODE >= 2 ? 2 : (ti.nk < p.nacc ? ti.nk : p.nacc);
             float v[EC];
             const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)cbase;
             if (active) {
@@ -488,8 +631,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                         float w[8];
                         tmem_ld8(lane_base + (uint32_t)(q * BN + c0), w);
 #pragma unroll
-                        for (int jj = 0; jj < 8; ++jj) v[c0 + jj] += w[jj];
+                        for (int jj = 0; jj < 8; ++jj)
+                            v[c0 + jj] += MODE == 3 ? w[jj] * (1.f / 2048.f) : w[jj];
                     }
+                }
+                if constexpr (MODE == 3) {
+                    const long long row = ti.m0 + quarter * 32 + lane;
+                    const float rinv =
+                        row < p.M ? pow2_inv(p.rscale[ti.grp * p.rs_ld + row]) : 0.f;
+                    const float* ci = p.g.cinv[ti.grp];
+                    const int nb = ti.n0 + cbase;
+#pragma unroll
+                    for (int c = 0; c < EC; ++c)
+                        v[c] *= rinv * (nb + c < N ? ci[nb + c] : 0.f);
                 }
             }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -657,6 +811,26 @@ static int make_map(CUtensorMap* m, const float* base, long long inner, long lon
     return ATOM_OK;
 }
 
+// 2-D fp16 tensor map for mode 3's weights: `inner` contiguous K elements, `outer` rows `ld`
+// elements apart, box of 32 x box_rows (64 bytes per row) with 64-byte swizzle.
+static int make_map16(CUtensorMap* m, const void* base, long long inner, long long outer,
+                      long long ld, int box_rows) {
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled (fp16) failed (%d): inner %lld outer %lld ld %lld",
+                  (int)r, inner, outer, ld);
+        return ATOM_ERR_ARG;
+    }
+    return ATOM_OK;
+}
+
 // Accumulators per tile. The tensor core's fp32 accumulation rounds each k-step's sum toward
 // zero, so its error grows with the number of steps in one accumulator; spreading the stages
 // over 4 accumulators (summed in the epilogue with round-to-nearest) divides that by 4.
@@ -722,7 +896,7 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
     Args p;
     p.M = M; p.ldc = ldc; p.ldt = ldt; p.C = C; p.Cpre = Cpre; p.T1 = T1; p.T2 = T2;
     p.idx1 = idx1; p.idx2 = idx2; p.act = act; p.accumulate = accumulate;
-    p.nacc = MODE == 2 ? 2 : g_nacc;
+    p.nacc = MODE >= 2 ? 2 : g_nacc;
     p.g.ngroups = g->ngroups;
     int dev = 0, nsm = 148;
     cudaGetDevice(&dev);
@@ -749,13 +923,22 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
     // traffic than they gain); the raw partials are added in split order by a second kernel
     int ksplit = 1;
     const long long mpad = mblocks * BM;
-    if (scratch && tma_out && !T1 && !T2 && count_tiles(BN) * 2 <= nsm) {
+    // mode 3 keeps its row scales (groups x mpad floats) at the start of the scratch; split-K
+    // partials follow
+    const long long rs_floats = MODE == 3 ? (g->ngroups * mpad + 63) / 64 * 64 : 0;
+    if (MODE == 3 && (!scratch || scratch_floats < rs_floats)) {
+        set_error("gemm_tc: precision 3 needs a scratch of %lld floats", rs_floats);
+        return ATOM_ERR_ARG;
+    }
+    float* part = scratch ? scratch + rs_floats : nullptr;
+    const long long part_floats = scratch ? scratch_floats - rs_floats : 0;
+    if (part && tma_out && !T1 && !T2 && count_tiles(BN) * 2 <= nsm) {
         int min_nk = 1 << 30;
         for (int i = 0; i < g->ngroups; ++i) min_nk = min_nk < g->K[i] / BK ? min_nk : g->K[i] / BK;
         int sk = (int)(nsm / count_tiles(BN));
         sk = sk < 8 ? sk : 8;
         sk = min_nk < 16 ? 1 : (sk < min_nk / 4 ? sk : min_nk / 4);
-        while (sk >= 2 && (long long)sk * mpad * ldc > scratch_floats) --sk;
+        while (sk >= 2 && (long long)sk * mpad * ldc > part_floats) --sk;
         if (sk >= 2) ksplit = sk;
     }
     p.ksplit = ksplit;
@@ -778,12 +961,22 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
         p.g.N[i] = g->N[i];
         p.g.t_col[i] = g->t_col[i];
         p.g.bias[i] = g->bias[i];
+        p.g.cinv[i] = MODE == 3 ? g->Bh_inv[i] : nullptr;
         p.g.tile_start[i] = tiles;
         tiles += ceil_div(g->N[i], bn);
-        if (int s = make_map(&maps.b[i], g->Bt[i], g->K[i], g->N[i], g->K[i], BN)) return s;
-        if (MODE == 2)
-            if (int s = make_map(&maps.l[i], g->Bt_lo[i], g->K[i], g->N[i], g->K[i], BN)) return s;
+        if (MODE == 3) {
+            if (int s = make_map16(&maps.b[i], g->Bh[i], g->K[i], g->N[i], g->K[i], BN)) return s;
+            if (int s = make_map16(&maps.l[i], g->Bh_lo[i], g->K[i], g->N[i], g->K[i], BN))
+                return s;
+        } else {
+            if (int s = make_map(&maps.b[i], g->Bt[i], g->K[i], g->N[i], g->K[i], BN)) return s;
+            if (MODE == 2)
+                if (int s = make_map(&maps.l[i], g->Bt_lo[i], g->K[i], g->N[i], g->K[i], BN))
+                    return s;
+        }
     }
+    p.rscale = MODE == 3 ? scratch : nullptr;
+    p.rs_ld = mpad;
     p.g.tile_start[g->ngroups] = tiles;
     if (tma_out) {
         for (int i = 0; i < g->ngroups; ++i) {
@@ -792,7 +985,7 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
                 if (int s = make_map(&maps.cp[i], Cpre + g->c_col[i], g->N[i], M, ldc, 32))
                     return s;
             if (ksplit > 1)
-                if (int s = make_map(&maps.pm[i], scratch + g->c_col[i], g->N[i],
+                if (int s = make_map(&maps.pm[i], part + g->c_col[i], g->N[i],
                                      ksplit * mpad, ldc, 32))
                     return s;
         }
@@ -803,6 +996,10 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
         return ATOM_ERR_ARG;
     }
     const int grid = (int)(ntiles < nsm ? ntiles : nsm);
+    if (MODE == 3) {
+        row_scale_kernel<<<ceil_div(M * 32, 256), 256, 0, st>>>(A, lda, M, p.g, mpad, scratch);
+        if (int s = check_launch("gemm_tc row scales")) return s;
+    }
     if (tma_out && (T1 || T2))
         gemm_tc_kernel<BN, MODE, true><<<grid, kThreads, CF::kSmem, st>>>(maps, p, tiles,
                                                                          (int)ntiles);
@@ -814,10 +1011,10 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
         for (int i = 0; i < g->ngroups; ++i) {
             const long long n4 = M * (g->N[i] / 4);
             splitk_reduce_kernel<<<ceil_div(n4, 256), 256, 0, st>>>(
-                scratch, ksplit, mpad, ldc, M, g->c_col[i], g->N[i], g->bias[i], act, Cpre,
+                part, ksplit, mpad, ldc, M, g->c_col[i], g->N[i], g->bias[i], act, Cpre,
                 accumulate, C);
+            if (int s = check_launch("gemm_tc split-K reduce")) return s;
         }
-        return check_launch("gemm_tc split-K reduce");
     }
     return ATOM_OK;
 }
@@ -827,14 +1024,24 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
 // True when the tensor-core path can run this problem: every K a multiple of 32, K-major weight
 // copies present, TMA-compatible strides and alignment.
 bool gemm_tc_supported(const float* A, long long lda, const atom_gemm_groups* g, int precision) {
-    if (precision != 1 && precision != 2) return false;
+    if (precision < 1 || precision > 3) return false;
     if (g->ngroups > 8 || lda % 4 != 0 || !aligned16(A)) return false;
     for (int i = 0; i < g->ngroups; ++i) {
         if (g->K[i] <= 0 || g->K[i] % tc::BK != 0 || g->a_col[i] % 4 != 0) return false;
         if (!g->Bt[i] || !aligned16(g->Bt[i])) return false;
-        if (precision == 2 && (!g->Bt_lo[i] || !aligned16(g->Bt_lo[i]))) return false;
+        if (precision >= 2 && (!g->Bt_lo[i] || !aligned16(g->Bt_lo[i]))) return false;
     }
     return true;
+}
+
+// Mode 3 also needs the fp16 weight halves, their column scales and a scratch for the row
+// scales; without them the launch runs as mode 2 (same accuracy class).
+static bool f16_ready(long long M, const atom_gemm_groups* g, long long scratch_floats) {
+    for (int i = 0; i < g->ngroups; ++i)
+        if (!g->Bh[i] || !g->Bh_lo[i] || !g->Bh_inv[i] || !aligned16(g->Bh[i]) ||
+            !aligned16(g->Bh_lo[i]))
+            return false;
+    return scratch_floats >= (g->ngroups * (ceil_div(M, tc::BM) * tc::BM) + 63) / 64 * 64;
 }
 
 int gemm_tc(const float* A, long long lda, long long M, const atom_gemm_groups* g, float* C,
@@ -842,7 +1049,10 @@ int gemm_tc(const float* A, long long lda, long long M, const atom_gemm_groups* 
             const int* idx2, long long ldt, int act, int accumulate, int precision,
             float* scratch, long long scratch_floats, cudaStream_t st) {
     if (int s = tc::encoder()) return s;
-    if (precision == 2)
+    if (precision == 3 && scratch && f16_ready(M, g, scratch_floats))
+        return tc::launch<192, 3>(A, lda, M, g, C, ldc, Cpre, T1, T2, idx1, idx2, ldt, act,
+                                  accumulate, scratch, scratch_floats, st);
+    if (precision >= 2)
         return tc::launch<192, 2>(A, lda, M, g, C, ldc, Cpre, T1, T2, idx1, idx2, ldt, act,
                                   accumulate, scratch, scratch_floats, st);
     return tc::launch<128, 1>(A, lda, M, g, C, ldc, Cpre, T1, T2, idx1, idx2, ldt, act,

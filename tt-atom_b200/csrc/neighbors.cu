@@ -335,7 +335,7 @@ extern "C" int atom_sender_csr(const int* edge_src, int64_t E, int64_t N, int* s
                                                               send_eid);
         sort_segments_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(N, send_ptr, send_eid);
     }
-    ATOM_CHECK_LAUNCH("sender_csr");
+    ATOM_CHECK_LAUNCHES("sender_csr", E > 0 ? 6 : 3);
     return ATOM_OK;
 }
 
@@ -406,6 +406,6 @@ extern "C" int atom_sender_csr_noalloc(const int* edge_src, int64_t E, int64_t N
                                                               send_eid);
         sort_segments_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(N, send_ptr, send_eid);
     }
-    ATOM_CHECK_LAUNCH("sender_csr_noalloc");
+    ATOM_CHECK_LAUNCHES("sender_csr_noalloc", E > 0 ? 6 : 3);
     return ATOM_OK;
 }

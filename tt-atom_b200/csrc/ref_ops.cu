@@ -164,7 +164,12 @@ extern "C" int atom_last_error(char* buf, size_t n) {
     return (int)len;
 }
 
-extern "C" int atom_abi_version(void) { return 1; }
+extern "C" int atom_abi_version(void) { return 2; }
+
+extern "C" int atom_launch_count(int64_t* n) {
+    if (n) *n = atom::g_launches.load(std::memory_order_relaxed);
+    return ATOM_OK;
+}
 
 extern "C" int atom_fused_rotate(const float* x, const float* coef, int64_t E, int n_in,
                                  int n_out, int W, int nnz, const int* deg, const int* ks,

@@ -23,12 +23,14 @@ class GemmGroups(ctypes.Structure):
     _fields_ = [("ngroups", c_int), ("a_col", c_int * 8), ("K", c_int * 8), ("c_col", c_int * 8),
                 ("N", c_int * 8), ("ldb", c_int * 8), ("t_col", c_int * 8),
                 ("B", c_void_p * 8), ("bias", c_void_p * 8), ("Bt", c_void_p * 8),
-                ("Bt_lo", c_void_p * 8)]
+                ("Bt_lo", c_void_p * 8), ("Bh", c_void_p * 8), ("Bh_lo", c_void_p * 8),
+                ("Bh_inv", c_void_p * 8)]
 
 
 _SIGS = {
     "atom_last_error": (ctypes.c_char_p, ctypes.c_size_t),
     "atom_abi_version": (),
+    "atom_launch_count": (ctypes.POINTER(c_int64),),
     "atom_fused_rotate": (c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p,
                           c_void_p, c_void_p, c_void_p, c_void_p),
     "atom_fused_rotate_gc": (c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p,

@@ -33,23 +33,40 @@ from . import _lib as L
 from ._lib import ptr
 
 # kernels launched per entry point (all others launch one)
-_LAUNCHES = {"atom_edge_geometry": 2, "atom_forces_virial": 3}
-_counter = [0]
+call = L.call
+
+# "fp32": FMA-pipe GEMMs; "3xtf32": tcgen05 tensor cores with the tf32 hi/lo operand split
+# (fp32-level accuracy); "3xf16": the same three products on fp16 hi/lo pairs with
+# power-of-two row and column scales (fp32-level accuracy at twice the tf32 MMA rate);
+# "tf32": tensor cores, one pass (looser, ~1e-3 relative per product).
+PRECISIONS = {"fp32": 0, "tf32": 1, "3xtf32": 2, "3xf16": 3}
 
 
-def call(name, *args):
-    _counter[0] += _LAUNCHES.get(name, 1)
-    return L.call(name, *args)
-
-# "fp32": FMA-pipe GEMMs; "3xtf32": tcgen05 tensor cores with the hi/lo operand split
-# (fp32-level accuracy); "tf32": tensor cores, one pass (looser, ~1e-3 relative per product).
-PRECISIONS = {"fp32": 0, "tf32": 1, "3xtf32": 2}
+def launch_count():
+    """Kernels the library has launched so far (its own counter)."""
+    n = L.ctypes.c_int64(0)
+    L.call("atom_launch_count", L.ctypes.byref(n))
+    return n.value
 
 
 def _split_tf32(t):
     """(hi, lo): hi = t with the low 13 mantissa bits cleared, lo = t - hi (exact)."""
     hi = (t.contiguous().view(torch.int32) & -8192).view(torch.float32)
     return hi.contiguous(), (t - hi).contiguous()
+
+
+def _split_f16(t):
+    """Mode-3 weight halves of a K-major weight t [N, K]: per row n the power-of-two scale
+    s = 2^(14 - floor(log2 max |t[n]|)) (1 for a zero row), hi = fp16(t s),
+    lo = fp16((t s - hi) 2^11); returns (hi, lo, 1 / s)."""
+    mx = t.abs().amax(dim=1)
+    e = torch.floor(torch.log2(torch.where(mx > 0, mx, torch.ones_like(mx))))
+    sh = torch.clamp(14.0 - e, -126.0, 126.0)
+    s = torch.where(mx > 0, torch.exp2(sh), torch.ones_like(mx))
+    y = t * s[:, None]
+    hi = y.half()
+    lo = ((y - hi.float()) * 2048.0).half()
+    return hi.contiguous(), lo.contiguous(), (1.0 / s).contiguous()
 
 
 def _dev(t, device):
@@ -74,10 +91,17 @@ class _Groups:
             g.B[i] = B.data_ptr()
             self.keep.append(B)
             # K-major copies for the tensor-core kernel (hi part, lo part)
-            hi, lo = _split_tf32(B[:d["K"], :d["N"]].t().contiguous())
+            Bt = B[:d["K"], :d["N"]].t().contiguous()
+            hi, lo = _split_tf32(Bt)
             g.Bt[i] = hi.data_ptr()
             g.Bt_lo[i] = lo.data_ptr()
             self.keep += [hi, lo]
+            # fp16 halves with per-column scales for the fp16-pair mode
+            h16, l16, inv = _split_f16(Bt)
+            g.Bh[i] = h16.data_ptr()
+            g.Bh_lo[i] = l16.data_ptr()
+            g.Bh_inv[i] = inv.data_ptr()
+            self.keep += [h16, l16, inv]
             b = d.get("bias")
             g.bias[i] = b.data_ptr() if b is not None else None
             if b is not None:
@@ -313,10 +337,10 @@ class UMAEngine:
     def launches_per_step(self, ws, forces=True, virial=True):
         """Number of this library's kernels one ``run`` launches (counted, not estimated)."""
         torch.cuda.synchronize()
-        c0 = _counter[0]
+        c0 = launch_count()
         self.run(ws, ws.pos, forces=forces, virial=virial)
         torch.cuda.synchronize()
-        return _counter[0] - c0
+        return launch_count() - c0
 
     def so2_flop(self, E):
         """Algorithmic FLOPs of one forward so2_1 grouped GEMM over E edges."""

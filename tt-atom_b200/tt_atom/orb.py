@@ -122,13 +122,13 @@ class OrbEngine:
         self._gemm(tmp1, Hd, M, m["f2"], h2, self.C, s=s)
 
     def launches_per_step(self, ws, forces=True, virial=True):
-        """Number of this library's kernels one ``run`` launches (counted)."""
-        from .engine import _counter
+        """Number of this library's kernels one ``run`` launches (the library's own counter)."""
+        from .engine import launch_count
         torch.cuda.synchronize()
-        c0 = _counter[0]
+        c0 = launch_count()
         self.run(ws, forces=forces, virial=virial)
         torch.cuda.synchronize()
-        return _counter[0] - c0
+        return launch_count() - c0
 
     def time_kernels(self, ws, reps=5):
         """Device time of the dominant kernel: the layer-0 edge-MLP hidden GEMM
