@@ -193,6 +193,36 @@ def test_traced_calculate_with_stress_is_bit_exact():
         assert e0 == e1 and np.array_equal(f0, f1) and np.array_equal(s0, s1)
 
 
+def test_traced_step_survives_a_same_size_topology_change():
+    """MD moves atoms across neighbour ranks every step: with the cap the edge count stays the
+    same while the edge set changes. The calculator then copies the new topology into the
+    workspace's own arrays and replays the captured step instead of capturing again; results
+    equal a fresh eager evaluation bit for bit."""
+    from tt_atom.ase_compat import SimpleAtoms
+    cfg = configs.model_config("uma-s-1")
+    b = WeightBundle.from_arrays(configs.random_bundle_arrays(cfg, seed=0))
+    s = configs.fcc_alloy(reps=(3, 3, 3), seed=2)
+    rng = np.random.default_rng(5)
+    calc = TTAtomCalculator(b, trace=True)
+    a = SimpleAtoms(s["Z"], s["pos"], s["cell"], True)
+    calc.calculate(a, ("energy", "forces", "stress"))
+    step, src0 = calc._step, calc._ws.graph.src.clone()
+    assert step is not None
+    changed = 0
+    for k in range(3):
+        p = s["pos"] + rng.normal(0.0, 0.15, s["pos"].shape)
+        a = SimpleAtoms(s["Z"], p, s["cell"], True)
+        calc.calculate(a, ("energy", "forces", "stress"))
+        assert calc._step is step                        # no new capture
+        changed += int(not torch.equal(calc._ws.graph.src, src0))
+        ref = TTAtomCalculator(b, trace=False)
+        ref.calculate(SimpleAtoms(s["Z"], p, s["cell"], True), ("energy", "forces", "stress"))
+        assert calc.results["energy"] == ref.results["energy"]
+        assert np.array_equal(calc.results["forces"], ref.results["forces"])
+        assert np.array_equal(calc.results["stress"], ref.results["stress"])
+    assert changed > 0                                   # the topology did change
+
+
 def test_calculator_api_and_errors():
     from tt_atom.ase_compat import SimpleAtoms
     cfg = configs.model_config("tiny")

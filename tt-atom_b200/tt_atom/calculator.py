@@ -100,15 +100,22 @@ class TTAtomCalculator(_AseCalculator):
         reuse = (trace and self._ws is not None and self._ws_key == key
                  and g.same_topology(self._ws.graph) and torch.equal(self._se, se))
         if not reuse:
+            keep = False
             if self._ws is not None and self._ws.fits(g):
-                self._ws.rebind(g, se)              # same sizes: reuse the buffers
+                # same sizes: the new topology is copied into the workspace's own arrays, so a
+                # captured step stays valid (unchunked: no host-side plan depends on the
+                # topology) and is replayed on it
+                keep = self._ws_key == key and self._ws.chunks is None
+                self._ws.rebind(g, se)
             else:
                 self._ws = self._step = None        # free the old buffers first
                 chunk = self.chunk_edges
                 if chunk == "auto":
                     chunk = self.engine.choose_chunk_edges(g)
                 self._ws = self.engine.workspace(g, se, chunk_edges=chunk)
-            self._ws_key, self._se, self._step = key, se, None
+            self._ws_key, self._se = key, se
+            if not keep:
+                self._step = None
         ws = self._ws
         ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))
         if trace:

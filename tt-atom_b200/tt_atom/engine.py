@@ -23,6 +23,7 @@ Weight re-layouts done once at load time:
 """
 from __future__ import annotations
 
+import dataclasses
 import math
 
 import numpy as np
@@ -716,8 +717,16 @@ class Workspace:
     reverse pass recomputes each chunk's forward chain. This is how a cell whose full per-edge
     workspace exceeds device memory runs on one GPU."""
 
+    # device arrays of the topology; the workspace keeps its own copies at fixed addresses
+    _TOPOLOGY = ("Z", "sys_id", "sys_ptr", "src", "tgt", "img", "shifts", "recv_ptr",
+                 "send_ptr", "send_eid", "zs", "zt")
+
     def __init__(self, eng, graph, sys_emb, chunk_edges=None):
-        self.graph = graph
+        # a graph whose arrays belong to this workspace: a same-size topology is copied into
+        # them (rebind), so a step captured on these buffers stays valid
+        self.graph = dataclasses.replace(
+            graph, **{k: getattr(graph, k).clone() for k in self._TOPOLOGY})
+        graph = self.graph
         dev = eng.device
         N, E = graph.N, graph.E
         C, H, EC, NB, G, NL = eng.C, eng.H, eng.EC, eng.NB, eng.G, eng.NL
@@ -771,14 +780,22 @@ class Workspace:
 
     def fits(self, graph):
         return (graph.N == self.graph.N and graph.E == self.graph.E
-                and graph.nsys == self.graph.nsys)
+                and graph.nsys == self.graph.nsys and graph.periodic == self.graph.periodic
+                and all(getattr(graph, k).shape == getattr(self.graph, k).shape
+                        for k in self._TOPOLOGY))
 
     def rebind(self, graph, sys_emb):
-        """Point this workspace at another graph of the same sizes (new topology, same
-        buffers) and recompute the pos-independent node embeddings
-        l0 = sphere[Z] + sys_emb and the per-node system embedding."""
+        """Copy another graph of the same sizes into this workspace's topology arrays (new
+        topology, same buffers and addresses) and recompute the pos-independent node
+        embeddings l0 = sphere[Z] + sys_emb and the per-node system embedding."""
         assert graph.N == self.pos.shape[0]
-        self.graph = graph
+        if graph is not self.graph:
+            if not self.fits(graph):
+                raise ValueError("rebind needs a graph of the workspace's sizes")
+            for k in self._TOPOLOGY:
+                getattr(self.graph, k).copy_(getattr(graph, k))
+            self.graph.sys_ptr_host = list(graph.sys_ptr_host)
+        graph = self.graph
         eng, N, eng_C = self._eng, graph.N, self._eng.C
         if self.chunk_edges is not None:
             self.chunks = _plan_chunks(graph, self.chunk_edges, L.stream_ptr())
