@@ -59,7 +59,7 @@ def _run(shape, sysd, precision):
     return E, F, V, r
 
 
-@pytest.mark.parametrize("precision", ["fp32", "3xtf32"])
+@pytest.mark.parametrize("precision", ["fp32", "3xtf32", "3xf16"])
 @pytest.mark.parametrize("shape,sysname", [("orb-tiny", "mol"), ("orb-v3", "sio2")])
 def test_orb_energy_forces_stress_vs_oracle(shape, sysname, precision):
     if sysname == "mol":
@@ -73,6 +73,32 @@ def test_orb_energy_forces_stress_vs_oracle(shape, sysname, precision):
     if V is not None:
         vol = abs(np.linalg.det(sysd["cell"].astype(np.float64)))
         assert (V.float() - r["virial"]).abs().max() / vol <= S_ABS
+
+
+def test_orb_trace_replays_bit_exact_across_topology_changes():
+    """OrbCalculator(trace=True) captures the model pass once and replays it, also after the
+    capped edge set changes at the same size (the workspace's topology arrays are updated in
+    place); energies, forces and stresses equal the eager calculator bit for bit."""
+    from tt_atom.ase_compat import SimpleAtoms
+    cfg = configs.orb_config("orb-v3")
+    w = configs.orb_random_weights(cfg, seed=0)
+    sysd = configs.amorphous_sio2(n_si=40, n_o=80, seed=3)
+    rng = np.random.default_rng(1)
+    tr, ea = OrbCalculator(w, cfg, trace=True), OrbCalculator(w, cfg)
+    step = None
+    for k in range(3):
+        p = sysd["pos"] + (rng.normal(0.0, 0.1, sysd["pos"].shape) if k else 0.0)
+        out = []
+        for calc in (tr, ea):
+            calc.calculate(SimpleAtoms(sysd["Z"], p, sysd["cell"], True),
+                           ("energy", "forces", "stress"))
+            out.append((calc.results["energy"], calc.results["forces"].copy(),
+                        calc.results["stress"].copy()))
+        if step is None:
+            step = tr._step
+        assert tr._step is step
+        (e0, f0, s0), (e1, f1, s1) = out
+        assert e0 == e1 and np.array_equal(f0, f1) and np.array_equal(s0, s1)
 
 
 def test_zbl_pair_repulsion_vs_oracle():

@@ -30,7 +30,7 @@ def bundle_from_fixture(g):
     return WeightBundle.from_arrays(arrs), cfg
 
 
-PRECISIONS = ["fp32", "3xtf32"]
+PRECISIONS = ["fp32", "3xtf32", "3xf16"]
 
 
 def engine_eval(bundle, pos, Z, cell=None, pbc=None, stress=False, trace=False, calc=None,

@@ -17,13 +17,15 @@ host when the weights carry them). The ZBL pair repulsion runs on the GPU (``ato
 """
 from __future__ import annotations
 
+import dataclasses
+
 import numpy as np
 import torch
 
 from . import _lib as L
 from ._lib import ptr
 from .ase_compat import _AseCalculator, all_changes, atoms_volume, voigt_6
-from .engine import PRECISIONS, _Groups, _dev, call
+from .engine import PRECISIONS, CapturedStep, Workspace, _Groups, _dev, call
 from .graph import build_graph
 
 
@@ -278,8 +280,14 @@ class OrbEngine:
 
 
 class OrbWorkspace:
+    _TOPOLOGY = Workspace._TOPOLOGY
+
     def __init__(self, eng, graph):
-        self.graph = graph
+        # the workspace's own topology arrays (fixed addresses: a captured step stays valid
+        # when a same-size edge set is copied in)
+        self.graph = dataclasses.replace(
+            graph, **{k: getattr(graph, k).clone() for k in self._TOPOLOGY})
+        graph = self.graph
         dev = eng.device
         N, E, C, Hd, NL = graph.N, graph.E, eng.C, eng.Hd, eng.NL
         f = lambda *sh: torch.empty(*sh, device=dev, dtype=torch.float32)  # noqa: E731
@@ -322,10 +330,19 @@ class OrbWorkspace:
         from .engine import Workspace
         return Workspace.nbytes(self)
 
+    def fits(self, graph):
+        return Workspace.fits(self, graph)
+
     def rebind(self, graph):
-        """Point the workspace at a graph of the same sizes; recompute the node input rows
-        (the species embedding lookup)."""
-        self.graph = graph
+        """Copy a graph of the same sizes into the workspace's topology arrays; recompute the
+        node input rows (the species embedding lookup)."""
+        if graph is not self.graph:
+            if not self.fits(graph):
+                raise ValueError("rebind needs a graph of the workspace's sizes")
+            for k in self._TOPOLOGY:
+                getattr(self.graph, k).copy_(getattr(graph, k))
+            self.graph.sys_ptr_host = list(graph.sys_ptr_host)
+        graph = self.graph
         eng = self._eng
         call("atom_node_embed", ptr(graph.Z), None, ptr(eng.emb), ptr(eng.zero_row), graph.N,
              eng.D0, ptr(self.x0), L.stream_ptr())
@@ -355,9 +372,13 @@ class OrbCalculator(_AseCalculator):
     implemented_properties = ["energy", "free_energy", "energies", "forces", "stress"]
 
     def __init__(self, weights, cfg=None, device=None, device_id=0, precision="3xtf32",
-                 max_num_neighbors="config", zbl=True, **kwargs):
+                 max_num_neighbors="config", zbl=True, trace=False, **kwargs):
         super().__init__(**kwargs)
         self.zbl = zbl
+        # trace: the model pass is captured as a CUDA graph and replayed (also after the edge
+        # set changes, as long as its sizes do not), like TTAtomCalculator(trace=True)
+        self.trace = trace
+        self._step = self._step_key = None
         if cfg is None:
             from .weights import WeightBundle
             b = WeightBundle.load(weights) if isinstance(weights, str) else weights
@@ -408,13 +429,21 @@ class OrbCalculator(_AseCalculator):
                         device=self.device)
         if g.E == 0:
             raise ValueError("no edges within cutoff — system too sparse for this model")
-        if self._ws is None or self._ws.graph.N != g.N or self._ws.graph.E != g.E:
+        if self._ws is None or not self._ws.fits(g):
+            self._ws = self._step = None        # free the old buffers first
             self._ws = self.engine.workspace(g)
         else:
             self._ws.rebind(g)                  # same sizes: reuse the buffers
         ws = self._ws
         ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))
-        self.engine.run(ws, forces=forces, virial=stress)
+        key = (g.N, g.E, bool(forces), bool(stress))
+        if self.trace:
+            if self._step is None or self._step_key != key:
+                self._step = CapturedStep(self.engine, ws, forces=forces, virial=stress)
+                self._step_key = key
+            self._step()
+        else:
+            self.engine.run(ws, forces=forces, virial=stress)
         E = float(ws.energy.double().cpu()[0])
         return E, ws.forces.double().cpu(), (ws.virial.double().cpu() if stress else None)
 
