@@ -91,6 +91,7 @@ def gemm(A, lda, M, groups, C, ldc, Cpre, T1, T2, i1, i2, ldt, act, acc, precisi
     split-K partials); other modes get no scratch (plain atom_gemm)."""
     sc = None
     if precision == 3:
+        groups.ensure_f16()
         sc = torch.empty(8 * ((M + 127) // 128 * 128) * max(ldc, 64) + 1024, device=dev)
     call("atom_gemm_ex", ptr(A), lda, M, ctypes.byref(groups.struct), ptr(C), ldc, ptr(Cpre),
          ptr(T1), ptr(T2), ptr(i1), ptr(i2), ldt, act, acc, precision, ptr(sc),
@@ -182,7 +183,7 @@ def test_gemm_split_k_with_scratch(M, precision):
     B1, B2 = rnd(K1, N1, seed=1) * 0.1, rnd(K2, N2, seed=2) * 0.1
     bias1, bias2 = rnd(N1, seed=3), rnd(N2, seed=4)
     g = _Groups([dict(a_col=0, K=K1, c_col=0, N=N1, B=B1, bias=bias1),
-                 dict(a_col=K1, K=K2, c_col=N1 + 4, N=N2, B=B2, bias=bias2)])
+                 dict(a_col=K1, K=K2, c_col=N1 + 4, N=N2, B=B2, bias=bias2)]).ensure_f16()
     ldc = N1 + 4 + N2 + 4
     mpad = (M + 127) // 128 * 128
     scratch = torch.empty(8 * mpad * ldc, device=dev)
@@ -311,7 +312,7 @@ def test_gemm_f16_pair_without_scratch_runs_as_3xtf32():
     from tt_atom.engine import _Groups
     M, K, N = 500, 128, 192
     A, B = rnd(M, K, seed=31), rnd(K, N, seed=32)
-    g = _Groups([dict(a_col=0, K=K, c_col=0, N=N, B=B)])
+    g = _Groups([dict(a_col=0, K=K, c_col=0, N=N, B=B)]).ensure_f16()
     C2, C3 = torch.empty(M, N, device=dev), torch.empty(M, N, device=dev)
     call("atom_gemm", ptr(A), K, M, ctypes.byref(g.struct), ptr(C2), N, None, None, None, None,
          None, 0, 0, 0, 2, s())

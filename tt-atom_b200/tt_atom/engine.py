@@ -79,6 +79,8 @@ class _Groups:
 
     def __init__(self, groups):
         self.keep = []
+        self._tf32 = []
+        self._f16 = False
         g = L.GemmGroups()
         g.ngroups = len(groups)
         for i, d in enumerate(groups):
@@ -92,22 +94,29 @@ class _Groups:
             g.B[i] = B.data_ptr()
             self.keep.append(B)
             # K-major copies for the tensor-core kernel (hi part, lo part)
-            Bt = B[:d["K"], :d["N"]].t().contiguous()
-            hi, lo = _split_tf32(Bt)
+            hi, lo = _split_tf32(B[:d["K"], :d["N"]].t().contiguous())
             g.Bt[i] = hi.data_ptr()
             g.Bt_lo[i] = lo.data_ptr()
             self.keep += [hi, lo]
-            # fp16 halves with per-column scales for the fp16-pair mode
-            h16, l16, inv = _split_f16(Bt)
-            g.Bh[i] = h16.data_ptr()
-            g.Bh_lo[i] = l16.data_ptr()
-            g.Bh_inv[i] = inv.data_ptr()
-            self.keep += [h16, l16, inv]
+            self._tf32.append((hi, lo))
             b = d.get("bias")
             g.bias[i] = b.data_ptr() if b is not None else None
             if b is not None:
                 self.keep.append(b)
         self.struct = g
+
+    def ensure_f16(self):
+        """Add the fp16-pair mode's weight halves and column scales (made on first use from the
+        tf32 pair, whose sum is the weight exactly); without them that mode runs as 3xTF32."""
+        if not self._f16:
+            for i, (hi, lo) in enumerate(self._tf32):
+                h16, l16, inv = _split_f16(hi + lo)
+                self.struct.Bh[i] = h16.data_ptr()
+                self.struct.Bh_lo[i] = l16.data_ptr()
+                self.struct.Bh_inv[i] = inv.data_ptr()
+                self.keep += [h16, l16, inv]
+            self._f16 = True
+        return self
 
 
 def _so2_blocks(W_m0, b_m0, W_m, cin, hout, extra):
@@ -295,6 +304,8 @@ class UMAEngine:
               idx2=None, ldt=0, act=0, accumulate=0, stream=0):
         # the workspace's scratch lets node-level launches (few rows) split K over more CTAs
         sc = self._scratch
+        if self.precision == 3:
+            groups.ensure_f16()
         call("atom_gemm_ex", ptr(A), lda, M, groups.struct, ptr(Cout), ldc, ptr(Cpre), ptr(T1),
              ptr(T2), ptr(idx1), ptr(idx2), ldt, act, accumulate, self.precision, ptr(sc),
              sc.numel() if sc is not None else 0, stream)

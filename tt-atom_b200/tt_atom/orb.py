@@ -106,6 +106,8 @@ class OrbEngine:
               idx2=None, ldt=0, act=0, accumulate=0, s=0):
         # the workspace's scratch lets node-level launches (few rows) split K over more CTAs
         sc = self._scratch
+        if self.precision == 3:
+            groups.ensure_f16()
         call("atom_gemm_ex", ptr(A), lda, M, groups.struct, ptr(Cout), ldc, ptr(Cpre), ptr(T1),
              ptr(T2), ptr(idx1), ptr(idx2), ldt, act, accumulate, self.precision, ptr(sc),
              sc.numel() if sc is not None else 0, s)
