@@ -224,28 +224,58 @@ __device__ __forceinline__ void rotate_back_acc_s(const float* w, const float* y
 }
 
 // out[n] = resid[n] + sum over edges e received by n (CSR order) of env[e] * Wig(e)^T Y[e]
+// The coefficients and envelopes of 32 received edges at a time are staged in shared memory
+// (coalesced loads by the whole block) instead of 35 broadcast loads per thread and edge; two
+// edges' rows are loaded before either is accumulated. The fma order per output is unchanged.
+constexpr int kRbChunk = 32;
 __global__ void __launch_bounds__(kCP) rotate_back_reduce_kernel(
     const float* __restrict__ Y, const float* __restrict__ coef, const float* __restrict__ env,
     long long N, int C, const int* __restrict__ recv_ptr, const float* __restrict__ resid,
     float* __restrict__ out) {
+    __shared__ float sw[kRbChunk][kNnz + 1];      // 35 coefficients + the envelope
     const long long n = blockIdx.x;
     const int e0 = recv_ptr[n], e1 = recv_ptr[n + 1];
-    for (int c = threadIdx.x; c < C; c += kCP) {
+    for (int cb = 0; cb < C; cb += kCP) {
+        const int c = cb + threadIdx.x;
+        const bool active = c < C;
         float acc[kNsph];
 #pragma unroll
-        for (int j = 0; j < kNsph; ++j) acc[j] = resid ? resid[(n * kNsph + j) * C + c] : 0.f;
-        for (int e = e0; e < e1; ++e) {
-            float w[kNnz];
-            load_coef(coef, e, w);
-            const float s = __ldg(env + e);
-            float y[kNsph];
-            const float* ye = Y + (long long)e * kNsph * C;
+        for (int j = 0; j < kNsph; ++j)
+            acc[j] = (active && resid) ? resid[(n * kNsph + j) * C + c] : 0.f;
+        for (int eb = e0; eb < e1; eb += kRbChunk) {
+            const int ne = min(kRbChunk, e1 - eb);
+            __syncthreads();                       // the previous chunk has been read
+            for (int i = threadIdx.x; i < ne * (kNnz + 1); i += kCP) {
+                const int k = i / (kNnz + 1), j = i - k * (kNnz + 1);
+                sw[k][j] = j < kNnz ? coef[(long long)(eb + k) * kNnz + j] : env[eb + k];
+            }
+            __syncthreads();
+            if (!active) continue;
+            int k = 0;
+            for (; k + 1 < ne; k += 2) {
+                float ya[kNsph], yb[kNsph];
+                const float* pa = Y + (long long)(eb + k) * kNsph * C + c;
+                const float* pb = pa + (long long)kNsph * C;
 #pragma unroll
-            for (int r = 0; r < kNsph; ++r) y[r] = ye[r * C + c];
-            rotate_back_acc_s(w, y, s, acc);
+                for (int r = 0; r < kNsph; ++r) {
+                    ya[r] = pa[r * C];
+                    yb[r] = pb[r * C];
+                }
+                rotate_back_acc_s(sw[k], ya, sw[k][kNnz], acc);
+                rotate_back_acc_s(sw[k + 1], yb, sw[k + 1][kNnz], acc);
+            }
+            if (k < ne) {
+                float ya[kNsph];
+                const float* pa = Y + (long long)(eb + k) * kNsph * C + c;
+#pragma unroll
+                for (int r = 0; r < kNsph; ++r) ya[r] = pa[r * C];
+                rotate_back_acc_s(sw[k], ya, sw[k][kNnz], acc);
+            }
         }
+        if (active) {
 #pragma unroll
-        for (int j = 0; j < kNsph; ++j) out[(n * kNsph + j) * C + c] = acc[j];
+            for (int j = 0; j < kNsph; ++j) out[(n * kNsph + j) * C + c] = acc[j];
+        }
     }
 }
 
