@@ -88,6 +88,19 @@ __device__ __forceinline__ void load_coef(const float* __restrict__ coef, long l
     for (int k = 0; k < kNnz; ++k) w[k] = __ldg(coef + e * kNnz + k);
 }
 
+// The same row for a warp that owns edge e: one coalesced load per lane (lanes 0-2 also load
+// the last three), then register broadcasts instead of 35 loads per lane.
+__device__ __forceinline__ void load_coef_warp(const float* __restrict__ coef, long long e,
+                                               int lane, float* w) {
+    const float* row = coef + e * kNnz;
+    const float a = __ldg(row + lane);
+    const float b = lane < kNnz - 32 ? __ldg(row + 32 + lane) : 0.f;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) w[k] = __shfl_sync(0xffffffffu, a, k);
+#pragma unroll
+    for (int k = 32; k < kNnz; ++k) w[k] = __shfl_sync(0xffffffffu, b, k - 32);
+}
+
 // -------------------------------------------------------------------------- rotate-in (fwd)
 __global__ void __launch_bounds__(256) rotate_in_kernel(
     const float* __restrict__ x, const int* __restrict__ src, const int* __restrict__ tgt,
@@ -97,7 +110,7 @@ __global__ void __launch_bounds__(256) rotate_in_kernel(
     int lane = threadIdx.x & 31;
     if (e >= E) return;
     float w[kNnz];
-    load_coef(coef, e, w);
+    load_coef_warp(coef, e, lane, w);
     const float* xs = x + (long long)__ldg(src + e) * kNsph * C;
     const float* xt = x + (long long)__ldg(tgt + e) * kNsph * C;
     const int W2 = 2 * C;
@@ -290,7 +303,7 @@ __global__ void __launch_bounds__(256, 2) rotate_back_bwd_kernel(
     int lane = threadIdx.x & 31;
     if (e >= E) return;
     float w[kNnz];
-    load_coef(coef, e, w);
+    load_coef_warp(coef, e, lane, w);
     float s = env[e];
     const float* gt = gx + (long long)tgt[e] * kNsph * C;
     const float* ye = Y + e * kNsph * C;
@@ -341,7 +354,7 @@ __global__ void __launch_bounds__(64) rotate_in_bwd_edge_kernel(
     if (e >= E) return;
     const int W2 = 2 * C;
     float w[kNnz];
-    load_coef(coef, e, w);
+    load_coef_warp(coef, e, lane, w);
     const float* ga = gA + e * kNsph * W2;
     const float* rr = rad + e * ldr + rad_col;
     float* gr = g_rot + e * kNsph * W2;
@@ -394,6 +407,7 @@ __device__ __forceinline__ void wig_t_acc(const float* w, const float4* g, float
 }
 
 // ------------------------------------------------------------ rotate-in VJP (node part)
+constexpr int kNbChunk = 16;   // edges per staged coefficient chunk (even: pairs stay aligned)
 // kSplit warps share one node: warp w walks part w of the node's (received, then sent) edge
 // list; the partial sums are added in warp order through shared memory.
 template <int kSplit>
@@ -402,6 +416,7 @@ __global__ void __launch_bounds__(32 * kSplit) rotate_in_bwd_node_kernel(
     const int* __restrict__ recv_ptr, const int* __restrict__ send_ptr,
     const int* __restrict__ send_eid, int accumulate, float* __restrict__ gx) {
     extern __shared__ float4 part[];    // [kSplit - 1][9][32] per 128-channel chunk
+    __shared__ float swc[kSplit][kNbChunk][kNnz];
     const long long n = blockIdx.x;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int W2 = 2 * C;
@@ -410,38 +425,55 @@ __global__ void __launch_bounds__(32 * kSplit) rotate_in_bwd_node_kernel(
     const int nr = r1 - r0, total = nr + (s1 - s0);
     const int chunk = (total + kSplit - 1) / kSplit;
     const int k0 = wid * chunk, k1 = min(total, k0 + chunk);
-    for (int c = lane * 4; c < C; c += 128) {
+    // every lane runs every channel pass (the staging below needs the whole warp); lanes past
+    // C only help stage
+    for (int cb = 0; cb < C; cb += 128) {
+        const int c = cb + lane * 4;
+        const bool act = c < C;
         float4 acc[kNsph];
 #pragma unroll
         for (int j = 0; j < kNsph; ++j)
-            acc[j] = (accumulate && wid == 0) ? ld4(gx + (n * kNsph + j) * C + c) : f4(0.f);
-        int k = k0;
-        for (; k + 1 < k1; k += 2) {
-            const int ea = k < nr ? r0 + k : send_eid[s0 + k - nr];
-            const int eb = k + 1 < nr ? r0 + k + 1 : send_eid[s0 + k + 1 - nr];
-            const float* ga = g_rot + (long long)ea * kNsph * W2 + (k < nr ? C : 0);
-            const float* gb = g_rot + (long long)eb * kNsph * W2 + (k + 1 < nr ? C : 0);
-            float wa[kNnz], wb[kNnz];
-            load_coef(coef, ea, wa);
-            load_coef(coef, eb, wb);
-            float4 g1[kNsph], g2[kNsph];
-#pragma unroll
-            for (int r = 0; r < kNsph; ++r) {
-                g1[r] = ld4(ga + r * W2 + c);
-                g2[r] = ld4(gb + r * W2 + c);
+            acc[j] = (act && accumulate && wid == 0) ? ld4(gx + (n * kNsph + j) * C + c)
+                                                      : f4(0.f);
+        // this warp's edges in chunks of kNbChunk: their coefficient rows are staged in shared
+        // memory by the whole warp (instead of 35 broadcast loads per lane and edge); edges are
+        // still taken in pairs from k0 in list order, so the sums are unchanged
+        float(*sw)[kNnz] = swc[wid];
+        for (int kb = k0; kb < k1; kb += kNbChunk) {
+            const int ne = min(kNbChunk, k1 - kb);
+            __syncwarp();
+            for (int i = lane; i < ne * kNnz; i += 32) {
+                const int q = i / kNnz, j = i - q * kNnz, kk = kb + q;
+                const int e = kk < nr ? r0 + kk : send_eid[s0 + kk - nr];
+                sw[q][j] = coef[(long long)e * kNnz + j];
             }
-            wig_t_acc(wa, g1, acc);
-            wig_t_acc(wb, g2, acc);
-        }
-        if (k < k1) {
-            const int ea = k < nr ? r0 + k : send_eid[s0 + k - nr];
-            const float* ga = g_rot + (long long)ea * kNsph * W2 + (k < nr ? C : 0);
-            float wa[kNnz];
-            load_coef(coef, ea, wa);
-            float4 g1[kNsph];
+            __syncwarp();
+            if (!act) continue;
+            int q = 0;
+            for (; q + 1 < ne; q += 2) {
+                const int k = kb + q;
+                const int ea = k < nr ? r0 + k : send_eid[s0 + k - nr];
+                const int eb = k + 1 < nr ? r0 + k + 1 : send_eid[s0 + k + 1 - nr];
+                const float* ga = g_rot + (long long)ea * kNsph * W2 + (k < nr ? C : 0);
+                const float* gb = g_rot + (long long)eb * kNsph * W2 + (k + 1 < nr ? C : 0);
+                float4 g1[kNsph], g2[kNsph];
 #pragma unroll
-            for (int r = 0; r < kNsph; ++r) g1[r] = ld4(ga + r * W2 + c);
-            wig_t_acc(wa, g1, acc);
+                for (int r = 0; r < kNsph; ++r) {
+                    g1[r] = ld4(ga + r * W2 + c);
+                    g2[r] = ld4(gb + r * W2 + c);
+                }
+                wig_t_acc(sw[q], g1, acc);
+                wig_t_acc(sw[q + 1], g2, acc);
+            }
+            if (q < ne) {
+                const int k = kb + q;
+                const int ea = k < nr ? r0 + k : send_eid[s0 + k - nr];
+                const float* ga = g_rot + (long long)ea * kNsph * W2 + (k < nr ? C : 0);
+                float4 g1[kNsph];
+#pragma unroll
+                for (int r = 0; r < kNsph; ++r) g1[r] = ld4(ga + r * W2 + c);
+                wig_t_acc(sw[q], g1, acc);
+            }
         }
         if (kSplit > 1) {
             if (wid > 0) {
@@ -460,7 +492,7 @@ __global__ void __launch_bounds__(32 * kSplit) rotate_in_bwd_node_kernel(
             }
             __syncthreads();
         }
-        if (wid == 0) {
+        if (wid == 0 && act) {
 #pragma unroll
             for (int j = 0; j < kNsph; ++j) st4(gx + (n * kNsph + j) * C + c, acc[j]);
         }
