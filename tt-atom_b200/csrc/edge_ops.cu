@@ -343,8 +343,10 @@ __global__ void __launch_bounds__(256, 2) rotate_back_bwd_kernel(
 }
 
 // ------------------------------------------------------------ rotate-in VJP (edge part)
-// launched in 64-thread blocks (finer block retirement at 255 registers: 1.89 -> 1.77 ms)
-__global__ void __launch_bounds__(64) rotate_in_bwd_edge_kernel(
+// launched in 64-thread blocks (finer block retirement: 1.89 -> 1.77 ms per step at 255
+// registers), capped at 204 registers for 5 blocks per SM (76 bytes of spills; 1.74 -> 1.57 ms;
+// 6 blocks per SM measured slower, 8 about the same)
+__global__ void __launch_bounds__(64, 5) rotate_in_bwd_edge_kernel(
     const float* __restrict__ gA, const float* __restrict__ rot, const float* __restrict__ rad,
     long long ldr, int rad_col, const float* __restrict__ x, const int* __restrict__ src,
     const int* __restrict__ tgt, const float* __restrict__ coef, long long E, int C,
