@@ -412,8 +412,10 @@ __device__ __forceinline__ void wig_t_acc(const float* w, const float4* g, float
 constexpr int kNbChunk = 16;   // edges per staged coefficient chunk (even: pairs stay aligned)
 // kSplit warps share one node: warp w walks part w of the node's (received, then sent) edge
 // list; the partial sums are added in warp order through shared memory.
+// Capped at 128 registers (8 blocks per SM): 0.55 -> 0.44 ms per step against the 140-register
+// build; 12 and 16 blocks per SM spill and measured slower.
 template <int kSplit>
-__global__ void __launch_bounds__(32 * kSplit) rotate_in_bwd_node_kernel(
+__global__ void __launch_bounds__(32 * kSplit, 8) rotate_in_bwd_node_kernel(
     const float* __restrict__ g_rot, const float* __restrict__ coef, long long N, int C,
     const int* __restrict__ recv_ptr, const int* __restrict__ send_ptr,
     const int* __restrict__ send_eid, int accumulate, float* __restrict__ gx) {
