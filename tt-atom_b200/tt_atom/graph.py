@@ -33,6 +33,39 @@ def image_shifts(cell, pbc, cutoff):
     return cells @ cell
 
 
+_SHIFT_CACHE = {}
+_SYS_CACHE = {}
+
+
+def _device_shifts(cell, pbc, cutoff, dev):
+    """``image_shifts`` on the device, cached per (cell, pbc, cutoff, device): MD and relaxation
+    call the neighbour list every step with the same cell."""
+    key = (np.asarray(cell, np.float32).tobytes(), tuple(np.broadcast_to(np.asarray(pbc, bool), 3)),
+           float(cutoff), str(dev))
+    t = _SHIFT_CACHE.get(key)
+    if t is None:
+        if len(_SHIFT_CACHE) > 64:
+            _SHIFT_CACHE.clear()
+        t = _SHIFT_CACHE[key] = image_shifts(cell, pbc, cutoff).to(dev).contiguous()
+    return t
+
+
+def _device_sys(sys_ptr, dev):
+    """(sys_id [N], sys_ptr [nsys + 1]) int32 device tensors for atom offsets ``sys_ptr``, cached."""
+    key = (tuple(sys_ptr), str(dev))
+    v = _SYS_CACHE.get(key)
+    if v is None:
+        if len(_SYS_CACHE) > 64:
+            _SYS_CACHE.clear()
+        N = sys_ptr[-1]
+        sys_id = torch.empty(N, dtype=torch.int32)
+        for k in range(len(sys_ptr) - 1):
+            sys_id[sys_ptr[k]:sys_ptr[k + 1]] = k
+        v = _SYS_CACHE[key] = (sys_id.to(dev),
+                               torch.tensor(sys_ptr, dtype=torch.int32, device=dev))
+    return v
+
+
 def csd_embedding(w, charge, spin, C, dataset="omat"):
     """System (charge / spin / dataset) embedding [nsys, C], tt_atom/geometry.py:23-45. Host
     glue: a few hundred flops per system, computed once per system."""
@@ -96,6 +129,7 @@ def build_graph(pos, Z, cutoff, cell=None, pbc=None, max_neighbors=None, sys_ptr
     """Neighbour list of one system, or of several aperiodic systems stored back to back
     (``sys_ptr`` atom offsets; no edges between systems), on the GPU."""
     dev = torch.device(device)
+    pos_host = None if torch.is_tensor(pos) else np.asarray(pos, dtype=np.float32)
     pos = torch.as_tensor(pos, dtype=torch.float32).to(dev).contiguous()
     N = pos.shape[0]
     Zt = torch.as_tensor(np.asarray(Z), dtype=torch.int32).to(dev).contiguous()
@@ -106,8 +140,8 @@ def build_graph(pos, Z, cutoff, cell=None, pbc=None, max_neighbors=None, sys_ptr
     nsys = len(sys_ptr) - 1
     if periodic and nsys != 1:
         raise ValueError("periodic batches are built one system at a time")
-    shifts = (image_shifts(cell, pbc, cutoff) if periodic
-              else torch.zeros(1, 3)).to(dev).contiguous()
+    shifts = (_device_shifts(cell, pbc, cutoff, dev) if periodic
+              else torch.zeros(1, 3, device=dev))
     S = shifts.shape[0]
     s = L.stream_ptr(stream)
     if max_cand is None:
@@ -117,7 +151,10 @@ def build_graph(pos, Z, cutoff, cell=None, pbc=None, max_neighbors=None, sys_ptr
     small = torch.empty(nsys + 2, dtype=torch.int64, device=dev)
     sp_host = L.host_i64(sys_ptr)
     need = ctypes.c_int(0)
-    pos_np = pos.detach().cpu().numpy() if periodic else None
+    # the bounding box from the caller's host array when there is one (no device round trip)
+    pos_np = None
+    if periodic:
+        pos_np = pos_host if pos_host is not None else pos.detach().cpu().numpy()
     bbox = (L.host_f32(list(pos_np.min(0)) + list(pos_np.max(0)))
             if periodic and N > 0 else None)
     while True:
@@ -152,11 +189,8 @@ def build_graph(pos, Z, cutoff, cell=None, pbc=None, max_neighbors=None, sys_ptr
     zs = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
     zt = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
     call("atom_edge_species", ptr(Zt), ptr(src), ptr(tgt), E, ptr(zs), ptr(zt), s)
-    sys_id = torch.empty(N, dtype=torch.int32)
-    for k in range(nsys):
-        sys_id[sys_ptr[k]:sys_ptr[k + 1]] = k
-    return Graph(N=N, E=E, nsys=nsys, periodic=periodic, Z=Zt, sys_id=sys_id.to(dev),
-                 sys_ptr=torch.tensor(sys_ptr, dtype=torch.int32, device=dev),
+    sys_id, sys_ptr_d = _device_sys(sys_ptr, dev)
+    return Graph(N=N, E=E, nsys=nsys, periodic=periodic, Z=Zt, sys_id=sys_id, sys_ptr=sys_ptr_d,
                  sys_ptr_host=sys_ptr, src=src, tgt=tgt, img=img, shifts=shifts,
                  recv_ptr=recv_ptr, send_ptr=send_ptr, send_eid=send_eid, zs=zs[:E], zt=zt[:E])
 
