@@ -405,7 +405,12 @@ def run_ours(args):
         "roofline": {"bound": "tensor", "kernel": kern["name"], "achieved": achieved,
                      "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16,
                      "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)",
-                     "traffic": traffic, "launch_ms": kern["ms"], "flop_per_launch": kern["flop"]},
+                     "traffic": traffic, "launch_ms": kern["ms"], "flop_per_launch": kern["flop"],
+                     # the split modes issue three MMAs per product (hi*hi, hi*lo, lo*hi): the
+                     # tensor pipe does 3x the algorithmic FLOPs, at tf32 rate (3xTF32) or at
+                     # f16 rate (fp16 pair)
+                     "mma_products": 3 if eng.precision in (2, 3) else 1,
+                     "mma_work_tflops": achieved * (3 if eng.precision in (2, 3) else 1)},
         "clocks": clocks,
     }
     if edge is not None:
