@@ -1,0 +1,28 @@
+"""Host-side caches of the neighbour-list builder (no GPU): the image-shift table and the
+per-system index tensors are reused for identical inputs and rebuilt when the cell, the
+periodic axes, the cutoff or the system offsets change."""
+import numpy as np
+import torch
+
+from tt_atom import graph as G
+
+
+def test_image_shift_cache_keys_on_cell_pbc_and_cutoff():
+    cell = np.diag([7.1, 7.1, 7.1]).astype(np.float32)
+    a = G._device_shifts(cell, [True] * 3, 6.0, "cpu")
+    assert G._device_shifts(cell.copy(), [True] * 3, 6.0, "cpu") is a
+    assert torch.equal(a, G.image_shifts(cell, [True] * 3, 6.0))
+    b = G._device_shifts(cell * 1.01, [True] * 3, 6.0, "cpu")
+    assert b is not a and not torch.equal(a, b)
+    c = G._device_shifts(cell, [True, True, False], 6.0, "cpu")
+    assert c.shape[0] < a.shape[0]
+    d = G._device_shifts(cell, [True] * 3, 8.0, "cpu")     # two image layers per axis
+    assert d.shape[0] == 125 and a.shape[0] == 27
+
+
+def test_system_index_cache():
+    sid, sp = G._device_sys([0, 3, 7], "cpu")
+    assert sid.tolist() == [0, 0, 0, 1, 1, 1, 1] and sp.tolist() == [0, 3, 7]
+    assert G._device_sys([0, 3, 7], "cpu")[0] is sid
+    sid2, _ = G._device_sys([0, 4, 7], "cpu")
+    assert sid2.tolist() == [0, 0, 0, 0, 1, 1, 1]
