@@ -16,7 +16,7 @@ import numpy as np
 import torch
 
 from .ase_compat import _AseCalculator, all_changes, atoms_volume, voigt_6
-from .engine import CapturedStep, UMAEngine
+from .engine import CapturedStep, UMAEngine, to_host
 from .graph import build_graph, csd_embedding
 from .weights import WeightBundle
 
@@ -126,9 +126,8 @@ class TTAtomCalculator(_AseCalculator):
             self.engine.run(ws, ws.pos, forces=forces, virial=stress)
         if device_out:
             return ws.energy, ws.forces if forces else None, ws.virial if stress else None
-        E = ws.energy.double().cpu()
-        F = ws.forces.double().cpu() if forces else None
-        V = ws.virial.double().cpu() if stress else None
+        E, F, V = to_host(ws.energy, ws.forces if forces else None,
+                          ws.virial if stress else None)
         return E, F, V
 
     # ------------------------------------------------------------------------------- ASE

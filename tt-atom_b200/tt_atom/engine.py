@@ -43,6 +43,23 @@ call = L.call
 PRECISIONS = {"fp32": 0, "tf32": 1, "3xtf32": 2, "3xf16": 3}
 
 
+def to_host(*ts):
+    """float64 host copies of several device result tensors through one device-to-host copy
+    (one synchronisation instead of one per tensor); None entries stay None."""
+    live = [t for t in ts if t is not None]
+    if not live:
+        return [None] * len(ts)
+    flat = torch.cat([t.reshape(-1).to(torch.float64) for t in live]).cpu()
+    out, o = [], 0
+    for t in ts:
+        if t is None:
+            out.append(None)
+            continue
+        out.append(flat[o:o + t.numel()].reshape(t.shape))
+        o += t.numel()
+    return out
+
+
 def launch_count():
     """Kernels the library has launched so far (its own counter)."""
     n = L.ctypes.c_int64(0)

@@ -25,7 +25,7 @@ import torch
 from . import _lib as L
 from ._lib import ptr
 from .ase_compat import _AseCalculator, all_changes, atoms_volume, voigt_6
-from .engine import PRECISIONS, CapturedStep, Workspace, _Groups, _dev, call
+from .engine import PRECISIONS, CapturedStep, Workspace, _Groups, _dev, call, to_host
 from .graph import build_graph
 
 
@@ -398,7 +398,13 @@ class OrbCalculator(_AseCalculator):
     def _zbl(self, ws, stress, scale=None):
         """ZBL energy (``scale`` times the pair sum: 1 / N, the per-node mean, by default),
         forces and virial on ``ws``'s graph (its edge vectors ``ws.ev`` are those of the last
-        ``engine.run``)."""
+        ``engine.run``), as host values."""
+        E, F, V = to_host(*self._zbl_launch(ws, stress, scale))
+        return float(E[0]), F, V
+
+    def _zbl_launch(self, ws, stress, scale=None):
+        """Launch the ZBL term (see ``_zbl``); returns its device tensors (energy [1] float64,
+        forces [N, 3], virial [3, 3] or None)."""
         g, N, E = ws.graph, ws.graph.N, ws.graph.E
         if getattr(ws, "zbl_gev", None) is None or ws.zbl_gev.shape[0] != max(E, 1):
             f = lambda *sh, dt=torch.float32: torch.empty(*sh, device=self.device, dtype=dt)  # noqa: E731
@@ -412,8 +418,7 @@ class OrbCalculator(_AseCalculator):
         call("atom_forces_virial", ptr(ws.zbl_gev), ptr(ws.ev), E, N, ptr(g.recv_ptr),
              ptr(g.send_ptr), ptr(g.send_eid), ptr(ws.zbl_F),
              ptr(ws.zbl_V) if stress else None, ptr(ws.vscratch), s)
-        return (float(ws.zbl_E.cpu()[0]), ws.zbl_F.double().cpu(),
-                ws.zbl_V.double().cpu() if stress else None)
+        return ws.zbl_E, ws.zbl_F, (ws.zbl_V if stress else None)
 
     def _evaluate_direct(self, pos, Z, cell, pbc, stress=False):
         """Direct checkpoints: raw energy, raw per-atom forces [N, 3] (net force removed) and
@@ -426,7 +431,7 @@ class OrbCalculator(_AseCalculator):
         S = ws.sraw[0, :6].double().cpu() if stress else None
         return E, F, S
 
-    def _evaluate(self, pos, Z, cell, pbc, forces=True, stress=False):
+    def _evaluate(self, pos, Z, cell, pbc, forces=True, stress=False, device_out=False):
         g = build_graph(pos, Z, self.cfg["cutoff"], cell, pbc, max_neighbors=self.max_nbrs,
                         device=self.device)
         if g.E == 0:
@@ -446,8 +451,10 @@ class OrbCalculator(_AseCalculator):
             self._step()
         else:
             self.engine.run(ws, forces=forces, virial=stress)
-        E = float(ws.energy.double().cpu()[0])
-        return E, ws.forces.double().cpu(), (ws.virial.double().cpu() if stress else None)
+        if device_out:      # device tensors the next call overwrites
+            return ws.energy, ws.forces, (ws.virial if stress else None)
+        E, F, V = to_host(ws.energy, ws.forces, ws.virial if stress else None)
+        return float(E[0]), F, V
 
     def calculate(self, atoms=None, properties=("energy", "forces"), system_changes=all_changes):
         super().calculate(atoms, properties, system_changes)
@@ -458,7 +465,12 @@ class OrbCalculator(_AseCalculator):
         want_stress = cell is not None and ("stress" in properties or bool(pbc.all()))
         if self.engine.direct:
             return self._calculate_direct(atoms, pos, Z, cell, pbc, properties, want_stress)
-        E, F, V = self._evaluate(pos, Z, cell, pbc if pbc.any() else None, True, want_stress)
+        # model pass and ZBL term on the device, then one read-back of all their results
+        Ed, Fd, Vd = self._evaluate(pos, Z, cell, pbc if pbc.any() else None, True, want_stress,
+                                    device_out=True)
+        zb = self._zbl_launch(self._ws, want_stress) if self.zbl else (None, None, None)
+        E, F, V, Ez, Fz, Vz = to_host(Ed, Fd, Vd, *zb)
+        E = float(E[0])
         n = len(Z)
         w = self._w
         scale = 1.0
@@ -473,7 +485,7 @@ class OrbCalculator(_AseCalculator):
         if V is not None:
             V = scale * V
         if self.zbl:
-            Ez, Fz, Vz = self._zbl(self._ws, V is not None)
+            Ez = float(Ez[0])
             self.results["energy"] = self.results["free_energy"] = E = E + Ez
             self.results["energies"] = np.full(n, E / n)
             self.results["forces"] = self.results["forces"] + Fz.numpy()
