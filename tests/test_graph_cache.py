@@ -1,4 +1,4 @@
-"""Host-side caches of the neighbour-list builder (no GPU): the image-shift table and the
+"""Host-side helpers (no GPU). The neighbour-list builder's caches: the image-shift table and the
 per-system index tensors are reused for identical inputs and rebuilt when the cell, the
 periodic axes, the cutoff or the system offsets change."""
 import numpy as np
@@ -26,3 +26,15 @@ def test_system_index_cache():
     assert G._device_sys([0, 3, 7], "cpu")[0] is sid
     sid2, _ = G._device_sys([0, 4, 7], "cpu")
     assert sid2.tolist() == [0, 0, 0, 0, 1, 1, 1]
+
+
+def test_to_host_returns_float64_copies_in_order():
+    """One read-back for several result tensors: shapes and values kept, float64, None kept."""
+    from tt_atom.engine import to_host
+    a = torch.arange(3, dtype=torch.float32)
+    b = torch.arange(6, dtype=torch.float32).reshape(2, 3) / 7
+    c = torch.tensor([1.5], dtype=torch.float64)
+    x, y, z, w = to_host(a, None, b, c)
+    assert y is None and x.dtype == torch.float64 and z.shape == (2, 3)
+    assert torch.equal(x, a.double()) and torch.equal(z, b.double()) and torch.equal(w, c)
+    assert to_host(None, None) == [None, None]
