@@ -1,6 +1,6 @@
-"""Host-side helpers (no GPU). The neighbour-list builder's caches: the image-shift table and the
-per-system index tensors are reused for identical inputs and rebuilt when the cell, the
-periodic axes, the cutoff or the system offsets change."""
+"""Host-side helpers (no GPU): the neighbour-list builder's caches (the image-shift table and
+the per-system index tensors are reused for identical inputs and rebuilt when the cell, the
+periodic axes, the cutoff or the system offsets change) and the single read-back of results."""
 import numpy as np
 import torch
 
