@@ -97,25 +97,29 @@ class TTAtomCalculator(_AseCalculator):
             raise ValueError("no edges within cutoff — system too sparse for this model")
         se = csd_embedding(self._w, charges, spins, self.C, dataset=self.task)
         key = (g.N, g.E, bool(stress), bool(forces))
-        reuse = (trace and self._ws is not None and self._ws_key == key
-                 and g.same_topology(self._ws.graph) and torch.equal(self._se, se))
-        if not reuse:
-            keep = False
-            if self._ws is not None and self._ws.fits(g):
-                # same sizes: the new topology is copied into the workspace's own arrays, so a
-                # captured step stays valid (unchunked: no host-side plan depends on the
-                # topology) and is replayed on it
-                keep = self._ws_key == key and self._ws.chunks is None
-                self._ws.rebind(g, se)
-            else:
-                self._ws = self._step = None        # free the old buffers first
-                chunk = self.chunk_edges
-                if chunk == "auto":
-                    chunk = self.engine.choose_chunk_edges(g)
-                self._ws = self.engine.workspace(g, se, chunk_edges=chunk)
-            self._ws_key, self._se = key, se
+        if self._ws is not None and self._ws.fits(g) and self._ws.chunks is None:
+            # same sizes: the (possibly unchanged) topology is copied into the workspace's own
+            # arrays, asynchronously, instead of comparing it first; the captured step stays
+            # valid and is replayed on them
+            keep = self._ws_key == key
+            self._ws.rebind(g, se)
+        elif self._ws is not None and self._ws.fits(g):
+            # chunked: the chunk plans are host-side launch parameters of a captured step, so it
+            # is kept only while the topology is unchanged
+            keep = (self._ws_key == key and g.same_topology(self._ws.graph)
+                    and self._se is not None and torch.equal(self._se, se))
             if not keep:
-                self._step = None
+                self._ws.rebind(g, se)
+        else:
+            keep = False
+            self._ws = self._step = None            # free the old buffers first
+            chunk = self.chunk_edges
+            if chunk == "auto":
+                chunk = self.engine.choose_chunk_edges(g)
+            self._ws = self.engine.workspace(g, se, chunk_edges=chunk)
+        self._ws_key, self._se = key, se
+        if not keep:
+            self._step = None
         ws = self._ws
         ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))
         if trace:
