@@ -43,6 +43,12 @@ WORKLOADS = {
     "fe65k": "uma-s-1-shape eSCN-MD, periodic 65536-atom bcc Fe, slab-decomposed, E+F+stress",
     "screen": "uma-s-1-shape eSCN-MD, 512 molecules (10-60 atoms) partitioned over GPUs, E+F",
 }
+DATA = {
+    "uma": "synthetic (seeded fcc Cu/Ni, random-init weights)",
+    "orb": "synthetic (seeded amorphous SiO2, random-init weights)",
+    "fe65k": "synthetic (seeded bcc Fe, random-init weights)",
+    "screen": "synthetic (seeded molecules, random-init weights)",
+}
 
 
 def peaks():
@@ -393,7 +399,7 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": "atom-steps/s", "n_gpus": ws_n,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-        "data": "synthetic (seeded fcc Cu/Ni, random-init weights)",
+        "data": DATA[args.workload],
         "config": {"workload": WORKLOADS[args.workload], "atoms_per_gpu": N, "edges_per_gpu": ws.graph.E,
                    "cutoff": cfg["cutoff"], "max_neighbors": cfg["max_neighbors"],
                    "precision": eng_precision, "parallelism": f"replicas x{ws_n}",
@@ -515,7 +521,7 @@ def run_reference(args):
            "steps": steps, "warmup": args.warmup,
            "ms_per_step": 1e3 * cpu["seconds_per_step"], "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-           "data": "synthetic (seeded fcc Cu/Ni, random-init weights)",
+           "data": DATA[args.workload],
            "config": {"workload": WORKLOADS[args.workload], "sample": cpu["sample"]},
            "impl": "reference", "cpu_baseline": cpu,
            "e2e": {"value": cpu["value"], "unit": "atom-steps/s", "h2d_bytes_per_step": 0,
