@@ -241,3 +241,17 @@ def test_calculator_api_and_errors():
         sparse.get_potential_energy()
     with pytest.raises(ValueError, match="task_name"):
         TTAtomCalculator(b, task_name="omol")
+    # a bundle carrying its merge reference: batches must share its reduced composition and its
+    # (charge, spin) (tt_atom/calculator.py:193-217)
+    arrs = dict(configs.random_bundle_arrays(cfg, seed=0))
+    m = configs.tiny_molecule()
+    arrs.update({"ref@energy": np.array([0.0]), "ref@forces": np.zeros((24, 3)),
+                 "ref@pos": m["pos"], "ref@atomic_numbers": np.asarray(m["Z"]),
+                 "ref@charge": np.array([0.0]), "ref@spin": np.array([0.0])})
+    calc_r = TTAtomCalculator(WeightBundle.from_arrays(arrs))
+    out = calc_r.evaluate_batch([dict(pos=m["pos"], Z=m["Z"]), dict(pos=m["pos"] + 0.01, Z=m["Z"])])
+    assert out["energy"].shape == (2,)
+    with pytest.raises(ValueError, match="different reduced composition"):
+        calc_r.evaluate_batch([dict(pos=m["pos"], Z=m["Z"]), dict(pos=m["pos"][:23], Z=m["Z"][:23])])
+    with pytest.raises(ValueError, match=r"\(charge, spin\)"):
+        calc_r.evaluate_batch([dict(pos=m["pos"], Z=m["Z"], charge=1.0)])

@@ -38,3 +38,21 @@ def test_to_host_returns_float64_copies_in_order():
     assert y is None and x.dtype == torch.float64 and z.shape == (2, 3)
     assert torch.equal(x, a.double()) and torch.equal(z, b.double()) and torch.equal(w, c)
     assert to_host(None, None) == [None, None]
+
+
+def test_reduced_composition_and_bundle_reference():
+    """The merged-bundle composition key (counts divided by their gcd) and the bundle's embedded
+    reference system (``ref@`` entries; None without them)."""
+    from tt_atom.weights import WeightBundle, reduced_composition
+    assert reduced_composition([1, 1, 8]) == ((1, 2), (8, 1))
+    assert reduced_composition([8, 1, 1, 1, 8, 1]) == ((1, 2), (8, 1))     # H4O2 ~ H2O
+    assert reduced_composition([6, 1, 1, 1, 1]) != reduced_composition([6, 1, 1])
+    cfg = b'{"task": "omol"}'
+    arrs = {"config": np.frombuffer(cfg, dtype=np.uint8)}
+    assert WeightBundle.from_arrays(arrs).reference is None
+    arrs.update({"ref@energy": np.array([-1.5]), "ref@forces": np.zeros((3, 3)),
+                 "ref@pos": np.zeros((3, 3)), "ref@atomic_numbers": np.array([8, 1, 1]),
+                 "ref@charge": np.array([0.0]), "ref@spin": np.array([1.0])})
+    ref = WeightBundle.from_arrays(arrs).reference
+    assert ref["energy"] == -1.5 and ref["spin"] == 1.0 and ref["cell"] is None
+    assert reduced_composition(ref["atomic_numbers"]) == ((1, 2), (8, 1))

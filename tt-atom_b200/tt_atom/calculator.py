@@ -18,7 +18,7 @@ import torch
 from .ase_compat import _AseCalculator, all_changes, atoms_volume, voigt_6
 from .engine import CapturedStep, UMAEngine, to_host
 from .graph import build_graph, csd_embedding
-from .weights import WeightBundle
+from .weights import WeightBundle, reduced_composition
 
 
 def _fields(system):
@@ -87,12 +87,12 @@ class TTAtomCalculator(_AseCalculator):
                            max_neighbors=self.max_neighbors, sys_ptr=sys_ptr, device=self.device)
 
     def _evaluate(self, pos, Z, cell, pbc, charges, spins, sys_ptr=None, forces=True,
-                  stress=False, trace=False, device_out=False):
+                  stress=False, trace=False, device_out=False, graph=None):
         """Raw (unnormalised) per-system energies [nsys], forces [N, 3], virial [3, 3]|None,
         as float64 host tensors, or (``device_out``) as float32 device tensors that the next
         call overwrites (``pos`` may then be a device tensor too: nothing crosses to the host
         but the neighbour-list size)."""
-        g = self._graph(pos, Z, cell, pbc, sys_ptr)
+        g = graph if graph is not None else self._graph(pos, Z, cell, pbc, sys_ptr)
         if g.E == 0:
             raise ValueError("no edges within cutoff — system too sparse for this model")
         se = csd_embedding(self._w, charges, spins, self.C, dataset=self.task)
@@ -158,6 +158,27 @@ class TTAtomCalculator(_AseCalculator):
         (tt_atom/calculator.py:168-236). Returns dict(energy [K], forces list or None)."""
         if len(systems) == 0:
             raise ValueError("empty batch")
+        # a merged bundle bakes the expert routing for one reduced composition and one (charge,
+        # spin): with its reference system embedded, every batched system is checked against it
+        # (tt_atom/calculator.py:193-217; same errors)
+        ref = self.bundle.reference if hasattr(self.bundle, "reference") else None
+        if ref is not None:
+            want_comp = reduced_composition(ref["atomic_numbers"])
+            want_cs = (float(ref["charge"]), float(ref["spin"]))
+            for k, system in enumerate(systems):
+                _, Z_k, chg_k, spin_k, _, _ = _fields(system)
+                if reduced_composition(np.asarray(Z_k).tolist()) != want_comp:
+                    raise ValueError(
+                        f"batched system {k} has a different reduced composition than this "
+                        "bundle. A merged uma-s-1 bundle bakes the MoLE routing for one reduced "
+                        "composition, so every system in a batch must share it (e.g. conformers "
+                        "/ an MD ensemble of one molecule); evaluate other compositions with "
+                        "their own bundle.")
+                if (chg_k, spin_k) != want_cs:
+                    raise ValueError(
+                        f"batched system {k} has (charge, spin)=({chg_k}, {spin_k}) but this "
+                        f"bundle was merged for {want_cs}. The MoLE routing bakes one "
+                        "charge/spin; every system in a batch must share it.")
         pos_all, Z_all, chg, spn, ptr_ = [], [], [], [], [0]
         for k, s in enumerate(systems):
             pos, Z, c, sp, cell, pbc = _fields(s)
@@ -177,7 +198,7 @@ class TTAtomCalculator(_AseCalculator):
             if int(cnt[ptr_[k]:ptr_[k + 1]].sum()) == 0:
                 raise ValueError(f"system {k} has no edges within cutoff — too sparse for this model")
         E, F, _ = self._evaluate(pos, Z, None, None, chg, spn, sys_ptr=ptr_, forces=want_forces,
-                                 trace=trace)
+                                 trace=trace, graph=g)
         energies, forces_out = [], []
         for k in range(len(systems)):
             ek = self.scale_rmsd * float(E[k]) + self.scale_mean

@@ -5,7 +5,9 @@ the reference exports."""
 from __future__ import annotations
 
 import json
+import math
 import pathlib
+from collections import Counter
 
 import numpy as np
 import torch
@@ -59,7 +61,16 @@ class WeightBundle:
 
     @property
     def reference(self):
-        return None
+        """The system a merged bundle was made for and its energy / forces, from the bundle's
+        ``ref@`` entries (tt_atom/weights.py:45-59), or None when it carries none (random-init
+        bundles)."""
+        if not self.has("ref@energy"):
+            return None
+        arr = lambda k: np.array(self._d[k], copy=True) if self.has(k) else None  # noqa: E731
+        return dict(energy=float(self._d["ref@energy"][0]), forces=arr("ref@forces"),
+                    pos=arr("ref@pos"), atomic_numbers=arr("ref@atomic_numbers"),
+                    charge=float(self._d["ref@charge"][0]), spin=float(self._d["ref@spin"][0]),
+                    cell=arr("ref@cell"), pbc=arr("ref@pbc"))
 
     def tables(self):
         """The fixed geometry tables the engine needs (to_m, grid projections, Gaussian basis)."""
@@ -69,6 +80,16 @@ class WeightBundle:
 
     def save(self, path):
         np.savez(path, **{k: np.asarray(self._d[k]) for k in self.files})
+
+
+def reduced_composition(numbers):
+    """Sorted ((Z, count / gcd of all counts), ...): the composition key a merged bundle's expert
+    routing depends on, so H2O and H4O2 share it (tt_atom/bundle_cache.py:45-52)."""
+    counts = Counter(int(z) for z in numbers)
+    g = 0
+    for c in counts.values():
+        g = math.gcd(g, c)
+    return tuple(sorted((z, c // g) for z, c in counts.items()))
 
 
 def random_bundle(cfg_name="uma-s-1", seed=0):
