@@ -161,3 +161,30 @@ def test_direct_checkpoint_heads_vs_oracle():
     assert np.abs(calc.results["stress"] - ref_s).max() <= 1e-6
     # net force removed (before the per-component normaliser's mean is added back)
     assert np.abs((calc.results["forces"] - fm).sum(0)).max() <= 1e-3 * fs
+
+
+def test_calculator_dispatches_orb_bundles(tmp_path):
+    """tt_atom.Calculator picks the family from the bundle (tt_atom/auto.py:40-89): an Orb bundle
+    gives an OrbCalculator whose results equal a directly built one; `task` is UMA-only."""
+    import json
+
+    import tt_atom
+    from tt_atom.ase_compat import SimpleAtoms
+    cfg = configs.orb_config("orb-tiny")
+    w = configs.orb_random_weights(cfg, seed=0)
+    arrs = {"config": np.frombuffer(json.dumps(cfg).encode(), dtype=np.uint8)}
+    arrs.update({f"w@{k}": v.numpy() for k, v in w.items()})
+    path = tmp_path / "orb_tiny.npz"
+    np.savez(path, **arrs)
+    m = configs.tiny_molecule()
+    a = SimpleAtoms(m["Z"], m["pos"])
+    calc = tt_atom.Calculator(a, str(path))
+    assert isinstance(calc, OrbCalculator) and a.calc is calc
+    e = a.get_potential_energy()
+    ref = OrbCalculator(w, cfg)
+    b = SimpleAtoms(m["Z"], m["pos"])
+    b.calc = ref
+    assert e == b.get_potential_energy()
+    assert np.array_equal(a.get_forces(), b.get_forces())
+    with pytest.raises(ValueError, match="applies only to UMA"):
+        tt_atom.Calculator(None, str(path), task="omat")
