@@ -92,3 +92,23 @@ def test_multicardsim_relax_and_md_without_ase(tmp_path):
                                                                temp=300.0, seed=1)) as sim:
         out = sim.run([(m["pos"], m["Z"]) for m in mols])
     assert all(r["ok"] for r in out), [r.get("error") for r in out]
+
+
+def test_native_relax_and_md_with_the_orb_calculator():
+    """The GPU-resident loops also drive an OrbCalculator (its energy normaliser and ZBL term
+    applied on the device): FIRE lowers the energy and ends at what a fresh single point gives;
+    a few Langevin steps run."""
+    from tt_atom.orb import OrbCalculator
+    cfg = configs.orb_config("orb-tiny")
+    w = configs.orb_random_weights(cfg, seed=0)
+    m = configs.tiny_molecule(seed=0)
+    atoms = SimpleAtoms(m["Z"], m["pos"])
+    atoms.calc = OrbCalculator(w, cfg)
+    e0 = float(atoms.get_potential_energy())
+    res = relax_atoms(atoms, fmax=1e-3, steps=30, native=True)
+    assert res["nsteps"] > 0 and res["energy"] < e0
+    fresh = SimpleAtoms(atoms.get_atomic_numbers(), atoms.get_positions())
+    fresh.calc = OrbCalculator(w, cfg)
+    assert abs(float(fresh.get_potential_energy()) - res["energy"]) <= 1e-5 * max(1.0, abs(res["energy"]))
+    out = md_atoms(atoms, steps=5, dt=0.5, temp=300.0, seed=3, native=True)
+    assert out["nsteps"] == 5 and np.isfinite(out["energy"])

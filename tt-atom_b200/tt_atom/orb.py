@@ -494,6 +494,41 @@ class OrbCalculator(_AseCalculator):
         if V is not None:
             self.results["stress"] = voigt_6(V.numpy() / atoms_volume(atoms))
 
+    def _device_energy_forces(self, pos, Z, cell, pbc):
+        """Energy (float64 device scalar) and forces ([N, 3] float64 on the device) as
+        ``calculate`` reports them -- normaliser and ZBL term included -- for the GPU-resident
+        relaxation / MD loops; ``pos`` may be a device tensor. Direct checkpoints go through
+        their heads on the host and are copied back."""
+        n = len(Z)
+        if self.engine.direct:
+            E, F, _ = self._evaluate_direct(pos, Z, cell, pbc, False)
+            w = self._w
+            var = w.get("forces_head.normalizer.bn.running_var")
+            if var is not None:
+                mu = w.get("forces_head.normalizer.bn.running_mean")
+                F = F * float(var.double().sqrt()) + (float(mu) if mu is not None else 0.0)
+            if "energy_head.normalizer.bn.running_var" in w:
+                E = (E * float(w["energy_head.normalizer.bn.running_var"].double().sqrt())
+                     + float(w["energy_head.normalizer.bn.running_mean"])) * n
+                E += float(w["energy_head.reference.linear.weight"].double().reshape(-1)[Z].sum())
+            if self.zbl:
+                Ez, Fz, _ = self._zbl(self._ws, False, scale=1.0)
+                E, F = E + Ez, F + Fz
+            return (torch.tensor(E, dtype=torch.float64, device=self.device),
+                    F.to(self.device))
+        Ed, Fd, _ = self._evaluate(pos, Z, cell, pbc, True, False, device_out=True)
+        E, F = Ed[0].double(), Fd.double()
+        w = self._w
+        if "energy_head.normalizer.bn.running_var" in w:
+            sigma = float(w["energy_head.normalizer.bn.running_var"].double().sqrt())
+            E = (E * sigma + float(w["energy_head.normalizer.bn.running_mean"])) * n
+            E = E + float(w["energy_head.reference.linear.weight"].double().reshape(-1)[Z].sum())
+            F = F * (sigma * n)
+        if self.zbl:
+            zE, zF, _ = self._zbl_launch(self._ws, False)
+            E, F = E + zE[0], F + zF.double()
+        return E, F
+
     def _calculate_direct(self, atoms, pos, Z, cell, pbc, properties, want_stress):
         """Direct checkpoints (tt_atom/orb_calculator.py:137-186): energy through the energy
         head's normaliser, forces and stress from their heads through their own normalisers,

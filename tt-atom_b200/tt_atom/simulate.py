@@ -19,8 +19,8 @@ from .ase_compat import HAVE_ASE
 
 
 def _native_forces(atoms):
-    """(force_fn, pos) for the atoms' TTAtomCalculator: force_fn(pos) returns the model's
-    (normalised) energy and forces [N, 3] as device tensors."""
+    """(force_fn, pos) for the atoms' tt_atom calculator (UMA or Orb): force_fn(pos) returns
+    the energy and forces [N, 3] that ``calculate`` reports, as device tensors."""
     calc = atoms.calc
     if calc is None or not hasattr(calc, "_evaluate"):
         raise RuntimeError("the native loops need a tt_atom calculator attached to the atoms")
@@ -36,6 +36,15 @@ def _native_forces(atoms):
         cell_t = torch.tensor(cell, dtype=torch.float64, device=dev)
         inv = torch.linalg.inv(cell_t)
         wrap_mask = torch.tensor(pbc, device=dev)
+    if hasattr(calc, "_device_energy_forces"):          # Orb: its own normaliser and ZBL term
+        def orb_force_fn(p):
+            q = p
+            if periodic:
+                frac = p @ inv
+                frac = torch.where(wrap_mask, frac - torch.floor(frac), frac)
+                q = frac @ cell_t
+            return calc._device_energy_forces(q.float(), Z, cell, pbc if periodic else None)
+        return orb_force_fn, pos
     ref = 0.0
     if getattr(calc, "elem_refs", None) is not None:
         ref = float(calc.elem_refs[torch.as_tensor(Z)].sum())
