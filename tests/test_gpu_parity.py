@@ -255,3 +255,23 @@ def test_calculator_api_and_errors():
         calc_r.evaluate_batch([dict(pos=m["pos"], Z=m["Z"]), dict(pos=m["pos"][:23], Z=m["Z"][:23])])
     with pytest.raises(ValueError, match=r"\(charge, spin\)"):
         calc_r.evaluate_batch([dict(pos=m["pos"], Z=m["Z"], charge=1.0)])
+
+
+def test_calculator_by_name_loads_the_cached_bundle(tmp_path):
+    """`tt_atom.Calculator(atoms, "uma-s-1", ...)` finds the merged bundle of the atoms'
+    (reduced composition, charge, spin, task) in the cache layout and gives the same results as
+    a calculator built on that bundle directly."""
+    import tt_atom
+    from tt_atom import bundle_cache as BC
+    from tt_atom.ase_compat import SimpleAtoms
+    cfg = configs.model_config("tiny")
+    b = WeightBundle.from_arrays(configs.random_bundle_arrays(cfg, seed=0))
+    m = configs.tiny_molecule()
+    b.save(BC.bundle_path("uma-s-1", b.task, m["Z"], 0, 1, cache_dir=tmp_path))
+    a = SimpleAtoms(m["Z"], m["pos"])
+    calc = tt_atom.Calculator(a, "uma-s-1", task=b.task, cache_dir=tmp_path)
+    assert a.calc is calc and a.info["spin"] == 1
+    ref = SimpleAtoms(m["Z"], m["pos"], info=dict(charge=0, spin=1))
+    ref.calc = TTAtomCalculator(b)
+    assert a.get_potential_energy() == ref.get_potential_energy()
+    assert np.array_equal(a.get_forces(), ref.get_forces())

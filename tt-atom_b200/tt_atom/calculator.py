@@ -82,6 +82,32 @@ class TTAtomCalculator(_AseCalculator):
         self._step = None
 
     # ------------------------------------------------------------------------------ core
+    @classmethod
+    def from_uma(cls, model="uma-s-1", task_name="omol", atoms=None, charge=0, spin=1,
+                 refenv=None, checkpoint=None, cache_dir=None, device=None, device_id=0,
+                 fast=False, trace=False, **kwargs):
+        """A calculator for ``atoms`` from the cached merged bundle of its (reduced composition,
+        charge, spin, task) (tt_atom/calculator.py:68-114). Charge / spin already on the atoms
+        win over the arguments, and the resolved values are stamped back onto the atoms so that
+        ``calculate`` reads what the bundle was merged for. A cache miss raises: building the
+        bundle needs the reference environment, which this build does not include."""
+        from . import bundle_cache as BC
+        if atoms is None:
+            raise ValueError(
+                "from_uma needs `atoms` to determine the composition — MoLE bakes one bundle per "
+                "reduced composition/charge/spin/task, so there is no way to pick (or build) a "
+                "bundle without the structure. Pass the Atoms you want to run.")
+        charge = atoms.info.get("charge", charge)
+        spin = atoms.info.get("spin", spin)
+        atoms.info.setdefault("charge", charge)
+        atoms.info.setdefault("spin", spin)
+        path = BC.cached(BC.bundle_path(model, task_name, atoms.get_atomic_numbers(), charge,
+                                        spin, cache_dir=cache_dir, checkpoint=checkpoint),
+                         f"{model} bundle (task {task_name}, charge {int(charge)}, spin "
+                         f"{int(spin)})")
+        return cls(WeightBundle.load(path), task_name=task_name, device=device,
+                   device_id=device_id, fast=fast, trace=trace, **kwargs)
+
     def _graph(self, pos, Z, cell, pbc, sys_ptr=None):
         return build_graph(pos, Z, self.cfg["cutoff"], cell, pbc,
                            max_neighbors=self.max_neighbors, sys_ptr=sys_ptr, device=self.device)

@@ -395,6 +395,17 @@ class OrbCalculator(_AseCalculator):
         self._ws = None
         self._rcov = torch.tensor(COVALENT_RADII, dtype=torch.float64, device=self.device)
 
+    @classmethod
+    def from_checkpoint(cls, checkpoint="orb-v3-conservative-inf-omat", refenv=None,
+                        cache_dir=None, device=None, device_id=0, fast=False, **kwargs):
+        """A calculator for a released Orb-v3 checkpoint from its cached exported weights
+        (tt_atom/orb_calculator.py:75-87). A cache miss raises: exporting the weights needs the
+        reference environment, which this build does not include."""
+        from . import bundle_cache as BC
+        from .weights import WeightBundle
+        path = BC.cached(BC.orb_weights_path(checkpoint, cache_dir), f"{checkpoint} weights")
+        return cls(WeightBundle.load(path), device=device, device_id=device_id, **kwargs)
+
     def _zbl(self, ws, stress, scale=None):
         """ZBL energy (``scale`` times the pair sum: 1 / N, the per-node mean, by default),
         forces and virial on ``ws``'s graph (its edge vectors ``ws.ev`` are those of the last
