@@ -329,7 +329,7 @@ def run_ours(args):
         from tt_atom.orb import OrbCalculator
         cfg = configs.orb_config("orb-v3")
         s = configs.amorphous_sio2()
-        calc = OrbCalculator(configs.orb_random_weights(cfg, seed=0), cfg, device=device,
+        calc = OrbCalculator(configs.orb_random_weights(cfg, seed=0), cfg=cfg, device=device,
                              precision=args.precision)
         cfg = dict(cfg, max_neighbors=cfg["max_num_neighbors"])
         evaluate = lambda: calc._evaluate(s["pos"], s["Z"], s["cell"], [True] * 3, True, True)  # noqa: E731

@@ -46,7 +46,7 @@ def test_orb_edge_features_and_vjp_vs_reference(fx):
 def _run(shape, sysd, precision):
     cfg = configs.orb_config(shape)
     w = configs.orb_random_weights(cfg, seed=0)
-    calc = OrbCalculator(w, cfg, precision=precision)
+    calc = OrbCalculator(w, cfg=cfg, precision=precision)
     periodic = sysd["pbc"]
     E, F, V = calc._evaluate(sysd["pos"], sysd["Z"], sysd["cell"] if periodic else None,
                              [True] * 3 if periodic else None, True, periodic)
@@ -84,7 +84,7 @@ def test_orb_trace_replays_bit_exact_across_topology_changes():
     w = configs.orb_random_weights(cfg, seed=0)
     sysd = configs.amorphous_sio2(n_si=40, n_o=80, seed=3)
     rng = np.random.default_rng(1)
-    tr, ea = OrbCalculator(w, cfg, trace=True), OrbCalculator(w, cfg)
+    tr, ea = OrbCalculator(w, cfg=cfg, trace=True), OrbCalculator(w, cfg=cfg)
     step = None
     for k in range(3):
         p = sysd["pos"] + (rng.normal(0.0, 0.1, sysd["pos"].shape) if k else 0.0)
@@ -113,7 +113,7 @@ def test_zbl_pair_repulsion_vs_oracle():
     pos, cell = 0.85 * s["pos"], 0.85 * s["cell"]
     res = {}
     for zbl in (False, True):
-        calc = OrbCalculator(w, cfg, zbl=zbl, max_num_neighbors=None)
+        calc = OrbCalculator(w, cfg=cfg, zbl=zbl, max_num_neighbors=None)
         a = SimpleAtoms(s["Z"], pos, cell, True)
         calc.calculate(a, ("energy", "forces", "stress"))
         res[zbl] = (calc.results["energy"], calc.results["forces"], calc.results["stress"], calc)
@@ -142,7 +142,7 @@ def test_direct_checkpoint_heads_vs_oracle():
     cfg = configs.orb_config("orb-tiny")
     w = configs.orb_random_weights(cfg, seed=1, direct=True)
     s = configs.amorphous_sio2(n_si=20, n_o=40, seed=4)
-    calc = OrbCalculator(w, cfg, zbl=False, max_num_neighbors=None)
+    calc = OrbCalculator(w, cfg=cfg, zbl=False, max_num_neighbors=None)
     assert calc.engine.direct and calc.engine.has_stress_head
     a = SimpleAtoms(s["Z"], s["pos"], s["cell"], True)
     calc.calculate(a, ("energy", "forces", "stress"))
@@ -181,7 +181,7 @@ def test_calculator_dispatches_orb_bundles(tmp_path):
     calc = tt_atom.Calculator(a, str(path))
     assert isinstance(calc, OrbCalculator) and a.calc is calc
     e = a.get_potential_energy()
-    ref = OrbCalculator(w, cfg)
+    ref = OrbCalculator(w, cfg=cfg)
     b = SimpleAtoms(m["Z"], m["pos"])
     b.calc = ref
     assert e == b.get_potential_energy()

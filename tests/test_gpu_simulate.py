@@ -103,12 +103,12 @@ def test_native_relax_and_md_with_the_orb_calculator():
     w = configs.orb_random_weights(cfg, seed=0)
     m = configs.tiny_molecule(seed=0)
     atoms = SimpleAtoms(m["Z"], m["pos"])
-    atoms.calc = OrbCalculator(w, cfg)
+    atoms.calc = OrbCalculator(w, cfg=cfg)
     e0 = float(atoms.get_potential_energy())
     res = relax_atoms(atoms, fmax=1e-3, steps=30, native=True)
     assert res["nsteps"] > 0 and res["energy"] < e0
     fresh = SimpleAtoms(atoms.get_atomic_numbers(), atoms.get_positions())
-    fresh.calc = OrbCalculator(w, cfg)
+    fresh.calc = OrbCalculator(w, cfg=cfg)
     assert abs(float(fresh.get_potential_energy()) - res["energy"]) <= 1e-5 * max(1.0, abs(res["energy"]))
     out = md_atoms(atoms, steps=5, dt=0.5, temp=300.0, seed=3, native=True)
     assert out["nsteps"] == 5 and np.isfinite(out["energy"])

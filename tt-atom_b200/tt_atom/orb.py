@@ -373,8 +373,14 @@ class OrbCalculator(_AseCalculator):
 
     implemented_properties = ["energy", "free_energy", "energies", "forces", "stress"]
 
-    def __init__(self, weights, cfg=None, device=None, device_id=0, precision="3xtf32",
-                 max_num_neighbors="config", zbl=True, trace=False, **kwargs):
+    def __init__(self, weights, device=None, device_id=0, fast=False, bucketing=False, *,
+                 cfg=None, precision="3xtf32", max_num_neighbors="config", zbl=True,
+                 trace=False, **kwargs):
+        """The reference's signature (tt_atom/orb_calculator.py:26): ``weights`` a bundle (or its
+        path) or, with ``cfg``, a weight dict. ``fast`` and ``bucketing`` are accepted for
+        compatibility: they select device compile and padding policies of the reference that have
+        no counterpart here (edge counts need no padding to shape buckets on this GPU, and
+        results are the same)."""
         super().__init__(**kwargs)
         self.zbl = zbl
         # trace: the model pass is captured as a CUDA graph and replayed (also after the edge
