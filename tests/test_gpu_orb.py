@@ -188,3 +188,21 @@ def test_calculator_dispatches_orb_bundles(tmp_path):
     assert np.array_equal(a.get_forces(), b.get_forces())
     with pytest.raises(ValueError, match="applies only to UMA"):
         tt_atom.Calculator(None, str(path), task="omat")
+
+
+def test_orb_evaluate_batch_matches_single_systems():
+    """evaluate_batch (the reference's Orb batch API): per-system energies and forces equal what
+    calculate gives for each system alone; mixed sizes allowed."""
+    from tt_atom.ase_compat import SimpleAtoms
+    cfg = configs.orb_config("orb-tiny")
+    w = configs.orb_random_weights(cfg, seed=0)
+    sysl = configs.screening_set(count=3, seed=11)
+    calc = OrbCalculator(w, cfg=cfg, max_num_neighbors=None)
+    out = calc.evaluate_batch(sysl)
+    assert out["energy"].shape == (3,) and len(out["forces"]) == 3
+    for k, s in enumerate(sysl):
+        a = SimpleAtoms(s["Z"], s["pos"])
+        a.calc = OrbCalculator(w, cfg=cfg, max_num_neighbors=None)
+        assert out["energy"][k] == a.get_potential_energy()
+        assert np.array_equal(out["forces"][k], a.get_forces())
+    assert calc.evaluate_batch(sysl, properties=("energy",))["forces"] is None

@@ -546,6 +546,29 @@ class OrbCalculator(_AseCalculator):
             E, F = E + zE[0], F + zF.double()
         return E, F
 
+    def evaluate_batch(self, systems, properties=("energy", "forces")):
+        """Energies (and forces) of several systems (tt_atom/orb_calculator.py:217-327): the same
+        result dict, ``energy`` [K] and ``forces`` (list of [N_k, 3]) or None. Orb bakes no
+        per-composition routing, so compositions, charges and spins may mix. Evaluated one system
+        per device pass through ``calculate`` (same normaliser and ZBL term), not as one
+        disjoint-union pass."""
+        from .calculator import _fields
+        from .ase_compat import SimpleAtoms
+        if len(systems) == 0:
+            raise ValueError("empty batch")
+        want_forces = "forces" in properties
+        props = ("energy", "forces") if want_forces else ("energy",)
+        energies, forces = [], []
+        for s in systems:
+            pos, Z, charge, spin, cell, pbc = _fields(s)
+            a = SimpleAtoms(Z, pos, cell, pbc if pbc is not None else False,
+                            info=dict(charge=charge, spin=spin))
+            self.calculate(a, props)
+            energies.append(float(self.results["energy"]))
+            if want_forces:
+                forces.append(np.asarray(self.results["forces"], dtype=np.float64).copy())
+        return dict(energy=np.array(energies), forces=forces if want_forces else None)
+
     def _calculate_direct(self, atoms, pos, Z, cell, pbc, properties, want_stress):
         """Direct checkpoints (tt_atom/orb_calculator.py:137-186): energy through the energy
         head's normaliser, forces and stress from their heads through their own normalisers,
