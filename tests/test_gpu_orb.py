@@ -206,3 +206,6 @@ def test_orb_evaluate_batch_matches_single_systems():
         assert out["energy"][k] == a.get_potential_energy()
         assert np.array_equal(out["forces"][k], a.get_forces())
     assert calc.evaluate_batch(sysl, properties=("energy",))["forces"] is None
+    calc.close()
+    assert calc._ws is None
+    assert calc.evaluate_batch(sysl[:1])["energy"][0] == out["energy"][0]     # usable again

@@ -546,6 +546,11 @@ class OrbCalculator(_AseCalculator):
             E, F = E + zE[0], F + zF.double()
         return E, F
 
+    def close(self):
+        """Release the device workspace and any captured step (tt_atom/ase_base.py:33)."""
+        self._ws = None
+        self._step = self._step_key = None
+
     def evaluate_batch(self, systems, properties=("energy", "forces")):
         """Energies (and forces) of several systems (tt_atom/orb_calculator.py:217-327): the same
         result dict, ``energy`` [K] and ``forces`` (list of [N_k, 3]) or None. Orb bakes no
