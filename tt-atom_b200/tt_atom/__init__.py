@@ -1,9 +1,14 @@
-"""tt_atom (B200 build): the eSCN-MD (UMA) energy + force + stress path on sm_100a.
+"""tt_atom (B200 build): the eSCN-MD (UMA) and Orb-v3 energy + force + stress path on sm_100a.
 
 Drop-in surface of the reference package for this path:
-  Calculator, TTAtomCalculator   ASE calculators (tt_atom/auto.py:40, tt_atom/calculator.py:23)
+  Calculator                     family dispatch by bundle or model name (tt_atom/auto.py:40)
+  TTAtomCalculator               UMA ASE calculator, evaluate_batch, from_uma (calculator.py:23)
+  orb.OrbCalculator              Orb ASE calculator, evaluate_batch, from_checkpoint
+                                 (tt_atom/orb_calculator.py:26)
   MultiCard, MultiCardSim        one process per GPU (tt_atom/batch.py:218,338)
+  simulate.relax_atoms, md_atoms FIRE / Langevin, GPU-resident without ASE (simulate.py:15-74)
   radius_graph                   device neighbour list (tt_atom/geometry.py:48)
+  bundle_cache                   the reference's bundle cache layout (bundle_cache.py)
 """
 from .calculator import TTAtomCalculator
 from .weights import WeightBundle
