@@ -112,3 +112,34 @@ def test_native_relax_and_md_with_the_orb_calculator():
     assert abs(float(fresh.get_potential_energy()) - res["energy"]) <= 1e-5 * max(1.0, abs(res["energy"]))
     out = md_atoms(atoms, steps=5, dt=0.5, temp=300.0, seed=3, native=True)
     assert out["nsteps"] == 5 and np.isfinite(out["energy"])
+
+
+def test_multicard_energies_for_uma_and_orb_bundles(tmp_path):
+    """MultiCard (tt_atom/batch.py:218-243) detects the family from the bundle: its energies
+    equal a calculator's on the same structures, for a UMA bundle and for an Orb bundle (Orb
+    energy with its normaliser and ZBL term)."""
+    import json
+
+    from tt_atom import MultiCard
+    from tt_atom.orb import OrbCalculator
+    mols = [configs.tiny_molecule(seed=k) for k in range(3)]
+    systems = [(m["pos"], m["Z"]) for m in mols]
+    cfg, b = _tiny()
+    upath = str(tmp_path / "uma_tiny.npz")
+    np.savez(upath, **configs.random_bundle_arrays(cfg, seed=0))
+    ocfg = configs.orb_config("orb-tiny")
+    ow = configs.orb_random_weights(ocfg, seed=0)
+    arrs = {"config": np.frombuffer(json.dumps(ocfg).encode(), dtype=np.uint8)}
+    arrs.update({f"w@{k}": v.numpy() for k, v in ow.items()})
+    opath = str(tmp_path / "orb_tiny.npz")
+    np.savez(opath, **arrs)
+    for path, make in ((upath, lambda: TTAtomCalculator(b)),
+                       (opath, lambda: OrbCalculator(ow, cfg=ocfg))):
+        with MultiCard(path, device_ids=(0,)) as pool:
+            en, edges = pool.energies(systems)
+        assert edges > 0
+        calc = make()
+        for e, m in zip(en, mols):
+            a = SimpleAtoms(m["Z"], m["pos"])
+            a.calc = calc
+            assert abs(e - float(a.get_potential_energy())) <= 1e-6 * max(1.0, abs(e)), path

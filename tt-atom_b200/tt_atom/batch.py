@@ -50,10 +50,20 @@ class _WorkerPool:
 
 
 def _energy_worker(device_id, weights_path, in_q, out_q):
+    # the family comes from the bundle's config (tt_atom/batch.py:218-230): UMA bundles give the
+    # eSCN-MD energy, Orb bundles the Orb energy with its normaliser and ZBL term
     try:
         _pin_worker(device_id)
         from .calculator import TTAtomCalculator
-        calc = TTAtomCalculator(weights_path, device_id=0)
+        from .weights import WeightBundle
+        bundle = WeightBundle.load(weights_path)
+        if "latent_dim" in bundle.config:
+            from .ase_compat import SimpleAtoms
+            from .orb import OrbCalculator
+            orb = OrbCalculator(bundle, device_id=0)
+        else:
+            orb = None
+            calc = TTAtomCalculator(bundle, device_id=0)
     except Exception as e:  # noqa: BLE001
         out_q.put(("error", f"{type(e).__name__}: {e}"))
         return
@@ -64,6 +74,11 @@ def _energy_worker(device_id, weights_path, in_q, out_q):
             break
         idx, pos, Z = job
         try:
+            if orb is not None:
+                a = SimpleAtoms(Z, pos)
+                orb.calculate(a, ("energy",))
+                out_q.put((idx, float(orb.results["energy"]), orb._ws.graph.E))
+                continue
             E, _, _ = calc._evaluate(pos, Z, None, None, [0.0], [0.0], forces=False)
             g = calc._ws.graph
             out_q.put((idx, calc.scale_rmsd * float(E[0]) + calc.scale_mean, g.E))
