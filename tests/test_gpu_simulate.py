@@ -143,3 +143,23 @@ def test_multicard_energies_for_uma_and_orb_bundles(tmp_path):
             a = SimpleAtoms(m["Z"], m["pos"])
             a.calc = calc
             assert abs(e - float(a.get_potential_energy())) <= 1e-6 * max(1.0, abs(e)), path
+
+
+def test_multicardsim_by_model_name_uses_the_bundle_cache(tmp_path):
+    """MultiCardSim("uma-s-1", ...) picks each structure's merged bundle from the cache by
+    (reduced composition, charge, spin), as the reference's workers do; energies equal a
+    calculator on that bundle."""
+    from tt_atom import MultiCardSim
+    from tt_atom import bundle_cache as BC
+    cfg, b = _tiny()
+    mols = [configs.tiny_molecule(seed=k) for k in range(2)]
+    b.save(BC.bundle_path("uma-s-1", b.task, mols[0]["Z"], 0, 0, cache_dir=tmp_path))
+    with MultiCardSim("uma-s-1", device_ids=(0,), task=b.task, cache_dir=str(tmp_path),
+                      sim_params=dict(mode="energy")) as sim:
+        out = sim.run([dict(pos=m["pos"], Z=m["Z"], charge=0, spin=0) for m in mols])
+    assert all(r["ok"] for r in out), [r.get("error") for r in out]
+    calc = TTAtomCalculator(b)
+    for r, m in zip(out, mols):
+        a = SimpleAtoms(m["Z"], m["pos"], info=dict(charge=0, spin=0))
+        a.calc = calc
+        assert abs(r["energy"] - float(a.get_potential_energy())) <= 1e-6 * max(1.0, abs(r["energy"]))

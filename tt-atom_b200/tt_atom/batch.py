@@ -103,7 +103,7 @@ class MultiCard(_WorkerPool):
         return out, total
 
 
-def _sim_worker(device_id, model, task, trace, sim_params, in_q, out_q):
+def _sim_worker(device_id, model, task, trace, sim_params, cache_dir, in_q, out_q):
     try:
         _pin_worker(device_id)
         from . import Calculator
@@ -112,7 +112,13 @@ def _sim_worker(device_id, model, task, trace, sim_params, in_q, out_q):
         out_q.put(("error", f"{type(e).__name__}: {e}"))
         return
     mode = sim_params["mode"]
-    calc = None
+    # one calculator per bundle: a bundle path or an Orb checkpoint serves every structure; a
+    # UMA model name needs the merged bundle of each (reduced composition, charge, spin)
+    # (tt_atom/batch.py:262-295)
+    import os
+    from .weights import reduced_composition
+    per_system = not os.path.exists(str(model)) and str(model).lower().startswith("uma")
+    calcs = {}
     out_q.put(("ready", device_id))
     while True:
         job = in_q.get()
@@ -122,8 +128,6 @@ def _sim_worker(device_id, model, task, trace, sim_params, in_q, out_q):
         try:
             if d.get("fail"):
                 raise RuntimeError(d["fail"])
-            if calc is None:
-                calc = Calculator(None, model, task=task, device_id=0, trace=trace)
             if HAVE_ASE:
                 from ase import Atoms
                 atoms = Atoms(numbers=d["Z"], positions=d["pos"], cell=d.get("cell"),
@@ -131,7 +135,12 @@ def _sim_worker(device_id, model, task, trace, sim_params, in_q, out_q):
             else:
                 atoms = SimpleAtoms(d["Z"], d["pos"], d.get("cell"), d.get("pbc", False))
             atoms.info.update(charge=d.get("charge", 0.0), spin=d.get("spin", 0.0))
-            atoms.calc = calc
+            key = ((reduced_composition(np.asarray(d["Z"]).tolist()), atoms.info["charge"],
+                    atoms.info["spin"]) if per_system else "all")
+            if key not in calcs:
+                calcs[key] = Calculator(atoms if per_system else None, model, task=task,
+                                        device_id=0, trace=trace, cache_dir=cache_dir)
+            atoms.calc = calcs[key]
             if mode == "energy":
                 res = dict(energy=float(atoms.get_potential_energy()),
                            forces=np.asarray(atoms.get_forces(), dtype=np.float64),
@@ -164,7 +173,8 @@ class MultiCardSim(_WorkerPool):
         if sim_params is None or sim_params.get("mode") not in ("relax", "md", "energy"):
             raise ValueError("sim_params must be a dict with mode 'relax', 'md', or 'energy'")
         self.sim_params = sim_params
-        super().__init__(_sim_worker, [(d, model, task, trace, sim_params) for d in device_ids])
+        super().__init__(_sim_worker,
+                         [(d, model, task, trace, sim_params, cache_dir) for d in device_ids])
 
     def run(self, systems):
         for i, s in enumerate(systems):
