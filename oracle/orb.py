@@ -12,6 +12,9 @@ restates, in fp32 torch on the CPU, the reference's Orb port:
 * interaction     -- tt_atom/orb_model.py:225-266 (sigmoid attention x cutoff, gathered edge
                      input, two segment sums, node MLP, residuals)
 * energy head     -- tt_atom/orb_model.py:307-338 (node mean -> Linear-SiLU-Linear)
+* conditioning    -- tt_atom/orb_model.py:32-57, 219-237 (OrbMol checkpoints: a closed-form
+                     sin / cos embedding of the system's charge and spin, projected per layer
+                     and added to the nodes at the layer's start)
 * forces / stress -- autograd of the raw (normalised-space) energy w.r.t. positions and a
                      symmetric strain leaf on the edge vectors (tt_atom/orb_geometry.py:83-88)
 
@@ -81,8 +84,22 @@ def mlp_norm(x, w, p):
     return h * inv * w[f"{p}.layer_norm.weight"]
 
 
-def interaction(nodes, edges, w, p, senders, receivers, cut):
+def charge_spin_embedding(w, charge, spin):
+    """[1, latent] embedding of a system's total charge and spin: [sin, cos] of value * W * 2 pi
+    for each, a zero spin giving zeros (tt_atom/orb_model.py:32-57)."""
+    def emb(v, W, is_spin):
+        x = float(v) * W * 2.0 * math.pi
+        e = torch.cat([torch.sin(x), torch.cos(x)])
+        return torch.zeros_like(e) if is_spin and v == 0 else e
+    return torch.cat([emb(charge, w["conditioner.charge_embedding.W"], False),
+                      emb(spin, w["conditioner.spin_embedding.W"], True)])[None]
+
+
+def interaction(nodes, edges, w, p, senders, receivers, cut, cond=None):
     N = nodes.shape[0]
+    if cond is not None and f"{p}._cond_node_proj.weight" in w:
+        nodes = nodes + F.linear(cond, w[f"{p}._cond_node_proj.weight"],
+                                 w[f"{p}._cond_node_proj.bias"])
     ra = torch.sigmoid(F.linear(edges, w[f"{p}._receive_attn.weight"],
                                 w[f"{p}._receive_attn.bias"])) * cut[:, None]
     sa = torch.sigmoid(F.linear(edges, w[f"{p}._send_attn.weight"],
@@ -95,7 +112,8 @@ def interaction(nodes, edges, w, p, senders, receivers, cut):
     return nodes + un, edges + ue
 
 
-def energy_forces(w, cfg, pos, Z, edge_index, shift=None, compute_stress=False):
+def energy_forces(w, cfg, pos, Z, edge_index, shift=None, compute_stress=False, charge=0.0,
+                  spin=0.0):
     """Raw (normalised-space) energy, forces = -dE/dpos and virial dE/dstrain. ``edge_index``
     is the UMA-convention graph [src, tgt]; Orb uses senders = tgt, receivers = src."""
     src, tgt = edge_index[0], edge_index[1]
@@ -111,8 +129,11 @@ def energy_forces(w, cfg, pos, Z, edge_index, shift=None, compute_stress=False):
     feat, cut = edge_features(vec, cfg["cutoff"], cfg["num_bases"])
     nodes = mlp_norm(w["atom_emb.embeddings.weight"][Z], w, "_encoder._node_fn")
     edges = mlp_norm(feat, w, "_encoder._edge_fn")
+    cond = (charge_spin_embedding(w, charge, spin)
+            if "conditioner.charge_embedding.W" in w else None)
     for i in range(cfg["num_message_passing_steps"]):
-        nodes, edges = interaction(nodes, edges, w, f"gnn_stacks.{i}", senders, receivers, cut)
+        nodes, edges = interaction(nodes, edges, w, f"gnn_stacks.{i}", senders, receivers, cut,
+                                   cond)
     mean = nodes.mean(0, keepdim=True)
     h = F.silu(F.linear(mean, w["energy_head.mlp.NN-0.weight"], w["energy_head.mlp.NN-0.bias"]))
     E = F.linear(h, w["energy_head.mlp.NN-1.weight"], w["energy_head.mlp.NN-1.bias"]).reshape(())
@@ -152,7 +173,7 @@ def zbl_energy_forces_virial(Z, src, tgt, pos, shift, rcov, node_aggregation="me
     return float(E.detach()), -gp, gs
 
 
-def direct_predict(w, cfg, pos, Z, edge_index, shift=None):
+def direct_predict(w, cfg, pos, Z, edge_index, shift=None, charge=0.0, spin=0.0):
     """Direct checkpoints: raw energy, raw per-atom forces with the net force removed and raw
     Voigt-6 stress from the final node features (tt_atom/orb_model.py:307-436: EnergyHead,
     ForceHead, StressHead), one forward pass without autograd."""
@@ -165,9 +186,11 @@ def direct_predict(w, cfg, pos, Z, edge_index, shift=None):
         feat, cut = edge_features(vec, cfg["cutoff"], cfg["num_bases"])
         nodes = mlp_norm(w["atom_emb.embeddings.weight"][Z], w, "_encoder._node_fn")
         edges = mlp_norm(feat, w, "_encoder._edge_fn")
+        cond = (charge_spin_embedding(w, charge, spin)
+                if "conditioner.charge_embedding.W" in w else None)
         for i in range(cfg["num_message_passing_steps"]):
             nodes, edges = interaction(nodes, edges, w, f"gnn_stacks.{i}", senders, receivers,
-                                       cut)
+                                       cut, cond)
         mean = nodes.mean(0, keepdim=True)
 
         def head(x, p):

@@ -209,3 +209,27 @@ def test_orb_evaluate_batch_matches_single_systems():
     calc.close()
     assert calc._ws is None
     assert calc.evaluate_batch(sysl[:1])["energy"][0] == out["energy"][0]     # usable again
+
+
+def test_orbmol_charge_spin_conditioning_vs_oracle():
+    """OrbMol checkpoints (tt_atom/orb_model.py:32-57, 219-237): each layer adds the projected
+    charge / spin embedding to its input nodes. Energy and forces match the oracle restatement
+    for a charged, spin-polarised system and for charge 0 / spin 0 (whose spin embedding is
+    zero), and the conditioning changes the energy."""
+    cfg = configs.orb_config("orb-tiny")
+    w = configs.orb_random_weights(cfg, seed=0, cond=True)
+    m = configs.tiny_molecule()
+    calc = OrbCalculator(w, cfg=cfg)
+    assert calc.engine.has_cond
+    pos = torch.from_numpy(m["pos"])
+    ei, _ = O.neighbor_list(pos, cfg["cutoff"], None, None, cfg["max_num_neighbors"])
+    energies = []
+    for charge, spin in ((1.0, 2.0), (0.0, 0.0)):
+        E, F, _ = calc._evaluate(m["pos"], m["Z"], None, None, True, False, charge=charge,
+                                 spin=spin)
+        r = OB.energy_forces(w, cfg, pos, torch.from_numpy(m["Z"]), ei, None, False,
+                             charge=charge, spin=spin)
+        assert abs(E - float(r["energy"])) <= E_REL * max(abs(float(r["energy"])), 1.0)
+        assert (F.float() - r["forces"]).abs().max() <= F_ABS
+        energies.append(E)
+    assert energies[0] != energies[1]

@@ -254,10 +254,12 @@ def orb_config(name):
     return cfg
 
 
-def orb_random_weights(cfg, seed=0, direct=False):
+def orb_random_weights(cfg, seed=0, direct=False, cond=False):
     """Random-init Orb weights with the reference's key names (gns.MoleculeGNS naming as read by
     tt_atom/orb_model.py:127-338 in the reference); ``direct`` adds the force and stress heads
-    and their normalisers of direct checkpoints (tt_atom/orb_model.py:358-457)."""
+    and their normalisers of direct checkpoints (tt_atom/orb_model.py:358-457); ``cond`` the
+    charge / spin conditioning of OrbMol checkpoints (embedding frequencies and per-layer node
+    projections, tt_atom/orb_model.py:32-57, 219-237)."""
     g = torch.Generator().manual_seed(seed)
     C, Hd, L = cfg["latent_dim"], cfg["hidden_dim"], cfg["num_message_passing_steps"]
     w = {}
@@ -282,6 +284,11 @@ def orb_random_weights(cfg, seed=0, direct=False):
         mlpnorm(f"{p}._node_mlp", 3 * C)
         lin(f"{p}._receive_attn", 1, C)
         lin(f"{p}._send_attn", 1, C)
+        if cond:
+            lin(f"{p}._cond_node_proj", C, C)
+    if cond:
+        w["conditioner.charge_embedding.W"] = torch.randn(C // 4, generator=g)
+        w["conditioner.spin_embedding.W"] = torch.randn(C // 4, generator=g)
     lin("energy_head.mlp.NN-0", cfg["head_hidden"], C)
     lin("energy_head.mlp.NN-1", 1, cfg["head_hidden"])
     if direct:

@@ -58,6 +58,16 @@ class OrbEngine:
 
         self.emb = d(w["atom_emb.embeddings.weight"])
         self.zero_row = torch.zeros(1, self.D0, device=self.device)
+        # OrbMol checkpoints condition on the system's charge and spin: a fixed embedding,
+        # projected per layer and added to the nodes at the layer's start
+        # (tt_atom/orb_model.py:32-57, 219-237); the host keeps the small weights
+        self.has_cond = "conditioner.charge_embedding.W" in w
+        if self.has_cond:
+            self.cond_w = (w["conditioner.charge_embedding.W"].double(),
+                           w["conditioner.spin_embedding.W"].double())
+            self.cond_proj = [(w[f"gnn_stacks.{i}._cond_node_proj.weight"].double(),
+                               w[f"gnn_stacks.{i}._cond_node_proj.bias"].double())
+                              for i in range(self.NL)]
         self.enc_n = mlpnorm("_encoder._node_fn")
         self.enc_e = mlpnorm("_encoder._edge_fn")
         self.layers = []
@@ -114,6 +124,22 @@ class OrbEngine:
 
     def workspace(self, graph):
         return OrbWorkspace(self, graph)
+
+    def set_condition(self, ws, charge=0.0, spin=0.0):
+        """Per-layer conditioning rows of a system's total charge and spin into ``ws.cond``
+        (outside any captured step, which reads them from there): [sin, cos] of value * W *
+        2 pi for each, a zero spin giving zeros, projected by each layer's node projection."""
+        if not self.has_cond:
+            return
+        import math
+
+        def emb(v, W, is_spin):
+            x = float(v) * W * 2.0 * math.pi
+            e = torch.cat([torch.sin(x), torch.cos(x)])
+            return torch.zeros_like(e) if is_spin and v == 0 else e
+        c = torch.cat([emb(charge, self.cond_w[0], False), emb(spin, self.cond_w[1], True)])
+        rows = torch.stack([W @ c + b for W, b in self.cond_proj]).float()
+        ws.cond.copy_(rows)
 
     # ---------------------------------------------------------------------------- forward
     def _mlpnorm_fwd(self, m, X, ldx, M, a0, a1, h2, tmp0, tmp1, s, first=None):
@@ -179,6 +205,8 @@ class OrbEngine:
              ptr(ws.edges[0]), C, None, 0, None, 0, s)
         for i, lay in enumerate(self.layers):
             nodes, edges = ws.node_in[i], ws.edges[i]
+            if self.has_cond:           # the layer's input nodes += its conditioning row
+                call("atom_row_broadcast", ptr(ws.cond[i]), N, C, 1.0, ptr(nodes), C3, 1, s)
             call("atom_orb_attention", ptr(edges), E, C, ptr(lay["wr"]), lay["br"],
                  ptr(lay["ws"]), lay["bs"], ptr(ws.cut), ptr(ws.lin[i]), ptr(ws.att[i]), s)
             em, nm = lay["em"], lay["nm"]
@@ -298,6 +326,7 @@ class OrbWorkspace:
         self.gemm_scratch = f(8 * ((N + 127) // 128) * 128 * max(2 * Hd, 3 * C))
         self.feat, self.cut, self.ev = f(E, 16 * eng.nb), f(E), f(E, 3)
         self.x0 = f(N, eng.D0)
+        self.cond = torch.zeros(eng.NL, eng.C, device=dev)      # conditioning rows per layer
         self._eng = eng
         self.rebind(graph)
         # per layer (+1 slot at the end for the encoder)
@@ -437,10 +466,10 @@ class OrbCalculator(_AseCalculator):
              ptr(ws.zbl_V) if stress else None, ptr(ws.vscratch), s)
         return ws.zbl_E, ws.zbl_F, (ws.zbl_V if stress else None)
 
-    def _evaluate_direct(self, pos, Z, cell, pbc, stress=False):
+    def _evaluate_direct(self, pos, Z, cell, pbc, stress=False, charge=0.0, spin=0.0):
         """Direct checkpoints: raw energy, raw per-atom forces [N, 3] (net force removed) and
         raw Voigt-6 stress (or None) from one forward pass and the heads."""
-        self._evaluate(pos, Z, cell, pbc, forces=False, stress=False)
+        self._evaluate(pos, Z, cell, pbc, forces=False, stress=False, charge=charge, spin=spin)
         ws = self._ws
         self.engine.direct_heads(ws, stress=stress)
         E = float(ws.energy.double().cpu()[0])
@@ -448,7 +477,8 @@ class OrbCalculator(_AseCalculator):
         S = ws.sraw[0, :6].double().cpu() if stress else None
         return E, F, S
 
-    def _evaluate(self, pos, Z, cell, pbc, forces=True, stress=False, device_out=False):
+    def _evaluate(self, pos, Z, cell, pbc, forces=True, stress=False, device_out=False,
+                  charge=0.0, spin=0.0):
         g = build_graph(pos, Z, self.cfg["cutoff"], cell, pbc, max_neighbors=self.max_nbrs,
                         device=self.device)
         if g.E == 0:
@@ -460,6 +490,7 @@ class OrbCalculator(_AseCalculator):
             self._ws.rebind(g)                  # same sizes: reuse the buffers
         ws = self._ws
         ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))
+        self.engine.set_condition(ws, charge, spin)       # OrbMol checkpoints only
         key = (g.N, g.E, bool(forces), bool(stress))
         if self.trace:
             if self._step is None or self._step_key != key:
@@ -480,11 +511,14 @@ class OrbCalculator(_AseCalculator):
         pbc = np.asarray(atoms.get_pbc())
         cell = np.asarray(atoms.get_cell(), np.float32) if pbc.any() else None
         want_stress = cell is not None and ("stress" in properties or bool(pbc.all()))
+        charge = float(atoms.info.get("charge", 0.0))
+        spin = float(atoms.info.get("spin", 0.0))
         if self.engine.direct:
-            return self._calculate_direct(atoms, pos, Z, cell, pbc, properties, want_stress)
+            return self._calculate_direct(atoms, pos, Z, cell, pbc, properties, want_stress,
+                                          charge, spin)
         # model pass and ZBL term on the device, then one read-back of all their results
         Ed, Fd, Vd = self._evaluate(pos, Z, cell, pbc if pbc.any() else None, True, want_stress,
-                                    device_out=True)
+                                    device_out=True, charge=charge, spin=spin)
         zb = self._zbl_launch(self._ws, want_stress) if self.zbl else (None, None, None)
         E, F, V, Ez, Fz, Vz = to_host(Ed, Fd, Vd, *zb)
         E = float(E[0])
@@ -511,14 +545,14 @@ class OrbCalculator(_AseCalculator):
         if V is not None:
             self.results["stress"] = voigt_6(V.numpy() / atoms_volume(atoms))
 
-    def _device_energy_forces(self, pos, Z, cell, pbc):
+    def _device_energy_forces(self, pos, Z, cell, pbc, charge=0.0, spin=0.0):
         """Energy (float64 device scalar) and forces ([N, 3] float64 on the device) as
         ``calculate`` reports them -- normaliser and ZBL term included -- for the GPU-resident
         relaxation / MD loops; ``pos`` may be a device tensor. Direct checkpoints go through
         their heads on the host and are copied back."""
         n = len(Z)
         if self.engine.direct:
-            E, F, _ = self._evaluate_direct(pos, Z, cell, pbc, False)
+            E, F, _ = self._evaluate_direct(pos, Z, cell, pbc, False, charge, spin)
             w = self._w
             var = w.get("forces_head.normalizer.bn.running_var")
             if var is not None:
@@ -533,7 +567,8 @@ class OrbCalculator(_AseCalculator):
                 E, F = E + Ez, F + Fz
             return (torch.tensor(E, dtype=torch.float64, device=self.device),
                     F.to(self.device))
-        Ed, Fd, _ = self._evaluate(pos, Z, cell, pbc, True, False, device_out=True)
+        Ed, Fd, _ = self._evaluate(pos, Z, cell, pbc, True, False, device_out=True, charge=charge,
+                                   spin=spin)
         E, F = Ed[0].double(), Fd.double()
         w = self._w
         if "energy_head.normalizer.bn.running_var" in w:
@@ -574,7 +609,8 @@ class OrbCalculator(_AseCalculator):
                 forces.append(np.asarray(self.results["forces"], dtype=np.float64).copy())
         return dict(energy=np.array(energies), forces=forces if want_forces else None)
 
-    def _calculate_direct(self, atoms, pos, Z, cell, pbc, properties, want_stress):
+    def _calculate_direct(self, atoms, pos, Z, cell, pbc, properties, want_stress, charge=0.0,
+                          spin=0.0):
         """Direct checkpoints (tt_atom/orb_calculator.py:137-186): energy through the energy
         head's normaliser, forces and stress from their heads through their own normalisers,
         each plus the ZBL term summed over atoms."""
@@ -582,7 +618,8 @@ class OrbCalculator(_AseCalculator):
             raise ValueError("stress requested but this direct checkpoint carries no "
                              "stress_head weights.")
         want_stress = want_stress and self.engine.has_stress_head
-        E, F, S = self._evaluate_direct(pos, Z, cell, pbc if pbc.any() else None, want_stress)
+        E, F, S = self._evaluate_direct(pos, Z, cell, pbc if pbc.any() else None, want_stress,
+                                        charge, spin)
         n = len(Z)
         w = self._w
 

@@ -43,7 +43,8 @@ def _native_forces(atoms):
                 frac = p @ inv
                 frac = torch.where(wrap_mask, frac - torch.floor(frac), frac)
                 q = frac @ cell_t
-            return calc._device_energy_forces(q.float(), Z, cell, pbc if periodic else None)
+            return calc._device_energy_forces(q.float(), Z, cell, pbc if periodic else None,
+                                              charge, spin)
         return orb_force_fn, pos
     ref = 0.0
     if getattr(calc, "elem_refs", None) is not None:
