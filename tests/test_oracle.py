@@ -151,3 +151,22 @@ def test_covalent_radii_table_matches_ase_when_available():
     assert len(COVALENT_RADII) == 119 and COVALENT_RADII[14] == 1.11 and COVALENT_RADII[8] == 0.66
     ase_data = pytest.importorskip("ase.data")
     assert np.allclose(np.asarray(ase_data.covalent_radii), np.asarray(COVALENT_RADII))
+
+
+def test_orb_charge_spin_embedding_restatement():
+    """The OrbMol conditioning embedding of the oracle (tt_atom/orb_model.py:32-57): latent
+    width, [sin, cos] halves per quantity, a zero spin giving zeros, charge-dependent."""
+    import torch
+
+    from oracle import orb as OB
+    from tt_atom import configs
+    cfg = configs.orb_config("orb-tiny")
+    w = configs.orb_random_weights(cfg, seed=0, cond=True)
+    C = cfg["latent_dim"]
+    e = OB.charge_spin_embedding(w, 1.0, 0.0)
+    assert e.shape == (1, C)
+    assert torch.all(e[0, C // 2:] == 0)                        # spin 0 -> zero spin half
+    x = w["conditioner.charge_embedding.W"] * 2 * torch.pi
+    assert torch.allclose(e[0, :C // 4], torch.sin(x)) and torch.allclose(e[0, C // 4:C // 2], torch.cos(x))
+    assert not torch.equal(OB.charge_spin_embedding(w, -1.0, 2.0)[0, :C // 2], e[0, :C // 2])
+    assert torch.any(OB.charge_spin_embedding(w, 0.0, 2.0)[0, C // 2:] != 0)
