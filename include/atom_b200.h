@@ -118,7 +118,8 @@ int atom_neighbor_list(const float* pos, int64_t N, const int64_t* sys_ptr_host,
 int atom_exclusive_scan(const int* cnt, int64_t n, int* ptr, int* total_host, void* stream);
 
 /* Sender CSR: send_ptr[N+1] and send_eid[E] (edge ids grouped by source, ascending), from
- * edge_src[E]. scratch: N int32. */
+ * edge_src[E]. scratch: N int32. Every edge_src value must lie in [0, N) (not checked on the
+ * device); E above INT_MAX returns ATOM_ERR_CAPACITY (edge ids are int32). */
 int atom_sender_csr(const int* edge_src, int64_t E, int64_t N, int* scratch, int* send_ptr,
                     int* send_eid, void* stream);
 
@@ -131,7 +132,9 @@ int atom_sender_csr(const int* edge_src, int64_t E, int64_t N, int* scratch, int
  * on a device looks up the array's device address (cudaGetSymbolAddress) with that device
  * current, so make that first call before any stream capture. Calls share the array: calls
  * that overlap on the GPU (other streams, other host threads) race and must be serialised by
- * the caller. Allocates nothing (no cudaMalloc / cudaFree). Output equals atom_sender_csr's. */
+ * the caller. Allocates nothing (no cudaMalloc / cudaFree). Output equals atom_sender_csr's.
+ * As there, every edge_src value must lie in [0, N) -- an id outside it would count into the
+ * shared array past node N -- and E above INT_MAX returns ATOM_ERR_CAPACITY. */
 #define ATOM_NOALLOC_MAX_NODES (1 << 20)
 int atom_sender_csr_noalloc(const int* edge_src, int64_t E, int64_t N, int* send_ptr,
                             int* send_eid, void* stream);
@@ -218,6 +221,14 @@ int atom_gemm_ex(const float* A, int64_t lda, int64_t M, const atom_gemm_groups*
 /* Reads and clears the device-side error code of the tensor-core kernels (0 = none; a bounded
  * wait expired otherwise). Synchronises `stream`. */
 int atom_device_error(int* code_host, void* stream);
+
+/* Test hook for the bounded waits: one thread runs the tensor-core kernels' own bounded
+ * mbarrier wait on a barrier that nothing arrives on, for budget_cycles SM clocks (1 ..
+ * 2e9), then gives up and records ATOM_WAIT_SELFTEST_CODE in the device-side error code,
+ * exactly as an expired wait inside a GEMM does; atom_device_error then reports it. No
+ * counterpart in the reference (its device waits are not bounded). */
+#define ATOM_WAIT_SELFTEST_CODE 7
+int atom_wait_selftest(int64_t budget_cycles, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Edge-side fused ops of the edgewise block (tt_atom/edgewise.py:39-87, forces.py:352-418).

@@ -9,7 +9,6 @@ array's leftover contents from the first call do not leak into the second.
 
 The file name sorts last so that a run stopping at the first failure has run every other test.
 """
-import ctypes
 
 import pytest
 import torch
@@ -52,6 +51,38 @@ def test_noalloc_sender_csr_matches_allocating_entry_point_twice():
         torch.cuda.synchronize()
         assert torch.equal(p_new, p_ref)
         assert torch.equal(e_new, e_ref)
+
+
+def _free_bytes():
+    return torch.cuda.mem_get_info()[0]      # cudaMemGetInfo: device-wide free bytes
+
+
+def test_noalloc_sender_csr_allocates_nothing():
+    """The point of the entry point: a call after the first on this device changes the
+    device's free memory by not a byte (the first call only looks up the static array)."""
+    src = _edges(13, 3000, 60000)
+    p, e = _noalloc(src, 3000)          # warm-up: the one-time set-up
+    torch.cuda.synchronize()
+    before = _free_bytes()
+    call("atom_sender_csr_noalloc", ptr(src), src.numel(), 3000, ptr(p), ptr(e), L.stream_ptr())
+    torch.cuda.synchronize()
+    assert _free_bytes() == before
+
+
+def test_noalloc_sender_csr_empty_inputs():
+    # E = 0: every node's range is empty, send_ptr all zeros
+    N = 257
+    src = torch.zeros(1, dtype=torch.int32, device="cuda")
+    send_ptr = torch.full((N + 1,), -7, dtype=torch.int32, device="cuda")
+    send_eid = torch.full((1,), -7, dtype=torch.int32, device="cuda")
+    call("atom_sender_csr_noalloc", ptr(src), 0, N, ptr(send_ptr), ptr(send_eid), L.stream_ptr())
+    torch.cuda.synchronize()
+    assert int(send_ptr.abs().sum()) == 0
+    assert int(send_eid[0]) == -7
+    # N = 0: nothing to do, nothing written
+    call("atom_sender_csr_noalloc", ptr(src), 0, 0, ptr(send_ptr), ptr(send_eid), L.stream_ptr())
+    torch.cuda.synchronize()
+    assert int(send_ptr.abs().sum()) == 0
 
 
 def test_noalloc_sender_csr_rejects_oversize():

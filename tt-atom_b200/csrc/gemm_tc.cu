@@ -115,10 +115,11 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
 }
 // Bounded wait; false (and an error code) when the clock budget expires or another CTA of
 // the grid has already failed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int code,
+                                          long long budget = kWaitCycles) {
     const long long t0 = clock64();
     while (!mbar_try(b, parity)) {
-        if (clock64() - t0 > kWaitCycles) {
+        if (clock64() - t0 > budget) {
             atomicCAS(&g_tc_error, 0, code);
             return false;
         }
@@ -1060,6 +1061,32 @@ int gemm_tc(const float* A, long long lda, long long M, const atom_gemm_groups* 
 }
 
 }  // namespace atom
+
+namespace atom {
+namespace tc {
+// One thread waits, with the GEMM's own bounded wait, on an mbarrier that nothing arrives on:
+// the wait gives up after `budget` clocks and records `code` in g_tc_error, exactly as an
+// expired wait inside the GEMM does.
+__global__ void wait_selftest_kernel(long long budget, int code) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_wait(&bar, 0u, code, budget);
+}
+}  // namespace tc
+}  // namespace atom
+
+extern "C" int atom_wait_selftest(int64_t budget_cycles, void* stream) {
+    if (budget_cycles <= 0 || budget_cycles > atom::tc::kWaitCycles) {
+        atom::set_error("atom_wait_selftest: budget_cycles must be in [1, %lld]",
+                        atom::tc::kWaitCycles);
+        return ATOM_ERR_ARG;
+    }
+    atom::tc::wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(budget_cycles,
+                                                                        ATOM_WAIT_SELFTEST_CODE);
+    return atom::check_launch("atom_wait_selftest");
+}
 
 extern "C" int atom_device_error(int* code_host, void* stream) {
     int h = 0;

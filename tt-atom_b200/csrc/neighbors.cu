@@ -16,6 +16,7 @@
 // Optional cap (not in the reference): keep per receiver the max_nbrs candidates with the
 // smallest distance measure (aperiodic: distance, periodic: squared distance), ties broken by
 // candidate order; survivors keep candidate order.
+#include <climits>
 #include "common.cuh"
 
 namespace atom {
@@ -325,6 +326,11 @@ extern "C" int atom_exclusive_scan(const int* cnt, int64_t n, int* ptr, int* tot
 extern "C" int atom_sender_csr(const int* edge_src, int64_t E, int64_t N, int* scratch,
                                int* send_ptr, int* send_eid, void* stream) {
     cudaStream_t st = (cudaStream_t)stream;
+    ATOM_REQUIRE(N >= 0 && E >= 0, "sender_csr: negative size");
+    if (E > INT_MAX) {
+        set_error("sender_csr: E = %lld exceeds the int32 edge ids of the CSR", (long long)E);
+        return ATOM_ERR_CAPACITY;
+    }
     if (N == 0) return ATOM_OK;
     zero_int_kernel<<<ceil_div(N, 256), 256, 0, st>>>(scratch, N);
     if (E > 0) count_src_kernel<<<ceil_div(E, 256), 256, 0, st>>>(edge_src, E, scratch);
@@ -385,6 +391,11 @@ static int noalloc_scratch(int** out) {
 extern "C" int atom_sender_csr_noalloc(const int* edge_src, int64_t E, int64_t N, int* send_ptr,
                                        int* send_eid, void* stream) {
     ATOM_REQUIRE(N >= 0 && E >= 0, "sender_csr_noalloc: negative size");
+    if (E > INT_MAX) {
+        set_error("sender_csr_noalloc: E = %lld exceeds the int32 edge ids of the CSR",
+                  (long long)E);
+        return ATOM_ERR_CAPACITY;
+    }
     if (N > ATOM_NOALLOC_MAX_NODES) {
         set_error("sender_csr_noalloc: N = %lld exceeds the built-in scratch of %d nodes; use "
                   "atom_sender_csr with caller-provided scratch", (long long)N,

@@ -60,6 +60,7 @@ _SIGS = {
                      c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int,
                      c_int, c_void_p, c_int64, c_void_p),
     "atom_device_error": (c_void_p, c_void_p),
+    "atom_wait_selftest": (c_int64, c_void_p),
     "atom_rotate_in": (c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_int64,
                        c_int, c_void_p, c_void_p, c_void_p),
     "atom_gate_fwd": (c_void_p, c_int64, c_int, c_void_p, c_void_p),
@@ -155,6 +156,18 @@ def call(name, *args):
     if rc != 0:
         raise AtomError(name, rc)
     return rc
+
+
+def check_device(stream=None):
+    """Reads (and clears) the device-side error code of the tensor-core kernels and raises
+    RuntimeError if a bounded wait expired since the last check: the results of every launch
+    since then are incomplete and must not be returned. Synchronises the stream."""
+    code = ctypes.c_int(0)
+    call("atom_device_error", ctypes.byref(code), stream_ptr(stream))
+    if code.value != 0:
+        raise RuntimeError(
+            f"a bounded device-side wait in the tensor-core GEMM expired (code {code.value}); "
+            "the results of this evaluation are incomplete and were discarded")
 
 
 def ptr(t):

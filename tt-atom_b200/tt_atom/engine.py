@@ -49,6 +49,9 @@ def to_host(*ts):
     live = [t for t in ts if t is not None]
     if not live:
         return [None] * len(ts)
+    if any(t.is_cuda for t in live):
+        # a GEMM whose bounded wait expired leaves its outputs incomplete: refuse them
+        L.check_device()
     flat = torch.cat([t.reshape(-1).to(torch.float64) for t in live]).cpu()
     out, o = [], 0
     for t in ts:

@@ -14,6 +14,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
+from . import _lib as _L
 from . import dynamics as D
 from .ase_compat import HAVE_ASE
 
@@ -81,6 +82,7 @@ def relax_atoms(atoms, *, fmax=0.05, steps=200, logfile=None, native=None):
         def log(n, E, F):
             print(f"  FIRE {n:4d}  E={float(E):.6f}  fmax={float(F.norm(dim=1).max()):.4f}")
     res = D.fire(force_fn, pos, fmax=fmax, steps=steps, callback=log)
+    _L.check_device()
     atoms.set_positions(pos.cpu().numpy())
     F = res["forces"].cpu().numpy()
     return dict(energy=res["energy"], forces=F, fmax=res["fmax"], nsteps=res["nsteps"],
@@ -123,6 +125,7 @@ def md_atoms(atoms, *, steps=100, dt=1.0, temp=300.0, logfile=None, seed=None, n
                 print(f"  step {n:4d}  E={float(E):.5f}  T={D.temperature(v, m):.1f} K")
     res = D.langevin(force_fn, pos, m, steps, dt_fs=dt, temp=temp, friction_fs=friction,
                      generator=gen, callback=log)
+    _L.check_device()
     atoms.set_positions(pos.cpu().numpy())
     return dict(energy=res["energy"], forces=res["forces"].cpu().numpy(), nsteps=steps,
                 temp=float(temp), dt=float(dt))
