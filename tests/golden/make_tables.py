@@ -8,9 +8,11 @@ random-init bundles used for synthetic benchmarks take them from this file.
 
 The values are read out of the reference's committed golden fixture
 (tests/data/golden_tiny.npz, produced by fairchem's eSCNMDBackbone), so that this framework uses
-exactly the tables the reference's parity tests were generated with. Usage:
+exactly the tables the reference's parity tests were generated with. The table ships inside
+the package (tt-atom_b200/tt_atom/data/lmax2_tables.npz); this generator is test
+infrastructure and lives beside the other fixture generators. Usage:
 
-    python make_tables.py <reference_root>
+    python tests/golden/make_tables.py <reference_root>
 """
 import pathlib
 import sys
@@ -23,7 +25,8 @@ def main(ref_root):
     out = {f"Jd_{l}": z[f"w@Jd_{l}"].astype(np.float32) for l in range(3)}
     for k in ("to_m", "to_grid_mat", "from_grid_mat"):
         out[k] = z[f"host@{k}"].astype(np.float32)
-    dst = pathlib.Path(__file__).with_name("lmax2_tables.npz")
+    dst = (pathlib.Path(__file__).resolve().parents[2] / "tt-atom_b200" / "tt_atom" / "data"
+           / "lmax2_tables.npz")
     np.savez(dst, **out)
     print("wrote", dst, {k: v.shape for k, v in out.items()})
 

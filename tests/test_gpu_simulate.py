@@ -163,3 +163,29 @@ def test_multicardsim_by_model_name_uses_the_bundle_cache(tmp_path):
         a = SimpleAtoms(m["Z"], m["pos"], info=dict(charge=0, spin=0))
         a.calc = calc
         assert abs(r["energy"] - float(a.get_potential_energy())) <= 1e-6 * max(1.0, abs(r["energy"]))
+
+
+def test_multicardsim_poisoned_structure_fails_alone(tmp_path):
+    """One structure with no edges within the cutoff (two atoms 20 A apart) comes back as
+    {ok: False, error, tb} with the calculator's error; the others return the energies a
+    calculator gives (tt_atom/batch.py:318-325)."""
+    from tt_atom import MultiCardSim
+    cfg, b = _tiny()
+    path = str(tmp_path / "tiny.npz")
+    np.savez(path, **configs.random_bundle_arrays(cfg, seed=0))
+    mols = [configs.tiny_molecule(seed=k) for k in range(3)]
+    lonely = dict(pos=np.array([[0.0, 0.0, 0.0], [20.0, 0.0, 0.0]], np.float32),
+                  Z=np.array([6, 8], np.int64))
+    systems = [dict(pos=mols[0]["pos"], Z=mols[0]["Z"]), lonely,
+               dict(pos=mols[1]["pos"], Z=mols[1]["Z"]), dict(pos=mols[2]["pos"], Z=mols[2]["Z"])]
+    with MultiCardSim(path, device_ids=(0,), sim_params=dict(mode="energy")) as sim:
+        out = sim.run(systems)
+    assert out[1]["ok"] is False
+    assert out[1]["error"].startswith("ValueError: no edges within cutoff")
+    assert "Traceback" in out[1]["tb"]
+    calc = TTAtomCalculator(b)
+    for r, m in zip([out[0], out[2], out[3]], mols):
+        assert r["ok"], r.get("error")
+        a = SimpleAtoms(m["Z"], m["pos"])
+        a.calc = calc
+        assert abs(r["energy"] - float(a.get_potential_energy())) <= 1e-6 * max(1.0, abs(r["energy"]))
