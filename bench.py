@@ -14,8 +14,13 @@ cutoff 6 A, at most 30 neighbours), random-init fp32 weights (seed 0).
 * Multi-GPU (torchrun, N ranks): each rank runs its own replica structure (independent
   systems, no collective on the data path); value = all ranks' atoms x steps / max-over-ranks
   time ("scaling": "weak").
+* The same launch also measures, at the same N, the two partitioned configurations and adds
+  them as keys of the line: ``screen`` (config 4: 512 molecules dealt over the ranks, no
+  collectives, through ``evaluate_batch``) and ``slab`` (config 5: the 65,536-atom bcc Fe cell
+  slab-decomposed over the ranks, NCCL halo exchange per layer and an all-reduce of energy and
+  virial, with the collectives' CUDA-event time per step and the limiting one named).
 * ``--impl reference``: the reference's CPU path (this repo's CPU restatement of it, the oracle)
-  on the box's host cores, on a bounded sample of the workload.
+  on the box's host cores, on the same full workload, median of the timed steps.
 """
 from __future__ import annotations
 
@@ -177,27 +182,56 @@ def make_workload(device, cells=(10, 10, 5), precision="3xtf32"):
     return cfg, bundle, s, calc
 
 
-def run_slab(args):
+def init_dist():
+    """(world size, rank, local rank, device): one process per GPU, NCCL when N > 1."""
+    ws_n, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws_n > 1:
+        import torch.distributed as dist
+        if not dist.is_initialized():
+            dist.init_process_group("nccl", device_id=device)
+    return ws_n, rank, local, device
+
+
+def _max_over_ranks(values, device, ws_n):
+    t = torch.tensor(values, device=device, dtype=torch.float64)
+    if ws_n > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def _barrier(ws_n):
+    torch.cuda.synchronize()
+    if ws_n > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def measure_slab(args, steps, warmup):
     """Config 5: one 65,536-atom cell split into slabs over the ranks, halo exchange per layer
-    (NCCL point-to-point), energy and virial all-reduced; value = atoms x steps / max time."""
+    (NCCL point-to-point), energy and virial all-reduced; value = atoms x steps / max time.
+    The halo exchanges and the all-reduce are timed with CUDA events on the compute stream
+    (each exchange's span includes waiting for the slowest peer). Returns rank 0's dict."""
     import torch.distributed as dist
     from tt_atom import configs
     from tt_atom.engine import UMAEngine
     from tt_atom.graph import build_graph, csd_embedding
     from tt_atom.slab import DistExchange, local_graph, plans_for, run_partition, slab_order
     from tt_atom.weights import WeightBundle
-    ws_n, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if ws_n > 1:
-        dist.init_process_group("nccl", device_id=device)
+    ws_n, rank, local, device = init_dist()
     cfg = configs.model_config("uma-s-1")
     b = WeightBundle.from_arrays(configs.random_bundle_arrays(cfg, seed=0))
     s = configs.bcc_iron()
     perm, ranges = slab_order(s["pos"], s["cell"], ws_n)
     pos = torch.from_numpy(s["pos"][perm]).to(device)
+    torch.cuda.synchronize()
+    t_nl = time.perf_counter()
     g = build_graph(pos, s["Z"][perm], cfg["cutoff"], s["cell"], [True] * 3,
                     max_neighbors=cfg["max_neighbors"], device=device)
+    torch.cuda.synchronize()
+    t_nl = time.perf_counter() - t_nl
     plan = plans_for(g, ranges)[rank]
     lg = local_graph(g, plan)
     E_total = g.E
@@ -209,118 +243,129 @@ def run_slab(args):
     chunk = args.chunk_edges if args.chunk_edges > 0 else (262144 if ws_n == 1 else None)
     ws = eng.workspace(lg, se, chunk_edges=chunk)
     ws.pos.copy_(pos[plan.global_ids.to(device)])
-    exch = DistExchange(plan)
+    exch = DistExchange(plan, timed=True)
     red = torch.zeros(10, device=device, dtype=torch.float64)
+    ar_events = []
 
-    def step():
+    def step(timed=False):
         run_partition(eng, ws, exch, forces=True, virial=True)
         red[0] = ws.energy[0]
         red[1:] = ws.virial.reshape(-1)
         if ws_n > 1:
+            if timed:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
             dist.all_reduce(red)
-    for _ in range(args.warmup):
+            if timed:
+                e1.record()
+                ar_events.append((e0, e1))
+    for _ in range(warmup):
         step()
-    torch.cuda.synchronize()
-    if ws_n > 1:
-        dist.barrier()
+    _barrier(ws_n)
+    exch.reset_timing()
     clk = ClockSampler(local)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
-    for _ in range(args.steps):
-        step()
+    for _ in range(steps):
+        step(timed=True)
     t1.record()
     torch.cuda.synchronize()
-    ms = torch.tensor([t0.elapsed_time(t1)], device=device)
     clocks = clk.stop()
-    if ws_n > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms)
-    if rank == 0:
-        N = len(s["Z"])
-        hbm, bf16, src = peaks()
-        out = {"metric": METRIC, "value": N * args.steps / (ms / 1e3), "unit": "atom-steps/s",
-               "n_gpus": ws_n, "steps": args.steps, "warmup": args.warmup,
-               "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-               "vs_baseline": None, "dtype": "fp32",
-               "data": "synthetic (seeded bcc Fe, random-init weights)",
-               "config": {"workload": WORKLOADS["fe65k"], "atoms": N, "edges": E_total,
-                          "edges_rank0": lg.E, "halo_rank0": plan.n_halo,
-                          "precision": args.precision, "parallelism": f"slab x{ws_n}",
-                          "chunk_edges": chunk,
-                          "chunks": len(ws.chunks) if ws.chunks else None,
-                          "workspace_GB_rank0": round(ws.nbytes() / 1e9, 1)},
-               "energy": float(red[0]), "clocks": clocks}
-        print(json.dumps(out))
-    if ws_n > 1:
-        dist.destroy_process_group()
+    ms = t0.elapsed_time(t1)
+    halo = exch.timing_ms()
+    ar_ms = sum(a.elapsed_time(b_) for a, b_ in ar_events)
+    ms, halo_fwd, halo_rev, ar_ms = _max_over_ranks(
+        [ms, halo["forward"], halo["reverse"], ar_ms], device, ws_n)
+    N = len(s["Z"])
+    per = lambda v: v / steps  # noqa: E731
+    out = {"metric": METRIC, "value": N * steps / (ms / 1e3), "unit": "atom-steps/s",
+           "n_gpus": ws_n, "steps": steps, "warmup": warmup, "ms_per_step": ms / steps,
+           "scaling": "strong", "dtype": "fp32",
+           "data": "synthetic (seeded bcc Fe, random-init weights)",
+           "config": {"workload": WORKLOADS["fe65k"], "atoms": N, "edges": E_total,
+                      "edges_rank0": lg.E, "halo_rank0": plan.n_halo,
+                      "precision": args.precision, "parallelism": f"slab x{ws_n}",
+                      "chunk_edges": chunk, "chunks": len(ws.chunks) if ws.chunks else None,
+                      "workspace_GB_rank0": round(ws.nbytes() / 1e9, 1)},
+           "energy": float(red[0]), "clocks": clocks,
+           # CUDA-event spans on the compute stream per step, max over ranks; a halo span
+           # includes waiting for the slowest peer to reach the exchange
+           "collectives_ms_per_step": {
+               "halo_forward": per(halo_fwd), "halo_reverse": per(halo_rev),
+               "energy_virial_allreduce": per(ar_ms),
+               "exchanges_per_step": exch.count_per_step(steps),
+               "halo_bytes_per_layer_rank0": plan.n_halo * 9 * cfg["sphere_channels"] * 4},
+           "neighbor_list_s": round(t_nl, 3)}
+    lim = max(("halo_forward", per(halo_fwd)), ("halo_reverse", per(halo_rev)),
+              ("energy_virial_allreduce", per(ar_ms)), key=lambda kv: kv[1])
+    out["collectives_ms_per_step"]["limiting"] = lim[0] if ws_n > 1 else None
+    del ws, eng, lg, plan
+    torch.cuda.empty_cache()
+    return out
 
 
-def run_screen(args):
+def measure_screen(args, steps, warmup):
     """Config 4: 512 independent molecules split over the ranks (no collective on the data
-    path); each rank evaluates its share as disjoint-union batches. A step is one pass over all
-    512 molecules; value = total atoms / max-over-ranks step time."""
-    import torch.distributed as dist
+    path); each rank evaluates its share as disjoint-union batches through the public
+    ``evaluate_batch``. A step is one pass over all 512 molecules; value = total atoms / max
+    over ranks of the step time. Returns rank 0's dict."""
     from tt_atom import configs
     from tt_atom.calculator import TTAtomCalculator
     from tt_atom.weights import WeightBundle
-    ws_n, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if ws_n > 1:
-        dist.init_process_group("nccl", device_id=device)
+    ws_n, rank, local, device = init_dist()
     cfg = configs.model_config("uma-s-1")
     calc = TTAtomCalculator(WeightBundle.from_arrays(configs.random_bundle_arrays(cfg, seed=0)),
                             device=device, precision=args.precision)
     mols = configs.screening_set()
-    mine = mols[rank::ws_n]
+    # partition: molecules sorted by size and dealt round-robin, so ranks get equal work
+    order = sorted(range(len(mols)), key=lambda i: -len(mols[i]["Z"]))
+    mine = [mols[i] for i in order[rank::ws_n]]
     bs = 64
     batches = [mine[i:i + bs] for i in range(0, len(mine), bs)]
 
     def step():
         for bt in batches:
             calc.evaluate_batch(bt)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
-    torch.cuda.synchronize()
-    if ws_n > 1:
-        dist.barrier()
+    _barrier(ws_n)
     clk = ClockSampler(local)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     t1.record()
     torch.cuda.synchronize()
     clocks = clk.stop()
-    ms = torch.tensor([t0.elapsed_time(t1)], device=device)
-    if ws_n > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms)
+    (ms,) = _max_over_ranks([t0.elapsed_time(t1)], device, ws_n)
+    N = sum(len(m["Z"]) for m in mols)
+    out = {"metric": "atom-steps/s (E+F)", "value": N * steps / (ms / 1e3),
+           "unit": "atom-steps/s", "n_gpus": ws_n, "steps": steps, "warmup": warmup,
+           "ms_per_step": ms / steps, "scaling": "strong", "dtype": "fp32",
+           "data": "synthetic (seeded molecules, random-init weights)",
+           "config": {"workload": WORKLOADS["screen"], "molecules": len(mols), "atoms": N,
+                      "batch": bs, "precision": args.precision,
+                      "parallelism": f"partition x{ws_n}, no collectives",
+                      "timing": "end to end through evaluate_batch (host inputs, GPU "
+                                "neighbour lists, host results)"},
+           "clocks": clocks}
+    del calc
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_standalone(args, measure):
+    out = measure(args, args.steps, args.warmup)
+    ws_n, rank, _ = dist_env()
     if rank == 0:
-        N = sum(len(m["Z"]) for m in mols)
-        print(json.dumps({
-            "metric": "atom-steps/s (E+F)", "value": N * args.steps / (ms / 1e3),
-            "unit": "atom-steps/s", "n_gpus": ws_n, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic (seeded molecules, random-init weights)",
-            "config": {"workload": WORKLOADS["screen"], "molecules": len(mols), "atoms": N,
-                       "batch": bs, "precision": args.precision,
-                       "parallelism": f"partition x{ws_n}, no collectives",
-                       "timing": "end to end through evaluate_batch (host inputs, GPU "
-                                 "neighbour lists, host results)"},
-            "clocks": clocks}))
+        out.update(higher_is_better=True, vs_baseline=None)
+        print(json.dumps(out))
     if ws_n > 1:
-        dist.destroy_process_group()
+        torch.distributed.destroy_process_group()
 
 
 def run_ours(args):
-    ws_n, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if ws_n > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=device)
+    ws_n, rank, local, device = init_dist()
     from tt_atom.ase_compat import SimpleAtoms
     from tt_atom.engine import CapturedStep
     cells = tuple(int(v) for v in args.cells.split(","))
@@ -339,11 +384,16 @@ def run_ours(args):
                                           forces=True, stress=True)
     N = len(s["Z"])
     cell, pbc = s["cell"], [True] * 3
-    # ---- device step on a fixed topology (CUDA graph)
+    # positions re-jittered every step (0.01 A, seeded): each step evaluates new coordinates
+    rng = np.random.default_rng(1234)
+    jit = [(s["pos"] + rng.normal(0.0, 0.01, s["pos"].shape)).astype(np.float32)
+           for _ in range(max(args.steps, 1))]
+    # ---- device step on a fixed topology (CUDA graph), positions resident in HBM
     evaluate()
     ws = calc._ws
     eng = calc.engine
     step = CapturedStep(eng, ws, forces=True, virial=True)
+    pos_dev = torch.from_numpy(np.stack(jit)).to(device)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -353,7 +403,8 @@ def run_ours(args):
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
-    for _ in range(args.steps):
+    for k in range(args.steps):
+        ws.pos.copy_(pos_dev[k])
         step()
     t1.record()
     torch.cuda.synchronize()
@@ -372,9 +423,11 @@ def run_ours(args):
         calc.calculate(atoms, ("energy", "forces", "stress"))
     torch.cuda.synchronize()
     e2e_steps = max(3, min(args.steps, 20))
+    jit_atoms = [SimpleAtoms(s["Z"], jit[k % len(jit)], cell, True) for k in range(e2e_steps)]
     te = time.perf_counter()
-    for _ in range(e2e_steps):
-        calc.calculate(atoms, ("energy", "forces", "stress"))
+    for a in jit_atoms:
+        # host positions in; the neighbour list is rebuilt and compared on every call
+        calc.calculate(a, ("energy", "forces", "stress"))
     te = time.perf_counter() - te
     e2e_ms = 1e3 * te / e2e_steps
     ms_t = torch.tensor([ms, e2e_ms], device=device)
@@ -382,10 +435,6 @@ def run_ours(args):
         import torch.distributed as dist
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms, e2e_ms = ms_t.tolist()
-    if rank != 0:
-        if ws_n > 1:
-            torch.distributed.destroy_process_group()
-        return
     eng_precision = {0: "fp32", 1: "tf32", 2: "3xtf32", 3: "3xf16"}[eng.precision]
     ms_step = ms / args.steps
     value = N * ws_n * args.steps / (ms / 1e3)
@@ -400,10 +449,9 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": DATA[args.workload],
-        "config": {"workload": WORKLOADS[args.workload], "atoms_per_gpu": N, "edges_per_gpu": ws.graph.E,
-                   "cutoff": cfg["cutoff"], "max_neighbors": cfg["max_neighbors"],
-                   "precision": eng_precision, "parallelism": f"replicas x{ws_n}",
-                   "l2": "per-step working set %.1f GB > 126 MB L2" % (ws.nbytes() / 1e9)},
+        "config": workload_config(args.workload, N, ws.graph.E, cfg, ws_n),
+        "precision": eng_precision,
+        "workspace_GB": round(ws.nbytes() / 1e9, 2),
         "e2e": {"value": N * ws_n / (e2e_ms / 1e3), "unit": "atom-steps/s",
                 "h2d_bytes_per_step": N * 3 * 4 + N * 8,
                 "d2h_bytes_per_step": 8 + N * 3 * 8 + 9 * 8},
@@ -428,30 +476,52 @@ def run_ours(args):
                                 "launch_ms": edge["ms"], "bytes_per_launch": edge["bytes"]}
     if cells != (10, 10, 5):
         out["config"]["workload"] += f" (reduced: {cells} cells, not the headline size)"
-    if not args.no_cpu:
-        out["cpu_baseline"] = cpu_baseline(bounded=True, workload=args.workload)
-    print(json.dumps(out))
+    out["config"]["positions"] = "re-jittered every step (0.01 A)"
+    del step, ws, calc, eng, pos_dev
+    torch.cuda.empty_cache()
+    if args.workload == "uma" and not args.no_partitioned:
+        # the partitioned configurations at this N, from the same launch: config 4 (screening,
+        # no collectives) and config 5 (65,536-atom slab, halo exchange + all-reduce)
+        out["screen"] = measure_screen(args, steps=5, warmup=2)
+        out["slab"] = measure_slab(args, steps=3, warmup=2)
+    if rank == 0:
+        if not args.no_cpu:
+            cpu = cpu_baseline(bounded=True, workload=args.workload)
+            cpu.pop("cfg")
+            out["cpu_baseline"] = cpu
+        print(json.dumps(out))
     if ws_n > 1:
         torch.distributed.destroy_process_group()
 
 
+def workload_config(workload, atoms, edges, cfg, ws_n):
+    """The ``config`` object of both arms (this build's and the reference's): the same keys
+    and values for the same workload, so the two lines describe one configuration."""
+    return {"workload": WORKLOADS[workload], "atoms_per_gpu": atoms, "edges_per_gpu": edges,
+            "cutoff": cfg["cutoff"], "max_neighbors": cfg["max_neighbors"],
+            "parallelism": f"replicas x{ws_n}",
+            "l2": "inputs larger than L2: the per-step working set (GBs) exceeds the 126 MB "
+                  "L2, no flush"}
+
+
 def _cpu_sample_orb():
-    """Bounded CPU sample for the Orb workload: the same model, 300-atom SiO2 at 2.2 g/cm^3."""
+    """The CPU baseline's Orb workload: config 3 itself (1,002-atom SiO2 at 2.2 g/cm^3)."""
     from tt_atom import configs
     cfg = configs.orb_config("orb-v3")
-    return cfg, configs.orb_random_weights(cfg, seed=0), configs.amorphous_sio2(100, 200, seed=2)
+    return cfg, configs.orb_random_weights(cfg, seed=0), configs.amorphous_sio2()
 
 
 def _cpu_sample():
-    """The bounded CPU sample: the same model and alloy, 4x4x4 fcc cells (256 atoms)."""
+    """The CPU baseline's UMA workload: config 2 itself (10x10x5 fcc cells, 2,000 atoms, the
+    same model, weights and cap as the device arm)."""
     from tt_atom import configs
     cfg = configs.model_config("uma-s-1")
     arrs = configs.random_bundle_arrays(cfg, seed=0)
-    s = configs.fcc_alloy(reps=(4, 4, 4), seed=1)
+    s = configs.fcc_alloy(reps=(10, 10, 5), seed=1)
     return cfg, arrs, s
 
 
-def cpu_baseline(bounded=True, steps=1, warmup=0, workload="uma"):
+def cpu_baseline(bounded=True, steps=3, warmup=1, workload="uma"):
     if workload == "orb":
         return _cpu_baseline_orb(steps, warmup)
     from oracle import uma as O
@@ -467,8 +537,11 @@ def cpu_baseline(bounded=True, steps=1, warmup=0, workload="uma"):
     pos = torch.from_numpy(s["pos"])
     cell = torch.from_numpy(s["cell"])
 
+    edges = [0]
+
     def one():
         ei, sh = O.neighbor_list(pos, cfg["cutoff"], cell, [True] * 3, cfg["max_neighbors"])
+        edges[0] = int(ei.shape[1])
         return O.energy_forces(w, cfg, tables, pos, torch.from_numpy(s["Z"]), ei, sh,
                                compute_stress=True)
     for _ in range(warmup):
@@ -481,8 +554,11 @@ def cpu_baseline(bounded=True, steps=1, warmup=0, workload="uma"):
     n = len(s["Z"])
     v = n / statistics.median(times)
     return {"value": v, "unit": "atom-steps/s", "cores": threads, "kind": "port",
-            "sample": f"{n}-atom fcc Cu/Ni (4x4x4 cells), same model/cap, E+F+stress, "
-                      f"median of {steps} step(s)", "seconds_per_step": statistics.median(times)}
+            "sample": f"the full workload: {n}-atom fcc Cu/Ni (10x10x5 cells), same model, "
+                      f"weights and cap, neighbour list + E+F+stress per step, median of "
+                      f"{steps} step(s) after {warmup} warm-up",
+            "seconds_per_step": statistics.median(times), "atoms": n, "edges": edges[0],
+            "cfg": cfg}
 
 
 def _cpu_baseline_orb(steps, warmup):
@@ -493,8 +569,11 @@ def _cpu_baseline_orb(steps, warmup):
     cfg, w, s = _cpu_sample_orb()
     pos, cell = torch.from_numpy(s["pos"]), torch.from_numpy(s["cell"])
 
+    edges = [0]
+
     def one():
         ei, sh = O.neighbor_list(pos, cfg["cutoff"], cell, [True] * 3, cfg["max_num_neighbors"])
+        edges[0] = int(ei.shape[1])
         return OB.energy_forces(w, cfg, pos, torch.from_numpy(s["Z"]), ei, sh,
                                 compute_stress=True)
     for _ in range(warmup):
@@ -506,9 +585,12 @@ def _cpu_baseline_orb(steps, warmup):
         times.append(time.perf_counter() - t0)
     n = len(s["Z"])
     return {"value": n / statistics.median(times), "unit": "atom-steps/s", "cores": threads,
-            "kind": "port", "sample": f"{n}-atom amorphous SiO2, same model/cap, E+F+stress, "
-                                      f"median of {steps} step(s)",
-            "seconds_per_step": statistics.median(times)}
+            "kind": "port", "sample": f"the full workload: {n}-atom amorphous SiO2, same "
+                                      f"model, weights and cap, neighbour list + E+F+stress "
+                                      f"per step, median of {steps} step(s) after {warmup} "
+                                      f"warm-up",
+            "seconds_per_step": statistics.median(times), "atoms": n, "edges": edges[0],
+            "cfg": dict(cfg, max_neighbors=cfg["max_num_neighbors"])}
 
 
 def run_reference(args):
@@ -517,12 +599,14 @@ def run_reference(args):
         return
     steps = args.steps
     cpu = cpu_baseline(bounded=True, steps=steps, warmup=args.warmup, workload=args.workload)
+    cfg = cpu.pop("cfg")
     out = {"metric": METRIC, "value": cpu["value"], "unit": "atom-steps/s", "n_gpus": ws_n,
            "steps": steps, "warmup": args.warmup,
            "ms_per_step": 1e3 * cpu["seconds_per_step"], "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
            "data": DATA[args.workload],
-           "config": {"workload": WORKLOADS[args.workload], "sample": cpu["sample"]},
+           "config": workload_config(args.workload, cpu["atoms"], cpu["edges"], cfg, ws_n),
+           "precision": "fp32 (torch CPU)",
            "impl": "reference", "cpu_baseline": cpu,
            "e2e": {"value": cpu["value"], "unit": "atom-steps/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
@@ -537,6 +621,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cells", default="10,10,5", help="fcc cells (profiling uses a smaller cell)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-partitioned", action="store_true",
+                    help="uma workload: skip the config-4 / config-5 measurements")
     ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "3xf16", "fp32", "tf32"])
     ap.add_argument("--chunk-edges", type=int, default=0,
                     help="fe65k: receiver-chunk size of the edge stages (0: automatic, chunked "
@@ -549,9 +635,9 @@ def main():
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "fe65k":
-        run_slab(args)
+        run_standalone(args, measure_slab)
     elif args.workload == "screen":
-        run_screen(args)
+        run_standalone(args, measure_screen)
     else:
         run_ours(args)
 

@@ -103,8 +103,29 @@ class Plan:
 class DistExchange:
     """Halo exchange between ranks of a torch.distributed process group (point-to-point)."""
 
-    def __init__(self, plan, group=None):
+    def __init__(self, plan, group=None, timed=False):
         self.p, self.group = plan, group
+        # timed: CUDA events on the current stream bracket each exchange (its span includes
+        # waiting for the slowest peer); read with timing_ms() after a synchronize
+        self.timed = timed
+        self.reset_timing()
+
+    def reset_timing(self):
+        self._events = {"forward": [], "reverse": []}
+
+    def timing_ms(self):
+        return {k: sum(a.elapsed_time(b) for a, b in v) for k, v in self._events.items()}
+
+    def count_per_step(self, steps):
+        return {k: len(v) // max(steps, 1) for k, v in self._events.items()}
+
+    def _span(self, kind):
+        if not self.timed:
+            return None
+        pair = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        pair[0].record()
+        self._events[kind].append(pair)
+        return pair[1]
 
     def _p2p(self, sends, recvs):
         import torch.distributed as dist
@@ -117,6 +138,7 @@ class DistExchange:
     def forward(self, x):
         """Fill halo rows of x [N_local, ...] with their owners' rows."""
         p = self.p
+        end = self._span("forward")
         sends = [(q, x[idx].contiguous()) for q, idx in p.send_idx.items()]
         recvs = [(q, torch.empty((c,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device))
                  for q, c in p.recv_count.items()]
@@ -124,11 +146,14 @@ class DistExchange:
         for q, buf in recvs:
             lo, hi = p.halo_block[q]
             x[lo:hi] = buf
+        if end is not None:
+            end.record()
 
     def reverse(self, g):
         """Send halo rows of the adjoint g to their owners, add the received rows into owned
         rows (peers in rank order), zero the halo rows."""
         p = self.p
+        end = self._span("reverse")
         sends = [(q, g[p.halo_block[q][0]:p.halo_block[q][1]].contiguous())
                  for q in p.recv_count]
         recvs = [(q, torch.empty((idx.numel(),) + tuple(g.shape[1:]), dtype=g.dtype,
@@ -137,6 +162,8 @@ class DistExchange:
         for q, buf in sorted(recvs, key=lambda t: t[0]):
             g.index_add_(0, p.send_idx[q], buf)
         g[p.n_own:] = 0
+        if end is not None:
+            end.record()
 
 
 class LockstepGroup:
