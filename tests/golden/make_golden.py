@@ -14,6 +14,9 @@ It writes two kinds of fixture (all fp32, npz):
   reference's OWN CPU path: ``tt_atom.geometry.radius_graph`` + ``HostGeometry`` +
   ``tests/mirror.py`` + torch autograd, with the strain leaf of tt_atom/forces.py:515-524 for the
   virial. These pin the neighbour list (edge_index, shifts: bit-exact) and E/F/virial.
+* ``ref_orb_geometry.npz`` / ``ref_orb_host_terms.npz`` -- the reference's Orb edge features and
+  their VJP, its host ZBL pair repulsion (energy, forces, stress) and its energy normaliser, on
+  seeded inputs.
 
 Nothing at test time reads the reference; the tests read only these files.
 """
@@ -117,12 +120,76 @@ def _orb_geometry(ref_root, out):
     print("wrote", out, "E", ei.shape[1])
 
 
+def _orb_host_terms(ref_root, out, covalent_radii):
+    """The reference's host-side Orb terms on seeded inputs: the ZBL pair repulsion
+    (tt_atom/orb_model.py:491-587: energy with per-node mean and sum aggregation, forces through
+    its own autograd, Voigt stress) and the energy head's normaliser ``host_energy_denormalize``
+    (:590-600). They read ``ase.data.covalent_radii``; ASE is not installed here, so a stand-in
+    module carries this framework's covalent-radius table (the table itself stays unpinned;
+    the ZBL formula, the Z + 1 indexing convention, the envelope and the aggregation are what
+    this pins)."""
+    import types
+    ase = types.ModuleType("ase")
+    ase.data = types.ModuleType("ase.data")
+    ase.data.covalent_radii = np.asarray(covalent_radii, dtype=np.float64)
+    sys.modules["ase"], sys.modules["ase.data"] = ase, ase.data
+    for mod in [m for m in sys.modules if m == "tt_atom" or m.startswith("tt_atom.")]:
+        del sys.modules[mod]
+    sys.path[:] = [p for p in sys.path if not p.endswith("tt-atom_b200")]
+    sys.path.insert(0, str(ref_root))
+    from tt_atom.geometry import radius_graph
+    from tt_atom.orb_model import (host_energy_denormalize, host_zbl_energy, host_zbl_forces,
+                                   host_zbl_stress)
+    g = torch.Generator().manual_seed(9)
+    arrays = {}
+    # a compressed periodic SiO2-like cell (many pairs inside the covalent-radius sums) and an
+    # aperiodic cluster with short contacts
+    n = 48
+    cell = torch.diag(torch.tensor([7.2, 7.6, 8.0]))
+    pos_p = torch.rand(n, 3, generator=g) @ cell
+    Z_p = torch.where(torch.rand(n, generator=g) < 1 / 3, 14, 8).long()
+    pos_m = torch.rand(24, 3, generator=g) * 5.0
+    Z_m = torch.tensor([1, 6, 7, 8, 9, 16] * 4).long()
+    for tag, pos, Z, c in (("p", pos_p, Z_p, cell), ("m", pos_m, Z_m, None)):
+        ei, shift = radius_graph(pos, 5.0, cell=c, pbc=[True] * 3 if c is not None else None)
+        senders, receivers = ei[1], ei[0]
+        vec = pos[receivers].double() - pos[senders].double()
+        if c is not None:
+            vec = vec + shift.double()
+        arrays[f"{tag}_pos"], arrays[f"{tag}_Z"] = pos.numpy(), Z.numpy()
+        arrays[f"{tag}_edge_index"], arrays[f"{tag}_shift"] = ei.numpy(), shift.numpy()
+        for agg in ("mean", "sum"):
+            e = host_zbl_energy(Z, senders, receivers, vec, node_aggregation=agg)
+            f = host_zbl_forces(Z, senders, receivers, pos,
+                                shift.double() if c is not None else None, node_aggregation=agg)
+            arrays[f"{tag}_zbl_energy_{agg}"] = np.float64(e)
+            arrays[f"{tag}_zbl_forces_{agg}"] = f.numpy()
+            if c is not None:
+                st = host_zbl_stress(Z, senders, receivers, vec, c, node_aggregation=agg)
+                arrays[f"{tag}_zbl_stress_{agg}"] = st.numpy()
+        if c is not None:
+            arrays["p_cell"] = c.numpy()
+    raw = torch.randn(3, generator=g, dtype=torch.float64)
+    mean = torch.randn(1, generator=g, dtype=torch.float64)
+    var = torch.rand(1, generator=g, dtype=torch.float64) + 0.5
+    refw = torch.randn(118, generator=g, dtype=torch.float64)
+    arrays.update(denorm_raw=raw.numpy(), denorm_mean=mean.numpy(), denorm_var=var.numpy(),
+                  denorm_ref=refw.numpy())
+    arrays["denorm_out"] = np.array([
+        float(host_energy_denormalize(raw[k], Z_p, len(Z_p), running_mean=mean,
+                                      running_var=var, ref_weight=refw)) for k in range(3)])
+    np.savez_compressed(HERE / out, **arrays)
+    del sys.modules["ase"], sys.modules["ase.data"]
+    print("wrote", out, {k: np.shape(v) for k, v in arrays.items() if k.endswith("edge_index")})
+
+
 def main(ref_root):
     ref_root = pathlib.Path(ref_root)
     _reduce_fairchem(ref_root, "golden_tiny.npz", "ref_golden_tiny.npz")
     _reduce_fairchem(ref_root, "golden_bulk_tiny.npz", "ref_golden_bulk.npz")
     sys.path.insert(0, str(REPO / "tt-atom_b200"))
     from tt_atom import configs                              # seeded inputs and weights
+    from tt_atom.orb import COVALENT_RADII
     cfg = configs.model_config("tiny")
     w = configs.random_weights(cfg, seed=0)
     t = configs.lmax2_tables()
@@ -133,6 +200,7 @@ def main(ref_root):
     _run_reference(ref_root, "ref_run_tiny_molecule.npz", cfg, w, tables, mol, False)
     _run_reference(ref_root, "ref_run_tiny_fcc.npz", cfg, w, tables, fcc, True)
     _orb_geometry(ref_root, "ref_orb_geometry.npz")
+    _orb_host_terms(ref_root, "ref_orb_host_terms.npz", COVALENT_RADII)
 
 
 if __name__ == "__main__":

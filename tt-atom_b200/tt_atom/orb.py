@@ -393,6 +393,21 @@ COVALENT_RADII = (
     2.06, 2.00, 1.96, 1.90, 1.87, 1.80, 1.69) + (0.20,) * 22
 
 
+def energy_denormalize(raw, Z, weights):
+    """The energy head's normaliser (tt_atom/orb_model.py:590-600, ``EnergyHead.denormalize``):
+    undo the scalar normaliser's affine (running mean / variance), undo the per-atom average
+    (times the atom count) and add the per-element linear reference energies. ``raw`` may be a
+    Python float or a (device) tensor; weights without a normaliser return ``raw`` unchanged."""
+    w = weights
+    if "energy_head.normalizer.bn.running_var" not in w:
+        return raw
+    sigma = float(w["energy_head.normalizer.bn.running_var"].double().sqrt())
+    mean = float(w["energy_head.normalizer.bn.running_mean"])
+    Z = np.asarray(Z, dtype=np.int64)
+    ref = float(w["energy_head.reference.linear.weight"].double().reshape(-1)[Z].sum())
+    return (raw * sigma + mean) * len(Z) + ref
+
+
 class OrbCalculator(_AseCalculator):
     """ASE calculator for Orb-v3 conservative bundles (tt_atom/orb_calculator.py:28-215):
     energy, forces = -dE/dpos and stress from the strain virial. Energies are the raw model
@@ -526,10 +541,8 @@ class OrbCalculator(_AseCalculator):
         w = self._w
         scale = 1.0
         if "energy_head.normalizer.bn.running_var" in w:
-            sigma = float(w["energy_head.normalizer.bn.running_var"].double().sqrt())
-            E = (E * sigma + float(w["energy_head.normalizer.bn.running_mean"])) * n
-            E += float(w["energy_head.reference.linear.weight"].double().reshape(-1)[Z].sum())
-            scale = sigma * n
+            E = energy_denormalize(E, Z, w)
+            scale = float(w["energy_head.normalizer.bn.running_var"].double().sqrt()) * n
         self.results["energy"] = self.results["free_energy"] = E
         self.results["energies"] = np.full(n, E / n)
         self.results["forces"] = (scale * F).numpy()
@@ -558,10 +571,7 @@ class OrbCalculator(_AseCalculator):
             if var is not None:
                 mu = w.get("forces_head.normalizer.bn.running_mean")
                 F = F * float(var.double().sqrt()) + (float(mu) if mu is not None else 0.0)
-            if "energy_head.normalizer.bn.running_var" in w:
-                E = (E * float(w["energy_head.normalizer.bn.running_var"].double().sqrt())
-                     + float(w["energy_head.normalizer.bn.running_mean"])) * n
-                E += float(w["energy_head.reference.linear.weight"].double().reshape(-1)[Z].sum())
+            E = energy_denormalize(E, Z, w)
             if self.zbl:
                 Ez, Fz, _ = self._zbl(self._ws, False, scale=1.0)
                 E, F = E + Ez, F + Fz
@@ -572,10 +582,8 @@ class OrbCalculator(_AseCalculator):
         E, F = Ed[0].double(), Fd.double()
         w = self._w
         if "energy_head.normalizer.bn.running_var" in w:
-            sigma = float(w["energy_head.normalizer.bn.running_var"].double().sqrt())
-            E = (E * sigma + float(w["energy_head.normalizer.bn.running_mean"])) * n
-            E = E + float(w["energy_head.reference.linear.weight"].double().reshape(-1)[Z].sum())
-            F = F * (sigma * n)
+            E = energy_denormalize(E, Z, w)
+            F = F * (float(w["energy_head.normalizer.bn.running_var"].double().sqrt()) * n)
         if self.zbl:
             zE, zF, _ = self._zbl_launch(self._ws, False)
             E, F = E + zE[0], F + zF.double()
@@ -629,9 +637,7 @@ class OrbCalculator(_AseCalculator):
             if var is None:
                 return x
             return x * float(var.double().sqrt()) + (float(mu) if mu is not None else 0.0)
-        if "energy_head.normalizer.bn.running_var" in w:
-            E = aff(E, "energy_head.normalizer.bn") * n
-            E += float(w["energy_head.reference.linear.weight"].double().reshape(-1)[Z].sum())
+        E = energy_denormalize(E, Z, w)
         F = aff(F, "forces_head.normalizer.bn")
         if S is not None:
             S = torch.cat([aff(S[:3], "stress_head.diag_normalizer.bn"),
