@@ -113,6 +113,30 @@ int atom_neighbor_list(const float* pos, int64_t N, const int64_t* sys_ptr_host,
                        const float* bbox_host, void* small_scratch, int* need_host,
                        void* stream);
 
+/* Device-resident rebuild of one system's neighbour list into an existing edge set's arrays,
+ * for a caller that replays a step on fixed-size buffers (relaxation, MD, repeated single
+ * points): same predicate, order and cap as atom_neighbor_list, no host synchronisation and no
+ * host round trip, so it can be captured in a CUDA graph together with the step.
+ * Scratch: cand_idx / cand_d [N * max_cand], recv_cnt [N], stage_ptr [N + 1], box_scratch
+ * [6] floats (periodic: the bounding box for image pruning is computed on the device),
+ * status [4] int32. When no receiver has more than max_cand candidates and the new edge count
+ * equals E_expected, the edges (receiver-major) and recv_ptr [N + 1] are written to the
+ * caller's arrays and status[0] = ATOM_REFRESH_OK; otherwise those arrays are left unchanged,
+ * status[0] = ATOM_REFRESH_OVERFLOW or ATOM_REFRESH_SIZE_CHANGED, status[1] = the new edge
+ * count and status[2] = the largest candidate count when it overflowed. Read status after the
+ * stream has run it and fall back to atom_neighbor_list when it is not OK. The sender CSR and
+ * per-edge species are then refreshed with atom_sender_csr / atom_edge_species (also
+ * capturable). Replaces the per-step host radius_graph of tt_atom/trace.py:83-215's callers
+ * (tt_atom/calculator.py:256-277), which this path keeps on the device. */
+#define ATOM_REFRESH_OK 0
+#define ATOM_REFRESH_OVERFLOW 1
+#define ATOM_REFRESH_SIZE_CHANGED 2
+int atom_neighbor_refresh(const float* pos, int64_t N, const float* shifts, int nshift,
+                          float cutoff, int periodic, int max_nbrs, int max_cand, int* cand_idx,
+                          float* cand_d, int* recv_cnt, int* stage_ptr, float* box_scratch,
+                          int* status, int64_t E_expected, int* recv_ptr, int* edge_src,
+                          int* edge_tgt, int* edge_img, void* stream);
+
 /* Exclusive prefix sum of n int32 counts: ptr[0] = 0, ptr[i+1] = ptr[i] + cnt[i]; also copies
  * the total to *total_host (synchronous on `stream`) when total_host is not NULL. */
 int atom_exclusive_scan(const int* cnt, int64_t n, int* ptr, int* total_host, void* stream);

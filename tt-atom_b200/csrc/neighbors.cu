@@ -50,14 +50,25 @@ __global__ void nl_collect_kernel(const float* __restrict__ pos, long long N,
                                   const long long* __restrict__ sys_ptr, int nsys,
                                   const float* __restrict__ shifts, int S, float cutoff,
                                   float cut2, int periodic, int max_nbrs, int max_cand,
-                                  BBox box, int* __restrict__ cand_idx,
+                                  BBox box, const float* __restrict__ box_dev,
+                                  int* __restrict__ cand_idx,
                                   float* __restrict__ cand_d, int* __restrict__ recv_cnt,
                                   int* __restrict__ need) {
     long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
     if (i >= N) return;
-    int k = find_sys(sys_ptr, nsys, i);
-    long long lo = sys_ptr[k], hi = sys_ptr[k + 1];
+    long long lo = 0, hi = N;          // sys_ptr NULL: one system
+    if (sys_ptr) {
+        int k = find_sys(sys_ptr, nsys, i);
+        lo = sys_ptr[k];
+        hi = sys_ptr[k + 1];
+    }
+    if (box_dev) {                     // bounding box computed on the device
+        for (int k = 0; k < 3; ++k) {
+            box.lo[k] = box_dev[k];
+            box.hi[k] = box_dev[3 + k];
+        }
+    }
     float pix = pos[i * 3 + 0], piy = pos[i * 3 + 1], piz = pos[i * 3 + 2];
     // surviving images for this receiver (all lanes compute the same list)
     unsigned char surv[256];
@@ -244,9 +255,113 @@ __global__ void sort_segments_kernel(long long N, const int* __restrict__ ptr,
     }
 }
 
+// ------------------------------------------------------------ device-resident refresh
+// Bounding box of the positions (one block): lo[3], hi[3] into box.
+__global__ void bbox_kernel(const float* __restrict__ pos, long long N, float* __restrict__ box) {
+    __shared__ float red[6][32];
+    float v[6] = {3.0e38f, 3.0e38f, 3.0e38f, -3.0e38f, -3.0e38f, -3.0e38f};
+    for (long long i = threadIdx.x; i < N; i += blockDim.x) {
+        for (int k = 0; k < 3; ++k) {
+            float p = pos[i * 3 + k];
+            v[k] = fminf(v[k], p);
+            v[3 + k] = fmaxf(v[3 + k], p);
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int k = 0; k < 6; ++k) {
+        for (int o = 16; o > 0; o >>= 1) {
+            float w = __shfl_xor_sync(0xffffffffu, v[k], o);
+            v[k] = k < 3 ? fminf(v[k], w) : fmaxf(v[k], w);
+        }
+        if (lane == 0) red[k][warp] = v[k];
+    }
+    __syncthreads();
+    if (threadIdx.x < 6) {
+        const int k = threadIdx.x, nw = blockDim.x >> 5;
+        float r = red[k][0];
+        for (int w = 1; w < nw; ++w) r = k < 3 ? fminf(r, red[k][w]) : fmaxf(r, red[k][w]);
+        box[k] = r;
+    }
+}
+
+// Commit the rebuilt list: when no receiver overflowed its candidate slots and the new edge
+// count equals the caller's, write the edges (receiver-major) and the receiver CSR into the
+// caller's arrays; otherwise leave them untouched and record why in status.
+__global__ void nl_commit_kernel(long long N, int S, int max_cand,
+                                 const int* __restrict__ cand_idx,
+                                 const int* __restrict__ recv_cnt,
+                                 const int* __restrict__ stage_ptr, long long E_expected,
+                                 int* __restrict__ status, int* __restrict__ recv_ptr,
+                                 int* __restrict__ esrc, int* __restrict__ etgt,
+                                 int* __restrict__ eimg) {
+    const long long total = stage_ptr[N];
+    const int overflow = status[2];          // written by the collect pass (atomicMax)
+    long long gt = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (overflow > 0 || total != E_expected) {
+        if (gt == 0) {
+            status[0] = overflow > 0 ? ATOM_REFRESH_OVERFLOW : ATOM_REFRESH_SIZE_CHANGED;
+            status[1] = (int)total;
+        }
+        return;
+    }
+    if (gt == 0) {
+        status[0] = ATOM_REFRESH_OK;
+        status[1] = (int)total;
+    }
+    for (long long t = gt; t <= N; t += (long long)gridDim.x * blockDim.x) recv_ptr[t] = stage_ptr[t];
+    long long i = gt >> 5;
+    int lane = threadIdx.x & 31;
+    if (i >= N) return;
+    int n = recv_cnt[i], o = stage_ptr[i];
+    const int* ci = cand_idx + i * (long long)max_cand;
+    for (int a = lane; a < n; a += 32) {
+        int t = ci[a];
+        esrc[o + a] = t / S;
+        etgt[o + a] = (int)i;
+        eimg[o + a] = t % S;
+    }
+}
+
 }  // namespace atom
 
 using namespace atom;
+
+extern "C" int atom_neighbor_refresh(const float* pos, int64_t N, const float* shifts,
+                                     int nshift, float cutoff, int periodic, int max_nbrs,
+                                     int max_cand, int* cand_idx, float* cand_d, int* recv_cnt,
+                                     int* stage_ptr, float* box_scratch, int* status,
+                                     int64_t E_expected, int* recv_ptr, int* edge_src,
+                                     int* edge_tgt, int* edge_img, void* stream) {
+    ATOM_REQUIRE(N >= 1 && nshift >= 1 && nshift <= 255 && max_cand >= 1,
+                 "neighbor_refresh: N, nshift (1..255) and max_cand must be positive");
+    ATOM_REQUIRE(N * (long long)nshift < (1LL << 31), "N * nshift too large for this kernel");
+    ATOM_REQUIRE(E_expected >= 0 && E_expected <= INT_MAX, "E_expected out of range");
+    ATOM_REQUIRE(cand_idx && cand_d && recv_cnt && stage_ptr && status && recv_ptr && edge_src &&
+                     edge_tgt && edge_img && (!periodic || box_scratch),
+                 "neighbor_refresh: a required buffer is NULL");
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t ce = cudaMemsetAsync(status, 0, 4 * sizeof(int), st);
+    if (ce != cudaSuccess) {
+        set_error("neighbor_refresh: %s", cudaGetErrorString(ce));
+        return ATOM_ERR_CUDA;
+    }
+    BBox box;
+    for (int k = 0; k < 3; ++k) {
+        box.lo[k] = -3.0e38f;
+        box.hi[k] = 3.0e38f;
+    }
+    if (periodic) bbox_kernel<<<1, 1024, 0, st>>>(pos, N, box_scratch);
+    float cut2 = (float)((double)cutoff * (double)cutoff);
+    nl_collect_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(
+        pos, N, nullptr, 1, shifts, nshift, cutoff, cut2, periodic, max_nbrs, max_cand, box,
+        periodic ? box_scratch : nullptr, cand_idx, cand_d, recv_cnt, status + 2);
+    scan_kernel<<<1, 1024, 0, st>>>(recv_cnt, N, stage_ptr);
+    nl_commit_kernel<<<ceil_div((N + 1) * 32, 256), 256, 0, st>>>(
+        N, nshift, max_cand, cand_idx, recv_cnt, stage_ptr, E_expected, status, recv_ptr,
+        edge_src, edge_tgt, edge_img);
+    ATOM_CHECK_LAUNCHES("neighbor_refresh", periodic ? 4 : 3);
+    return ATOM_OK;
+}
 
 extern "C" int atom_neighbor_list(const float* pos, int64_t N, const int64_t* sys_ptr_host,
                                   int nsys, const float* shifts, int nshift, float cutoff,
@@ -283,7 +398,7 @@ extern "C" int atom_neighbor_list(const float* pos, int64_t N, const int64_t* sy
         }
         nl_collect_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(
             pos, N, sp, nsys, shifts, nshift, cutoff, cut2, periodic, max_nbrs, max_cand, box,
-            cand_idx, cand_d, recv_cnt, dneed);
+            nullptr, cand_idx, cand_d, recv_cnt, dneed);
         ATOM_CHECK_LAUNCH("neighbor_list collect");
         int h = 0;
         ce = cudaMemcpyAsync(&h, dneed, sizeof(int), cudaMemcpyDeviceToHost, st);

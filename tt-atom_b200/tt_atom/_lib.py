@@ -42,6 +42,9 @@ _SIGS = {
     "atom_neighbor_list": (c_void_p, c_int64, c_void_p, c_int, c_void_p, c_int, c_float, c_int,
                            c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                            c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p),
+    "atom_neighbor_refresh": (c_void_p, c_int64, c_void_p, c_int, c_float, c_int, c_int, c_int,
+                              c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                              c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p),
     "atom_exclusive_scan": (c_void_p, c_int64, c_void_p, c_void_p, c_void_p),
     "atom_sender_csr": (c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p),
     "atom_sender_csr_noalloc": (c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p),

@@ -118,6 +118,12 @@ class TTAtomCalculator(_AseCalculator):
         as float64 host tensors, or (``device_out``) as float32 device tensors that the next
         call overwrites (``pos`` may then be a device tensor too: nothing crosses to the host
         but the neighbour-list size)."""
+        fast = None
+        if trace and graph is None and sys_ptr is None:
+            fast = self._device_refresh_step(pos, Z, cell, pbc, charges, spins, forces, stress,
+                                             device_out)
+            if fast is not None:
+                return fast
         g = graph if graph is not None else self._graph(pos, Z, cell, pbc, sys_ptr)
         if g.E == 0:
             raise ValueError("no edges within cutoff — system too sparse for this model")
@@ -138,7 +144,7 @@ class TTAtomCalculator(_AseCalculator):
                 self._ws.rebind(g, se)
         else:
             keep = False
-            self._ws = self._step = None            # free the old buffers first
+            self._ws = self._step = self._full_step = None   # free the old buffers first
             chunk = self.chunk_edges
             if chunk == "auto":
                 chunk = self.engine.choose_chunk_edges(g)
@@ -154,10 +160,60 @@ class TTAtomCalculator(_AseCalculator):
             self._step()
         else:
             self.engine.run(ws, ws.pos, forces=forces, virial=stress)
+        # the next traced call on this system (same atoms, cell, charge and spin) may rebuild
+        # its neighbour list on the device inside the captured step
+        self._refresh_key = None
+        if trace and sys_ptr is None and graph is None and ws.chunks is None and g.nsys == 1:
+            self._refresh_key = self._system_key(Z, cell, pbc, charges, spins, forces, stress)
         if device_out:
             return ws.energy, ws.forces if forces else None, ws.virial if stress else None
         E, F, V = to_host(ws.energy, ws.forces if forces else None,
                           ws.virial if stress else None)
+        return E, F, V
+
+    def _system_key(self, Z, cell, pbc, charges, spins, forces, stress):
+        Z = np.asarray(Z, dtype=np.int64)
+        return (Z.shape[0], Z.tobytes(), None if cell is None else
+                np.asarray(cell, np.float32).tobytes(),
+                None if pbc is None else tuple(np.broadcast_to(np.asarray(pbc, bool), 3)),
+                tuple(float(c) for c in charges), tuple(float(v) for v in spins), bool(forces),
+                bool(stress))
+
+    def _device_refresh_step(self, pos, Z, cell, pbc, charges, spins, forces, stress,
+                             device_out):
+        """Traced evaluation of the same system as the previous call with new positions: one
+        captured graph rebuilds the neighbour list on the device into the workspace's arrays
+        and runs the step; one read-back returns the results and the refresh status. None
+        when this path does not apply or the refresh could not keep the edge count (the caller
+        then rebuilds the graph on the host side and re-captures)."""
+        from .graph import TopologyRefresh
+        ws = self._ws
+        if (ws is None or getattr(self, "_refresh_key", None) is None or
+                self._refresh_key != self._system_key(Z, cell, pbc, charges, spins, forces,
+                                                      stress)):
+            return None
+        full = getattr(self, "_full_step", None)
+        if full is None or full[0] is not ws:
+            refresh = TopologyRefresh(ws.graph)
+            ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))
+            step = CapturedStep(self.engine, ws, forces=forces, virial=stress,
+                                prelude=lambda st: refresh.launch(ws.pos, st))
+            self._full_step = full = (ws, refresh, step)
+        else:
+            ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))
+        _, refresh, step = full
+        step()
+        if device_out:
+            if int(refresh.status[0]) != TopologyRefresh.OK:
+                self._refresh_key = self._full_step = None
+                return None
+            return ws.energy, ws.forces if forces else None, ws.virial if stress else None
+        E, F, V, st = to_host(ws.energy, ws.forces if forces else None,
+                              ws.virial if stress else None, refresh.status[:1])
+        if int(st[0]) != TopologyRefresh.OK:
+            # another edge count (or candidate overflow): the step ran on the old topology
+            self._refresh_key = self._full_step = None
+            return None
         return E, F, V
 
     # ------------------------------------------------------------------------------- ASE
@@ -238,3 +294,5 @@ class TTAtomCalculator(_AseCalculator):
     def close(self):
         self._ws = None
         self._step = None
+        self._full_step = None
+        self._refresh_key = None

@@ -826,6 +826,7 @@ class Workspace:
             for k in self._TOPOLOGY:
                 getattr(self.graph, k).copy_(getattr(graph, k))
             self.graph.sys_ptr_host = list(graph.sys_ptr_host)
+            self.graph.max_cand = max(self.graph.max_cand, graph.max_cand)
         graph = self.graph
         eng, N, eng_C = self._eng, graph.N, self._eng.C
         if self.chunk_edges is not None:
@@ -856,16 +857,22 @@ class CapturedStep:
     """A CUDA graph of one full E+F(+virial) step on a fixed topology (the CUDA-graph
     counterpart of tt_atom/trace.py:83-215): positions are refreshed in place, then replayed."""
 
-    def __init__(self, eng, ws, forces=True, virial=False, warmup=1):
+    def __init__(self, eng, ws, forces=True, virial=False, warmup=1, prelude=None):
+        """``prelude(stream)``, when given, issues launches that run before the step inside
+        the same graph (the device-resident neighbour-list refresh)."""
         self.eng, self.ws = eng, ws
         self.stream = torch.cuda.Stream(device=eng.device)
         self.stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(self.stream):
             for _ in range(warmup):
+                if prelude is not None:
+                    prelude(self.stream)
                 eng.run(ws, ws.pos, forces=forces, virial=virial, stream=self.stream)
         torch.cuda.current_stream().wait_stream(self.stream)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=self.stream):
+            if prelude is not None:
+                prelude(self.stream)
             eng.run(ws, ws.pos, forces=forces, virial=virial, stream=self.stream)
 
     def __call__(self, pos=None):

@@ -107,6 +107,9 @@ class Graph:
     send_eid: torch.Tensor   # [E]
     zs: torch.Tensor         # [E] species of source
     zt: torch.Tensor         # [E] species of target
+    max_cand: int = 64       # candidate slots per receiver the build needed
+    cutoff: float = 0.0
+    max_neighbors: int = 0   # 0: uncapped
 
     def reference_order(self):
         """(edge_index [2, E] int64, image index [E]) in the reference's edge order: periodic
@@ -192,7 +195,47 @@ def build_graph(pos, Z, cutoff, cell=None, pbc=None, max_neighbors=None, sys_ptr
     sys_id, sys_ptr_d = _device_sys(sys_ptr, dev)
     return Graph(N=N, E=E, nsys=nsys, periodic=periodic, Z=Zt, sys_id=sys_id, sys_ptr=sys_ptr_d,
                  sys_ptr_host=sys_ptr, src=src, tgt=tgt, img=img, shifts=shifts,
-                 recv_ptr=recv_ptr, send_ptr=send_ptr, send_eid=send_eid, zs=zs[:E], zt=zt[:E])
+                 recv_ptr=recv_ptr, send_ptr=send_ptr, send_eid=send_eid, zs=zs[:E], zt=zt[:E],
+                 max_cand=max_cand, cutoff=float(cutoff), max_neighbors=cap)
+
+
+class TopologyRefresh:
+    """Rebuilds one system's neighbour list on the device, in place, into a graph's own arrays
+    (``atom_neighbor_refresh`` + sender CSR + edge species): no host synchronisation, so the
+    launches can be captured in a CUDA graph together with the step that uses the graph.
+
+    The edge count is fixed by the arrays: when the new list has a different number of edges,
+    or a receiver overflows its candidate slots, the arrays keep the previous topology and
+    ``status[0]`` says so (``ATOM_REFRESH_*``); the caller reads it after the stream has run
+    and rebuilds through ``build_graph`` then. Candidate slots get headroom over what the
+    first build needed, for atoms that move."""
+
+    OK, OVERFLOW, SIZE_CHANGED = 0, 1, 2
+
+    def __init__(self, graph, headroom=32):
+        if graph.nsys != 1:
+            raise ValueError("the device refresh handles one system")
+        dev = graph.src.device
+        N = graph.N
+        self.g = graph
+        self.max_cand = int(graph.max_cand) + headroom
+        i32 = lambda n: torch.empty(max(n, 1), dtype=torch.int32, device=dev)  # noqa: E731
+        self.cand_idx = i32(N * self.max_cand)
+        self.cand_d = torch.empty(max(N * self.max_cand, 1), dtype=torch.float32, device=dev)
+        self.recv_cnt, self.stage_ptr, self.csr_scratch = i32(N), i32(N + 1), i32(N)
+        self.box = torch.empty(6, dtype=torch.float32, device=dev)
+        self.status = torch.zeros(4, dtype=torch.int32, device=dev)
+
+    def launch(self, pos, stream=None):
+        g, s = self.g, L.stream_ptr(stream)
+        call("atom_neighbor_refresh", ptr(pos), g.N, ptr(g.shifts), g.shifts.shape[0],
+             float(g.cutoff), int(g.periodic), int(g.max_neighbors), self.max_cand,
+             ptr(self.cand_idx), ptr(self.cand_d), ptr(self.recv_cnt), ptr(self.stage_ptr),
+             ptr(self.box), ptr(self.status), g.E, ptr(g.recv_ptr), ptr(g.src), ptr(g.tgt),
+             ptr(g.img), s)
+        call("atom_sender_csr", ptr(g.src), g.E, g.N, ptr(self.csr_scratch), ptr(g.send_ptr),
+             ptr(g.send_eid), s)
+        call("atom_edge_species", ptr(g.Z), ptr(g.src), ptr(g.tgt), g.E, ptr(g.zs), ptr(g.zt), s)
 
 
 def radius_graph(pos, cutoff, cell=None, pbc=None, max_neighbors=None, device="cuda"):
