@@ -89,6 +89,29 @@ int atom_fused_ln_bw(const float* g, const float* x, const float* n, const float
  * the same fp32 predicate and the same edge order, plus an optional per-receiver cap.
  * ---------------------------------------------------------------------------------------- */
 
+/* Cell list of one fully periodic system (optional argument of atom_neighbor_list and
+ * atom_neighbor_refresh; NULL: all-pairs candidates with bounding-box image pruning). Atoms are
+ * binned by wrapped fractional coordinates (pos @ inv_cell, row-major, computed in double)
+ * into nb[0] x nb[1] x nb[2] bins; a receiver scans reach[k] bins on either side along lattice
+ * direction k. Every bin must be at least the cutoff wide across its lattice planes with
+ * reach = 1, or reach = ceil(cutoff |b_k| nb_k) otherwise (b_k: reciprocal vector, column k of
+ * inv_cell). img_r[k]: the image offsets -r..r of the shifts table (cartesian-product order,
+ * first axis slowest). Device scratch: atom_bin [N], atom_off [3 N], bin_cnt [nbins],
+ * bin_ptr [nbins + 1], bin_atoms [N] int32. The edge list is identical to the all-pairs one;
+ * max_cand must not exceed 256. No counterpart in the reference (its radius_graph is
+ * all-pairs, tt_atom/geometry.py:48-81). */
+typedef struct {
+    double inv_cell[9];
+    int nb[3];
+    int reach[3];
+    int img_r[3];
+    int* atom_bin;
+    int* atom_off;
+    int* bin_cnt;
+    int* bin_ptr;
+    int* bin_atoms;
+} atom_cell_grid;
+
 /* Neighbour list of `nsys` independent systems stored back to back (sys_ptr[nsys+1] atom
  * offsets, host array). Each system is periodic with `nshift` image shifts (shifts [nshift,3],
  * device; the zero shift alone for aperiodic systems) -- all systems share pbc and shifts.
@@ -111,7 +134,7 @@ int atom_neighbor_list(const float* pos, int64_t N, const int64_t* sys_ptr_host,
                        int max_cand, int* cand_idx, float* cand_d, int* recv_cnt,
                        const int* recv_ptr, int* edge_src, int* edge_tgt, int* edge_img,
                        const float* bbox_host, void* small_scratch, int* need_host,
-                       void* stream);
+                       const atom_cell_grid* grid, void* stream);
 
 /* Device-resident rebuild of one system's neighbour list into an existing edge set's arrays,
  * for a caller that replays a step on fixed-size buffers (relaxation, MD, repeated single
@@ -135,7 +158,8 @@ int atom_neighbor_refresh(const float* pos, int64_t N, const float* shifts, int 
                           float cutoff, int periodic, int max_nbrs, int max_cand, int* cand_idx,
                           float* cand_d, int* recv_cnt, int* stage_ptr, float* box_scratch,
                           int* status, int64_t E_expected, int* recv_ptr, int* edge_src,
-                          int* edge_tgt, int* edge_img, void* stream);
+                          int* edge_tgt, int* edge_img, const atom_cell_grid* grid,
+                          void* stream);
 
 /* Exclusive prefix sum of n int32 counts: ptr[0] = 0, ptr[i+1] = ptr[i] + cnt[i]; also copies
  * the total to *total_host (synchronous on `stream`) when total_host is not NULL. */

@@ -86,7 +86,7 @@ def test_run_end_to_end_on_the_gpu(tmp_path, capsys):
     lonely = tmp_path / "lonely.xyz"
     lonely.write_text("2\n\nC 0 0 0\nO 20 0 0\n")
     calc = TTAtomCalculator(WeightBundle.from_arrays(arrs))
-    a = SimpleAtoms(m["Z"], m["pos"])
+    a = SimpleAtoms(m["Z"], m["pos"], info=dict(charge=0.0, spin=1.0))   # the CLI defaults
     a.calc = calc
     e_ref = float(a.get_potential_energy())
     # single GPU

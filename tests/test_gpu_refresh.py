@@ -97,3 +97,45 @@ def test_traced_calculator_refreshes_on_the_device_and_falls_back():
             c.calculate(SimpleAtoms(m["Z"], p), ("energy", "forces"))
         assert traced.results["energy"] == eager.results["energy"]
         assert np.array_equal(traced.results["forces"], eager.results["forces"])
+
+
+def _random_cell(rng, n, skew):
+    a = np.diag(rng.uniform(5.0, 14.0, 3))
+    if skew:
+        a[1, 0], a[2, 0], a[2, 1] = rng.uniform(-2.5, 2.5, 3)
+    frac = rng.uniform(-0.3, 1.3, (n, 3))         # atoms outside the cell too
+    return (frac @ a).astype(np.float32), a.astype(np.float32)
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_cell_list_equals_all_pairs(seed):
+    """The cell-list candidates give the all-pairs edge list bit for bit: orthogonal and
+    triclinic cells, cells narrower than the cutoff (several images per axis), atoms outside
+    the cell, with and without the cap."""
+    rng = np.random.default_rng(seed)
+    n = int(rng.integers(20, 400))
+    pos, cell = _random_cell(rng, n, skew=seed % 2 == 1)
+    Z = np.ones(n, np.int64)
+    for cap in (None, 12):
+        a = build_graph(pos, Z, 6.0, cell, [True] * 3, max_neighbors=cap, use_cells=True)
+        b = build_graph(pos, Z, 6.0, cell, [True] * 3, max_neighbors=cap, use_cells=False)
+        assert a.cell_grid is not None and b.cell_grid is None
+        assert a.E == b.E
+        for k in ("src", "tgt", "img", "recv_ptr"):
+            assert torch.equal(getattr(a, k), getattr(b, k)), (seed, cap, k)
+
+
+@pytest.mark.parametrize("name", ["fcc2000", "sio2", "fe65k"])
+def test_cell_list_on_the_benchmark_cells(name):
+    if name == "fcc2000":
+        s, cap = configs.fcc_alloy(reps=(10, 10, 5), seed=1), 30
+    elif name == "sio2":
+        s, cap = configs.amorphous_sio2(), 20
+    else:
+        s, cap = configs.bcc_iron(reps=(12, 12, 12)), 30
+    a = build_graph(s["pos"], s["Z"], 6.0, s["cell"], [True] * 3, max_neighbors=cap)
+    b = build_graph(s["pos"], s["Z"], 6.0, s["cell"], [True] * 3, max_neighbors=cap,
+                    use_cells=False)
+    assert a.E == b.E == cap * len(s["Z"])
+    for k in ("src", "tgt", "img", "recv_ptr", "send_ptr", "send_eid"):
+        assert torch.equal(getattr(a, k), getattr(b, k)), k

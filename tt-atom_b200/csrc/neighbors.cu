@@ -36,6 +36,38 @@ __device__ __forceinline__ int find_sys(const long long* sp, int nsys, long long
     return lo;
 }
 
+// The cap: rank each of a receiver's cnt candidates (in candidate order) by (key, position),
+// drop those ranked >= max_nbrs and compact the survivors in place, in order. Whole warp.
+__device__ int cap_candidates(int* ci, float* cd, int cnt, int max_nbrs, int lane) {
+    for (int a = lane; a < cnt; a += 32) {
+        float ka = cd[a];
+        int rank = 0;
+        for (int b = 0; b < cnt; ++b) {
+            float kb = cd[b];
+            rank += (kb < ka) || (kb == ka && b < a);
+        }
+        if (rank >= max_nbrs) ci[a] |= (int)0x80000000;
+    }
+    __syncwarp();
+    int w = 0;
+    for (int base = 0; base < cnt; base += 32) {
+        int a = base + lane;
+        int v = a < cnt ? ci[a] : (int)0x80000000;
+        float d = a < cnt ? cd[a] : 0.f;
+        bool s = v >= 0;
+        unsigned m = __ballot_sync(0xffffffffu, s);
+        __syncwarp();
+        if (s) {
+            int slot = w + __popc(m & ((1u << lane) - 1u));
+            ci[slot] = v;
+            cd[slot] = d;
+        }
+        __syncwarp();
+        w += __popc(m);
+    }
+    return w;
+}
+
 // Pass 1: one warp per receiver, candidates in (j, c) order tested 32 at a time; the survivors
 // are appended in order (ballot + popc) to the receiver's candidate slots.
 // Images that cannot hold a neighbour of receiver i are skipped: image c is kept only if the
@@ -133,37 +165,165 @@ __global__ void nl_collect_kernel(const float* __restrict__ pos, long long N,
     }
     int kept = cnt;
     __syncwarp();
-    if (max_nbrs > 0 && cnt > max_nbrs) {
-        // rank of each candidate by (key, position); drop those ranked >= max_nbrs
-        for (int a = lane; a < cnt; a += 32) {
-            float ka = cd[a];
-            int rank = 0;
-            for (int b = 0; b < cnt; ++b) {
-                float kb = cd[b];
-                rank += (kb < ka) || (kb == ka && b < a);
-            }
-            if (rank >= max_nbrs) ci[a] |= (int)0x80000000;
-        }
-        __syncwarp();
-        // compact survivors in place, in order
-        int w = 0;
-        for (int base = 0; base < cnt; base += 32) {
-            int a = base + lane;
-            int v = a < cnt ? ci[a] : (int)0x80000000;
-            float d = a < cnt ? cd[a] : 0.f;
-            bool s = v >= 0;
-            unsigned m = __ballot_sync(0xffffffffu, s);
-            __syncwarp();
-            if (s) {
-                int slot = w + __popc(m & ((1u << lane) - 1u));
-                ci[slot] = v;
-                cd[slot] = d;
-            }
-            __syncwarp();
-            w += __popc(m);
-        }
-        kept = w;
+    if (max_nbrs > 0 && cnt > max_nbrs) kept = cap_candidates(ci, cd, cnt, max_nbrs, lane);
+    if (lane == 0) recv_cnt[i] = kept;
+}
+
+// ------------------------------------------------------------------------ cell list
+// Periodic single systems: atoms are binned by their wrapped fractional coordinates
+// w = f - floor(f), f = pos @ inv_cell (double), into nb[0] x nb[1] x nb[2] bins whose width
+// along lattice direction k is at least the cutoff (plus slack) measured across the lattice
+// planes. A receiver scans the bins within reach[k] of its own (27 for nb >= 3), each bin
+// taken with the lattice translation L its extended index implies. Atom j seen in bin-extended
+// position L stands for the image pos[j] + shift[c] with integer offset
+// o = n_i + L - n_j (n = floor(f)); the candidate exists only when o lies in the shifts
+// table's range [-r, r]^3, and it is then tested with exactly the brute-force expression on
+// pos[j] and shifts[c]. Each (j, o) is met at most once, and every pair within the cutoff lies
+// within reach, so the accepted set equals the brute force's. Candidates arrive in bin order;
+// they are sorted back into (j, c) order before the cap is applied, so the result is the
+// brute force's bit for bit.
+
+__device__ __forceinline__ void frac_of(const float* __restrict__ pos, long long j,
+                                       const atom_cell_grid& G, double f[3]) {
+    const double p0 = pos[j * 3], p1 = pos[j * 3 + 1], p2 = pos[j * 3 + 2];
+    for (int k = 0; k < 3; ++k)
+        f[k] = p0 * G.inv_cell[0 * 3 + k] + p1 * G.inv_cell[1 * 3 + k] + p2 * G.inv_cell[2 * 3 + k];
+}
+
+__device__ __forceinline__ void wrap_bin(const double f[3], const int nb[3], int b[3], int n[3]) {
+    for (int k = 0; k < 3; ++k) {
+        const double fl = floor(f[k]);
+        const double w = f[k] - fl;
+        n[k] = (int)fl;
+        int bk = (int)(w * nb[k]);
+        b[k] = bk < 0 ? 0 : (bk >= nb[k] ? nb[k] - 1 : bk);
     }
+}
+
+__global__ void cl_bin_kernel(const float* __restrict__ pos, long long N, atom_cell_grid G) {
+    long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= N) return;
+    double f[3];
+    int b[3], n[3];
+    frac_of(pos, j, G, f);
+    wrap_bin(f, G.nb, b, n);
+    const int bin = (b[0] * G.nb[1] + b[1]) * G.nb[2] + b[2];
+    G.atom_bin[j] = bin;
+    for (int k = 0; k < 3; ++k) G.atom_off[j * 3 + k] = n[k];
+    atomicAdd(G.bin_cnt + bin, 1);
+}
+
+__global__ void cl_fill_kernel(long long N, atom_cell_grid G) {
+    long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= N) return;
+    const int bin = G.atom_bin[j];
+    const int slot = atomicAdd(G.bin_cnt + bin, 1);     // bin_cnt was cleared after the scan
+    G.bin_atoms[G.bin_ptr[bin] + slot] = (int)j;
+}
+
+constexpr int kSortPerLane = 8;    // candidates a lane holds while sorting (max_cand <= 256)
+
+__global__ void nl_collect_cells_kernel(const float* __restrict__ pos, long long N,
+                                        const float* __restrict__ shifts, int S, float cut2,
+                                        int max_nbrs, int max_cand, atom_cell_grid G,
+                                        int* __restrict__ cand_idx, float* __restrict__ cand_d,
+                                        int* __restrict__ recv_cnt, int* __restrict__ need) {
+    long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (i >= N) return;
+    const float pix = pos[i * 3 + 0], piy = pos[i * 3 + 1], piz = pos[i * 3 + 2];
+    double f[3];
+    int bi[3], ni[3];
+    frac_of(pos, i, G, f);
+    wrap_bin(f, G.nb, bi, ni);
+    const int w1 = 2 * G.img_r[1] + 1, w2 = 2 * G.img_r[2] + 1;
+    int* ci = cand_idx + i * (long long)max_cand;
+    float* cd = cand_d + i * (long long)max_cand;
+    const float tiny = 1e-8f;
+    int cnt = 0;
+    for (int e0 = bi[0] - G.reach[0]; e0 <= bi[0] + G.reach[0]; ++e0)
+        for (int e1 = bi[1] - G.reach[1]; e1 <= bi[1] + G.reach[1]; ++e1)
+            for (int e2 = bi[2] - G.reach[2]; e2 <= bi[2] + G.reach[2]; ++e2) {
+                const int e[3] = {e0, e1, e2};
+                int bin = 0, L[3];
+                for (int k = 0; k < 3; ++k) {
+                    int q = e[k] % G.nb[k];
+                    if (q < 0) q += G.nb[k];
+                    L[k] = (e[k] - q) / G.nb[k];
+                    bin = bin * G.nb[k] + q;
+                }
+                const int a0 = G.bin_ptr[bin], a1 = G.bin_ptr[bin + 1];
+                for (int base = a0; base < a1; base += 32) {
+                    const int t = base + lane;
+                    bool keep = false;
+                    int tidx = 0;
+                    float key = 0.f;
+                    if (t < a1) {
+                        const int j = G.bin_atoms[t];
+                        int o[3];
+                        bool inr = true;
+                        for (int k = 0; k < 3; ++k) {
+                            o[k] = ni[k] + L[k] - G.atom_off[j * 3 + k];
+                            inr = inr && o[k] >= -G.img_r[k] && o[k] <= G.img_r[k];
+                        }
+                        if (inr) {
+                            const int c = ((o[0] + G.img_r[0]) * w1 + (o[1] + G.img_r[1])) * w2 +
+                                          (o[2] + G.img_r[2]);
+                            const float qx = __fadd_rn(pos[j * 3 + 0], shifts[c * 3 + 0]);
+                            const float qy = __fadd_rn(pos[j * 3 + 1], shifts[c * 3 + 1]);
+                            const float qz = __fadd_rn(pos[j * 3 + 2], shifts[c * 3 + 2]);
+                            const float dx = __fsub_rn(pix, qx), dy = __fsub_rn(piy, qy),
+                                        dz = __fsub_rn(piz, qz);
+                            const float d2 = __fadd_rn(
+                                __fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)), __fmul_rn(dz, dz));
+                            keep = (d2 <= cut2) && (d2 > tiny);
+                            key = d2;
+                            tidx = j * S + c;
+                        }
+                    }
+                    const unsigned m = __ballot_sync(0xffffffffu, keep);
+                    if (keep) {
+                        const int slot = cnt + __popc(m & ((1u << lane) - 1u));
+                        if (slot < max_cand) {
+                            ci[slot] = tidx;
+                            cd[slot] = key;
+                        }
+                    }
+                    cnt += __popc(m);
+                }
+            }
+    if (cnt > max_cand) {
+        if (lane == 0) {
+            atomicMax(need, cnt);
+            recv_cnt[i] = 0;
+        }
+        return;
+    }
+    __syncwarp();
+    // back into (j, c) order: rank of each candidate by its index, then scatter
+    int vi[kSortPerLane], rk[kSortPerLane];
+    float vd[kSortPerLane];
+#pragma unroll
+    for (int q = 0; q < kSortPerLane; ++q) {
+        const int a = lane + 32 * q;
+        vi[q] = a < cnt ? ci[a] : 0;
+        vd[q] = a < cnt ? cd[a] : 0.f;
+        int r = 0;
+        if (a < cnt)
+            for (int b = 0; b < cnt; ++b) r += ci[b] < vi[q];
+        rk[q] = r;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < kSortPerLane; ++q) {
+        if (lane + 32 * q < cnt) {
+            ci[rk[q]] = vi[q];
+            cd[rk[q]] = vd[q];
+        }
+    }
+    __syncwarp();
+    int kept = cnt;
+    if (max_nbrs > 0 && cnt > max_nbrs) kept = cap_candidates(ci, cd, cnt, max_nbrs, lane);
     if (lane == 0) recv_cnt[i] = kept;
 }
 
@@ -322,6 +482,39 @@ __global__ void nl_commit_kernel(long long N, int S, int max_cand,
     }
 }
 
+// Bins of the cell list (see nl_collect_cells_kernel); 5 launches, no host synchronisation.
+static int build_bins(const float* pos, long long N, const atom_cell_grid& G, cudaStream_t st) {
+    const long long nbins = (long long)G.nb[0] * G.nb[1] * G.nb[2];
+    cudaError_t ce = cudaMemsetAsync(G.bin_cnt, 0, nbins * sizeof(int), st);
+    if (ce == cudaSuccess) {
+        cl_bin_kernel<<<ceil_div(N, 256), 256, 0, st>>>(pos, N, G);
+        scan_kernel<<<1, 1024, 0, st>>>(G.bin_cnt, nbins, G.bin_ptr);
+        ce = cudaMemsetAsync(G.bin_cnt, 0, nbins * sizeof(int), st);
+    }
+    if (ce == cudaSuccess) cl_fill_kernel<<<ceil_div(N, 256), 256, 0, st>>>(N, G);
+    if (ce != cudaSuccess) {
+        set_error("cell list: %s", cudaGetErrorString(ce));
+        return ATOM_ERR_CUDA;
+    }
+    return check_launch("cell list bins", 3);
+}
+
+static int check_grid(const atom_cell_grid* g, int max_cand, int nshift) {
+    if (!g) return ATOM_OK;
+    ATOM_REQUIRE(max_cand <= 32 * kSortPerLane, "cell list: max_cand above %d",
+                 32 * kSortPerLane);
+    for (int k = 0; k < 3; ++k)
+        ATOM_REQUIRE(g->nb[k] >= 1 && g->reach[k] >= 1 && g->img_r[k] >= 0,
+                     "cell list: bad grid on axis %d", k);
+    ATOM_REQUIRE((2 * g->img_r[0] + 1) * (2 * g->img_r[1] + 1) * (2 * g->img_r[2] + 1) == nshift,
+                 "cell list: image ranges do not match nshift");
+    ATOM_REQUIRE((long long)g->nb[0] * g->nb[1] * g->nb[2] <= (1LL << 24),
+                 "cell list: too many bins");
+    ATOM_REQUIRE(g->atom_bin && g->atom_off && g->bin_cnt && g->bin_ptr && g->bin_atoms,
+                 "cell list: a scratch buffer is NULL");
+    return ATOM_OK;
+}
+
 }  // namespace atom
 
 using namespace atom;
@@ -331,7 +524,8 @@ extern "C" int atom_neighbor_refresh(const float* pos, int64_t N, const float* s
                                      int max_cand, int* cand_idx, float* cand_d, int* recv_cnt,
                                      int* stage_ptr, float* box_scratch, int* status,
                                      int64_t E_expected, int* recv_ptr, int* edge_src,
-                                     int* edge_tgt, int* edge_img, void* stream) {
+                                     int* edge_tgt, int* edge_img,
+                                     const atom_cell_grid* grid, void* stream) {
     ATOM_REQUIRE(N >= 1 && nshift >= 1 && nshift <= 255 && max_cand >= 1,
                  "neighbor_refresh: N, nshift (1..255) and max_cand must be positive");
     ATOM_REQUIRE(N * (long long)nshift < (1LL << 31), "N * nshift too large for this kernel");
@@ -339,6 +533,8 @@ extern "C" int atom_neighbor_refresh(const float* pos, int64_t N, const float* s
     ATOM_REQUIRE(cand_idx && cand_d && recv_cnt && stage_ptr && status && recv_ptr && edge_src &&
                      edge_tgt && edge_img && (!periodic || box_scratch),
                  "neighbor_refresh: a required buffer is NULL");
+    ATOM_REQUIRE(!grid || periodic, "the cell list takes a periodic system");
+    if (int s = check_grid(grid, max_cand, nshift)) return s;
     cudaStream_t st = (cudaStream_t)stream;
     cudaError_t ce = cudaMemsetAsync(status, 0, 4 * sizeof(int), st);
     if (ce != cudaSuccess) {
@@ -350,16 +546,23 @@ extern "C" int atom_neighbor_refresh(const float* pos, int64_t N, const float* s
         box.lo[k] = -3.0e38f;
         box.hi[k] = 3.0e38f;
     }
-    if (periodic) bbox_kernel<<<1, 1024, 0, st>>>(pos, N, box_scratch);
     float cut2 = (float)((double)cutoff * (double)cutoff);
-    nl_collect_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(
-        pos, N, nullptr, 1, shifts, nshift, cutoff, cut2, periodic, max_nbrs, max_cand, box,
-        periodic ? box_scratch : nullptr, cand_idx, cand_d, recv_cnt, status + 2);
+    if (grid) {
+        if (int s2 = build_bins(pos, N, *grid, st)) return s2;
+        nl_collect_cells_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(
+            pos, N, shifts, nshift, cut2, max_nbrs, max_cand, *grid, cand_idx, cand_d, recv_cnt,
+            status + 2);
+    } else {
+        if (periodic) bbox_kernel<<<1, 1024, 0, st>>>(pos, N, box_scratch);
+        nl_collect_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(
+            pos, N, nullptr, 1, shifts, nshift, cutoff, cut2, periodic, max_nbrs, max_cand, box,
+            periodic ? box_scratch : nullptr, cand_idx, cand_d, recv_cnt, status + 2);
+    }
     scan_kernel<<<1, 1024, 0, st>>>(recv_cnt, N, stage_ptr);
     nl_commit_kernel<<<ceil_div((N + 1) * 32, 256), 256, 0, st>>>(
         N, nshift, max_cand, cand_idx, recv_cnt, stage_ptr, E_expected, status, recv_ptr,
         edge_src, edge_tgt, edge_img);
-    ATOM_CHECK_LAUNCHES("neighbor_refresh", periodic ? 4 : 3);
+    ATOM_CHECK_LAUNCHES("neighbor_refresh", (periodic && !grid) ? 4 : 3);
     return ATOM_OK;
 }
 
@@ -369,12 +572,14 @@ extern "C" int atom_neighbor_list(const float* pos, int64_t N, const int64_t* sy
                                   float* cand_d, int* recv_cnt, const int* recv_ptr,
                                   int* edge_src, int* edge_tgt, int* edge_img,
                                   const float* bbox_host, void* small_scratch, int* need_host,
-                                  void* stream) {
+                                  const atom_cell_grid* grid, void* stream) {
     ATOM_REQUIRE(nsys >= 1 && nsys <= 1 << 20, "nsys out of range");
     ATOM_REQUIRE(nshift >= 1 && max_cand >= 1, "nshift and max_cand must be positive");
     ATOM_REQUIRE(nshift <= 255, "at most 255 periodic images (cell too small for the cutoff)");
     ATOM_REQUIRE(sys_ptr_host[0] == 0 && sys_ptr_host[nsys] == N, "sys_ptr must span [0, N)");
     ATOM_REQUIRE(N * (long long)nshift < (1LL << 31), "N * nshift too large for this kernel");
+    ATOM_REQUIRE(!grid || (nsys == 1 && periodic), "the cell list takes one periodic system");
+    if (int s = check_grid(grid, max_cand, nshift)) return s;
     cudaStream_t st = (cudaStream_t)stream;
     if (N == 0) return ATOM_OK;
     ATOM_REQUIRE(small_scratch && (reinterpret_cast<uintptr_t>(small_scratch) & 7u) == 0,
@@ -396,9 +601,16 @@ extern "C" int atom_neighbor_list(const float* pos, int64_t N, const int64_t* sy
             box.lo[k] = bbox_host ? bbox_host[k] : -3.0e38f;
             box.hi[k] = bbox_host ? bbox_host[3 + k] : 3.0e38f;
         }
-        nl_collect_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(
-            pos, N, sp, nsys, shifts, nshift, cutoff, cut2, periodic, max_nbrs, max_cand, box,
-            nullptr, cand_idx, cand_d, recv_cnt, dneed);
+        if (grid) {
+            if (int s2 = build_bins(pos, N, *grid, st)) return s2;
+            nl_collect_cells_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(
+                pos, N, shifts, nshift, cut2, max_nbrs, max_cand, *grid, cand_idx, cand_d,
+                recv_cnt, dneed);
+        } else {
+            nl_collect_kernel<<<ceil_div(N * 32, 256), 256, 0, st>>>(
+                pos, N, sp, nsys, shifts, nshift, cutoff, cut2, periodic, max_nbrs, max_cand,
+                box, nullptr, cand_idx, cand_d, recv_cnt, dneed);
+        }
         ATOM_CHECK_LAUNCH("neighbor_list collect");
         int h = 0;
         ce = cudaMemcpyAsync(&h, dneed, sizeof(int), cudaMemcpyDeviceToHost, st);

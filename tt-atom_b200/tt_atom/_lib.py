@@ -19,6 +19,13 @@ c_void_p, c_int, c_int64, c_float = ctypes.c_void_p, ctypes.c_int, ctypes.c_int6
 c_double = ctypes.c_double
 
 
+class CellGrid(ctypes.Structure):
+    """atom_cell_grid of include/atom_b200.h."""
+    _fields_ = [("inv_cell", c_double * 9), ("nb", c_int * 3), ("reach", c_int * 3),
+                ("img_r", c_int * 3), ("atom_bin", c_void_p), ("atom_off", c_void_p),
+                ("bin_cnt", c_void_p), ("bin_ptr", c_void_p), ("bin_atoms", c_void_p)]
+
+
 class GemmGroups(ctypes.Structure):
     _fields_ = [("ngroups", c_int), ("a_col", c_int * 8), ("K", c_int * 8), ("c_col", c_int * 8),
                 ("N", c_int * 8), ("ldb", c_int * 8), ("t_col", c_int * 8),
@@ -41,10 +48,12 @@ _SIGS = {
                          c_void_p, c_void_p),
     "atom_neighbor_list": (c_void_p, c_int64, c_void_p, c_int, c_void_p, c_int, c_float, c_int,
                            c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
-                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p),
+                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                           c_void_p),
     "atom_neighbor_refresh": (c_void_p, c_int64, c_void_p, c_int, c_float, c_int, c_int, c_int,
                               c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
-                              c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p),
+                              c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                              c_void_p),
     "atom_exclusive_scan": (c_void_p, c_int64, c_void_p, c_void_p, c_void_p),
     "atom_sender_csr": (c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p),
     "atom_sender_csr_noalloc": (c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p),

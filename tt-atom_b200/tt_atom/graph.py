@@ -18,19 +18,65 @@ from . import _lib as L
 from ._lib import call, ptr
 
 
-def image_shifts(cell, pbc, cutoff):
-    """Cartesian image shifts ``cells @ cell`` for integer offsets in [-r, r] per periodic axis,
-    r = ceil(cutoff * |b_k|) with b_k the reciprocal rows, in cartesian-product order -- the
-    host arithmetic of tt_atom/geometry.py:66-75, kept in torch fp32 on the CPU so the shifts
-    are the reference's bit for bit."""
+def image_reps(cell, pbc, cutoff):
+    """Image offsets r per axis, r = ceil(cutoff * |b_k|) with b_k the reciprocal rows (0 on
+    a non-periodic axis): the host arithmetic of tt_atom/geometry.py:66-75 in torch fp32."""
     cell = torch.as_tensor(cell, dtype=torch.float32).cpu()
     pbc = torch.as_tensor(pbc, dtype=torch.bool).reshape(-1).expand(3)
     recip = torch.linalg.inv(cell).transpose(0, 1)
-    reps = [int(math.ceil(float(cutoff * torch.linalg.norm(recip[k])))) if bool(pbc[k]) else 0
+    return [int(math.ceil(float(cutoff * torch.linalg.norm(recip[k])))) if bool(pbc[k]) else 0
             for k in range(3)]
-    ranges = [torch.arange(-r, r + 1, dtype=torch.float32) for r in reps]
+
+
+def image_shifts(cell, pbc, cutoff):
+    """Cartesian image shifts ``cells @ cell`` for integer offsets in [-r, r] per periodic axis
+    (``image_reps``), in cartesian-product order -- tt_atom/geometry.py:66-75, kept in torch
+    fp32 on the CPU so the shifts are the reference's bit for bit."""
+    cell = torch.as_tensor(cell, dtype=torch.float32).cpu()
+    ranges = [torch.arange(-r, r + 1, dtype=torch.float32) for r in image_reps(cell, pbc, cutoff)]
     cells = torch.cartesian_prod(*ranges).reshape(-1, 3)
     return cells @ cell
+
+
+MAX_CELL_CAND = 256       # the cell-list kernel sorts at most this many candidates per receiver
+
+
+def cell_grid_params(cell, pbc, cutoff, N):
+    """Bins of the cell list for a fully periodic cell (see atom_cell_grid): nb bins per
+    lattice direction, each at least the cutoff (plus slack) wide across its lattice planes,
+    and the reach in bins that covers the cutoff; None when the cell is not fully periodic."""
+    if cell is None or pbc is None or not bool(np.all(np.asarray(pbc))):
+        return None
+    c = np.asarray(cell, dtype=np.float32).astype(np.float64)
+    inv = np.linalg.inv(c)
+    rc = float(cutoff) * (1.0 + 1e-5) + 1e-4
+    bn = np.linalg.norm(inv, axis=0)            # |b_k|: columns of inv(cell)
+    nb = [max(1, min(512, int(math.floor(1.0 / (rc * b))))) for b in bn]
+    while nb[0] * nb[1] * nb[2] > max(64, 4 * N):  # no more bins than atoms need
+        k = int(np.argmax(nb))
+        nb[k] = max(1, nb[k] // 2)
+    reach = [max(1, int(math.ceil(rc * b * n))) for b, n in zip(bn, nb)]
+    return dict(inv=inv, nb=nb, reach=reach, img_r=image_reps(cell, pbc, cutoff))
+
+
+class CellScratch:
+    """Device scratch of the cell list for N atoms, and the ``CellGrid`` argument over it."""
+
+    def __init__(self, params, N, dev):
+        i32 = lambda n: torch.empty(max(n, 1), dtype=torch.int32, device=dev)  # noqa: E731
+        nbins = params["nb"][0] * params["nb"][1] * params["nb"][2]
+        self.t = [i32(N), i32(3 * N), i32(nbins), i32(nbins + 1), i32(N)]
+        g = L.CellGrid()
+        for k in range(9):
+            g.inv_cell[k] = float(params["inv"].reshape(-1)[k])
+        for k in range(3):
+            g.nb[k], g.reach[k], g.img_r[k] = (params["nb"][k], params["reach"][k],
+                                               params["img_r"][k])
+        g.atom_bin, g.atom_off, g.bin_cnt, g.bin_ptr, g.bin_atoms = [t.data_ptr() for t in self.t]
+        self.grid = g
+
+    def arg(self):
+        return ctypes.byref(self.grid)
 
 
 _SHIFT_CACHE = {}
@@ -110,6 +156,7 @@ class Graph:
     max_cand: int = 64       # candidate slots per receiver the build needed
     cutoff: float = 0.0
     max_neighbors: int = 0   # 0: uncapped
+    cell_grid: dict = None   # cell-list bins (fully periodic single systems), else None
 
     def reference_order(self):
         """(edge_index [2, E] int64, image index [E]) in the reference's edge order: periodic
@@ -128,9 +175,11 @@ class Graph:
 
 
 def build_graph(pos, Z, cutoff, cell=None, pbc=None, max_neighbors=None, sys_ptr=None,
-                device="cuda", max_cand=None, stream=None):
+                device="cuda", max_cand=None, stream=None, use_cells=True):
     """Neighbour list of one system, or of several aperiodic systems stored back to back
-    (``sys_ptr`` atom offsets; no edges between systems), on the GPU."""
+    (``sys_ptr`` atom offsets; no edges between systems), on the GPU. A fully periodic single
+    system takes its candidates from a cell list (``use_cells``), others from all pairs; the
+    edge list is the same either way."""
     dev = torch.device(device)
     pos_host = None if torch.is_tensor(pos) else np.asarray(pos, dtype=np.float32)
     pos = torch.as_tensor(pos, dtype=torch.float32).to(dev).contiguous()
@@ -160,13 +209,17 @@ def build_graph(pos, Z, cutoff, cell=None, pbc=None, max_neighbors=None, sys_ptr
         pos_np = pos_host if pos_host is not None else pos.detach().cpu().numpy()
     bbox = (L.host_f32(list(pos_np.min(0)) + list(pos_np.max(0)))
             if periodic and N > 0 else None)
+    grid_params = cell_grid_params(cell, pbc, cutoff, N) if (periodic and nsys == 1 and
+                                                             use_cells) else None
+    cells = CellScratch(grid_params, N, dev) if grid_params is not None else None
     while True:
         cand_idx = torch.empty(max(N * max_cand, 1), dtype=torch.int32, device=dev)
         cand_d = torch.empty(max(N * max_cand, 1), dtype=torch.float32, device=dev)
+        grid = cells.arg() if cells is not None and max_cand <= MAX_CELL_CAND else None
         rc = L.lib().atom_neighbor_list(ptr(pos), N, sp_host, nsys, ptr(shifts), S, float(cutoff),
                                         int(periodic), cap, max_cand, ptr(cand_idx), ptr(cand_d),
                                         ptr(recv_cnt), None, None, None, None, bbox,
-                                        ptr(small), ctypes.byref(need), s)
+                                        ptr(small), ctypes.byref(need), grid, s)
         if rc == L.ATOM_ERR_CAPACITY:
             max_cand = int(need.value * 1.25) + 32
             continue
@@ -182,7 +235,7 @@ def build_graph(pos, Z, cutoff, cell=None, pbc=None, max_neighbors=None, sys_ptr
     img = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
     call("atom_neighbor_list", ptr(pos), N, sp_host, nsys, ptr(shifts), S, float(cutoff),
          int(periodic), cap, max_cand, ptr(cand_idx), ptr(cand_d), ptr(recv_cnt), ptr(recv_ptr),
-         ptr(src), ptr(tgt), ptr(img), bbox, ptr(small), None, s)
+         ptr(src), ptr(tgt), ptr(img), bbox, ptr(small), None, None, s)
     src, tgt, img = src[:E], tgt[:E], img[:E]
     send_ptr = torch.empty(N + 1, dtype=torch.int32, device=dev)
     send_eid = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
@@ -196,7 +249,8 @@ def build_graph(pos, Z, cutoff, cell=None, pbc=None, max_neighbors=None, sys_ptr
     return Graph(N=N, E=E, nsys=nsys, periodic=periodic, Z=Zt, sys_id=sys_id, sys_ptr=sys_ptr_d,
                  sys_ptr_host=sys_ptr, src=src, tgt=tgt, img=img, shifts=shifts,
                  recv_ptr=recv_ptr, send_ptr=send_ptr, send_eid=send_eid, zs=zs[:E], zt=zt[:E],
-                 max_cand=max_cand, cutoff=float(cutoff), max_neighbors=cap)
+                 max_cand=max_cand, cutoff=float(cutoff), max_neighbors=cap,
+                 cell_grid=grid_params)
 
 
 class TopologyRefresh:
@@ -225,6 +279,8 @@ class TopologyRefresh:
         self.recv_cnt, self.stage_ptr, self.csr_scratch = i32(N), i32(N + 1), i32(N)
         self.box = torch.empty(6, dtype=torch.float32, device=dev)
         self.status = torch.zeros(4, dtype=torch.int32, device=dev)
+        self.cells = (CellScratch(graph.cell_grid, N, dev)
+                      if graph.cell_grid is not None and self.max_cand <= MAX_CELL_CAND else None)
 
     def launch(self, pos, stream=None):
         g, s = self.g, L.stream_ptr(stream)
@@ -232,7 +288,7 @@ class TopologyRefresh:
              float(g.cutoff), int(g.periodic), int(g.max_neighbors), self.max_cand,
              ptr(self.cand_idx), ptr(self.cand_d), ptr(self.recv_cnt), ptr(self.stage_ptr),
              ptr(self.box), ptr(self.status), g.E, ptr(g.recv_ptr), ptr(g.src), ptr(g.tgt),
-             ptr(g.img), s)
+             ptr(g.img), self.cells.arg() if self.cells is not None else None, s)
         call("atom_sender_csr", ptr(g.src), g.E, g.N, ptr(self.csr_scratch), ptr(g.send_ptr),
              ptr(g.send_eid), s)
         call("atom_edge_species", ptr(g.Z), ptr(g.src), ptr(g.tgt), g.E, ptr(g.zs), ptr(g.zt), s)
