@@ -397,6 +397,16 @@ def run_ours(args):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    if args.profile_one_step:
+        # one captured step between profiler start / stop (ncu --profile-from-start off)
+        torch.cuda.profiler.start()
+        ws.pos.copy_(pos_dev[0])
+        step()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"profiled": "one captured step", "launches_per_step":
+                          eng.launches_per_step(ws)}))
+        return
     if ws_n > 1:
         torch.distributed.barrier()
     clk = ClockSampler(local)
@@ -639,6 +649,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cells", default="10,10,5", help="fcc cells (profiling uses a smaller cell)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--profile-one-step", action="store_true",
+                    help="profile exactly one captured step (for ncu --profile-from-start off)")
     ap.add_argument("--no-partitioned", action="store_true",
                     help="uma workload: skip the config-4 / config-5 measurements")
     ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "3xf16", "fp32", "tf32"])
