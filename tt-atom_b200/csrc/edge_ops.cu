@@ -12,6 +12,10 @@
 // are warp reductions.
 #include "common.cuh"
 
+#ifndef ATOM_RBB_ROWS
+#define ATOM_RBB_ROWS 0
+#endif
+
 namespace atom {
 
 __device__ __forceinline__ float4 f4(float a) { return make_float4(a, a, a, a); }
@@ -214,7 +218,10 @@ __device__ __forceinline__ void rotate_back_acc(const float* w, const float4* y,
 // form (edges in CSR order), so results are identical, but four times as many warps stay in
 // flight, which this gather-bound reduction over ~30 edges per node needs at a few thousand
 // nodes.
-constexpr int kCP = 128;
+#ifndef ATOM_RBR_CP
+#define ATOM_RBR_CP 128
+#endif
+constexpr int kCP = ATOM_RBR_CP;
 
 // acc[j] += s * sum over rows r of degree l(j) of W[r][j - l^2] * y[r], one channel
 __device__ __forceinline__ void rotate_back_acc_s(const float* w, const float* y, float s,
@@ -295,7 +302,10 @@ __global__ void __launch_bounds__(kCP) rotate_back_reduce_kernel(
 // -------------------------------------------------------------- rotate-back VJP (per edge)
 // two blocks per SM (<= 128 registers): 16 warps in flight instead of 8 at its natural 179
 // registers; measured 0.96 -> 0.68 ms per step despite ~100 bytes of spills
-__global__ void __launch_bounds__(256, 2) rotate_back_bwd_kernel(
+#ifndef ATOM_RBB_MINB
+#define ATOM_RBB_MINB 2
+#endif
+__global__ void __launch_bounds__(256, ATOM_RBB_MINB) rotate_back_bwd_kernel(
     const float* __restrict__ gx, const int* __restrict__ tgt, const float* __restrict__ coef,
     const float* __restrict__ env, const float* __restrict__ Y, long long E, int C,
     float* __restrict__ gY, float* __restrict__ g_env, float* __restrict__ g_coef) {
@@ -313,6 +323,23 @@ __global__ void __launch_bounds__(256, 2) rotate_back_bwd_kernel(
     for (int k = 0; k < kNnz; ++k) pc[k] = 0.f;
     float penv = 0.f;
     for (int c = lane * 4; c < C; c += 128) {
+#if ATOM_RBB_ROWS
+        // row by row: one Y row and one rotated row live at a time (same sums, same order)
+        float4 v[kNsph];
+#pragma unroll
+        for (int j = 0; j < kNsph; ++j) v[j] = ld4(gt + j * C + c);
+#pragma unroll
+        for (int r = 0; r < kNsph; ++r) {
+            const float4 yr = ld4(ye + r * C + c);
+            const float4 R = wrow_rt(w, v, r);
+            penv += dot4(R, yr);
+            st4(ge + r * C + c, make_float4(s * R.x, s * R.y, s * R.z, s * R.w));
+            const int l = row_deg(r), o = row_off(r), c0 = deg_col0(l);
+#pragma unroll
+            for (int jj = 0; jj < 5; ++jj)
+                if (jj < 2 * l + 1) pc[o + jj] += dot4(v[c0 + jj], yr);
+        }
+#else
         float4 v[kNsph], y[kNsph];
 #pragma unroll
         for (int j = 0; j < kNsph; ++j) {
@@ -333,6 +360,7 @@ __global__ void __launch_bounds__(256, 2) rotate_back_bwd_kernel(
             const int l = row_deg(r), o = row_off(r), c0 = deg_col0(l);
             for (int jj = 0; jj < 2 * l + 1; ++jj) pc[o + jj] += dot4(v[c0 + jj], y[r]);
         }
+#endif
     }
     penv = warp_sum(penv);
     float tail[3];
@@ -346,7 +374,13 @@ __global__ void __launch_bounds__(256, 2) rotate_back_bwd_kernel(
 // launched in 64-thread blocks (finer block retirement: 1.89 -> 1.77 ms per step at 255
 // registers), capped at 204 registers for 5 blocks per SM (76 bytes of spills; 1.74 -> 1.57 ms;
 // 6 blocks per SM measured slower, 8 about the same)
-__global__ void __launch_bounds__(64, 5) rotate_in_bwd_edge_kernel(
+#ifndef ATOM_RIBE_MINB
+#define ATOM_RIBE_MINB 5
+#endif
+#ifndef ATOM_RIBE_THREADS
+#define ATOM_RIBE_THREADS 64
+#endif
+__global__ void __launch_bounds__(ATOM_RIBE_THREADS, ATOM_RIBE_MINB) rotate_in_bwd_edge_kernel(
     const float* __restrict__ gA, const float* __restrict__ rot, const float* __restrict__ rad,
     long long ldr, int rad_col, const float* __restrict__ x, const int* __restrict__ src,
     const int* __restrict__ tgt, const float* __restrict__ coef, long long E, int C,
@@ -651,7 +685,8 @@ extern "C" int atom_rotate_in_bwd_edge(const float* gA, const float* rot, const 
     if (int s = check_c(C)) return s;
     ATOM_REQUIRE(ldr % 4 == 0 && rad_col % 4 == 0, "rad must be float4-aligned");
     if (E == 0) return ATOM_OK;
-    rotate_in_bwd_edge_kernel<<<ceil_div((long long)E * 32, 64), 64, 0, (cudaStream_t)stream>>>(gA, rot, rad, ldr, rad_col, x, src, tgt, coef,
+    rotate_in_bwd_edge_kernel<<<ceil_div((long long)E * 32, ATOM_RIBE_THREADS), ATOM_RIBE_THREADS,
+                                0, (cudaStream_t)stream>>>(gA, rot, rad, ldr, rad_col, x, src, tgt, coef,
                                                 E, C, g_rot, g_rad, g_coef);
     ATOM_CHECK_LAUNCH("rotate_in_bwd_edge");
     return ATOM_OK;
