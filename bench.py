@@ -513,7 +513,7 @@ def run_ours(args):
         out["screen"] = measure_screen(args, steps=5, warmup=2)
         out["slab"] = measure_slab(args, steps=3, warmup=2)
     if rank == 0:
-        if not args.no_cpu:
+        if not args.no_cpu and ws_n == 1:        # the CPU baseline leg runs at N = 1 only
             cpu = cpu_baseline(bounded=True, workload=args.workload)
             cpu.pop("cfg")
             out["cpu_baseline"] = cpu
