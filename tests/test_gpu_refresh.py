@@ -139,3 +139,23 @@ def test_cell_list_on_the_benchmark_cells(name):
     assert a.E == b.E == cap * len(s["Z"])
     for k in ("src", "tgt", "img", "recv_ptr", "send_ptr", "send_eid"):
         assert torch.equal(getattr(a, k), getattr(b, k)), k
+
+
+def test_traced_orb_calculator_refreshes_on_the_device():
+    from tt_atom.orb import OrbCalculator
+    cfg = configs.orb_config("orb-v3")
+    w = configs.orb_random_weights(cfg, seed=0)
+    s = configs.amorphous_sio2(n_si=40, n_o=80, seed=2)
+    rng = np.random.default_rng(4)
+    traced = OrbCalculator(w, cfg=cfg, trace=True)
+    eager = OrbCalculator(w, cfg=cfg, trace=False)
+    used = 0
+    for k in range(4):
+        p = s["pos"] + rng.normal(0.0, 0.05, s["pos"].shape)
+        for c in (traced, eager):
+            c.calculate(SimpleAtoms(s["Z"], p, s["cell"], True), ("energy", "forces", "stress"))
+        used += int(getattr(traced, "_full_step", None) is not None)
+        assert traced.results["energy"] == eager.results["energy"]
+        assert np.array_equal(traced.results["forces"], eager.results["forces"])
+        assert np.array_equal(traced.results["stress"], eager.results["stress"])
+    assert used >= 2

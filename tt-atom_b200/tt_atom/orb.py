@@ -373,6 +373,7 @@ class OrbWorkspace:
             for k in self._TOPOLOGY:
                 getattr(self.graph, k).copy_(getattr(graph, k))
             self.graph.sys_ptr_host = list(graph.sys_ptr_host)
+            self.graph.max_cand = max(self.graph.max_cand, graph.max_cand)
         graph = self.graph
         eng = self._eng
         call("atom_node_embed", ptr(graph.Z), None, ptr(eng.emb), ptr(eng.zero_row), graph.N,
@@ -492,14 +493,55 @@ class OrbCalculator(_AseCalculator):
         S = ws.sraw[0, :6].double().cpu() if stress else None
         return E, F, S
 
+    def _system_key(self, Z, cell, pbc, forces, stress, charge, spin):
+        Z = np.asarray(Z, dtype=np.int64)
+        return (Z.shape[0], Z.tobytes(),
+                None if cell is None else np.asarray(cell, np.float32).tobytes(),
+                None if pbc is None else tuple(np.broadcast_to(np.asarray(pbc, bool), 3)),
+                bool(forces), bool(stress), float(charge), float(spin))
+
+    def _refresh_step(self, pos, key, forces, stress, device_out):
+        """Traced evaluation of the previous call's system at new positions: one captured graph
+        rebuilds the neighbour list on the device and runs the model pass (see
+        TTAtomCalculator); None when it does not apply or the edge count changed."""
+        from .graph import TopologyRefresh
+        ws = self._ws
+        if ws is None or getattr(self, "_refresh_key", None) != key:
+            return None
+        full = getattr(self, "_full_step", None)
+        ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))
+        if full is None or full[0] is not ws:
+            refresh = TopologyRefresh(ws.graph)
+            step = CapturedStep(self.engine, ws, forces=forces, virial=stress,
+                                prelude=lambda st: refresh.launch(ws.pos, st))
+            self._full_step = full = (ws, refresh, step)
+        _, refresh, step = full
+        step()
+        if device_out:
+            if int(refresh.status[0]) != TopologyRefresh.OK:
+                self._refresh_key = self._full_step = None
+                return None
+            return ws.energy, ws.forces, (ws.virial if stress else None)
+        E, F, V, st = to_host(ws.energy, ws.forces, ws.virial if stress else None,
+                              refresh.status[:1])
+        if int(st[0]) != TopologyRefresh.OK:
+            self._refresh_key = self._full_step = None
+            return None
+        return float(E[0]), F, V
+
     def _evaluate(self, pos, Z, cell, pbc, forces=True, stress=False, device_out=False,
                   charge=0.0, spin=0.0):
+        key = self._system_key(Z, cell, pbc, forces, stress, charge, spin)
+        if self.trace:
+            fast = self._refresh_step(pos, key, forces, stress, device_out)
+            if fast is not None:
+                return fast
         g = build_graph(pos, Z, self.cfg["cutoff"], cell, pbc, max_neighbors=self.max_nbrs,
                         device=self.device)
         if g.E == 0:
             raise ValueError("no edges within cutoff — system too sparse for this model")
         if self._ws is None or not self._ws.fits(g):
-            self._ws = self._step = None        # free the old buffers first
+            self._ws = self._step = self._full_step = None   # free the old buffers first
             self._ws = self.engine.workspace(g)
         else:
             self._ws.rebind(g)                  # same sizes: reuse the buffers
@@ -514,6 +556,8 @@ class OrbCalculator(_AseCalculator):
             self._step()
         else:
             self.engine.run(ws, forces=forces, virial=stress)
+        # a later traced call on this system may rebuild its list on the device in the graph
+        self._refresh_key = key if (self.trace and g.nsys == 1) else None
         if device_out:      # device tensors the next call overwrites
             return ws.energy, ws.forces, (ws.virial if stress else None)
         E, F, V = to_host(ws.energy, ws.forces, ws.virial if stress else None)
@@ -593,6 +637,7 @@ class OrbCalculator(_AseCalculator):
         """Release the device workspace and any captured step (tt_atom/ase_base.py:33)."""
         self._ws = None
         self._step = self._step_key = None
+        self._full_step = self._refresh_key = None
 
     def evaluate_batch(self, systems, properties=("energy", "forces")):
         """Energies (and forces) of several systems (tt_atom/orb_calculator.py:217-327): the same
