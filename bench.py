@@ -19,6 +19,8 @@ cutoff 6 A, at most 30 neighbours), random-init fp32 weights (seed 0).
   collectives, through ``evaluate_batch``) and ``slab`` (config 5: the 65,536-atom bcc Fe cell
   slab-decomposed over the ranks, NCCL halo exchange per layer and an all-reduce of energy and
   virial, with the collectives' CUDA-event time per step and the limiting one named).
+* ``orb``: config 3 (Orb-v3 shape, 1,002-atom SiO2) at the same N, device step and end to end.
+* ``md``: GPU-resident Langevin MD on the config-2 cell (neighbour list rebuilt every step).
 * ``--impl reference``: the reference's CPU path (this repo's CPU restatement of it, the oracle)
   on the box's host cores, on the same full workload, median of the timed steps.
 """
@@ -354,6 +356,66 @@ def measure_screen(args, steps, warmup):
     return out
 
 
+def measure_orb(args, steps, warmup):
+    """Config 3 at this N (replicas): the Orb-v3-shape 1,002-atom SiO2 step replayed from a
+    CUDA graph (value), end to end through ``OrbCalculator.calculate`` (e2e), and the
+    edge-MLP hidden GEMM's tensor roofline. Returns rank 0's dict."""
+    from tt_atom import configs
+    from tt_atom.ase_compat import SimpleAtoms
+    from tt_atom.engine import CapturedStep
+    from tt_atom.orb import OrbCalculator
+    ws_n, rank, local, device = init_dist()
+    cfg = configs.orb_config("orb-v3")
+    s = configs.amorphous_sio2()
+    calc = OrbCalculator(configs.orb_random_weights(cfg, seed=0), cfg=cfg, device=device,
+                         precision=args.precision)
+    calc._evaluate(s["pos"], s["Z"], s["cell"], [True] * 3, True, True)
+    ws, eng = calc._ws, calc.engine
+    step = CapturedStep(eng, ws, forces=True, virial=True)
+    for _ in range(warmup):
+        step()
+    _barrier(ws_n)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    kern = eng.time_kernels(ws, reps=3)
+    calc.trace = True
+    atoms = SimpleAtoms(s["Z"], s["pos"], s["cell"], True)
+    rng = np.random.default_rng(99)
+    jit = [SimpleAtoms(s["Z"], s["pos"] + rng.normal(0.0, 0.01, s["pos"].shape), s["cell"], True)
+           for _ in range(steps)]
+    for _ in range(max(1, warmup)):
+        calc.calculate(atoms, ("energy", "forces", "stress"))
+    torch.cuda.synchronize()
+    te = time.perf_counter()
+    for a in jit:
+        calc.calculate(a, ("energy", "forces", "stress"))
+    e2e_ms = 1e3 * (time.perf_counter() - te) / len(jit)
+    ms, e2e_ms = _max_over_ranks([ms, e2e_ms], device, ws_n)
+    N = len(s["Z"])
+    _, bf16, src = peaks()
+    ach = kern["flop"] / (kern["ms"] / 1e3) / 1e12
+    out = {"metric": METRIC, "value": N * ws_n * steps / (ms / 1e3), "unit": "atom-steps/s",
+           "n_gpus": ws_n, "steps": steps, "warmup": warmup, "ms_per_step": ms / steps,
+           "scaling": "weak", "dtype": "fp32", "data": DATA["orb"],
+           "config": workload_config("orb", N, ws.graph.E,
+                                     dict(cfg, max_neighbors=cfg["max_num_neighbors"]), ws_n),
+           "e2e": {"value": N * ws_n / (e2e_ms / 1e3), "unit": "atom-steps/s",
+                   "h2d_bytes_per_step": N * 3 * 4 + N * 8,
+                   "d2h_bytes_per_step": 8 + N * 3 * 8 + 9 * 8},
+           "roofline": {"bound": "tensor", "kernel": kern["name"], "achieved": ach,
+                        "peak": bf16, "unit": "TFLOP/s", "frac": ach / bf16,
+                        "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)",
+                        "launch_ms": kern["ms"]}}
+    del step, ws, calc, eng
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_standalone(args, measure):
     out = measure(args, args.steps, args.warmup)
     ws_n, rank, _ = dist_env()
@@ -512,6 +574,8 @@ def run_ours(args):
         # no collectives) and config 5 (65,536-atom slab, halo exchange + all-reduce)
         out["screen"] = measure_screen(args, steps=5, warmup=2)
         out["slab"] = measure_slab(args, steps=3, warmup=2)
+        # config 3 (Orb-v3 shape) at this N, from the same launch
+        out["orb"] = measure_orb(args, steps=20, warmup=3)
     if rank == 0:
         if not args.no_cpu and ws_n == 1:        # the CPU baseline leg runs at N = 1 only
             cpu = cpu_baseline(bounded=True, workload=args.workload)
