@@ -351,7 +351,8 @@ def measure_screen(args, steps, warmup):
                       "timing": "end to end through evaluate_batch (host inputs, GPU "
                                 "neighbour lists, host results)"},
            "clocks": clocks}
-    del calc
+    calc.close()
+    torch.cuda.synchronize()
     torch.cuda.empty_cache()
     return out
 
@@ -411,7 +412,9 @@ def measure_orb(args, steps, warmup):
                         "peak": bf16, "unit": "TFLOP/s", "frac": ach / bf16,
                         "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)",
                         "launch_ms": kern["ms"]}}
-    del step, ws, calc, eng
+    calc.close()
+    del step, ws, eng
+    torch.cuda.synchronize()
     torch.cuda.empty_cache()
     return out
 
@@ -567,7 +570,10 @@ def run_ours(args):
     if cells != (10, 10, 5):
         out["config"]["workload"] += f" (reduced: {cells} cells, not the headline size)"
     out["config"]["positions"] = "re-jittered every step (0.01 A)"
-    del step, ws, calc, eng, pos_dev
+    # release this workload's buffers and captured graphs before the next measurements
+    calc.close()
+    del step, ws, eng, pos_dev
+    torch.cuda.synchronize()
     torch.cuda.empty_cache()
     if args.workload == "uma" and not args.no_partitioned:
         # the partitioned configurations at this N, from the same launch: config 4 (screening,
