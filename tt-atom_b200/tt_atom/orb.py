@@ -531,9 +531,9 @@ class OrbCalculator(_AseCalculator):
 
     def _evaluate(self, pos, Z, cell, pbc, forces=True, stress=False, device_out=False,
                   charge=0.0, spin=0.0):
-        key = self._system_key(Z, cell, pbc, forces, stress, charge, spin)
+        skey = self._system_key(Z, cell, pbc, forces, stress, charge, spin)
         if self.trace:
-            fast = self._refresh_step(pos, key, forces, stress, device_out)
+            fast = self._refresh_step(pos, skey, forces, stress, device_out)
             if fast is not None:
                 return fast
         g = build_graph(pos, Z, self.cfg["cutoff"], cell, pbc, max_neighbors=self.max_nbrs,
@@ -557,7 +557,7 @@ class OrbCalculator(_AseCalculator):
         else:
             self.engine.run(ws, forces=forces, virial=stress)
         # a later traced call on this system may rebuild its list on the device in the graph
-        self._refresh_key = key if (self.trace and g.nsys == 1) else None
+        self._refresh_key = skey if (self.trace and g.nsys == 1) else None
         if device_out:      # device tensors the next call overwrites
             return ws.energy, ws.forces, (ws.virial if stress else None)
         E, F, V = to_host(ws.energy, ws.forces, ws.virial if stress else None)
