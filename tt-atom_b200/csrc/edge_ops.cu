@@ -15,6 +15,12 @@
 #ifndef ATOM_RBB_ROWS
 #define ATOM_RBB_ROWS 0
 #endif
+#ifndef ATOM_RBB_LEAN
+#define ATOM_RBB_LEAN 0
+#endif
+#ifndef ATOM_RIBE_LEAN
+#define ATOM_RIBE_LEAN 0
+#endif
 
 namespace atom {
 
@@ -370,6 +376,65 @@ __global__ void __launch_bounds__(256, ATOM_RBB_MINB) rotate_back_bwd_kernel(
     if (lane == 0) g_env[e] += penv;
 }
 
+// Lean form for C = 128 (one float4 per lane covers the row): the coefficients stay in the
+// lanes that loaded them and are broadcast by shuffles when used, and each coefficient adjoint
+// is summed over the warp as soon as its per-lane dot product exists, so neither the 35
+// coefficients nor 35 partial sums occupy registers per lane. More loads stay in flight.
+#ifndef ATOM_RBB_LEAN_MINB
+#define ATOM_RBB_LEAN_MINB 3
+#endif
+__global__ void __launch_bounds__(256, ATOM_RBB_LEAN_MINB) rotate_back_bwd_lean_kernel(
+    const float* __restrict__ gx, const int* __restrict__ tgt, const float* __restrict__ coef,
+    const float* __restrict__ env, const float* __restrict__ Y, long long E,
+    float* __restrict__ gY, float* __restrict__ g_env, float* __restrict__ g_coef) {
+    constexpr int C = 128;
+    const long long e = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (e >= E) return;
+    const float* cr = coef + e * kNnz;
+    const float wa = __ldg(cr + lane);
+    const float wb = lane < kNnz - 32 ? __ldg(cr + 32 + lane) : 0.f;
+    const float s = env[e];
+    const int c = lane * 4;
+    const float* gt = gx + (long long)tgt[e] * kNsph * C + c;
+    const float* ye = Y + e * kNsph * C + c;
+    float* ge = gY + e * kNsph * C + c;
+    float4 v[kNsph], y[kNsph];
+#pragma unroll
+    for (int j = 0; j < kNsph; ++j) {
+        v[j] = ld4(gt + j * C);
+        y[j] = ld4(ye + j * C);
+    }
+    float penv = 0.f, mine = 0.f, tail = 0.f;
+#pragma unroll
+    for (int r = 0; r < kNsph; ++r) {
+        const int l = row_deg(r), o = row_off(r), c0 = deg_col0(l);
+        float4 R = f4(0.f);
+#pragma unroll
+        for (int jj = 0; jj < 2 * l + 1; ++jj) {
+            const int k = o + jj;
+            const float wk = __shfl_sync(0xffffffffu, k < 32 ? wa : wb, k & 31);
+            fma4(R, wk, v[c0 + jj]);
+        }
+        penv += dot4(R, y[r]);
+        st4(ge + r * C, make_float4(s * R.x, s * R.y, s * R.z, s * R.w));
+#pragma unroll
+        for (int jj = 0; jj < 2 * l + 1; ++jj) {
+            const int k = o + jj;
+            const float d = warp_sum(dot4(v[c0 + jj], y[r]));
+            if (k < 32) {
+                if (lane == k) mine = d;
+            } else if (lane == k - 32) {
+                tail = d;
+            }
+        }
+    }
+    penv = warp_sum(penv);
+    g_coef[e * kNnz + lane] += s * mine;
+    if (lane < kNnz - 32) g_coef[e * kNnz + 32 + lane] += s * tail;
+    if (lane == 0) g_env[e] += penv;
+}
+
 // ------------------------------------------------------------ rotate-in VJP (edge part)
 // launched in 64-thread blocks (finer block retirement: 1.89 -> 1.77 ms per step at 255
 // registers), capped at 204 registers for 5 blocks per SM (76 bytes of spills; 1.74 -> 1.57 ms;
@@ -435,6 +500,83 @@ __global__ void __launch_bounds__(ATOM_RIBE_THREADS, ATOM_RIBE_MINB) rotate_in_b
     const float mine = warp_sum35(pc, tail);
     g_coef[e * kNnz + lane] += mine;
     if (lane < 3) g_coef[e * kNnz + 32 + lane] += tail[lane];
+}
+
+// Lean form for C = 128, as rotate_back_bwd_lean_kernel: coefficients broadcast by shuffles
+// from the lanes that loaded them, each coefficient adjoint summed over the warp per channel
+// half as soon as it exists (the two halves' sums then added), so the per-lane state is the
+// node rows and the radial-slice adjoints only.
+#ifndef ATOM_RIBE_LEAN_MINB
+#define ATOM_RIBE_LEAN_MINB 3
+#endif
+__global__ void __launch_bounds__(256, ATOM_RIBE_LEAN_MINB) rotate_in_bwd_edge_lean_kernel(
+    const float* __restrict__ gA, const float* __restrict__ rot, const float* __restrict__ rad,
+    long long ldr, int rad_col, const float* __restrict__ x, const int* __restrict__ src,
+    const int* __restrict__ tgt, const float* __restrict__ coef, long long E,
+    float* __restrict__ g_rot, float* __restrict__ g_rad, float* __restrict__ g_coef) {
+    constexpr int C = 128, W2 = 2 * C;
+    const long long e = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (e >= E) return;
+    const float* cr = coef + e * kNnz;
+    const float wa = __ldg(cr + lane);
+    const float wb = lane < kNnz - 32 ? __ldg(cr + 32 + lane) : 0.f;
+    const int c = lane * 4;
+    const float* ga = gA + e * kNsph * W2 + c;
+    const float* rr = rad + e * ldr + rad_col + c;
+    float* gr = g_rot + e * kNsph * W2 + c;
+    float* grd = g_rad + e * ldr + rad_col + c;
+    const float* xs = x + (long long)src[e] * kNsph * C + c;
+    const float* xt = x + (long long)tgt[e] * kNsph * C + c;
+    float mine = 0.f, tail = 0.f;
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+        const float* xh = half ? xt : xs;
+        const int ho = half * C;
+        float4 v[kNsph];
+#pragma unroll
+        for (int j = 0; j < kNsph; ++j) v[j] = ld4(xh + j * C);
+        float4 gsl[6];
+#pragma unroll
+        for (int q = 0; q < 6; ++q) gsl[q] = f4(0.f);
+        float hm = 0.f, ht = 0.f;
+#pragma unroll
+        for (int r = 0; r < kNsph; ++r) {
+            const int q = rad_slice(r), l = row_deg(r), o = row_off(r), c0 = deg_col0(l);
+            const float4 gav = ld4(ga + r * W2 + ho);
+            const float4 g = mul4(gav, ld4(rr + q * W2 + ho));
+            st4(gr + r * W2 + ho, g);
+            float4 rv;
+            if (rot) {
+                rv = ld4(rot + e * kNsph * W2 + r * W2 + ho + c);
+            } else {
+                rv = f4(0.f);
+#pragma unroll
+                for (int jj = 0; jj < 2 * l + 1; ++jj) {
+                    const int k = o + jj;
+                    fma4(rv, __shfl_sync(0xffffffffu, k < 32 ? wa : wb, k & 31), v[c0 + jj]);
+                }
+            }
+            const float4 p = mul4(gav, rv);
+            gsl[q].x += p.x; gsl[q].y += p.y; gsl[q].z += p.z; gsl[q].w += p.w;
+#pragma unroll
+            for (int jj = 0; jj < 2 * l + 1; ++jj) {
+                const int k = o + jj;
+                const float d = warp_sum(dot4(g, v[c0 + jj]));
+                if (k < 32) {
+                    if (lane == k) hm = d;
+                } else if (lane == k - 32) {
+                    ht = d;
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 6; ++q) st4(grd + q * W2 + ho, gsl[q]);
+        mine += hm;
+        tail += ht;
+    }
+    g_coef[e * kNnz + lane] += mine;
+    if (lane < kNnz - 32) g_coef[e * kNnz + 32 + lane] += tail;
 }
 
 // acc[j] += sum over rows r of degree l(j) of W[r][j - l^2] * g[r]   (Wig^T g)
@@ -673,7 +815,13 @@ extern "C" int atom_rotate_back_bwd(const float* gx, const int* tgt, const float
                                     float* gY, float* g_env, float* g_coef, void* stream) {
     if (int s = check_c(C)) return s;
     if (E == 0) return ATOM_OK;
-    rotate_back_bwd_kernel<<<WARP_GRID(E)>>>(gx, tgt, coef, env, Y, E, C, gY, g_env, g_coef);
+#if ATOM_RBB_LEAN
+    if (C == 128)
+        rotate_back_bwd_lean_kernel<<<WARP_GRID(E)>>>(gx, tgt, coef, env, Y, E, gY, g_env,
+                                                      g_coef);
+    else
+#endif
+        rotate_back_bwd_kernel<<<WARP_GRID(E)>>>(gx, tgt, coef, env, Y, E, C, gY, g_env, g_coef);
     ATOM_CHECK_LAUNCH("rotate_back_bwd");
     return ATOM_OK;
 }
@@ -685,6 +833,14 @@ extern "C" int atom_rotate_in_bwd_edge(const float* gA, const float* rot, const 
     if (int s = check_c(C)) return s;
     ATOM_REQUIRE(ldr % 4 == 0 && rad_col % 4 == 0, "rad must be float4-aligned");
     if (E == 0) return ATOM_OK;
+#if ATOM_RIBE_LEAN
+    if (C == 128) {
+        rotate_in_bwd_edge_lean_kernel<<<WARP_GRID(E)>>>(gA, rot, rad, ldr, rad_col, x, src, tgt,
+                                                         coef, E, g_rot, g_rad, g_coef);
+        ATOM_CHECK_LAUNCH("rotate_in_bwd_edge");
+        return ATOM_OK;
+    }
+#endif
     rotate_in_bwd_edge_kernel<<<ceil_div((long long)E * 32, ATOM_RIBE_THREADS), ATOM_RIBE_THREADS,
                                 0, (cudaStream_t)stream>>>(gA, rot, rad, ldr, rad_col, x, src, tgt, coef,
                                                 E, C, g_rot, g_rad, g_coef);
