@@ -488,6 +488,8 @@ def run_ours(args):
     # ---- dominant kernel, timed live with CUDA events on its own stream
     kern = eng.time_kernels(ws, reps=3)
     edge = eng.time_edge_kernel(ws, reps=3) if hasattr(eng, "time_edge_kernel") else None
+    edge_all = (eng.time_edge_kernels(ws, reps=5) if hasattr(eng, "time_edge_kernels")
+                and ws.chunks is None else None)
     # ---- end to end through the public API (host positions in, host results out)
     atoms = SimpleAtoms(s["Z"], s["pos"], cell, True)
     # the calculator's trace option (the reference's Calculator(trace=True)): the step is
@@ -567,6 +569,9 @@ def run_ours(args):
                                 "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
                                 "peak_source": f"{src} HBM copy (MEASURED_PEAKS.json)",
                                 "launch_ms": edge["ms"], "bytes_per_launch": edge["bytes"]}
+    if edge_all is not None:
+        # every HBM-bound edge kernel of layer 0 (forward and reverse) against the HBM roofline
+        out["edge_kernels"] = [dict(k, frac=k["gbs"] / hbm) for k in edge_all]
     if cells != (10, 10, 5):
         out["config"]["workload"] += f" (reduced: {cells} cells, not the headline size)"
     out["config"]["positions"] = "re-jittered every step (0.01 A)"

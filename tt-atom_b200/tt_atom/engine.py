@@ -428,6 +428,61 @@ class UMAEngine:
         return dict(name="rotate_in (Wigner rotation x radial)", ms=t0.elapsed_time(t1) / reps,
                     bytes=nbytes)
 
+    def time_edge_kernels(self, ws, reps=5, layer=0):
+        """CUDA-event time per launch of each HBM-bound edge kernel of one layer (forward and
+        reverse), run on ``ws``'s current buffers, with its algorithmic bytes per launch (each
+        input and output array once; node rows once per table) and the achieved rate. Needs a
+        workspace that has run a full step (unchunked)."""
+        g = ws.graph
+        E, N, C, H, i = g.E, g.N, self.C, self.H, layer
+        st = torch.cuda.Stream(device=self.device)
+        st.wait_stream(torch.cuda.current_stream())
+        s = st.cuda_stream
+        nodes = N * 9 * C
+        kern = [
+            ("rotate_in", lambda: call(
+                "atom_rotate_in", ptr(ws.nb[i]), ptr(g.src), ptr(g.tgt), ptr(ws.coef), E, C,
+                ptr(ws.RAD), self.ldr, self.rad_off[i], None, ptr(ws.A1), s),
+             nodes + E * (12 * C + 35 + 2 + 18 * C)),
+            ("gate_fwd", lambda: call("atom_gate_fwd", ptr(ws.Y1[i]), E, H, ptr(ws.Gt), s),
+             E * 20 * H),
+            ("rotate_back_reduce", lambda: call(
+                "atom_rotate_back_reduce", ptr(ws.Y2[i]), ptr(ws.coef), ptr(ws.env), N, C,
+                ptr(g.recv_ptr), ptr(ws.x[i]), ptr(ws.xm[i]), s),
+             E * (9 * C + 35 + 1) + 2 * nodes + N),
+            ("rotate_back_bwd", lambda: call(
+                "atom_rotate_back_bwd", ptr(ws.gx), ptr(g.tgt), ptr(ws.coef), ptr(ws.env),
+                ptr(ws.Y2[i]), E, C, ptr(ws.gY2), ptr(ws.g_env), ptr(ws.g_coef), s),
+             nodes + E * (9 * C + 2 * 35 + 2 + 1 + 9 * C)),
+            ("gate_bwd", lambda: call("atom_gate_bwd", ptr(ws.Y1[i]), ptr(ws.Gt), E, H,
+                                      ptr(ws.gY1), s), E * 31 * H),
+            ("rotate_in_bwd_edge", lambda: call(
+                "atom_rotate_in_bwd_edge", ptr(ws.A1), None, ptr(ws.RAD), self.ldr,
+                self.rad_off[i], ptr(ws.nb[i]), ptr(g.src), ptr(g.tgt), ptr(ws.coef), E, C,
+                ptr(ws.grot), ptr(ws.gRAD), ptr(ws.g_coef), s),
+             nodes + E * (18 * C + 12 * C + 2 * 35 + 2 + 18 * C + 12 * C)),
+            ("rotate_in_bwd_node", lambda: call(
+                "atom_rotate_in_bwd_node", ptr(ws.grot), ptr(ws.coef), N, C, ptr(g.recv_ptr),
+                ptr(g.send_ptr), ptr(g.send_eid), 0, ptr(ws.gn), s),
+             E * (18 * C + 2 * 35 + 1) + 2 * N + nodes),
+        ]
+        out = []
+        with torch.cuda.stream(st):
+            for name, fn, floats in kern:
+                fn()
+                t0 = torch.cuda.Event(enable_timing=True)
+                t1 = torch.cuda.Event(enable_timing=True)
+                t0.record(st)
+                for _ in range(reps):
+                    fn()
+                t1.record(st)
+                st.synchronize()
+                ms = t0.elapsed_time(t1) / reps
+                out.append(dict(kernel=name, ms=ms, bytes=4 * floats,
+                                gbs=4 * floats / (ms / 1e3) / 1e9))
+        torch.cuda.current_stream().wait_stream(st)
+        return out
+
     # --------------------------------------------------------------------------------- step
     def run(self, ws, pos, forces=True, virial=False, stream=None):
         """One E (+F, +virial) evaluation for ``pos`` [N, 3] (device fp32) on ``ws``'s graph.
