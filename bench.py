@@ -419,6 +419,55 @@ def measure_orb(args, steps, warmup):
     return out
 
 
+def measure_tiny(args, steps, warmup):
+    """Config 1 (the reference's CPU-runnable case): the tiny eSCN-MD model on the 24-atom
+    molecule, energy + forces, device step replayed from a CUDA graph and end to end through
+    ``calculate``. Launch-bound at this size; reported for completeness."""
+    from tt_atom import configs
+    from tt_atom.ase_compat import SimpleAtoms
+    from tt_atom.calculator import TTAtomCalculator
+    from tt_atom.engine import CapturedStep
+    from tt_atom.weights import WeightBundle
+    ws_n, rank, local, device = init_dist()
+    cfg = configs.model_config("tiny")
+    calc = TTAtomCalculator(WeightBundle.from_arrays(configs.random_bundle_arrays(cfg, seed=0)),
+                            device=device, precision=args.precision)
+    m = configs.tiny_molecule(seed=0)
+    calc._evaluate(m["pos"], m["Z"], None, None, [0.0], [0.0], forces=True)
+    step = CapturedStep(calc.engine, calc._ws, forces=True, virial=False)
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    calc.trace = True
+    atoms = SimpleAtoms(m["Z"], m["pos"])
+    for _ in range(max(1, warmup)):
+        calc.calculate(atoms)
+    te = time.perf_counter()
+    for _ in range(steps):
+        calc.calculate(atoms)
+    e2e_ms = 1e3 * (time.perf_counter() - te) / steps
+    ms, e2e_ms = _max_over_ranks([ms, e2e_ms], device, ws_n)
+    N = len(m["Z"])
+    calc.close()
+    return {"metric": "atom-steps/s (E+F)", "value": N * ws_n * steps / (ms / 1e3),
+            "unit": "atom-steps/s", "ms_per_step": ms / steps, "steps": steps,
+            "config": {"workload": "tiny eSCN-MD (16 channels, 2 layers), 24-atom molecule, E+F",
+                       "atoms_per_gpu": N, "edges_per_gpu": calc_edges(m, cfg)},
+            "e2e": {"value": N * ws_n / (e2e_ms / 1e3), "unit": "atom-steps/s"}}
+
+
+def calc_edges(m, cfg):
+    from tt_atom.graph import build_graph
+    return build_graph(m["pos"], m["Z"], cfg["cutoff"], max_neighbors=cfg.get("max_neighbors")).E
+
+
 def run_standalone(args, measure):
     out = measure(args, args.steps, args.warmup)
     ws_n, rank, _ = dist_env()
@@ -587,6 +636,7 @@ def run_ours(args):
         out["slab"] = measure_slab(args, steps=3, warmup=2)
         # config 3 (Orb-v3 shape) at this N, from the same launch
         out["orb"] = measure_orb(args, steps=20, warmup=3)
+        out["tiny"] = measure_tiny(args, steps=20, warmup=3)        # config 1
     if rank == 0:
         if not args.no_cpu and ws_n == 1:        # the CPU baseline leg runs at N = 1 only
             cpu = cpu_baseline(bounded=True, workload=args.workload)
