@@ -178,6 +178,36 @@ def _orb_host_terms(ref_root, out, covalent_radii):
     arrays["denorm_out"] = np.array([
         float(host_energy_denormalize(raw[k], Z_p, len(Z_p), running_mean=mean,
                                       running_var=var, ref_weight=refw)) for k in range(3)])
+    # the other host-side normalisers and the OrbMol conditioning vector
+    from tt_atom.orb_model import (host_charge_spin_embedding, host_conservative_force_denormalize,
+                                   host_conservative_stress, host_force_denormalize,
+                                   host_stress_denormalize)
+    fmean, fvar = torch.randn(1, generator=g, dtype=torch.float64), torch.rand(1, generator=g,
+                                                                               dtype=torch.float64) + 0.5
+    raw_f = torch.randn(7, 3, generator=g, dtype=torch.float64)
+    st = [torch.randn(1, generator=g, dtype=torch.float64) for _ in range(2)]
+    sv = [torch.rand(1, generator=g, dtype=torch.float64) + 0.5 for _ in range(2)]
+    raw_s = torch.randn(6, generator=g, dtype=torch.float64)
+    vir = torch.randn(3, 3, generator=g, dtype=torch.float64)
+    arrays.update(fnorm_mean=fmean.numpy(), fnorm_var=fvar.numpy(), fnorm_raw=raw_f.numpy(),
+                  fnorm_out=host_force_denormalize(raw_f, running_mean=fmean,
+                                                   running_var=fvar).numpy(),
+                  snorm_dmean=st[0].numpy(), snorm_omean=st[1].numpy(),
+                  snorm_dvar=sv[0].numpy(), snorm_ovar=sv[1].numpy(), snorm_raw=raw_s.numpy(),
+                  snorm_out=host_stress_denormalize(raw_s, diag_mean=st[0], diag_var=sv[0],
+                                                    offdiag_mean=st[1],
+                                                    offdiag_var=sv[1]).numpy(),
+                  cons_forces=host_conservative_force_denormalize(raw_f, 48,
+                                                                  running_var=var).numpy(),
+                  cons_virial=vir.numpy(),
+                  cons_stress=host_conservative_stress(vir, 48, cell, running_var=var).numpy())
+    W_c = torch.randn(128, generator=g, dtype=torch.float64)
+    W_s = torch.randn(128, generator=g, dtype=torch.float64)
+    cw = {"conditioner.charge_embedding.W": W_c, "conditioner.spin_embedding.W": W_s}
+    arrays.update(cs_Wc=W_c.numpy(), cs_Ws=W_s.numpy())
+    for tag, (q, sp) in {"a": (-1.0, 2.0), "b": (0.0, 0.0), "c": (2.0, 1.0)}.items():
+        arrays[f"cs_{tag}"] = np.array([q, sp])
+        arrays[f"cs_out_{tag}"] = host_charge_spin_embedding(cw, q, sp, 2, 512)[0].numpy()
     np.savez_compressed(HERE / out, **arrays)
     del sys.modules["ase"], sys.modules["ase.data"]
     print("wrote", out, {k: np.shape(v) for k, v in arrays.items() if k.endswith("edge_index")})

@@ -3,7 +3,8 @@ written by tests/golden/make_golden.py from tt_atom/orb_model.py:491-600 of the 
 
 * the ZBL pair repulsion (energy with per-node mean and sum aggregation, forces, Voigt stress):
   the float64 oracle restatement on CPU, and ``atom_orb_zbl`` on the GPU;
-* the energy head's normaliser: this package's ``energy_denormalize`` (pure host code).
+* the normalisers (energy head; conservative forces and stress; direct force and stress heads)
+  and OrbMol's charge / spin conditioning vector: this package's host functions.
 
 The fixture's covalent-radius table is this package's (ASE is not installed where the fixture
 was made), so the table is not pinned; the formula, the Z + 1 indexing, the envelope and the
@@ -13,7 +14,9 @@ import pytest
 import torch
 
 from oracle import orb as OB
-from tt_atom.orb import COVALENT_RADII, energy_denormalize
+from tt_atom.orb import (COVALENT_RADII, charge_spin_embedding, conservative_scale,
+                         conservative_stress, energy_denormalize, force_denormalize,
+                         stress_denormalize)
 
 TOL_E, TOL_F, TOL_S = 1e-9, 1e-7, 1e-9
 
@@ -56,6 +59,33 @@ def test_energy_denormalize_matches_reference(fx):
                                d["p_Z"], w)
         assert abs(float(t) - float(d["denorm_out"][k])) <= 1e-12 * max(1.0, abs(out))
     assert energy_denormalize(1.5, d["p_Z"], {}) == 1.5
+
+
+def test_head_normalisers_match_reference(fx):
+    d = fx("ref_orb_host_terms.npz").d
+    t = lambda k: torch.from_numpy(d[k])  # noqa: E731
+    w = {"forces_head.normalizer.bn.running_mean": t("fnorm_mean"),
+         "forces_head.normalizer.bn.running_var": t("fnorm_var"),
+         "stress_head.diag_normalizer.bn.running_mean": t("snorm_dmean"),
+         "stress_head.diag_normalizer.bn.running_var": t("snorm_dvar"),
+         "stress_head.offdiag_normalizer.bn.running_mean": t("snorm_omean"),
+         "stress_head.offdiag_normalizer.bn.running_var": t("snorm_ovar"),
+         "energy_head.normalizer.bn.running_var": t("denorm_var")}
+    assert np.abs(force_denormalize(t("fnorm_raw"), w).numpy() - d["fnorm_out"]).max() <= 1e-12
+    assert np.abs(stress_denormalize(t("snorm_raw"), w).numpy() - d["snorm_out"]).max() <= 1e-12
+    # conservative checkpoints: forces and stress of the raw energy through sigma * n
+    f = conservative_scale(w, 48) * d["fnorm_raw"]
+    assert np.abs(f - d["cons_forces"]).max() <= 1e-12 * np.abs(f).max()
+    s = conservative_stress(d["cons_virial"], 48, d["p_cell"], w)
+    assert np.abs(s - d["cons_stress"]).max() <= 1e-12 * np.abs(s).max()
+
+
+@pytest.mark.parametrize("tag", ["a", "b", "c"])
+def test_charge_spin_embedding_matches_reference(fx, tag):
+    d = fx("ref_orb_host_terms.npz").d
+    q, sp = d[f"cs_{tag}"]
+    e = charge_spin_embedding(torch.from_numpy(d["cs_Wc"]), torch.from_numpy(d["cs_Ws"]), q, sp)
+    assert np.abs(e.numpy() - d[f"cs_out_{tag}"]).max() <= 1e-12
 
 
 @pytest.mark.gpu

@@ -131,13 +131,7 @@ class OrbEngine:
         2 pi for each, a zero spin giving zeros, projected by each layer's node projection."""
         if not self.has_cond:
             return
-        import math
-
-        def emb(v, W, is_spin):
-            x = float(v) * W * 2.0 * math.pi
-            e = torch.cat([torch.sin(x), torch.cos(x)])
-            return torch.zeros_like(e) if is_spin and v == 0 else e
-        c = torch.cat([emb(charge, self.cond_w[0], False), emb(spin, self.cond_w[1], True)])
+        c = charge_spin_embedding(self.cond_w[0], self.cond_w[1], charge, spin)
         rows = torch.stack([W @ c + b for W, b in self.cond_proj]).float()
         ws.cond.copy_(rows)
 
@@ -394,6 +388,55 @@ COVALENT_RADII = (
     2.06, 2.00, 1.96, 1.90, 1.87, 1.80, 1.69) + (0.20,) * 22
 
 
+def charge_spin_embedding(charge_W, spin_W, charge, spin):
+    """OrbMol's charge / spin conditioning vector (tt_atom/orb_model.py:32-56): [sin, cos] of
+    value * W * 2 pi for the charge and for the spin, a zero spin giving zeros."""
+    import math
+
+    def emb(v, W, is_spin):
+        x = float(v) * W * 2.0 * math.pi
+        e = torch.cat([torch.sin(x), torch.cos(x)])
+        return torch.zeros_like(e) if is_spin and v == 0 else e
+    return torch.cat([emb(charge, charge_W, False), emb(spin, spin_W, True)])
+
+
+def _affine(x, weights, prefix):
+    """A scalar normaliser's inverse, x * sqrt(running_var) + running_mean (identity when the
+    weights carry no such normaliser)."""
+    var = weights.get(f"{prefix}.running_var")
+    if var is None:
+        return x
+    mu = weights.get(f"{prefix}.running_mean")
+    return x * float(var.double().sqrt()) + (float(mu) if mu is not None else 0.0)
+
+
+def force_denormalize(raw, weights):
+    """Direct checkpoints' force head normaliser (tt_atom/orb_model.py:438-442)."""
+    return _affine(raw, weights, "forces_head.normalizer.bn")
+
+
+def stress_denormalize(raw, weights):
+    """Direct checkpoints' stress head normalisers, diagonal and off-diagonal Voigt components
+    each through their own (tt_atom/orb_model.py:445-456)."""
+    return torch.cat([_affine(raw[:3], weights, "stress_head.diag_normalizer.bn"),
+                      _affine(raw[3:], weights, "stress_head.offdiag_normalizer.bn")])
+
+
+def conservative_scale(weights, n):
+    """Conservative checkpoints: forces and virial of the raw energy times sigma * n, the only
+    factor of the energy normaliser that survives differentiation (tt_atom/orb_model.py:459-488);
+    1 without a normaliser."""
+    var = weights.get("energy_head.normalizer.bn.running_var")
+    return 1.0 if var is None else float(var.double().sqrt()) * n
+
+
+def conservative_stress(virial, n, cell, weights):
+    """Voigt-6 stress of a conservative checkpoint from its raw virial: scaled by sigma * n,
+    divided by the cell volume, off-diagonal pairs averaged (tt_atom/orb_model.py:472-488)."""
+    vol = abs(float(np.linalg.det(np.asarray(cell, dtype=np.float64))))
+    return voigt_6(conservative_scale(weights, n) * np.asarray(virial, dtype=np.float64) / vol)
+
+
 def energy_denormalize(raw, Z, weights):
     """The energy head's normaliser (tt_atom/orb_model.py:590-600, ``EnergyHead.denormalize``):
     undo the scalar normaliser's affine (running mean / variance), undo the per-atom average
@@ -583,24 +626,21 @@ class OrbCalculator(_AseCalculator):
         E = float(E[0])
         n = len(Z)
         w = self._w
-        scale = 1.0
-        if "energy_head.normalizer.bn.running_var" in w:
-            E = energy_denormalize(E, Z, w)
-            scale = float(w["energy_head.normalizer.bn.running_var"].double().sqrt()) * n
+        E = energy_denormalize(E, Z, w)
+        scale = conservative_scale(w, n)
         self.results["energy"] = self.results["free_energy"] = E
         self.results["energies"] = np.full(n, E / n)
         self.results["forces"] = (scale * F).numpy()
-        if V is not None:
-            V = scale * V
+        S = conservative_stress(V.numpy(), n, atoms.get_cell(), w) if V is not None else None
         if self.zbl:
             Ez = float(Ez[0])
             self.results["energy"] = self.results["free_energy"] = E = E + Ez
             self.results["energies"] = np.full(n, E / n)
             self.results["forces"] = self.results["forces"] + Fz.numpy()
-            if V is not None:
-                V = V + Vz
-        if V is not None:
-            self.results["stress"] = voigt_6(V.numpy() / atoms_volume(atoms))
+            if S is not None:
+                S = S + voigt_6(Vz.numpy() / atoms_volume(atoms))
+        if S is not None:
+            self.results["stress"] = S
 
     def _device_energy_forces(self, pos, Z, cell, pbc, charge=0.0, spin=0.0):
         """Energy (float64 device scalar) and forces ([N, 3] float64 on the device) as
@@ -611,10 +651,7 @@ class OrbCalculator(_AseCalculator):
         if self.engine.direct:
             E, F, _ = self._evaluate_direct(pos, Z, cell, pbc, False, charge, spin)
             w = self._w
-            var = w.get("forces_head.normalizer.bn.running_var")
-            if var is not None:
-                mu = w.get("forces_head.normalizer.bn.running_mean")
-                F = F * float(var.double().sqrt()) + (float(mu) if mu is not None else 0.0)
+            F = force_denormalize(F, w)
             E = energy_denormalize(E, Z, w)
             if self.zbl:
                 Ez, Fz, _ = self._zbl(self._ws, False, scale=1.0)
@@ -625,9 +662,8 @@ class OrbCalculator(_AseCalculator):
                                    spin=spin)
         E, F = Ed[0].double(), Fd.double()
         w = self._w
-        if "energy_head.normalizer.bn.running_var" in w:
-            E = energy_denormalize(E, Z, w)
-            F = F * (float(w["energy_head.normalizer.bn.running_var"].double().sqrt()) * n)
+        E = energy_denormalize(E, Z, w)
+        F = F * conservative_scale(w, n)
         if self.zbl:
             zE, zF, _ = self._zbl_launch(self._ws, False)
             E, F = E + zE[0], F + zF.double()
@@ -676,17 +712,10 @@ class OrbCalculator(_AseCalculator):
         n = len(Z)
         w = self._w
 
-        def aff(x, p):
-            mu = w.get(f"{p}.running_mean")
-            var = w.get(f"{p}.running_var")
-            if var is None:
-                return x
-            return x * float(var.double().sqrt()) + (float(mu) if mu is not None else 0.0)
         E = energy_denormalize(E, Z, w)
-        F = aff(F, "forces_head.normalizer.bn")
+        F = force_denormalize(F, w)
         if S is not None:
-            S = torch.cat([aff(S[:3], "stress_head.diag_normalizer.bn"),
-                           aff(S[3:], "stress_head.offdiag_normalizer.bn")])
+            S = stress_denormalize(S, w)
         if self.zbl:
             Ez, Fz, Vz = self._zbl(self._ws, S is not None, scale=1.0)
             E = E + Ez
