@@ -15,8 +15,13 @@ It writes two kinds of fixture (all fp32, npz):
   ``tests/mirror.py`` + torch autograd, with the strain leaf of tt_atom/forces.py:515-524 for the
   virial. These pin the neighbour list (edge_index, shifts: bit-exact) and E/F/virial.
 * ``ref_orb_geometry.npz`` / ``ref_orb_host_terms.npz`` -- the reference's Orb edge features and
-  their VJP, its host ZBL pair repulsion (energy, forces, stress) and its energy normaliser, on
-  seeded inputs.
+  their VJP, its host ZBL pair repulsion (energy, forces, stress), its normalisers and its
+  charge / spin conditioning, on seeded inputs.
+* ``ref_run_orb.npz`` -- the reference's own Orb backbone forward and reverse pass (energy,
+  forces, virial) on seeded inputs and random-init weights, run on the CPU through
+  ``ttnn_cpu.py`` (an fp32 torch stand-in for the ttnn calls).
+* ``ref_run_spectral.npz`` -- the reference's spectral feed-forward (uma-s-1's) on seeded node
+  features, through the same stand-in.
 
 Nothing at test time reads the reference; the tests read only these files.
 """
@@ -213,6 +218,93 @@ def _orb_host_terms(ref_root, out, covalent_radii):
     print("wrote", out, {k: np.shape(v) for k, v in arrays.items() if k.endswith("edge_index")})
 
 
+def _orb_reference_run(ref_root, out, cases):
+    """The reference's own Orb forward and reverse pass (tt_atom/orb_model.py:92-338 and
+    tt_atom/orb_forces.py:307-372: encoder, attention interaction layers, energy head, the
+    hand-written VJP and the host autograd finish through tt_atom/orb_geometry.py), run on the
+    CPU through ``ttnn_cpu`` (an fp32 torch stand-in for the ttnn calls), on this framework's
+    seeded inputs and random-init weights. ``cases``: name -> (cfg, weights, system, charge,
+    spin). Writes raw (normalised-space) energy, forces and, for periodic cells, the virial,
+    with the inputs and the (uncapped) edge list."""
+    import os
+    sys.path.insert(0, str(HERE))
+    import ttnn_cpu
+    ttnn_cpu.install()
+    os.environ["TT_ATOM_ORB_FUSED_SILU_BW"] = "0"
+    os.environ["TT_ATOM_ORB_MINIMAL_MATMUL"] = "0"
+    for mod in [m for m in sys.modules if m == "tt_atom" or m.startswith("tt_atom.")]:
+        del sys.modules[mod]
+    sys.path[:] = [p for p in sys.path if not p.endswith("tt-atom_b200")]
+    sys.path.insert(0, str(ref_root))
+    from tt_atom.geometry import radius_graph
+    from tt_atom.orb_forces import energy_and_forces
+    from tt_atom.orb_model import (AttentionInteractionLayer, Encoder, EnergyHead,
+                                   host_charge_spin_embedding, host_node_features)
+    arrays = {}
+    for name, (cfg, w, sysd, charge, spin) in cases.items():
+        w = {k: v.float() for k, v in w.items()}
+        C, Hd = cfg["latent_dim"], cfg["hidden_dim"]
+        enc = Encoder(w, None, node_in=cfg["node_embed_size"], edge_in=cfg["edge_embed_size"],
+                      latent_dim=C, hidden_dim=Hd)
+        layers = [AttentionInteractionLayer(w, f"gnn_stacks.{i}", None, latent_dim=C,
+                                            hidden_dim=Hd)
+                  for i in range(cfg["num_message_passing_steps"])]
+        head = EnergyHead(w, None, latent_dim=C, hidden_dim=Hd)
+        pos = torch.from_numpy(sysd["pos"]).float()
+        Z = torch.from_numpy(sysd["Z"]).long()
+        periodic = bool(sysd["pbc"])
+        cell = torch.from_numpy(sysd["cell"]).float() if periodic else None
+        ei, shift = radius_graph(pos, cfg["cutoff"], cell=cell, pbc=[True] * 3 if periodic else None)
+        cond = None
+        if "conditioner.charge_embedding.W" in w:
+            cond = host_charge_spin_embedding(w, charge, spin, len(Z), C)
+        res = energy_and_forces(enc, layers, head, None, pos=pos, senders=ei[1], receivers=ei[0],
+                                atomic_numbers=Z, node_feat=host_node_features(w, Z),
+                                cell_shift=shift if periodic else None, r_max=cfg["cutoff"],
+                                num_bases=cfg["num_bases"], compute_stress=periodic,
+                                cond_nodes=cond)
+        arrays.update({f"{name}@pos": pos.numpy(), f"{name}@Z": Z.numpy(),
+                       f"{name}@edge_index": ei.numpy(), f"{name}@shift": shift.numpy(),
+                       f"{name}@energy": np.float64(res[0]), f"{name}@forces": res[1].numpy(),
+                       f"{name}@charge_spin": np.array([charge, spin])})
+        if periodic:
+            arrays[f"{name}@cell"] = cell.numpy()
+            arrays[f"{name}@virial"] = res[2].numpy()
+        print(" ", name, "N", len(Z), "E", ei.shape[1], "energy", float(res[0]))
+    np.savez_compressed(HERE / out, **arrays)
+    print("wrote", out)
+
+
+def _spectral_reference_run(ref_root, out, cases):
+    """The reference's spectral feed-forward (tt_atom/spectral.py:41-188, ``SpectralAtomwise``,
+    both its flat block-diagonal path and its per-degree path) on seeded node features, through
+    ``ttnn_cpu``. ``cases``: name -> (cfg, weights, prefix, N)."""
+    import os
+    sys.path.insert(0, str(HERE))
+    import ttnn_cpu
+    ttnn_cpu.install()
+    arrays = {}
+    for fused in ("1", "0"):
+        os.environ["TT_ATOM_SPECTRAL_FUSED"] = fused
+        for mod in [m for m in sys.modules if m == "tt_atom" or m.startswith("tt_atom.")]:
+            del sys.modules[mod]
+        sys.path[:] = [p for p in sys.path if not p.endswith("tt-atom_b200")]
+        if str(ref_root) not in sys.path:
+            sys.path.insert(0, str(ref_root))
+        from tt_atom.spectral import SpectralAtomwise
+        for name, (cfg, w, prefix, N) in cases.items():
+            g = torch.Generator().manual_seed(21)
+            x = torch.randn(N, 9, cfg["sphere_channels"], generator=g)
+            ff = SpectralAtomwise({k: v.float() for k, v in w.items()}, prefix, None,
+                                  sphere_channels=cfg["sphere_channels"],
+                                  hidden_channels=cfg["hidden_channels"], lmax=2, mmax=2)
+            arrays[f"{name}@x"] = x.numpy()
+            arrays[f"{name}@out_fused{fused}"] = ff(x).numpy()
+            print(" ", name, "fused", fused, "N", N)
+    np.savez_compressed(HERE / out, **arrays)
+    print("wrote", out)
+
+
 def main(ref_root):
     ref_root = pathlib.Path(ref_root)
     _reduce_fairchem(ref_root, "golden_tiny.npz", "ref_golden_tiny.npz")
@@ -231,6 +323,23 @@ def main(ref_root):
     _run_reference(ref_root, "ref_run_tiny_fcc.npz", cfg, w, tables, fcc, True)
     _orb_geometry(ref_root, "ref_orb_geometry.npz")
     _orb_host_terms(ref_root, "ref_orb_host_terms.npz", COVALENT_RADII)
+    tiny, v3 = configs.orb_config("orb-tiny"), configs.orb_config("orb-v3")
+    cases = {
+        "tiny_sio2": (tiny, configs.orb_random_weights(tiny, seed=0),
+                      configs.amorphous_sio2(n_si=20, n_o=40, seed=2), 0.0, 0.0),
+        "tiny_mol": (tiny, configs.orb_random_weights(tiny, seed=0), configs.tiny_molecule(seed=0),
+                     0.0, 0.0),
+        "tiny_omol": (tiny, configs.orb_random_weights(tiny, seed=3, cond=True),
+                      configs.tiny_molecule(seed=1), 1.0, 2.0),
+        "v3_sio2": (v3, configs.orb_random_weights(v3, seed=0),
+                    configs.amorphous_sio2(n_si=16, n_o=32, seed=5), 0.0, 0.0),
+    }
+    _orb_reference_run(ref_root, "ref_run_orb.npz", cases)
+    sp_tiny = configs.model_config("tiny", ff_type="spectral")
+    sp_s1 = configs.model_config("uma-s-1", ff_type="spectral")
+    _spectral_reference_run(ref_root, "ref_run_spectral.npz", {
+        "tiny": (sp_tiny, configs.random_weights(sp_tiny, seed=0), "blocks.1.atom_wise", 40),
+        "uma_s1": (sp_s1, configs.random_weights(sp_s1, seed=0), "blocks.3.atom_wise", 40)})
 
 
 if __name__ == "__main__":
