@@ -16,7 +16,7 @@ import numpy as np
 import torch
 
 from .ase_compat import _AseCalculator, all_changes, atoms_volume, voigt_6
-from .engine import CapturedStep, UMAEngine, to_host
+from .engine import CapturedStep, UMAEngine, to_host, upload_positions
 from .graph import build_graph, csd_embedding
 from .weights import WeightBundle, reduced_composition
 
@@ -153,7 +153,7 @@ class TTAtomCalculator(_AseCalculator):
         if not keep:
             self._step = None
         ws = self._ws
-        ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))
+        upload_positions(ws, pos)
         if trace:
             if self._step is None:
                 self._step = CapturedStep(self.engine, ws, forces=forces, virial=stress)
@@ -195,12 +195,12 @@ class TTAtomCalculator(_AseCalculator):
         full = getattr(self, "_full_step", None)
         if full is None or full[0] is not ws:
             refresh = TopologyRefresh(ws.graph)
-            ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))
+            upload_positions(ws, pos)
             step = CapturedStep(self.engine, ws, forces=forces, virial=stress,
                                 prelude=lambda st: refresh.launch(ws.pos, st))
             self._full_step = full = (ws, refresh, step)
         else:
-            ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))
+            upload_positions(ws, pos)
         _, refresh, step = full
         step()
         if device_out:

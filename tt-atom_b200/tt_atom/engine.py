@@ -63,6 +63,24 @@ def to_host(*ts):
     return out
 
 
+def upload_positions(ws, pos):
+    """Copy positions into ``ws.pos``: a device tensor directly; host values through a pinned
+    staging buffer of the workspace (asynchronous host-to-device copy, ordered on the current
+    stream; the staging buffer is reused only after its previous copy has completed)."""
+    if torch.is_tensor(pos) and pos.is_cuda:
+        ws.pos.copy_(pos)
+        return
+    pin = getattr(ws, "_pos_pinned", None)
+    if pin is None:
+        ws._pos_pinned = pin = torch.empty(ws.pos.shape, dtype=torch.float32, pin_memory=True)
+        ws._pos_event = torch.cuda.Event()
+    else:
+        ws._pos_event.synchronize()
+    pin.copy_(torch.as_tensor(pos, dtype=torch.float32).reshape(pin.shape))
+    ws.pos.copy_(pin, non_blocking=True)
+    ws._pos_event.record()
+
+
 def launch_count():
     """Kernels the library has launched so far (its own counter)."""
     n = L.ctypes.c_int64(0)

@@ -25,7 +25,8 @@ import torch
 from . import _lib as L
 from ._lib import ptr
 from .ase_compat import _AseCalculator, all_changes, atoms_volume, voigt_6
-from .engine import PRECISIONS, CapturedStep, Workspace, _Groups, _dev, call, to_host
+from .engine import (PRECISIONS, CapturedStep, Workspace, _Groups, _dev, call, to_host,
+                     upload_positions)
 from .graph import build_graph
 
 
@@ -552,7 +553,7 @@ class OrbCalculator(_AseCalculator):
         if ws is None or getattr(self, "_refresh_key", None) != key:
             return None
         full = getattr(self, "_full_step", None)
-        ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))
+        upload_positions(ws, pos)
         if full is None or full[0] is not ws:
             refresh = TopologyRefresh(ws.graph)
             step = CapturedStep(self.engine, ws, forces=forces, virial=stress,
@@ -589,7 +590,7 @@ class OrbCalculator(_AseCalculator):
         else:
             self._ws.rebind(g)                  # same sizes: reuse the buffers
         ws = self._ws
-        ws.pos.copy_(torch.as_tensor(pos, dtype=torch.float32))
+        upload_positions(ws, pos)
         self.engine.set_condition(ws, charge, spin)       # OrbMol checkpoints only
         key = (g.N, g.E, bool(forces), bool(stress))
         if self.trace:
