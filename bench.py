@@ -570,14 +570,13 @@ def run_ours(args):
         md_atoms(md_a, steps=md_steps, dt=1.0, temp=300.0, seed=2, native=True)
         torch.cuda.synchronize()
         tm = 1e3 * (time.perf_counter() - tm) / (md_steps + 1)   # +1: the initial force call
-        md = {"value": N / (tm / 1e3), "unit": "atom-steps/s", "ms_per_step": tm,
-              "steps": md_steps, "integrator": "BAOAB Langevin, 1 fs, 300 K, GPU-resident",
-              "timing": "host wall clock around the loop (one status read-back per step)"}
-    ms_t = torch.tensor([ms, e2e_ms], device=device)
-    if ws_n > 1:
-        import torch.distributed as dist
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms = ms_t.tolist()
+        md = {"unit": "atom-steps/s", "steps": md_steps,
+              "integrator": "BAOAB Langevin, 1 fs, 300 K, GPU-resident",
+              "timing": "host wall clock around the loop (one status read-back per step), "
+                        "max over ranks; every rank runs its own replica"}
+    ms, e2e_ms, tm = _max_over_ranks([ms, e2e_ms, tm if md is not None else 0.0], device, ws_n)
+    if md is not None:
+        md.update(value=N * ws_n / (tm / 1e3), ms_per_step=tm)
     eng_precision = {0: "fp32", 1: "tf32", 2: "3xtf32", 3: "3xf16"}[eng.precision]
     ms_step = ms / args.steps
     value = N * ws_n * args.steps / (ms / 1e3)
