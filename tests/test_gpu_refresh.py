@@ -159,3 +159,17 @@ def test_traced_orb_calculator_refreshes_on_the_device():
         assert np.array_equal(traced.results["forces"], eager.results["forces"])
         assert np.array_equal(traced.results["stress"], eager.results["stress"])
     assert used >= 2
+
+
+def test_traced_orb_calculator_falls_back_when_the_edge_count_changes():
+    from tt_atom.orb import OrbCalculator
+    cfg = configs.orb_config("orb-tiny")
+    w = configs.orb_random_weights(cfg, seed=0)
+    m = configs.tiny_molecule(seed=0)
+    traced = OrbCalculator(w, cfg=cfg, trace=True, max_num_neighbors=None)
+    eager = OrbCalculator(w, cfg=cfg, trace=False, max_num_neighbors=None)
+    for scale in (1.0, 1.0, 1.2, 1.2, 0.9):
+        for c in (traced, eager):
+            c.calculate(SimpleAtoms(m["Z"], m["pos"] * scale), ("energy", "forces"))
+        assert traced.results["energy"] == eager.results["energy"]
+        assert np.array_equal(traced.results["forces"], eager.results["forces"])

@@ -544,7 +544,7 @@ class OrbCalculator(_AseCalculator):
                 None if pbc is None else tuple(np.broadcast_to(np.asarray(pbc, bool), 3)),
                 bool(forces), bool(stress), float(charge), float(spin))
 
-    def _refresh_step(self, pos, key, forces, stress, device_out):
+    def _refresh_step(self, pos, key, forces, stress, device_out, defer_status=False):
         """Traced evaluation of the previous call's system at new positions: one captured graph
         rebuilds the neighbour list on the device and runs the model pass (see
         TTAtomCalculator); None when it does not apply or the edge count changed."""
@@ -562,6 +562,11 @@ class OrbCalculator(_AseCalculator):
         _, refresh, step = full
         step()
         if device_out:
+            if defer_status:
+                # the caller reads the status with its results (one read-back) and calls
+                # refresh_failed() when it is not OK
+                self._pending_status = refresh.status[:1]
+                return ws.energy, ws.forces, (ws.virial if stress else None)
             if int(refresh.status[0]) != TopologyRefresh.OK:
                 self._refresh_key = self._full_step = None
                 return None
@@ -574,10 +579,11 @@ class OrbCalculator(_AseCalculator):
         return float(E[0]), F, V
 
     def _evaluate(self, pos, Z, cell, pbc, forces=True, stress=False, device_out=False,
-                  charge=0.0, spin=0.0):
+                  charge=0.0, spin=0.0, defer_status=False):
         skey = self._system_key(Z, cell, pbc, forces, stress, charge, spin)
+        self._pending_status = None
         if self.trace:
-            fast = self._refresh_step(pos, skey, forces, stress, device_out)
+            fast = self._refresh_step(pos, skey, forces, stress, device_out, defer_status)
             if fast is not None:
                 return fast
         g = build_graph(pos, Z, self.cfg["cutoff"], cell, pbc, max_neighbors=self.max_nbrs,
@@ -619,11 +625,18 @@ class OrbCalculator(_AseCalculator):
         if self.engine.direct:
             return self._calculate_direct(atoms, pos, Z, cell, pbc, properties, want_stress,
                                           charge, spin)
-        # model pass and ZBL term on the device, then one read-back of all their results
+        # model pass and ZBL term on the device, then one read-back of all their results (and
+        # of the neighbour-list refresh status when the traced step rebuilt the list)
         Ed, Fd, Vd = self._evaluate(pos, Z, cell, pbc if pbc.any() else None, True, want_stress,
-                                    device_out=True, charge=charge, spin=spin)
+                                    device_out=True, charge=charge, spin=spin,
+                                    defer_status=True)
         zb = self._zbl_launch(self._ws, want_stress) if self.zbl else (None, None, None)
-        E, F, V, Ez, Fz, Vz = to_host(Ed, Fd, Vd, *zb)
+        status = self._pending_status
+        E, F, V, Ez, Fz, Vz, st = to_host(Ed, Fd, Vd, *zb, status)
+        if st is not None and int(st[0]) != 0:
+            # the edge count changed: the step ran on the old topology; rebuild and redo
+            self._refresh_key = self._full_step = None
+            return self.calculate(atoms, properties, system_changes)
         E = float(E[0])
         n = len(Z)
         w = self._w
