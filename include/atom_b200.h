@@ -266,6 +266,19 @@ int atom_gemm_ex(const float* A, int64_t lda, int64_t M, const atom_gemm_groups*
                  const int* idx1, const int* idx2, int64_t ldt, int act, int accumulate,
                  int precision, float* scratch, int64_t scratch_floats, void* stream);
 
+/* The so2_2 GEMM with the gate fused into its A operand (the reference's so2_conv_2 on
+ * GateActivation's output, tt_atom/activation.py:53-70 then tt_atom/so2.py:255-296): Y is the
+ * so2_1 output [M, ldy >= 11 H] = [gating rows 0, 1 | m-primed rows 0..8], H channels each; the
+ * GEMM's A operand is row 0 -> SiLU(row 0), row r >= 1 -> row r * sigmoid(gating row
+ * (r in {1, 3, 5} ? 0 : 1)), formed where the tensor-core kernel converts A, so the gated rows
+ * are never written to memory; the result equals atom_gate_fwd followed by atom_gemm_ex bit for
+ * bit. Groups address Y's columns (a_col >= 2 H, 32-aligned, within rows 0..8) and carry their
+ * biases as in atom_gemm_ex; no activation or accumulation. precision 2 or 3 only
+ * (ATOM_ERR_UNSUPPORTED otherwise, and when the operands do not suit the tensor-core kernel). */
+int atom_gemm_gated(const float* Y, int64_t ldy, int64_t M, const atom_gemm_groups* groups,
+                    int H, float* C, int64_t ldc, int precision, float* scratch,
+                    int64_t scratch_floats, void* stream);
+
 /* Reads and clears the device-side error code of the tensor-core kernels (0 = none; a bounded
  * wait expired otherwise). Synchronises `stream`. */
 int atom_device_error(int* code_host, void* stream);

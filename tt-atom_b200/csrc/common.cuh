@@ -85,5 +85,9 @@ __host__ __device__ constexpr int row_off(int r) {
          : r == 6 ? 20 : r == 7 ? 25 : 30;
 }
 __host__ __device__ constexpr int deg_col0(int l) { return l * l; }
+// Gating row (0 or 1) of vector row r = 1..8 in m-primed order (tt_atom/activation.py:19-26).
+__host__ __device__ constexpr int gate_row(int r) {
+    return (r == 1 || r == 3 || r == 5) ? 0 : 1;
+}
 
 }  // namespace atom

@@ -148,10 +148,6 @@ __global__ void __launch_bounds__(256) rotate_in_kernel(
 }
 
 // ------------------------------------------------------------------------------- gate
-// Gating row (0 or 1) of vector row r = 1..8 in m-primed order (tt_atom/activation.py:19-26).
-__host__ __device__ constexpr int gate_row(int r) {
-    return (r == 1 || r == 3 || r == 5) ? 0 : 1;
-}
 
 __global__ void gate_fwd_kernel(const float* __restrict__ Y, long long E, int H,
                                 float* __restrict__ G) {

@@ -20,6 +20,9 @@ int gemm_tc(const float* A, long long lda, long long M, const atom_gemm_groups* 
             long long ldc, float* Cpre, const float* T1, const float* T2, const int* idx1,
             const int* idx2, long long ldt, int act, int accumulate, int precision,
             float* scratch, long long scratch_floats, cudaStream_t st);
+int gemm_tc_gated(const float* Y, long long ldy, long long M, const atom_gemm_groups* g, int H,
+                  float* C, long long ldc, int precision, float* scratch,
+                  long long scratch_floats, cudaStream_t st);
 
 struct GemmArgs {
     const float* A;
@@ -170,6 +173,31 @@ extern "C" int atom_gemm_ex(const float* A, int64_t lda, int64_t M,
     gemm_fma_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
     ATOM_CHECK_LAUNCH("gemm");
     return ATOM_OK;
+}
+
+extern "C" int atom_gemm_gated(const float* Y, int64_t ldy, int64_t M,
+                               const atom_gemm_groups* groups, int H, float* Cout, int64_t ldc,
+                               int precision, float* scratch, int64_t scratch_floats,
+                               void* stream) {
+    ATOM_REQUIRE(groups && groups->ngroups >= 1 && groups->ngroups <= 8, "1..8 groups");
+    ATOM_REQUIRE(H > 0 && H % 32 == 0, "gemm_gated: H must be a positive multiple of 32");
+    if (precision < 2) {
+        set_error("gemm_gated: precision %d has no gated tensor-core path; apply "
+                  "atom_gate_fwd and atom_gemm_ex instead", precision);
+        return ATOM_ERR_UNSUPPORTED;
+    }
+    for (int g = 0; g < groups->ngroups; ++g)
+        ATOM_REQUIRE(groups->a_col[g] >= 2 * H && groups->a_col[g] % 32 == 0 &&
+                         groups->a_col[g] + groups->K[g] <= 11 * H && groups->K[g] % 32 == 0,
+                     "gemm_gated: group %d must read 32-aligned columns of rows 0..8 of Y", g);
+    ATOM_REQUIRE(ldy >= 11 * H, "gemm_gated: ldy < 11 H");
+    if (M == 0) return ATOM_OK;
+    if (!gemm_tc_supported(Y, ldy, groups, precision)) {
+        set_error("gemm_gated: operands not usable by the tensor-core kernel (alignment)");
+        return ATOM_ERR_UNSUPPORTED;
+    }
+    return gemm_tc_gated(Y, ldy, M, groups, H, Cout, ldc, precision, scratch, scratch_floats,
+                         (cudaStream_t)stream);
 }
 
 extern "C" int atom_gemm(const float* A, int64_t lda, int64_t M, const atom_gemm_groups* groups,

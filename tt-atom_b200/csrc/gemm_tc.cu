@@ -85,6 +85,13 @@ struct Args {
     int nacc;            // tensor-memory accumulators the K stages are spread over (1 or 4)
     const float* rscale; // mode 3: power-of-two scale of A per (group, row), rows rs_ld apart
     long long rs_ld;
+    // gated A (modes 2, 3; gH > 0): A is the so2_1 output Y [M, ld = gld] laid out as
+    // [gating rows 0, 1 | m-primed rows 0..8], gH channels each, and the A operand is the gate
+    // applied on the fly: SiLU on row 0, row r >= 1 times sigmoid(gating row gate_row(r)),
+    // the same expressions as the standalone gate kernel (tt_atom/activation.py:53-70)
+    const float* gsrc;
+    long long gld;
+    int gH;
     Groups g;
 };
 
@@ -240,6 +247,15 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
             smem_u32(bar))
         : "memory");
+}
+
+// The gate on four A elements of m-primed row grow: SiLU on row 0, otherwise times the
+// sigmoid of the gating values g[0..3] (silu_f / sigmoid_f: the standalone gate kernel's
+// expressions, so the gated operand is bit-identical to that kernel's output).
+__device__ __forceinline__ float4 gate4(float4 x, int grow, const float* g) {
+    if (grow == 0) return make_float4(silu_f(x.x), silu_f(x.y), silu_f(x.z), silu_f(x.w));
+    return make_float4(x.x * sigmoid_f(g[0]), x.y * sigmoid_f(g[1]), x.z * sigmoid_f(g[2]),
+                       x.w * sigmoid_f(g[3]));
 }
 
 __device__ __forceinline__ float4 ldg4(const float* q) {
@@ -545,9 +561,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                 TileInfo ti = tile_info(p, ntn, t);
                 float rs = 1.f;
                 if (MODE == 3 && ti.m0 + r < p.M) rs = p.rscale[ti.grp * p.rs_ld + ti.m0 + r];
+                const bool row_ok = ti.m0 + r < p.M;
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt, ++it) {
                     int s = it % S;
                     uint32_t ph = (it / S) & 1u;
+                    // gated A: this stage's 32 K elements are channels gc .. gc + 31 of one
+                    // m-primed row grow; its gating values are loaded before the TMA wait
+                    int grow = -1;
+                    float gv[BK];
+                    if (p.gH > 0) {
+                        const int x = p.g.a_col[ti.grp] + kt * BK;
+                        grow = x / p.gH - 2;
+                        const int gc = x - (grow + 2) * p.gH;
+                        if (grow > 0 && !row_ok) {
+#pragma unroll
+                            for (int k = 0; k < BK; ++k) gv[k] = 0.f;
+                        } else if (grow > 0) {
+                            const float* gp =
+                                p.gsrc + (ti.m0 + r) * p.gld + gate_row(grow) * p.gH + gc;
+#pragma unroll
+                            for (int c = 0; c < BK / 4; ++c) {
+                                const float4 q = __ldg(reinterpret_cast<const float4*>(gp) + c);
+                                gv[4 * c] = q.x;
+                                gv[4 * c + 1] = q.y;
+                                gv[4 * c + 2] = q.z;
+                                gv[4 * c + 3] = q.w;
+                            }
+                        }
+                    }
                     ok = mbar_wait(&full[s], ph, 3) &&
                          mbar_wait(&afree[it & 1u], ((it >> 1) & 1u) ^ 1u, 6) && !aborted();
                     ok = __all_sync(0xffffffffu, ok);
@@ -562,8 +603,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         uint32_t hi[BK / 2], lo[BK / 2];
 #pragma unroll
                         for (int c = 0; c < BK / 4; ++c) {
-                            const float4 x =
-                                *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) << 4));
+                            float4 x = *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) << 4));
+                            if (grow >= 0) x = gate4(x, grow, gv + 4 * c);
                             const float y[4] = {x.x * rs, x.y * rs, x.z * rs, x.w * rs};
 #pragma unroll
                             for (int k = 0; k < 2; ++k) {
@@ -581,8 +622,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         uint32_t hi[BK], lo[BK];
 #pragma unroll
                         for (int c = 0; c < BK / 4; ++c) {
-                            const float4 x =
-                                *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) << 4));
+                            float4 x = *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) << 4));
+                            if (grow >= 0) x = gate4(x, grow, gv + 4 * c);
                             const float xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
                             for (int k = 0; k < 4; ++k) {
@@ -874,7 +915,7 @@ template <int BN, int MODE>
 static int launch(const float* A, long long lda, long long M, const atom_gemm_groups* g,
                   float* C, long long ldc, float* Cpre, const float* T1, const float* T2,
                   const int* idx1, const int* idx2, long long ldt, int act, int accumulate,
-                  float* scratch, long long scratch_floats, cudaStream_t st) {
+                  float* scratch, long long scratch_floats, cudaStream_t st, int gate_H = 0) {
     using CF = Cfg<BN, MODE>;
     static bool attr_set = false;
     if (!attr_set) {
@@ -978,6 +1019,9 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
     }
     p.rscale = MODE == 3 ? scratch : nullptr;
     p.rs_ld = mpad;
+    p.gsrc = gate_H > 0 ? A : nullptr;
+    p.gld = lda;
+    p.gH = gate_H;
     p.g.tile_start[g->ngroups] = tiles;
     if (tma_out) {
         for (int i = 0; i < g->ngroups; ++i) {
@@ -1058,6 +1102,20 @@ int gemm_tc(const float* A, long long lda, long long M, const atom_gemm_groups* 
                                   accumulate, scratch, scratch_floats, st);
     return tc::launch<128, 1>(A, lda, M, g, C, ldc, Cpre, T1, T2, idx1, idx2, ldt, act,
                               accumulate, scratch, scratch_floats, st);
+}
+
+// The so2_2 GEMM on the gated so2_1 output (see Args::gH): precision 2 or 3 only (the gate is
+// applied where the split warps convert A); every group's A columns must lie in rows 0..8 of Y,
+// stage-aligned (a_col and gH multiples of 32).
+int gemm_tc_gated(const float* Y, long long ldy, long long M, const atom_gemm_groups* g, int H,
+                  float* C, long long ldc, int precision, float* scratch,
+                  long long scratch_floats, cudaStream_t st) {
+    if (int s = tc::encoder()) return s;
+    if (precision == 3 && scratch && f16_ready(M, g, scratch_floats))
+        return tc::launch<192, 3>(Y, ldy, M, g, C, ldc, nullptr, nullptr, nullptr, nullptr,
+                                  nullptr, 0, 0, 0, scratch, scratch_floats, st, H);
+    return tc::launch<192, 2>(Y, ldy, M, g, C, ldc, nullptr, nullptr, nullptr, nullptr, nullptr,
+                              0, 0, 0, scratch, scratch_floats, st, H);
 }
 
 }  // namespace atom

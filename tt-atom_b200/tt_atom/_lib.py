@@ -14,6 +14,7 @@ _LIB_PATH = pathlib.Path(__file__).resolve().with_name("libatomb200.so")
 _lib = None
 
 ATOM_ERR_CAPACITY = 3
+ATOM_ERR_UNSUPPORTED = 4
 
 c_void_p, c_int, c_int64, c_float = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
 c_double = ctypes.c_double
@@ -71,6 +72,8 @@ _SIGS = {
     "atom_gemm_ex": (c_void_p, c_int64, c_int64, ctypes.POINTER(GemmGroups), c_void_p, c_int64,
                      c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int,
                      c_int, c_void_p, c_int64, c_void_p),
+    "atom_gemm_gated": (c_void_p, c_int64, c_int64, ctypes.POINTER(GemmGroups), c_int, c_void_p,
+                        c_int64, c_int, c_void_p, c_int64, c_void_p),
     "atom_device_error": (c_void_p, c_void_p),
     "atom_wait_selftest": (c_int64, c_void_p),
     "atom_rotate_in": (c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_int64,

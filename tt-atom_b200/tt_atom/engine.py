@@ -286,7 +286,10 @@ class UMAEngine:
             blk = dict(
                 n1w=d(w[f"{p}.norm_1.affine_weight"]), n1b=d(w[f"{p}.norm_1.affine_bias"]),
                 n2w=d(w[f"{p}.norm_2.affine_weight"]), n2b=d(w[f"{p}.norm_2.affine_bias"]),
-                so2_1=_Groups(f1), so2_1_bw=_Groups(b1), so2_2=_Groups(f2_), so2_2_bw=_Groups(b2_))
+                so2_1=_Groups(f1), so2_1_bw=_Groups(b1), so2_2=_Groups(f2_), so2_2_bw=_Groups(b2_),
+                # the same so2_2 weights addressing the so2_1 output's rows directly (the gate
+                # applied inside the GEMM: atom_gemm_gated)
+                so2_2g=_Groups([dict(gr, a_col=gr["a_col"] + 2 * H) for gr in f2_]))
             a = f"{p}.atom_wise"
             if self.ff == "grid":
                 for key, gi in (("ga", 0), ("gb", 2), ("gc", 4)):
@@ -347,6 +350,27 @@ class UMAEngine:
         call("atom_gemm_ex", ptr(A), lda, M, groups.struct, ptr(Cout), ldc, ptr(Cpre), ptr(T1),
              ptr(T2), ptr(idx1), ptr(idx2), ldt, act, accumulate, self.precision, ptr(sc),
              sc.numel() if sc is not None else 0, stream)
+
+    # the gate of the edgewise block applied inside the so2_2 GEMM (tensor-core precisions);
+    # False: the standalone gate kernel, then the GEMM (same results bit for bit)
+    fuse_gate = True
+
+    def _gate_so2_2(self, ws, Y1, E, b, out, s):
+        """so2_2 on the gated so2_1 output Y1 [E, 11H] into ``out`` [E, 9C]."""
+        H, C = self.H, self.C
+        if self.fuse_gate and self.precision >= 2:
+            sc = self._scratch
+            if self.precision == 3:
+                b["so2_2g"].ensure_f16()
+            rc = L.lib().atom_gemm_gated(ptr(Y1), 11 * H, E, b["so2_2g"].struct, H, ptr(out),
+                                         9 * C, self.precision, ptr(sc),
+                                         sc.numel() if sc is not None else 0, s)
+            if rc == 0:
+                return
+            if rc != L.ATOM_ERR_UNSUPPORTED:
+                raise L.AtomError("atom_gemm_gated", rc)
+        call("atom_gate_fwd", ptr(Y1), E, H, ptr(ws.Gt), s)
+        self._gemm(ws.Gt, 9 * H, E, b["so2_2"], out, 9 * C, stream=s)
 
     def workspace_bytes(self, N, E, chunk_edges=None):
         """Approximate device bytes of a workspace for N atoms and E edges (unchunked, or
@@ -555,8 +579,7 @@ class UMAEngine:
                 call("atom_rotate_in", ptr(nb), ptr(g.src), ptr(g.tgt), ptr(ws.coef), E, C,
                      ptr(ws.RAD), self.ldr, self.rad_off[i], None, ptr(ws.A1), s)
                 self._gemm(ws.A1, 18 * C, E, b["so2_1"], ws.Y1[i], 11 * H, stream=s)
-                call("atom_gate_fwd", ptr(ws.Y1[i]), E, H, ptr(ws.Gt), s)
-                self._gemm(ws.Gt, 9 * H, E, b["so2_2"], ws.Y2[i], 9 * C, stream=s)
+                self._gate_so2_2(ws, ws.Y1[i], E, b, ws.Y2[i], s)
                 call("atom_rotate_back_reduce", ptr(ws.Y2[i]), ptr(ws.coef), ptr(ws.env), N, C,
                      ptr(g.recv_ptr), ptr(x), ptr(ws.xm[i]), s)
             else:
@@ -735,8 +758,7 @@ class UMAEngine:
         call("atom_rotate_in", ptr(ws.nb[i]), ptr(g.src[ch.e0:]), ptr(g.tgt[ch.e0:]),
              ptr(ws.coef[ch.e0:]), Ec, C, ptr(ws.RAD), ws.RAD.shape[1], 0, None, ptr(ws.A1), s)
         self._gemm(ws.A1, 18 * C, Ec, b["so2_1"], ws.Y1[0], 11 * H, stream=s)
-        call("atom_gate_fwd", ptr(ws.Y1[0]), Ec, H, ptr(ws.Gt), s)
-        self._gemm(ws.Gt, 9 * H, Ec, b["so2_2"], ws.Y2[0], 9 * C, stream=s)
+        self._gate_so2_2(ws, ws.Y1[0], Ec, b, ws.Y2[0], s)
 
     def _chunked_edge_bwd(self, ws, i, s):
         """Edgewise VJP of layer i, chunk by chunk (each chunk's forward chain recomputed):
