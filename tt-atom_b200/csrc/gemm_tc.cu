@@ -573,6 +573,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int x = p.g.a_col[ti.grp] + kt * BK;
                         grow = x / p.gH - 2;
                         const int gc = x - (grow + 2) * p.gH;
+                        // the next stage's gating line into L1 while this one is processed
+                        if (kt + 1 < ti.kt1 && row_ok) {
+                            const int xn = x + BK, gn = xn / p.gH - 2;
+                            if (gn > 0) {
+                                const float* pn = p.gsrc + (ti.m0 + r) * p.gld +
+                                                  gate_row(gn) * p.gH + (xn - (gn + 2) * p.gH);
+                                asm volatile("prefetch.global.L1 [%0];" ::"l"(pn));
+                            }
+                        }
                         if (grow > 0 && !row_ok) {
 #pragma unroll
                             for (int k = 0; k < BK; ++k) gv[k] = 0.f;

@@ -358,7 +358,7 @@ class UMAEngine:
     def _gate_so2_2(self, ws, Y1, E, b, out, s):
         """so2_2 on the gated so2_1 output Y1 [E, 11H] into ``out`` [E, 9C]."""
         H, C = self.H, self.C
-        if self.fuse_gate and self.precision >= 2:
+        if self.fuse_gate and self.precision >= 2 and H % 32 == 0:
             sc = self._scratch
             if self.precision == 3:
                 b["so2_2g"].ensure_f16()
