@@ -59,6 +59,13 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+// The gate's forward activations, from the fast exponential and the fast division intrinsics
+// (a few ulp; used wherever the gated so2_2 operand is formed, so that the standalone gate
+// kernel and the gate fused into the GEMM give the same bits).
+__device__ __forceinline__ float sigmoid_gate(float x) {
+    return __fdividef(1.0f, 1.0f + __expf(-x));
+}
+__device__ __forceinline__ float silu_gate(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 // d/dx silu(x) = s (1 + x (1 - s)), s = sigmoid(x)
 __device__ __forceinline__ float dsilu_f(float x) {
     float s = sigmoid_f(x);

@@ -157,8 +157,8 @@ __global__ void gate_fwd_kernel(const float* __restrict__ Y, long long E, int H,
     int c = (int)(t - e * H);
     const float* y = Y + e * 11LL * H;
     float* g = G + e * 9LL * H;
-    float s0 = sigmoid_f(y[c]), s1 = sigmoid_f(y[H + c]);
-    g[c] = silu_f(y[2 * H + c]);
+    float s0 = sigmoid_gate(y[c]), s1 = sigmoid_gate(y[H + c]);
+    g[c] = silu_gate(y[2 * H + c]);
 #pragma unroll
     for (int r = 1; r < kNsph; ++r) g[r * H + c] = y[(2 + r) * H + c] * (gate_row(r) ? s1 : s0);
 }

@@ -250,12 +250,13 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 }
 
 // The gate on four A elements of m-primed row grow: SiLU on row 0, otherwise times the
-// sigmoid of the gating values g[0..3] (silu_f / sigmoid_f: the standalone gate kernel's
+// sigmoid of the gating values g[0..3] (silu_gate / sigmoid_gate: the standalone gate kernel's
 // expressions, so the gated operand is bit-identical to that kernel's output).
 __device__ __forceinline__ float4 gate4(float4 x, int grow, const float* g) {
-    if (grow == 0) return make_float4(silu_f(x.x), silu_f(x.y), silu_f(x.z), silu_f(x.w));
-    return make_float4(x.x * sigmoid_f(g[0]), x.y * sigmoid_f(g[1]), x.z * sigmoid_f(g[2]),
-                       x.w * sigmoid_f(g[3]));
+    if (grow == 0)
+        return make_float4(silu_gate(x.x), silu_gate(x.y), silu_gate(x.z), silu_gate(x.w));
+    return make_float4(x.x * sigmoid_gate(g[0]), x.y * sigmoid_gate(g[1]),
+                       x.z * sigmoid_gate(g[2]), x.w * sigmoid_gate(g[3]));
 }
 
 __device__ __forceinline__ float4 ldg4(const float* q) {
