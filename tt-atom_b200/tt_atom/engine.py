@@ -351,9 +351,13 @@ class UMAEngine:
              ptr(T2), ptr(idx1), ptr(idx2), ldt, act, accumulate, self.precision, ptr(sc),
              sc.numel() if sc is not None else 0, stream)
 
-    # the gate of the edgewise block applied inside the so2_2 GEMM (tensor-core precisions);
-    # False: the standalone gate kernel, then the GEMM (same results bit for bit)
-    fuse_gate = True
+    # True: the gate of the edgewise block applied inside the so2_2 GEMM (tensor-core
+    # precisions, atom_gemm_gated); False (default): the standalone gate kernel, then the GEMM.
+    # Same results bit for bit. Measured on the 2,000-atom step: 17.53 ms fused against
+    # 17.18 ms separate (3xTF32), 18.58 against 18.16 ms (fp16 pair): the gating tile each K
+    # stage then reads adds a quarter to the GEMM's per-stage operand traffic, which costs more
+    # than the standalone pass over HBM.
+    fuse_gate = False
 
     def _gate_so2_2(self, ws, Y1, E, b, out, s):
         """so2_2 on the gated so2_1 output Y1 [E, 11H] into ``out`` [E, 9C]."""
