@@ -283,6 +283,11 @@ int atom_gemm_gated(const float* Y, int64_t ldy, int64_t M, const atom_gemm_grou
  * wait expired otherwise). Synchronises `stream`. */
 int atom_device_error(int* code_host, void* stream);
 
+/* Stream-ordered form of atom_device_error: copies the device-side error code into the device
+ * int *code_dev and clears it, without synchronising, so a caller can read it back together
+ * with a step's results in one copy. No counterpart in the reference. */
+int atom_device_error_take(int* code_dev, void* stream);
+
 /* Test hook for the bounded waits: one thread runs the tensor-core kernels' own bounded
  * mbarrier wait on a barrier that nothing arrives on, for budget_cycles SM clocks (1 ..
  * 2e9), then gives up and records ATOM_WAIT_SELFTEST_CODE in the device-side error code,

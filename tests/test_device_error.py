@@ -2,8 +2,8 @@
 
 The tensor-core GEMM bounds every mbarrier wait; on expiry it records a code in a device flag and
 its later CTAs return at entry, so the outputs of that step are incomplete. Every host read-back
-(``engine.to_host``) and the end of the GPU-resident relax / MD loops read the flag through
-``atom_device_error`` and raise. The CPU test fakes the library's answer; the GPU test makes the
+(``engine.to_host``) reads the flag back with the results (``atom_device_error_take``) and the
+end of the GPU-resident relax / MD loops reads it (``atom_device_error``); both raise. The CPU test fakes the library's answer; the GPU test makes the
 GEMM's own bounded wait run out on a barrier that nothing arrives on (a short budget, no fault)
 and checks that the calculator raises once and then recovers."""
 import ctypes
@@ -17,7 +17,8 @@ from tt_atom import engine as engine_mod
 
 
 class _FakeLib:
-    """Stands in for libatomb200.so: atom_device_error reports ``code`` once, then 0."""
+    """Stands in for libatomb200.so: the error code is ``code`` once, then 0 (both the
+    synchronous read and the stream-ordered take into a buffer)."""
 
     def __init__(self, code):
         self.code = code
@@ -26,6 +27,9 @@ class _FakeLib:
         ctypes.cast(code_ptr, ctypes.POINTER(ctypes.c_int))[0] = self.code
         self.code = 0
         return 0
+
+    def atom_device_error_take(self, code_ptr, stream):
+        return self.atom_device_error(code_ptr, stream)
 
     def atom_last_error(self, buf, n):
         return 0

@@ -1145,6 +1145,21 @@ __global__ void wait_selftest_kernel(long long budget, int code) {
 }  // namespace tc
 }  // namespace atom
 
+namespace atom {
+namespace tc {
+__global__ void take_error_kernel(int* dst) {
+    *dst = *(volatile int*)&g_tc_error;
+    g_tc_error = 0;
+}
+}  // namespace tc
+}  // namespace atom
+
+extern "C" int atom_device_error_take(int* code_dev, void* stream) {
+    ATOM_REQUIRE(code_dev, "atom_device_error_take: code_dev is NULL");
+    atom::tc::take_error_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(code_dev);
+    return atom::check_launch("atom_device_error_take");
+}
+
 extern "C" int atom_wait_selftest(int64_t budget_cycles, void* stream) {
     if (budget_cycles <= 0 || budget_cycles > atom::tc::kWaitCycles) {
         atom::set_error("atom_wait_selftest: budget_cycles must be in [1, %lld]",

@@ -49,10 +49,23 @@ def to_host(*ts):
     live = [t for t in ts if t is not None]
     if not live:
         return [None] * len(ts)
-    if any(t.is_cuda for t in live):
-        # a GEMM whose bounded wait expired leaves its outputs incomplete: refuse them
-        L.check_device()
-    flat = torch.cat([t.reshape(-1).to(torch.float64) for t in live]).cpu()
+    dev = next((t.device for t in live if t.is_cuda), None)
+    flag = None
+    if dev is not None:
+        # a GEMM whose bounded wait expired leaves its outputs incomplete: its error code is
+        # read back with the results (and cleared) and the results are refused
+        flag = _error_slot(dev)
+        L.call("atom_device_error_take", flag.data_ptr(), L.stream_ptr())
+    parts = [t.reshape(-1).to(torch.float64) for t in live]
+    if flag is not None:
+        parts.append(flag.to(device=parts[0].device, dtype=torch.float64))
+    flat = torch.cat(parts).cpu()
+    if flag is not None:
+        code = int(flat[-1])
+        if code != 0:
+            raise RuntimeError(
+                f"a bounded device-side wait in the tensor-core GEMM expired (code {code}); "
+                "the results of this evaluation are incomplete and were discarded")
     out, o = [], 0
     for t in ts:
         if t is None:
@@ -61,6 +74,17 @@ def to_host(*ts):
         out.append(flat[o:o + t.numel()].reshape(t.shape))
         o += t.numel()
     return out
+
+
+_ERROR_SLOTS = {}
+
+
+def _error_slot(dev):
+    """A one-int device buffer per device for the error code read back with results."""
+    t = _ERROR_SLOTS.get(str(dev))
+    if t is None:
+        t = _ERROR_SLOTS[str(dev)] = torch.zeros(1, dtype=torch.int32, device=dev)
+    return t
 
 
 def upload_positions(ws, pos):
