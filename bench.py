@@ -622,7 +622,7 @@ def run_ours(args):
         out["edge_kernels"] = [dict(k, frac=k["gbs"] / hbm) for k in edge_all]
     if cells != (10, 10, 5):
         out["config"]["workload"] += f" (reduced: {cells} cells, not the headline size)"
-    out["config"]["positions"] = "re-jittered every step (0.01 A)"
+    out["positions"] = "re-jittered every step (0.01 A)"
     # release this workload's buffers and captured graphs before the next measurements
     calc.close()
     del step, ws, eng, pos_dev
