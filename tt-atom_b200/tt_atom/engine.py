@@ -365,21 +365,11 @@ class UMAEngine:
     # ------------------------------------------------------------------------------ helpers
     _scratch = None
 
-    # 3xTF32 engines: launches whose every group has K <= small_k_max run as fp16 pairs (the
-    # same fp32-level accuracy class) when this is set. Short-K launches are bound by loading
-    # their operands (the weight halves dominate), and the fp16 pair halves the weight bytes.
-    small_k_f16 = False
-    small_k_max = 128
-
     def _gemm(self, A, lda, M, groups, Cout, ldc, *, Cpre=None, T1=None, T2=None, idx1=None,
               idx2=None, ldt=0, act=0, accumulate=0, stream=0):
         # the workspace's scratch lets node-level launches (few rows) split K over more CTAs
         sc = self._scratch
         prec = self.precision
-        if (prec == 2 and self.small_k_f16 and sc is not None
-                and max(groups.struct.K[i] for i in range(groups.struct.ngroups))
-                <= self.small_k_max):
-            prec = 3
         if prec == 3:
             groups.ensure_f16()
         call("atom_gemm_ex", ptr(A), lda, M, groups.struct, ptr(Cout), ldc, ptr(Cpre), ptr(T1),
