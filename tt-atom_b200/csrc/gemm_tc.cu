@@ -46,6 +46,9 @@
 #ifndef ATOM_TC_STAGES_1X
 #define ATOM_TC_STAGES_1X 5
 #endif
+#ifndef ATOM_TC_BN128
+#define ATOM_TC_BN128 0
+#endif
 #ifndef ATOM_TC_STAGES_F16
 #define ATOM_TC_STAGES_F16 4
 #endif
@@ -249,6 +252,18 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
         : "memory");
 }
 
+#ifndef ATOM_TC_FAST_SILU
+#define ATOM_TC_FAST_SILU 0
+#endif
+// SiLU of the epilogue (act = 1)
+__device__ __forceinline__ float epi_silu(float x) {
+#if ATOM_TC_FAST_SILU
+    return silu_gate(x);
+#else
+    return silu_f(x);
+#endif
+}
+
 // The gate on four A elements of m-primed row grow: SiLU on row 0, otherwise times the
 // sigmoid of the gating values g[0..3] (silu_gate / sigmoid_gate: the standalone gate kernel's
 // expressions, so the gated operand is bit-identical to that kernel's output).
@@ -298,7 +313,9 @@ struct Cfg {
     static constexpr uint32_t kStage = kTileA + kTileB + (MODE >= 2 ? kTileB : 0);
     static constexpr uint32_t kLoadBytes = kTileA + kTileB * (MODE >= 2 ? 2 : 1);  // TMA bytes
     static constexpr int kStages =
-        MODE == 3 ? ATOM_TC_STAGES_F16 : MODE == 2 ? ATOM_TC_STAGES_3X : ATOM_TC_STAGES_1X;
+        MODE == 3 ? ATOM_TC_STAGES_F16
+                  : MODE == 2 ? (BN <= 128 ? ATOM_TC_STAGES_3X + 1 : ATOM_TC_STAGES_3X)
+                              : ATOM_TC_STAGES_1X;
     // tensor-memory columns of one A slot (hi then lo): fp32 one K element per column, fp16 two
     static constexpr uint32_t kSlotCols = MODE == 3 ? BK : 2 * BK;
     static constexpr int kEpiCols = BN / 2;        // columns per epilogue warp
@@ -750,7 +767,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     const int jj = 4 * q + k;
                                     const float b = (bias && in) ? bias[x0 + jj] : 0.f;
                                     const float y = (v[c0 + jj] + b + t1v[k]) + t2v[k];
-                                    e[k] = silu ? silu_f(y) : y;
+                                    e[k] = silu ? epi_silu(y) : y;
                                 }
                                 buf[lane * 8 + (q ^ (lane & 7))] =
                                     make_float4(e[0], e[1], e[2], e[3]);
@@ -764,7 +781,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     const int jj = 4 * q + k;
                                     const float b = (bias && x0 + jj < N) ? bias[x0 + jj] : 0.f;
                                     const float y = v[c0 + jj] + b;
-                                    e[k] = silu ? silu_f(y) : y;
+                                    e[k] = silu ? epi_silu(y) : y;
                                 }
                                 buf[lane * 8 + (q ^ (lane & 7))] =
                                     make_float4(e[0], e[1], e[2], e[3]);
@@ -808,7 +825,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const long long off = m * p.ldc + ccol + n;
                     if (p.act == 1) {
                         if (p.Cpre) p.Cpre[off] = x;
-                        x = silu_f(x);
+                        x = epi_silu(x);
                     }
                     p.C[off] = p.accumulate ? p.C[off] + x : x;
                 }
@@ -915,7 +932,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ P, int S, long lo
         if (bias) x[k] += bias[n + k];
         if (act == 1) {
             if (Cpre) Cpre[off + k] = x[k];
-            x[k] = silu_f(x[k]);
+            x[k] = epi_silu(x[k]);
         }
         C[off + k] = accumulate ? C[off + k] + x[k] : x[k];
     }
@@ -1107,6 +1124,15 @@ int gemm_tc(const float* A, long long lda, long long M, const atom_gemm_groups* 
     if (precision == 3 && scratch && f16_ready(M, g, scratch_floats))
         return tc::launch<192, 3>(A, lda, M, g, C, ldc, Cpre, T1, T2, idx1, idx2, ldt, act,
                                   accumulate, scratch, scratch_floats, st);
+#if ATOM_TC_BN128
+    // launches whose groups are all at most 128 columns wide: 128-wide tiles (the epilogue
+    // warps split 64 + 64 columns instead of 96 + 32)
+    bool narrow = true;
+    for (int i = 0; i < g->ngroups; ++i) narrow = narrow && g->N[i] <= 128;
+    if (precision == 2 && narrow)
+        return tc::launch<128, 2>(A, lda, M, g, C, ldc, Cpre, T1, T2, idx1, idx2, ldt, act,
+                                  accumulate, scratch, scratch_floats, st);
+#endif
     if (precision >= 2)
         return tc::launch<192, 2>(A, lda, M, g, C, ldc, Cpre, T1, T2, idx1, idx2, ldt, act,
                                   accumulate, scratch, scratch_floats, st);
