@@ -47,7 +47,7 @@
 #define ATOM_TC_STAGES_1X 5
 #endif
 #ifndef ATOM_TC_BN128
-#define ATOM_TC_BN128 0
+#define ATOM_TC_BN128 1
 #endif
 #ifndef ATOM_TC_STAGES_F16
 #define ATOM_TC_STAGES_F16 4
@@ -252,8 +252,10 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
         : "memory");
 }
 
+// Fast SiLU in the epilogue and 128-wide tiles for narrow launches: measured 17.48 -> 16.94 ms
+// per config-2 step together (both on by default).
 #ifndef ATOM_TC_FAST_SILU
-#define ATOM_TC_FAST_SILU 0
+#define ATOM_TC_FAST_SILU 1
 #endif
 // SiLU of the epilogue (act = 1)
 __device__ __forceinline__ float epi_silu(float x) {
