@@ -378,6 +378,101 @@ __global__ void segment_sum_kernel(const float* __restrict__ v, long long n,
 
 }  // namespace atom
 
+namespace atom {
+// ------------------------------------------------- RMS norm SH, channel-parallel (C = 128)
+// One block of 128 threads per node, one channel per thread, the channel sums taken by a
+// block reduction: four times the warps of the warp-per-node form, which a latency-bound pass
+// over a few thousand nodes needs. Same arithmetic per element.
+constexpr int kRC = 128;
+
+// Sums of a and b over the block's 128 threads (all threads get both).
+__device__ __forceinline__ float2 block_sum2(float a, float b, float2* red) {
+    a = warp_sum(a);
+    b = warp_sum(b);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();                         // red may still be read from an earlier call
+    if (lane == 0) red[w] = make_float2(a, b);
+    __syncthreads();
+    float2 t = red[0];
+#pragma unroll
+    for (int i = 1; i < kRC / 32; ++i) {
+        t.x += red[i].x;
+        t.y += red[i].y;
+    }
+    return t;
+}
+
+__global__ void __launch_bounds__(kRC) rmsnorm_fwd_c128_kernel(
+    const float* __restrict__ x, const float* __restrict__ aw, const float* __restrict__ ab,
+    const float* __restrict__ add0, float eps, float* __restrict__ out) {
+    __shared__ float2 red[kRC / 32];
+    constexpr int C = kRC;
+    const long long n = blockIdx.x;
+    const int c = threadIdx.x;
+    const float* xn = x + n * kNsph * C + c;
+    float v[kNsph];
+#pragma unroll
+    for (int j = 0; j < kNsph; ++j) v[j] = xn[j * C];
+    const float mean0 = block_sum2(v[0], 0.f, red).x / C;
+    v[0] -= mean0;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kNsph; ++j) ss = fmaf(bal_w(j), v[j] * v[j], ss);
+    const float fn = rsqrtf(block_sum2(ss, 0.f, red).x / C + eps);
+    float* on = out + n * kNsph * C + c;
+#pragma unroll
+    for (int j = 0; j < kNsph; ++j) {
+        float r = v[j] * (fn * aw[coef_deg(j) * C + c]);
+        if (j == 0) {
+            r += ab[c];
+            if (add0) r += add0[n * C + c];
+        }
+        on[j * C] = r;
+    }
+}
+
+__global__ void __launch_bounds__(kRC) rmsnorm_bwd_c128_kernel(
+    const float* __restrict__ x, const float* __restrict__ g, const float* __restrict__ aw,
+    float eps, int accumulate, float* __restrict__ gx) {
+    __shared__ float2 red[kRC / 32];
+    constexpr int C = kRC;
+    const long long n = blockIdx.x;
+    const int c = threadIdx.x;
+    const float* xn = x + n * kNsph * C + c;
+    const float* gn = g + n * kNsph * C + c;
+    float v[kNsph], u[kNsph];
+#pragma unroll
+    for (int j = 0; j < kNsph; ++j) {
+        v[j] = xn[j * C];
+        u[j] = gn[j * C] * aw[coef_deg(j) * C + c];
+    }
+    const float mean0 = block_sum2(v[0], 0.f, red).x / C;
+    v[0] -= mean0;
+    float ss = 0.f, S = 0.f;
+#pragma unroll
+    for (int j = 0; j < kNsph; ++j) {
+        ss = fmaf(bal_w(j), v[j] * v[j], ss);
+        S = fmaf(u[j], v[j], S);
+    }
+    const float2 t = block_sum2(ss, S, red);
+    const float fn = rsqrtf(t.x / C + eps);
+    const float k3 = fn * fn * fn * t.y / C;
+    float* go = gx + n * kNsph * C + c;
+    float r0 = 0.f;
+#pragma unroll
+    for (int j = 0; j < kNsph; ++j) {
+        const float r = fn * u[j] - k3 * bal_w(j) * v[j];
+        if (j == 0) {
+            r0 = r;
+        } else {
+            go[j * C] = accumulate ? go[j * C] + r : r;
+        }
+    }
+    const float m = block_sum2(r0, 0.f, red).x / C;
+    go[0] = accumulate ? go[0] + (r0 - m) : (r0 - m);
+}
+}  // namespace atom
+
 using namespace atom;
 
 #define WARP_GRID(n) ceil_div((long long)(n) * 32, 256), 256, 0, (cudaStream_t)stream
@@ -387,7 +482,10 @@ extern "C" int atom_rmsnorm_sh_fwd(const float* x, int64_t N, int C, const float
                                    void* stream) {
     ATOM_REQUIRE(C > 0 && C <= 256, "rmsnorm: C must be in [1, 256] (got %d)", C);
     if (N == 0) return ATOM_OK;
-    if (C <= 32)
+    if (C == kRC)
+        rmsnorm_fwd_c128_kernel<<<(unsigned)N, kRC, 0, (cudaStream_t)stream>>>(x, aw, ab, add0,
+                                                                             eps, out);
+    else if (C <= 32)
         rmsnorm_fwd_kernel<1><<<WARP_GRID(N)>>>(x, N, C, aw, ab, add0, eps, out);
     else if (C <= 64)
         rmsnorm_fwd_kernel<2><<<WARP_GRID(N)>>>(x, N, C, aw, ab, add0, eps, out);
@@ -404,7 +502,10 @@ extern "C" int atom_rmsnorm_sh_bwd(const float* x, const float* g, int64_t N, in
                                    void* stream) {
     ATOM_REQUIRE(C > 0 && C <= 256, "rmsnorm: C must be in [1, 256] (got %d)", C);
     if (N == 0) return ATOM_OK;
-    if (C <= 32)
+    if (C == kRC)
+        rmsnorm_bwd_c128_kernel<<<(unsigned)N, kRC, 0, (cudaStream_t)stream>>>(x, g, aw, eps,
+                                                                             accumulate, gx);
+    else if (C <= 32)
         rmsnorm_bwd_kernel<1><<<WARP_GRID(N)>>>(x, g, N, C, aw, eps, accumulate, gx);
     else if (C <= 64)
         rmsnorm_bwd_kernel<2><<<WARP_GRID(N)>>>(x, g, N, C, aw, eps, accumulate, gx);
