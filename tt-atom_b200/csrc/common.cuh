@@ -66,6 +66,11 @@ __device__ __forceinline__ float sigmoid_gate(float x) {
     return __fdividef(1.0f, 1.0f + __expf(-x));
 }
 __device__ __forceinline__ float silu_gate(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+// Its derivative from the same sigmoid (radial LayerNorm + SiLU and the SiLU VJPs).
+__device__ __forceinline__ float dsilu_gate(float x) {
+    const float s = sigmoid_gate(x);
+    return s * (1.0f + x * (1.0f - s));
+}
 // d/dx silu(x) = s (1 + x (1 - s)), s = sigmoid(x)
 __device__ __forceinline__ float dsilu_f(float x) {
     float s = sigmoid_f(x);

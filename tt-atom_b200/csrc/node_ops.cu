@@ -159,7 +159,7 @@ __global__ void ln_silu_fwd_kernel(const float* __restrict__ X, long long rows, 
         v = fmaf(d, d, v);
     }
     float rstd = rsqrtf(warp_sum(v) / W + eps);
-    for (int c = lane; c < W; c += 32) yr[c] = silu_f((xr[c] - mean) * rstd * ga[c] + be[c]);
+    for (int c = lane; c < W; c += 32) yr[c] = silu_gate((xr[c] - mean) * rstd * ga[c] + be[c]);
 }
 
 // Register-resident forms for W = 128 * NV: each lane holds its 4 * NV elements of the row as
@@ -205,7 +205,7 @@ __global__ void ln_silu_fwd_v_kernel(const float* __restrict__ X, long long rows
         float o[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-            o[k] = silu_f((x[i][k] - mean) * rstd * f4get(ga, k) + f4get(be, k));
+            o[k] = silu_gate((x[i][k] - mean) * rstd * f4get(ga, k) + f4get(be, k));
         *reinterpret_cast<float4*>(yr + c) = make_float4(o[0], o[1], o[2], o[3]);
     }
 }
@@ -250,7 +250,7 @@ __global__ void ln_silu_bwd_v_kernel(const float* __restrict__ X, const float* g
         for (int k = 0; k < 4; ++k) {
             x[i][k] = (x[i][k] - mean) * rstd;                     // now x-hat
             const float gk = f4get(ga, k);
-            gy[i][k] = gy[i][k] * dsilu_f(x[i][k] * gk + f4get(be, k)) * gk;
+            gy[i][k] = gy[i][k] * dsilu_gate(x[i][k] * gk + f4get(be, k)) * gk;
             s1 += gy[i][k];
             s2 = fmaf(gy[i][k], x[i][k], s2);
         }
@@ -293,7 +293,7 @@ __global__ void ln_silu_bwd_kernel(const float* __restrict__ X, const float* gY,
     float s1 = 0.f, s2 = 0.f;
     for (int c = lane; c < W; c += 32) {
         float xh = (xr[c] - mean) * rstd;
-        float gy = gr[c] * dsilu_f(xh * ga[c] + be[c]) * ga[c];
+        float gy = gr[c] * dsilu_gate(xh * ga[c] + be[c]) * ga[c];
         s1 += gy;
         s2 = fmaf(gy, xh, s2);
     }
@@ -301,7 +301,7 @@ __global__ void ln_silu_bwd_kernel(const float* __restrict__ X, const float* gY,
     s2 = warp_sum(s2) / W;
     for (int c = lane; c < W; c += 32) {
         float xh = (xr[c] - mean) * rstd;
-        float gy = gr[c] * dsilu_f(xh * ga[c] + be[c]) * ga[c];
+        float gy = gr[c] * dsilu_gate(xh * ga[c] + be[c]) * ga[c];
         dr[c] = rstd * (gy - s1 - xh * s2);
     }
 }
@@ -345,7 +345,7 @@ __global__ void node_project_kernel(const float* __restrict__ in, long long N, i
 __global__ void silu_bwd_kernel(const float* g, const float* __restrict__ pre, long long n,
                                 float* out) {
     long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (t < n) out[t] = g[t] * dsilu_f(pre[t]);
+    if (t < n) out[t] = g[t] * dsilu_gate(pre[t]);
 }
 
 // four elements per thread (16-byte aligned arrays, n a multiple of 4); g and out may alias
@@ -354,8 +354,8 @@ __global__ void silu_bwd4_kernel(const float4* g, const float4* __restrict__ pre
     long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= n4) return;
     const float4 a = g[t], b = pre[t];
-    out[t] = make_float4(a.x * dsilu_f(b.x), a.y * dsilu_f(b.y), a.z * dsilu_f(b.z),
-                         a.w * dsilu_f(b.w));
+    out[t] = make_float4(a.x * dsilu_gate(b.x), a.y * dsilu_gate(b.y), a.z * dsilu_gate(b.z),
+                         a.w * dsilu_gate(b.w));
 }
 
 // Deterministic segmented sum: one 256-thread block per segment, strided partials then a
