@@ -279,8 +279,9 @@ int atom_gemm_gated(const float* Y, int64_t ldy, int64_t M, const atom_gemm_grou
                     int H, float* C, int64_t ldc, int precision, float* scratch,
                     int64_t scratch_floats, void* stream);
 
-/* Reads and clears the device-side error code of the tensor-core kernels (0 = none; a bounded
- * wait expired otherwise). Synchronises `stream`. */
+/* Reads and clears the device-side error code of the tensor-core kernels and the streamed edge
+ * kernels (0 = none; a bounded wait expired otherwise: codes 1-6 tensor-core pipeline waits,
+ * ATOM_WAIT_SELFTEST_CODE, ATOM_EDGE_WAIT_CODE). Synchronises `stream`. */
 int atom_device_error(int* code_host, void* stream);
 
 /* Stream-ordered form of atom_device_error: copies the device-side error code into the device
@@ -295,6 +296,14 @@ int atom_device_error_take(int* code_dev, void* stream);
  * counterpart in the reference (its device waits are not bounded). */
 #define ATOM_WAIT_SELFTEST_CODE 7
 int atom_wait_selftest(int64_t budget_cycles, void* stream);
+
+/* The same for the shared-memory rings of the streamed edge kernels (atom_rotate_in and
+ * atom_rotate_in_bwd_edge at C = 128): one warp runs the rings' bounded wait on a barrier whose
+ * bytes never arrive, for budget_cycles SM clocks (1 .. 2e9), then records
+ * ATOM_EDGE_WAIT_CODE, exactly as an expired wait inside those kernels does (which then also
+ * lets its copies in flight land before returning). No counterpart in the reference. */
+#define ATOM_EDGE_WAIT_CODE 8
+int atom_ring_wait_selftest(int64_t budget_cycles, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Edge-side fused ops of the edgewise block (tt_atom/edgewise.py:39-87, forces.py:352-418).

@@ -80,3 +80,24 @@ def test_expired_wait_makes_calculator_raise_then_recover():
     code = ctypes.c_int(-1)
     _lib.call("atom_device_error", ctypes.byref(code), s_ptr)
     assert code.value == 0
+
+
+@pytest.mark.gpu
+def test_expired_ring_wait_is_reported_and_cleared():
+    """The streamed edge kernels' bounded wait (a barrier whose bytes never arrive) gives up,
+    records ATOM_EDGE_WAIT_CODE, and the context stays usable."""
+    s_ptr = _lib.stream_ptr()
+    code = ctypes.c_int(-1)
+    _lib.call("atom_device_error", ctypes.byref(code), s_ptr)
+    _lib.call("atom_ring_wait_selftest", 2_000_000, s_ptr)
+    _lib.call("atom_device_error", ctypes.byref(code), s_ptr)
+    assert code.value == 8
+    _lib.call("atom_device_error", ctypes.byref(code), s_ptr)
+    assert code.value == 0
+    x = torch.ones(4, device="cuda")
+    assert float((x * 2).sum()) == 8.0
+
+
+def test_ring_wait_selftest_rejects_bad_budget():
+    with pytest.raises(_lib.AtomError):
+        _lib.call("atom_ring_wait_selftest", 0, None)

@@ -15,6 +15,9 @@ namespace atom {
 
 // Thread-local last error message read back through atom_last_error().
 void set_error(const char* fmt, ...);
+// Device address of the library's error word (0 = no error; a kernel whose bounded wait ran out
+// stores its code there with atomicCAS, and atom_device_error_take reads and clears it).
+int* device_error_word();
 
 // Kernels this library has launched (read through atom_launch_count): every launch site is
 // followed by exactly one check_launch, told how many launches it covers.

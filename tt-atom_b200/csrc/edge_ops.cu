@@ -21,6 +21,27 @@
 #ifndef ATOM_RIBE_LEAN
 #define ATOM_RIBE_LEAN 0
 #endif
+// rotate-in VJP (edge part) at C = 128 through the shared-memory ring (see
+// rotate_in_bwd_edge_bulk_kernel): on by default; warps per block and ring depth per warp
+#ifndef ATOM_RIBE_BULK
+#define ATOM_RIBE_BULK 1
+#endif
+#ifndef ATOM_RIBE_BULK_WARPS
+#define ATOM_RIBE_BULK_WARPS 8
+#endif
+#ifndef ATOM_RIBE_BULK_STAGES
+#define ATOM_RIBE_BULK_STAGES 1
+#endif
+// rotate_in at C = 128 through the same kind of ring
+#ifndef ATOM_RIN_BULK
+#define ATOM_RIN_BULK 1
+#endif
+#ifndef ATOM_RIN_BULK_WARPS
+#define ATOM_RIN_BULK_WARPS 8
+#endif
+#ifndef ATOM_RIN_BULK_STAGES
+#define ATOM_RIN_BULK_STAGES 1
+#endif
 
 namespace atom {
 
@@ -579,6 +600,289 @@ __global__ void __launch_bounds__(256, ATOM_RIBE_LEAN_MINB) rotate_in_bwd_edge_l
     if (lane < kNnz - 32) g_coef[e * kNnz + 32 + lane] += tail;
 }
 
+// ------------------------------------------------ per-warp streaming of edge rows (C = 128)
+// Persistent kernels in which every warp walks edges first, first + stride, ... (stride = warps
+// in the grid) with a ring of S slots in shared memory: lane 0 fetches an edge's rows with
+// cp.async.bulk (each row set contiguous in global memory) into a slot as soon as the warp has
+// finished reading the edge that used it, so the next edges' loads are in flight while the
+// warp computes. Outputs go straight to global memory with 512-byte coalesced stores.
+// Every wait on a slot is bounded (kRingWaitCycles of SM clock): on expiry the kernel records
+// ATOM_EDGE_WAIT_CODE in the library's error word, waits (bounded again) for the copies it still
+// has in flight, and the warp returns.
+constexpr int kRingC = 128;
+constexpr uint32_t kRowsX = kNsph * kRingC * 4;          // 4608 bytes: one node's rows
+constexpr uint32_t kRowsE2 = kNsph * 2 * kRingC * 4;     // 9216: an edge row of width 2C
+constexpr uint32_t kRowsRad = 6 * 2 * kRingC * 4;        // 6144: six radial slices of width 2C
+constexpr long long kRingWaitCycles = 2000000000LL;
+
+__device__ __forceinline__ uint32_t sm_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(sm_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait; false when the budget ran out
+__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, long long budget) {
+    const long long t0 = clock64();
+    while (!bar_try(b, parity))
+        if (clock64() - t0 > budget) return false;
+    return true;
+}
+__device__ __forceinline__ void bar_expect(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sm_u32(b)),
+                 "r"(bytes)
+                 : "memory");
+}
+// global -> shared bulk copy (both 16-byte aligned, bytes a multiple of 16), completing on b
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(sm_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(sm_u32(b))
+        : "memory");
+}
+
+// All lanes of a warp: bounded wait for a slot's barrier to complete phase `parity`; on expiry
+// lane 0 records ATOM_EDGE_WAIT_CODE in *err and every lane returns false.
+__device__ __forceinline__ bool ring_wait(uint64_t* b, uint32_t parity, long long budget,
+                                          int* err) {
+    if (__all_sync(0xffffffffu, bar_wait(b, parity, budget))) return true;
+    if ((threadIdx.x & 31) == 0) atomicCAS(err, 0, ATOM_EDGE_WAIT_CODE);
+    __syncwarp();
+    return false;
+}
+
+// Test hook: one warp waits, with the ring's own ring_wait, on a barrier that expects 16 bytes
+// no copy will bring, so the wait runs out after `budget` SM clocks and records its code.
+__global__ void ring_wait_selftest_kernel(long long budget, int* err) {
+    __shared__ uint64_t b;
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&b)));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        bar_expect(&b, 16);
+    }
+    __syncwarp();
+    ring_wait(&b, 0, budget, err);
+}
+
+// The warp's edge loop. pre(e): all lanes, before the wait for edge e's slot (register loads
+// whose latency the wait hides); fetch(e, slot, bar): lane 0, announces and issues edge e's
+// copies; body(e, slot): all lanes, reads the slot; post(e): all lanes, after the slot has been
+// handed to the next fetch (register-only work and stores). Returns false if a wait expired.
+template <int S, class Pre, class Fetch, class Body, class Post>
+__device__ __forceinline__ bool warp_stream(uint8_t* ring, uint64_t* bar, uint32_t slot_bytes,
+                                            long long first, long long stride, long long E,
+                                            int* err, Pre pre, Fetch fetch, Body body, Post post) {
+    const int lane = threadIdx.x & 31;
+    if (lane == 0) {
+        for (int s = 0; s < S; ++s)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&bar[s])));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int k = 0; k < S; ++k)
+            if (first + k * stride < E) fetch(first + k * stride, ring + (size_t)k * slot_bytes, &bar[k]);
+    }
+    __syncwarp();
+    int it = 0;
+    for (long long e = first; e < E; e += stride, ++it) {
+        const int s = it % S;
+        uint8_t* slot = ring + (size_t)s * slot_bytes;
+        pre(e);
+        if (!ring_wait(&bar[s], (uint32_t)(it / S) & 1u, kRingWaitCycles, err)) {
+            // give up: let the copies still in flight land before the warp's shared memory can
+            // be reused
+            if (lane == 0) {
+                for (int k = 0; k < S; ++k) {
+                    const int j = it + k;
+                    if (e + (long long)k * stride < E)
+                        bar_wait(&bar[j % S], (uint32_t)(j / S) & 1u, kRingWaitCycles);
+                }
+            }
+            __syncwarp();
+            return false;
+        }
+        body(e, reinterpret_cast<const float*>(slot));
+        // every lane is done reading the slot: order those reads before the async-proxy
+        // writes of the next fetch into it
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        const long long nxt = e + (long long)S * stride;
+        if (lane == 0 && nxt < E) fetch(nxt, slot, &bar[s]);
+        post(e);
+    }
+    return true;
+}
+
+// Launch shape of a streamed kernel: W warps per block, S slots per warp, one block per SM.
+template <int W, int S>
+struct RingShape {
+    static constexpr int kWarps = W, kStages = S;
+};
+
+// rotate-in VJP (edge part) at C = 128, streamed: the gA row, its six radial slices and the
+// source and target node rows (24 KB per edge) per slot; the arithmetic of
+// rotate_in_bwd_edge_kernel (recomputed rotated rows), so the results are bit-identical.
+// Measured at E = 60,000 (CUDA events): 0.390 -> 0.332 ms per launch (4.80 -> 5.63 TB/s) with
+// 8 warps of one slot per SM (4 x 2: 0.336, 3 x 3: 0.397, 2 x 4: 0.536).
+constexpr uint32_t kRibeSlot = kRowsE2 + kRowsRad + 2 * kRowsX;
+template <int W, int S>
+__global__ void __launch_bounds__(32 * W, 1) rotate_in_bwd_edge_bulk_kernel(
+    const float* __restrict__ gA, const float* __restrict__ rad, long long ldr, int rad_col,
+    const float* __restrict__ x, const int* __restrict__ src, const int* __restrict__ tgt,
+    const float* __restrict__ coef, long long E, float* __restrict__ g_rot,
+    float* __restrict__ g_rad, float* __restrict__ g_coef, int* err) {
+    constexpr int C = kRingC, W2 = 2 * C;
+    extern __shared__ __align__(128) uint8_t ring_smem[];
+    __shared__ uint64_t bars[W][S];
+    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31, c = lane * 4;
+    float wa = 0.f, wb = 0.f;
+    float pc[kNnz];
+    auto pre = [&](long long e) {
+        wa = __ldg(coef + e * kNnz + lane);
+        wb = lane < kNnz - 32 ? __ldg(coef + e * kNnz + 32 + lane) : 0.f;
+    };
+    auto fetch = [&](long long e, uint8_t* slot, uint64_t* b) {
+        const long long ns = __ldg(src + e), nt = __ldg(tgt + e);
+        bar_expect(b, kRibeSlot);
+        bulk_g2s(slot, gA + e * kNsph * W2, kRowsE2, b);
+        bulk_g2s(slot + kRowsE2, rad + e * ldr + rad_col, kRowsRad, b);
+        bulk_g2s(slot + kRowsE2 + kRowsRad, x + ns * kNsph * C, kRowsX, b);
+        bulk_g2s(slot + kRowsE2 + kRowsRad + kRowsX, x + nt * kNsph * C, kRowsX, b);
+    };
+    auto body = [&](long long e, const float* sl) {
+        float w[kNnz];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) w[k] = __shfl_sync(0xffffffffu, wa, k);
+#pragma unroll
+        for (int k = 32; k < kNnz; ++k) w[k] = __shfl_sync(0xffffffffu, wb, k - 32);
+        const float* ga = sl;
+        const float* rr = sl + kNsph * W2;
+        float* gr = g_rot + e * kNsph * W2 + c;
+        float* grd = g_rad + e * ldr + rad_col + c;
+#pragma unroll
+        for (int k = 0; k < kNnz; ++k) pc[k] = 0.f;
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+            const float* xh = sl + kNsph * W2 + 6 * W2 + half * kNsph * C + c;
+            const int ho = half * C + c;
+            float4 v[kNsph];
+#pragma unroll
+            for (int j = 0; j < kNsph; ++j) v[j] = ld4(xh + j * C);
+            float4 gsl[6];
+#pragma unroll
+            for (int q = 0; q < 6; ++q) gsl[q] = f4(0.f);
+#pragma unroll
+            for (int r = 0; r < kNsph; ++r) {
+                const int q = rad_slice(r);
+                const float4 gav = ld4(ga + r * W2 + ho);
+                const float4 g = mul4(gav, ld4(rr + q * W2 + ho));
+                st4(gr + r * W2 + half * C, g);
+                const float4 p = mul4(gav, wrow_rt(w, v, r));
+                gsl[q].x += p.x; gsl[q].y += p.y; gsl[q].z += p.z; gsl[q].w += p.w;
+                const int l = row_deg(r), o = row_off(r), c0 = deg_col0(l);
+#pragma unroll
+                for (int jj = 0; jj < 2 * l + 1; ++jj) pc[o + jj] += dot4(g, v[c0 + jj]);
+            }
+#pragma unroll
+            for (int q = 0; q < 6; ++q) st4(grd + q * W2 + half * C, gsl[q]);
+        }
+    };
+    auto post = [&](long long e) {
+        float tail[3];
+        const float mine = warp_sum35(pc, tail);
+        g_coef[e * kNnz + lane] += mine;
+        if (lane < kNnz - 32) g_coef[e * kNnz + 32 + lane] += tail[lane];
+    };
+    warp_stream<S>(ring_smem + (size_t)wid * S * kRibeSlot, bars[wid], kRibeSlot,
+                   (long long)blockIdx.x * W + wid, (long long)gridDim.x * W, E, err, pre, fetch,
+                   body, post);
+}
+
+// rotate-in at C = 128, streamed: the source and target node rows and the six radial slices
+// (15 KB per edge) per slot; the arithmetic of rotate_in_kernel with rad (bit-identical).
+// Measured at E = 60,000: 0.171 -> 0.160 ms per launch with 8 warps x 1 slot (12 x 1: 0.167,
+// 4 x 3: 0.197). The same ring for rotate_back_bwd (gx and Y rows, 9 KB per edge) measured
+// slower than its lean kernel at 24 warps per SM (0.116 -> 0.126 ms at 12 x 1, 0.160 at 8 x 2)
+// and is not built.
+constexpr uint32_t kRinSlot = 2 * kRowsX + kRowsRad;
+template <int W, int S>
+__global__ void __launch_bounds__(32 * W, 1) rotate_in_bulk_kernel(
+    const float* __restrict__ x, const int* __restrict__ src, const int* __restrict__ tgt,
+    const float* __restrict__ coef, long long E, const float* __restrict__ rad, long long ldr,
+    int rad_col, float* __restrict__ A, int* err) {
+    constexpr int C = kRingC, W2 = 2 * C;
+    extern __shared__ __align__(128) uint8_t ring_smem[];
+    __shared__ uint64_t bars[W][S];
+    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31, c = lane * 4;
+    float wa = 0.f, wb = 0.f;
+    auto pre = [&](long long e) {
+        wa = __ldg(coef + e * kNnz + lane);
+        wb = lane < kNnz - 32 ? __ldg(coef + e * kNnz + 32 + lane) : 0.f;
+    };
+    auto fetch = [&](long long e, uint8_t* slot, uint64_t* b) {
+        const long long ns = __ldg(src + e), nt = __ldg(tgt + e);
+        bar_expect(b, kRinSlot);
+        bulk_g2s(slot, x + ns * kNsph * C, kRowsX, b);
+        bulk_g2s(slot + kRowsX, x + nt * kNsph * C, kRowsX, b);
+        bulk_g2s(slot + 2 * kRowsX, rad + e * ldr + rad_col, kRowsRad, b);
+    };
+    auto body = [&](long long e, const float* sl) {
+        float w[kNnz];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) w[k] = __shfl_sync(0xffffffffu, wa, k);
+#pragma unroll
+        for (int k = 32; k < kNnz; ++k) w[k] = __shfl_sync(0xffffffffu, wb, k - 32);
+        float* rowA = A + e * kNsph * W2 + c;
+        const float* rr = sl + 2 * kNsph * C + c;
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+            const float* xh = sl + half * kNsph * C + c;
+            float4 v[kNsph];
+#pragma unroll
+            for (int j = 0; j < kNsph; ++j) v[j] = ld4(xh + j * C);
+#pragma unroll
+            for (int r = 0; r < kNsph; ++r) {
+                float4 o = wrow_rt(w, v, r);
+                o = mul4(o, ld4(rr + rad_slice(r) * W2 + half * C));
+                st4(rowA + r * W2 + half * C, o);
+            }
+        }
+    };
+    auto post = [](long long) {};
+    warp_stream<S>(ring_smem + (size_t)wid * S * kRinSlot, bars[wid], kRinSlot,
+                   (long long)blockIdx.x * W + wid, (long long)gridDim.x * W, E, err, pre, fetch,
+                   body, post);
+}
+
+// Launch of a streamed kernel: one block of W warps per SM (fewer when there are fewer edges),
+// W * S slots of `slot` bytes of dynamic shared memory (attribute set once per device).
+template <class K, class... Args>
+static int launch_streamed(K kernel, int W, int S, uint32_t slot, long long E, void* stream,
+                           const char* what, bool* attr_set, Args... args) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    ATOM_REQUIRE(dev >= 0 && dev < 64, "%s: device id %d", what, dev);
+    static int sms[64] = {};
+    if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    const size_t smem = (size_t)W * S * slot;
+    if (!attr_set[dev]) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr_set[dev] = true;
+    }
+    int* err = device_error_word();
+    ATOM_REQUIRE(err, "%s: no device error word", what);
+    const long long blocks = (E + W - 1) / W;
+    kernel<<<(unsigned)(blocks < sms[dev] ? blocks : sms[dev]), 32 * W, smem,
+             (cudaStream_t)stream>>>(args..., err);
+    return check_launch(what);
+}
+
 // acc[j] += sum over rows r of degree l(j) of W[r][j - l^2] * g[r]   (Wig^T g)
 __device__ __forceinline__ void wig_t_acc(const float* w, const float4* g, float4* acc) {
     rotate_back_acc(w, g, 1.f, acc);
@@ -772,12 +1076,31 @@ using namespace atom;
 #define WARP_GRID(n) ceil_div((long long)(n) * 32, 256), 256, 0, (cudaStream_t)stream
 #define CP_GRID(n) (unsigned)(n), kCP, 0, (cudaStream_t)stream
 
+extern "C" int atom_ring_wait_selftest(int64_t budget_cycles, void* stream) {
+    ATOM_REQUIRE(budget_cycles > 0 && budget_cycles <= kRingWaitCycles,
+                 "atom_ring_wait_selftest: budget_cycles must be in [1, %lld]", kRingWaitCycles);
+    int* err = device_error_word();
+    ATOM_REQUIRE(err, "atom_ring_wait_selftest: no device error word");
+    ring_wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(budget_cycles, err);
+    ATOM_CHECK_LAUNCH("atom_ring_wait_selftest");
+    return ATOM_OK;
+}
+
 extern "C" int atom_rotate_in(const float* x, const int* src, const int* tgt, const float* coef,
                               int64_t E, int C, const float* rad, int64_t ldr, int rad_col,
                               float* rot, float* A, void* stream) {
     if (int s = check_c(C)) return s;
     ATOM_REQUIRE(!rad || (ldr % 4 == 0 && rad_col % 4 == 0), "rad must be float4-aligned");
     if (E == 0) return ATOM_OK;
+#if ATOM_RIN_BULK
+    if (C == 128 && rad && !rot && aligned16(x) && aligned16(rad)) {
+        constexpr int W = ATOM_RIN_BULK_WARPS, S = ATOM_RIN_BULK_STAGES;
+        static bool attr[64] = {};
+        return launch_streamed(rotate_in_bulk_kernel<W, S>, W, S, kRinSlot, E, stream,
+                               "rotate_in", attr, x, src, tgt, coef, (long long)E, rad,
+                               (long long)ldr, rad_col, A);
+    }
+#endif
     rotate_in_kernel<<<WARP_GRID(E)>>>(x, src, tgt, coef, E, C, rad, ldr, rad_col, rot, A);
     ATOM_CHECK_LAUNCH("rotate_in");
     return ATOM_OK;
@@ -833,6 +1156,16 @@ extern "C" int atom_rotate_in_bwd_edge(const float* gA, const float* rot, const 
     if (int s = check_c(C)) return s;
     ATOM_REQUIRE(ldr % 4 == 0 && rad_col % 4 == 0, "rad must be float4-aligned");
     if (E == 0) return ATOM_OK;
+#if ATOM_RIBE_BULK
+    // the streamed kernel: C = 128, rows recomputed (rot NULL), every fetched row 16-byte aligned
+    if (C == 128 && !rot && aligned16(gA) && aligned16(rad) && aligned16(x)) {
+        constexpr int W = ATOM_RIBE_BULK_WARPS, S = ATOM_RIBE_BULK_STAGES;
+        static bool attr[64] = {};
+        return launch_streamed(rotate_in_bwd_edge_bulk_kernel<W, S>, W, S, kRibeSlot, E, stream,
+                               "rotate_in_bwd_edge", attr, gA, rad, (long long)ldr, rad_col, x,
+                               src, tgt, coef, (long long)E, g_rot, g_rad, g_coef);
+    }
+#endif
 #if ATOM_RIBE_LEAN
     if (C == 128) {
         rotate_in_bwd_edge_lean_kernel<<<WARP_GRID(E)>>>(gA, rot, rad, ldr, rad_col, x, src, tgt,

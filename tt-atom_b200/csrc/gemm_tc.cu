@@ -1182,6 +1182,18 @@ __global__ void take_error_kernel(int* dst) {
 }  // namespace tc
 }  // namespace atom
 
+int* atom::device_error_word() {
+    static int* addr[64] = {};      // per device of this process
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, atom::g_tc_error) == cudaSuccess)
+            addr[dev] = static_cast<int*>(p);
+    }
+    return addr[dev];
+}
+
 extern "C" int atom_device_error_take(int* code_dev, void* stream) {
     ATOM_REQUIRE(code_dev, "atom_device_error_take: code_dev is NULL");
     atom::tc::take_error_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(code_dev);

@@ -77,6 +77,7 @@ _SIGS = {
     "atom_device_error": (c_void_p, c_void_p),
     "atom_device_error_take": (c_void_p, c_void_p),
     "atom_wait_selftest": (c_int64, c_void_p),
+    "atom_ring_wait_selftest": (c_int64, c_void_p),
     "atom_rotate_in": (c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_int64,
                        c_int, c_void_p, c_void_p, c_void_p),
     "atom_gate_fwd": (c_void_p, c_int64, c_int, c_void_p, c_void_p),
