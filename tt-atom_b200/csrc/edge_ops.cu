@@ -809,7 +809,9 @@ __global__ void __launch_bounds__(32 * W, 1) rotate_in_bwd_edge_bulk_kernel(
 // Measured at E = 60,000: 0.171 -> 0.160 ms per launch with 8 warps x 1 slot (12 x 1: 0.167,
 // 4 x 3: 0.197). The same ring for rotate_back_bwd (gx and Y rows, 9 KB per edge) measured
 // slower than its lean kernel at 24 warps per SM (0.116 -> 0.126 ms at 12 x 1, 0.160 at 8 x 2)
-// and is not built.
+// and is not built; nor is a producer-warp ring for rotate_back_reduce (a node's received rows
+// in chunks of 4-8 edges, 1-3 blocks per SM: 0.068-0.118 ms against 0.063 ms for the
+// block-per-node kernel, whose many resident blocks hide the latency better).
 constexpr uint32_t kRinSlot = 2 * kRowsX + kRowsRad;
 template <int W, int S>
 __global__ void __launch_bounds__(32 * W, 1) rotate_in_bulk_kernel(
