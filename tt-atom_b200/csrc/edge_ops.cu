@@ -27,10 +27,10 @@
 #define ATOM_RIBE_BULK 1
 #endif
 #ifndef ATOM_RIBE_BULK_WARPS
-#define ATOM_RIBE_BULK_WARPS 8
+#define ATOM_RIBE_BULK_WARPS 4
 #endif
 #ifndef ATOM_RIBE_BULK_STAGES
-#define ATOM_RIBE_BULK_STAGES 1
+#define ATOM_RIBE_BULK_STAGES 2
 #endif
 // rotate_in at C = 128 through the same kind of ring
 #ifndef ATOM_RIN_BULK
@@ -728,8 +728,11 @@ struct RingShape {
 // rotate-in VJP (edge part) at C = 128, streamed: the gA row, its six radial slices and the
 // source and target node rows (24 KB per edge) per slot; the arithmetic of
 // rotate_in_bwd_edge_kernel (recomputed rotated rows), so the results are bit-identical.
-// Measured at E = 60,000 (CUDA events): 0.390 -> 0.332 ms per launch (4.80 -> 5.63 TB/s) with
-// 8 warps of one slot per SM (4 x 2: 0.336, 3 x 3: 0.397, 2 x 4: 0.536).
+// The coefficient adjoints accumulated by earlier kernels are read with the coefficients,
+// before the slot wait, so the final read-modify-write is a store. Measured at E = 60,000 (CUDA
+// events): 0.390 -> 0.308 ms per launch (4.80 -> 6.05 TB/s) with 4 warps of two slots per SM
+// (8 x 1: 0.332, 6 x 1: 0.320; before the adjoint prefetch 4 x 2 and 8 x 1 both ~0.332, 3 x 3
+// 0.397, 2 x 4 0.536).
 constexpr uint32_t kRibeSlot = kRowsE2 + kRowsRad + 2 * kRowsX;
 template <int W, int S>
 __global__ void __launch_bounds__(32 * W, 1) rotate_in_bwd_edge_bulk_kernel(
@@ -741,11 +744,15 @@ __global__ void __launch_bounds__(32 * W, 1) rotate_in_bwd_edge_bulk_kernel(
     extern __shared__ __align__(128) uint8_t ring_smem[];
     __shared__ uint64_t bars[W][S];
     const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31, c = lane * 4;
-    float wa = 0.f, wb = 0.f;
+    float wa = 0.f, wb = 0.f, ga0 = 0.f, gb0 = 0.f;
     float pc[kNnz];
     auto pre = [&](long long e) {
+        // this edge's coefficients and the coefficient adjoints accumulated so far, loaded
+        // while the slot's rows are still arriving
         wa = __ldg(coef + e * kNnz + lane);
         wb = lane < kNnz - 32 ? __ldg(coef + e * kNnz + 32 + lane) : 0.f;
+        ga0 = g_coef[e * kNnz + lane];
+        gb0 = lane < kNnz - 32 ? g_coef[e * kNnz + 32 + lane] : 0.f;
     };
     auto fetch = [&](long long e, uint8_t* slot, uint64_t* b) {
         const long long ns = __ldg(src + e), nt = __ldg(tgt + e);
@@ -796,8 +803,8 @@ __global__ void __launch_bounds__(32 * W, 1) rotate_in_bwd_edge_bulk_kernel(
     auto post = [&](long long e) {
         float tail[3];
         const float mine = warp_sum35(pc, tail);
-        g_coef[e * kNnz + lane] += mine;
-        if (lane < kNnz - 32) g_coef[e * kNnz + 32 + lane] += tail[lane];
+        g_coef[e * kNnz + lane] = ga0 + mine;
+        if (lane < kNnz - 32) g_coef[e * kNnz + 32 + lane] = gb0 + tail[lane];
     };
     warp_stream<S>(ring_smem + (size_t)wid * S * kRibeSlot, bars[wid], kRibeSlot,
                    (long long)blockIdx.x * W + wid, (long long)gridDim.x * W, E, err, pre, fetch,
