@@ -37,10 +37,10 @@
 #define ATOM_RIN_BULK 1
 #endif
 #ifndef ATOM_RIN_BULK_WARPS
-#define ATOM_RIN_BULK_WARPS 8
+#define ATOM_RIN_BULK_WARPS 7
 #endif
 #ifndef ATOM_RIN_BULK_STAGES
-#define ATOM_RIN_BULK_STAGES 1
+#define ATOM_RIN_BULK_STAGES 2
 #endif
 
 namespace atom {
@@ -813,10 +813,11 @@ __global__ void __launch_bounds__(32 * W, 1) rotate_in_bwd_edge_bulk_kernel(
 
 // rotate-in at C = 128, streamed: the source and target node rows and the six radial slices
 // (15 KB per edge) per slot; the arithmetic of rotate_in_kernel with rad (bit-identical).
-// Measured at E = 60,000: 0.171 -> 0.160 ms per launch with 8 warps x 1 slot (12 x 1: 0.167,
-// 4 x 3: 0.197). The same ring for rotate_back_bwd (gx and Y rows, 9 KB per edge) measured
+// Measured at E = 60,000: 0.171 -> 0.150 ms per launch (6.27 TB/s) with 7 warps x 2 slots
+// (8 x 1: 0.160, 6 x 2: 0.158, 12 x 1: 0.167, 4 x 2: 0.196, 4 x 3: 0.197). The same ring for rotate_back_bwd (gx and Y rows, 9 KB per edge) measured
 // slower than its lean kernel at 24 warps per SM (0.116 -> 0.126 ms at 12 x 1, 0.160 at 8 x 2)
-// and is not built; nor is a producer-warp ring for rotate_back_reduce (a node's received rows
+// and is not built (reading the lean kernel's adjoints early, as the VJP above does, made it
+// slower too: 0.117 -> 0.127 ms); nor is a producer-warp ring for rotate_back_reduce (a node's received rows
 // in chunks of 4-8 edges, 1-3 blocks per SM: 0.068-0.118 ms against 0.063 ms for the
 // block-per-node kernel, whose many resident blocks hide the latency better).
 constexpr uint32_t kRinSlot = 2 * kRowsX + kRowsRad;
