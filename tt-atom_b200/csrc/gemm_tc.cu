@@ -743,6 +743,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int c0 = 0; c0 < EC; c0 += 32) {
                     const int x0 = ti.n0 + cbase + c0;
                     if (x0 >= N || cbase + c0 >= p.bn) break;
+                    // gathered-table launches: the block's pre-activation values (accumulator +
+                    // bias + the two table rows) formed once, in place, before the staging
+                    // buffer is waited for, so the gathered loads overlap the previous store;
+                    // 16 columns at a time to bound the registers in flight
+                    if (TAB) {
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            // the second half's loads are not hoisted above the first half's use
+                            if (h) asm volatile("" ::: "memory");
+#pragma unroll
+                            for (int qq = 0; qq < 4; ++qq) {
+                                const int q = 4 * h + qq;
+                                // columns x0 + 4q .. + 3 are all inside or all outside the group
+                                // (N is a multiple of 4 on this path)
+                                const bool in = x0 + 4 * q < N;
+                                float4 a1 = make_float4(0.f, 0.f, 0.f, 0.f), a2 = a1;
+                                if (t1row && in) a1 = ldg4(t1row + x0 + 4 * q);
+                                if (t2row && in) a2 = ldg4(t2row + x0 + 4 * q);
+                                const float t1v[4] = {a1.x, a1.y, a1.z, a1.w};
+                                const float t2v[4] = {a2.x, a2.y, a2.z, a2.w};
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) {
+                                    const int jj = 4 * q + k;
+                                    const float b = (bias && in) ? bias[x0 + jj] : 0.f;
+                                    v[c0 + jj] = (v[c0 + jj] + b + t1v[k]) + t2v[k];
+                                }
+                            }
+                        }
+                    }
 #pragma unroll 1
                     for (int pass = 0; pass < 2; ++pass) {
                         // pass 0: pre-activation to Cpre (SiLU launches that keep it)
@@ -752,42 +781,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                             asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
                         __syncwarp();
                         float4* buf = reinterpret_cast<float4*>(mybuf);
-                        if (TAB) {
 #pragma unroll
-                            for (int q = 0; q < 8; ++q) {
-                                // columns x0 + 4q .. + 3 are all inside or all outside the group
-                                // (N is a multiple of 4 on this path)
-                                const bool in = x0 + 4 * q < N;
-                                float4 a1 = make_float4(0.f, 0.f, 0.f, 0.f), a2 = a1;
-                                if (t1row && in) a1 = ldg4(t1row + x0 + 4 * q);
-                                if (t2row && in) a2 = ldg4(t2row + x0 + 4 * q);
-                                const float t1v[4] = {a1.x, a1.y, a1.z, a1.w};
-                                const float t2v[4] = {a2.x, a2.y, a2.z, a2.w};
-                                float e[4];
+                        for (int q = 0; q < 8; ++q) {
+                            float e[4];
 #pragma unroll
-                                for (int k = 0; k < 4; ++k) {
-                                    const int jj = 4 * q + k;
-                                    const float b = (bias && in) ? bias[x0 + jj] : 0.f;
-                                    const float y = (v[c0 + jj] + b + t1v[k]) + t2v[k];
-                                    e[k] = silu ? epi_silu(y) : y;
-                                }
-                                buf[lane * 8 + (q ^ (lane & 7))] =
-                                    make_float4(e[0], e[1], e[2], e[3]);
+                            for (int k = 0; k < 4; ++k) {
+                                // (TAB: bias and table rows already added above)
+                                const int jj = 4 * q + k;
+                                const float b =
+                                    (!TAB && bias && x0 + jj < N) ? bias[x0 + jj] : 0.f;
+                                const float y = TAB ? v[c0 + jj] : v[c0 + jj] + b;
+                                e[k] = silu ? epi_silu(y) : y;
                             }
-                        } else {
-#pragma unroll
-                            for (int q = 0; q < 8; ++q) {
-                                float e[4];
-#pragma unroll
-                                for (int k = 0; k < 4; ++k) {
-                                    const int jj = 4 * q + k;
-                                    const float b = (bias && x0 + jj < N) ? bias[x0 + jj] : 0.f;
-                                    const float y = v[c0 + jj] + b;
-                                    e[k] = silu ? epi_silu(y) : y;
-                                }
-                                buf[lane * 8 + (q ^ (lane & 7))] =
-                                    make_float4(e[0], e[1], e[2], e[3]);
-                            }
+                            buf[lane * 8 + (q ^ (lane & 7))] = make_float4(e[0], e[1], e[2], e[3]);
                         }
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                         __syncwarp();
