@@ -36,6 +36,7 @@
 #include <cuda_fp16.h>
 
 #include <cstring>
+#include <numeric>
 
 #include "common.cuh"
 
@@ -1075,7 +1076,21 @@ static int launch(const float* A, long long lda, long long M, const atom_gemm_gr
         set_error("gemm_tc: too many tiles");
         return ATOM_ERR_ARG;
     }
-    const int grid = (int)(ntiles < nsm ? ntiles : nsm);
+    // Persistent CTAs walk the work items `grid` apart. When grid shares a factor with the
+    // items per row block (column tiles x K splits), a CTA meets the same column tiles in every
+    // round, and a group's narrow last tile then makes some CTAs' share much lighter than
+    // others' (e.g. N = 256 as 192 + 64 with 148 CTAs: the even CTAs get every wide tile). A
+    // grid coprime with that period, a few CTAs short of one per SM at most, rotates each CTA
+    // through the columns.
+    int grid = (int)(ntiles < nsm ? ntiles : nsm);
+    if (ntiles > nsm) {
+        const int period = tiles * ksplit;
+        for (int g = grid; g >= grid - 8 && g > 1; --g)
+            if (std::gcd(g, period) == 1) {
+                grid = g;
+                break;
+            }
+    }
     if (MODE == 3) {
         row_scale_kernel<<<ceil_div(M * 32, 256), 256, 0, st>>>(A, lda, M, p.g, mpad, scratch);
         if (int s = check_launch("gemm_tc row scales")) return s;
