@@ -341,6 +341,98 @@ __global__ void node_project_kernel(const float* __restrict__ in, long long N, i
     }
 }
 
+// The same on four channels per thread (C a multiple of 4, 16-byte aligned rows): one float4
+// per input row, the outputs accumulated over p in the same order (bit-identical results).
+// N = 2,000, C = 128 (CUDA events): 9 -> 42 rows 13.0 -> 11.1 us, 42 -> 9 rows (the kernel
+// below) 12.5 -> 10.8 us.
+template <int PT>
+__global__ void node_project4_kernel(const float* __restrict__ in, long long N, int C,
+                                     const float* __restrict__ M, int Q, int trans,
+                                     int accumulate, float* __restrict__ out) {
+    constexpr int P = PT;
+    extern __shared__ float sm[];   // [Q * P]
+    for (int i = threadIdx.x; i < Q * P; i += blockDim.x) {
+        int q = i / P, p = i - q * P;
+        sm[i] = trans ? M[p * Q + q] : M[q * P + p];
+    }
+    __syncthreads();
+    const int C4 = C >> 2;
+    long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= N * C4) return;
+    long long n = t / C4;
+    int c = (int)(t - n * C4) * 4;
+    const float* xin = in + n * (long long)P * C + c;
+    float* o = out + n * (long long)Q * C + c;
+    float4 v[P];
+#pragma unroll
+    for (int p = 0; p < P; ++p) v[p] = *reinterpret_cast<const float4*>(xin + (long long)p * C);
+    for (int q = 0; q < Q; ++q) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        const float* mr = sm + q * P;
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+            const float m = mr[p];
+            acc.x = fmaf(m, v[p].x, acc.x);
+            acc.y = fmaf(m, v[p].y, acc.y);
+            acc.z = fmaf(m, v[p].z, acc.z);
+            acc.w = fmaf(m, v[p].w, acc.w);
+        }
+        float4* op = reinterpret_cast<float4*>(o + (long long)q * C);
+        if (accumulate) {
+            const float4 b = *op;
+            acc = make_float4(b.x + acc.x, b.y + acc.y, b.z + acc.z, b.w + acc.w);
+        }
+        *op = acc;
+    }
+}
+
+// Many inputs, few outputs (P = 42 grid points -> Q = 9 coefficients): the loop over p is the
+// outer one, with the Q float4 accumulators in registers, so no p row is held; each output
+// still sums over p in ascending order (bit-identical to node_project_kernel).
+template <int P, int Q>
+__global__ void node_project4_pq_kernel(const float* __restrict__ in, long long N, int C,
+                                        const float* __restrict__ M, int trans, int accumulate,
+                                        float* __restrict__ out) {
+    __shared__ float sm[Q * P];
+    for (int i = threadIdx.x; i < Q * P; i += blockDim.x) {
+        int q = i / P, p = i - q * P;
+        sm[i] = trans ? M[p * Q + q] : M[q * P + p];
+    }
+    __syncthreads();
+    const int C4 = C >> 2;
+    long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= N * C4) return;
+    long long n = t / C4;
+    int c = (int)(t - n * C4) * 4;
+    const float* xin = in + n * (long long)P * C + c;
+    float* o = out + n * (long long)Q * C + c;
+    float4 acc[Q];
+#pragma unroll
+    for (int q = 0; q < Q; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 6
+    for (int p = 0; p < P; ++p) {
+        const float4 v = *reinterpret_cast<const float4*>(xin + (long long)p * C);
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+            const float m = sm[q * P + p];
+            acc[q].x = fmaf(m, v.x, acc[q].x);
+            acc[q].y = fmaf(m, v.y, acc[q].y);
+            acc[q].z = fmaf(m, v.z, acc[q].z);
+            acc[q].w = fmaf(m, v.w, acc[q].w);
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+        float4* op = reinterpret_cast<float4*>(o + (long long)q * C);
+        float4 a = acc[q];
+        if (accumulate) {
+            const float4 b = *op;
+            a = make_float4(b.x + a.x, b.y + a.y, b.z + a.z, b.w + a.w);
+        }
+        *op = a;
+    }
+}
+
 // g and out may alias (in-place)
 __global__ void silu_bwd_kernel(const float* g, const float* __restrict__ pre, long long n,
                                 float* out) {
@@ -564,8 +656,14 @@ extern "C" int atom_node_project(const float* in, int64_t N, int P, int C, const
     const unsigned grid = ceil_div(N * C, 128);
     const size_t sh = Q * P * sizeof(float);
     cudaStream_t st = (cudaStream_t)stream;
-    if (P == 9)
+    if (P == 9 && C % 4 == 0 && aligned16(in) && aligned16(out)) {
+        node_project4_kernel<9><<<ceil_div(N * (C / 4), 128), 128, sh, st>>>(in, N, C, M, Q, trans,
+                                                                           accumulate, out);
+    } else if (P == 9)
         node_project_kernel<9><<<grid, 128, sh, st>>>(in, N, P, C, M, Q, trans, accumulate, out);
+    else if (P == 42 && Q == 9 && C % 4 == 0 && aligned16(in) && aligned16(out))
+        node_project4_pq_kernel<42, 9><<<ceil_div(N * (C / 4), 128), 128, 0, st>>>(
+            in, N, C, M, trans, accumulate, out);
     else if (P == 42)
         node_project_kernel<42><<<grid, 128, sh, st>>>(in, N, P, C, M, Q, trans, accumulate, out);
     else
