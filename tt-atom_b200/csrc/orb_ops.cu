@@ -197,6 +197,67 @@ __global__ void rmsnorm_rows_kernel(const float* __restrict__ X, long long ldx, 
     }
 }
 
+// The same for W = 32 NW with the row held in registers: each lane's NW loads are all issued
+// before the reduction (lane l owns columns l, l + 32, ..., as above, so the sums and results
+// are bit-identical). Orb-v3 shape (W = 256): the whole step 6.66 -> 6.61 ms.
+template <int NW>
+__global__ void rmsnorm_rows_r_kernel(const float* __restrict__ X, long long ldx, long long rows,
+                                      const float* __restrict__ w, float eps, float* Y,
+                                      long long ldy, const float* R_in, long long ldr_in,
+                                      float* R_out, long long ldr_out) {
+    constexpr int W = 32 * NW;
+    long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* x = X + row * ldx;
+    float xv[NW];
+#pragma unroll
+    for (int i = 0; i < NW; ++i) xv[i] = x[lane + 32 * i];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) s = fmaf(xv[i], xv[i], s);
+    float inv = rsqrtf(warp_sum(s) / W + eps);
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+        const int c = lane + 32 * i;
+        float y = xv[i] * inv * w[c];
+        if (Y) Y[row * ldy + c] = y;
+        if (R_out) R_out[row * ldr_out + c] = R_in[row * ldr_in + c] + y;
+    }
+}
+
+template <int NW>
+__global__ void rmsnorm_rows_bwd_r_kernel(const float* __restrict__ X, const float* gY,
+                                          long long rows, const float* __restrict__ w, float eps,
+                                          float* dX) {
+    constexpr int W = 32 * NW;
+    long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* x = X + row * (long long)W;
+    const float* g = gY + row * (long long)W;
+    float xv[NW], gv[NW];
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+        xv[i] = x[lane + 32 * i];
+        gv[i] = g[lane + 32 * i];
+    }
+    float s = 0.f, t = 0.f;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+        const int c = lane + 32 * i;
+        s = fmaf(xv[i], xv[i], s);
+        t = fmaf(gv[i] * w[c], xv[i], t);
+    }
+    float inv = rsqrtf(warp_sum(s) / W + eps);
+    float k = inv * inv * inv * warp_sum(t) / W;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+        const int c = lane + 32 * i;
+        dX[row * (long long)W + c] = inv * gv[i] * w[c] - k * xv[i];
+    }
+}
+
 // dX = inv (u - xhat mean(u xhat)), u = gY w, xhat = X inv. dX may alias gY.
 __global__ void rmsnorm_rows_bwd_kernel(const float* __restrict__ X, const float* gY,
                                         long long rows, int W, const float* __restrict__ w,
@@ -479,8 +540,15 @@ extern "C" int atom_rmsnorm_rows(const float* X, int64_t ldx, int64_t rows, int 
     ATOM_REQUIRE(W > 0, "rmsnorm_rows: W must be positive");
     ATOM_REQUIRE(!R_out || R_in, "rmsnorm_rows: R_out needs R_in");
     if (rows == 0) return ATOM_OK;
-    rmsnorm_rows_kernel<<<WARPS(rows)>>>(X, ldx, rows, W, w, eps, Y, ldy, R_in, ldr_in, R_out,
-                                         ldr_out);
+    if (W == 256)
+        rmsnorm_rows_r_kernel<8><<<WARPS(rows)>>>(X, ldx, rows, w, eps, Y, ldy, R_in, ldr_in,
+                                                  R_out, ldr_out);
+    else if (W == 128)
+        rmsnorm_rows_r_kernel<4><<<WARPS(rows)>>>(X, ldx, rows, w, eps, Y, ldy, R_in, ldr_in,
+                                                  R_out, ldr_out);
+    else
+        rmsnorm_rows_kernel<<<WARPS(rows)>>>(X, ldx, rows, W, w, eps, Y, ldy, R_in, ldr_in, R_out,
+                                             ldr_out);
     ATOM_CHECK_LAUNCH("rmsnorm_rows");
     return ATOM_OK;
 }
@@ -489,7 +557,12 @@ extern "C" int atom_rmsnorm_rows_bwd(const float* X, const float* gY, int64_t ro
                                      const float* w, float eps, float* dX, void* stream) {
     ATOM_REQUIRE(W > 0, "rmsnorm_rows_bwd: W must be positive");
     if (rows == 0) return ATOM_OK;
-    rmsnorm_rows_bwd_kernel<<<WARPS(rows)>>>(X, gY, rows, W, w, eps, dX);
+    if (W == 256)
+        rmsnorm_rows_bwd_r_kernel<8><<<WARPS(rows)>>>(X, gY, rows, w, eps, dX);
+    else if (W == 128)
+        rmsnorm_rows_bwd_r_kernel<4><<<WARPS(rows)>>>(X, gY, rows, w, eps, dX);
+    else
+        rmsnorm_rows_bwd_kernel<<<WARPS(rows)>>>(X, gY, rows, W, w, eps, dX);
     ATOM_CHECK_LAUNCH("rmsnorm_rows_bwd");
     return ATOM_OK;
 }
